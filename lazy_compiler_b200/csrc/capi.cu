@@ -1,0 +1,91 @@
+// Library plumbing: version, per-thread error messages, device facts and the
+// library-owned reduction workspace.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "common.cuh"
+
+namespace {
+thread_local char g_message[512] = "";
+thread_local int g_status = LC_OK;
+
+std::mutex g_mutex;
+std::map<std::pair<int, cudaStream_t>, lc::ReduceWorkspace> g_workspaces;
+int g_sms[64] = {0};
+}  // namespace
+
+namespace lc {
+
+int fail(int code, const char *fmt, ...) {
+  va_list args;
+  va_start(args, fmt);
+  vsnprintf(g_message, sizeof(g_message), fmt, args);
+  va_end(args);
+  g_status = code;
+  return code;
+}
+
+int check_cuda(cudaError_t err, const char *what) {
+  if (err == cudaSuccess) return LC_OK;
+  return fail(LC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+}
+
+int check_launch(const char *what) { return check_cuda(cudaGetLastError(), what); }
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (g_sms[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    g_sms[dev] = n;
+  }
+  return g_sms[dev];
+}
+
+int reduce_workspace(cudaStream_t stream, ReduceWorkspace *out) {
+  int dev = 0;
+  if (int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  auto key = std::make_pair(dev, stream);
+  auto it = g_workspaces.find(key);
+  if (it != g_workspaces.end()) {
+    *out = it->second;
+    return LC_OK;
+  }
+  void *mem = nullptr;
+  const size_t bytes = kMaxPartials * sizeof(double) + 256;
+  if (cudaMalloc(&mem, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(LC_ERR_NOMEM, "reduction workspace: cudaMalloc(%zu) failed", bytes);
+  }
+  // synchronous memset: the counter must read zero before any kernel uses it
+  if (int rc = check_cuda(cudaMemset(mem, 0, bytes), "workspace memset")) {
+    cudaFree(mem);
+    return rc;
+  }
+  ReduceWorkspace ws;
+  ws.partials = static_cast<double *>(mem);
+  ws.counter = reinterpret_cast<unsigned int *>(static_cast<char *>(mem) +
+                                                kMaxPartials * sizeof(double));
+  g_workspaces.emplace(key, ws);
+  *out = ws;
+  return LC_OK;
+}
+
+}  // namespace lc
+
+extern "C" int lc_version(void) { return 1 * 10000 + 0 * 100 + 0; }
+
+extern "C" int lc_last_error(char *buf, size_t len) {
+  if (buf && len) {
+    strncpy(buf, g_message, len - 1);
+    buf[len - 1] = '\0';
+  }
+  return g_status;
+}

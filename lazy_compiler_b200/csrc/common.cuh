@@ -1,0 +1,116 @@
+// Shared helpers of liblazyb200.so: status/error reporting, device facts,
+// streaming memory access and block reductions.  sm_100a only.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "lazyb200.h"
+
+namespace lc {
+
+// Records a formatted message for lc_last_error() on this thread and returns code.
+int fail(int code, const char *fmt, ...);
+// Maps a pending launch error (cudaGetLastError) to LC_ERR_CUDA, else LC_OK.
+int check_launch(const char *what);
+// Maps a CUDA status to LC_ERR_CUDA with a message, else LC_OK.
+int check_cuda(cudaError_t err, const char *what);
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+inline bool aligned(const void *p, uintptr_t bytes) {
+  return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) == 0;
+}
+
+// Library-owned reduction workspace, one per (device, stream); created once
+// under a mutex.  `partials` holds kMaxPartials doubles, `counter` one
+// zero-initialised unsigned int that the last block of a reduction resets.
+struct ReduceWorkspace {
+  double *partials;
+  unsigned int *counter;
+};
+constexpr int kMaxPartials = 4096;
+int reduce_workspace(cudaStream_t stream, ReduceWorkspace *out);
+
+// ---------------------------------------------------------------- device side
+
+// 128-bit streaming load that bypasses L1 allocation (read-only data).
+__device__ __forceinline__ float4 ld_stream(const float4 *p) {
+  float4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint4 ld_stream_u4(const void *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+// 128-bit store with the evict-first (streaming) policy.
+__device__ __forceinline__ void st_stream(float4 *p, float4 v) {
+  asm volatile("st.global.cs.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void st_stream_u4(void *p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Error-free transformation (Knuth TwoSum): s + e == a + b exactly.
+struct CompSum {
+  float s = 0.f, c = 0.f;
+  __device__ __forceinline__ void add(float x) {
+    float t = __fadd_rn(s, x);
+    float bp = __fsub_rn(t, s);
+    float e = __fadd_rn(__fsub_rn(s, __fsub_rn(t, bp)), __fsub_rn(x, bp));
+    s = t;
+    c = __fadd_rn(c, e);
+  }
+  __device__ __forceinline__ double value() const { return (double)s + (double)c; }
+};
+
+template <class T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum; every thread receives the total.  `scratch` holds >= 32 T.
+// The combination order is fixed, so results are deterministic.
+template <class T>
+__device__ __forceinline__ T block_sum(T v, T *scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  __syncthreads();  // scratch may still be read by a previous call
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  T t = lane < nwarps ? scratch[lane] : T(0);
+  return warp_sum(t);
+}
+__device__ __forceinline__ float block_max(float v, float *scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = (blockDim.x + 31) >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float t = lane < nwarps ? scratch[lane] : -INFINITY;
+  return warp_max(t);
+}
+
+}  // namespace lc

@@ -1,0 +1,142 @@
+"""ctypes bindings of ``liblazyb200.so`` and the plan launcher.
+
+This is the "thin Python ctypes C-ABI layer" of the drop-in boundary: it
+takes the launch plan printed by ``compile.py`` and a mapping from meta.json
+argument names to device pointers, and calls the C-ABI entry point the plan
+names.  It plays the part of the reference's CUDA-driver launcher
+(tools/check_compiler.py:291-422 ``CudaDriver.run``: module load,
+cuLaunchKernel with `.u64` pointers in ``arg_order``), minus the PTX JIT:
+the kernels are prebuilt for sm_100a.
+
+There is no CPU fallback.  If the library is missing, :func:`library` raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIBRARY_PATH = Path(__file__).resolve().parent / "liblazyb200.so"
+
+LC_F32, LC_F16, LC_BF16 = 0, 1, 2
+DTYPE_CODES = {"f32": LC_F32, "f16": LC_F16, "bf16": LC_BF16}
+EPILOGUES = {"none": 0, "gelu_erf": 1, "gelu_tanh": 2}
+B_LAYOUTS = {"kn": 0, "nk": 1}
+STATUS = {0: "LC_OK", -1: "LC_ERR_INVALID", -2: "LC_ERR_ALIGN", -3: "LC_ERR_CUDA",
+          -4: "LC_ERR_TIMEOUT", -5: "LC_ERR_UNSUPPORTED", -6: "LC_ERR_NOMEM"}
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_INT = ctypes.c_int
+# name -> argument types (all return int status)
+SIGNATURES = {
+    "lc_version": [],
+    "lc_last_error": [ctypes.c_char_p, ctypes.c_size_t],
+    "lc_add_f32": [_P, _P, _P, _I64, _P],
+    "lc_axpb_f32": [_P, _P, _P, _P, _I64, _P],
+    "lc_relumul_f32": [_P, _P, _P, _I64, _P],
+    "lc_gelu": [_INT, _INT, _P, _P, _I64, _P],
+    "lc_sum_f32": [_P, _P, _I64, _P],
+    "lc_mean_f32": [_P, _P, _P, _I64, _P],
+    "lc_sum_partial_f32": [_P, _I64, _P, _P],
+    "lc_sum_finalize": [_P, _P, _P, _P],
+    "lc_rowsum_f32": [_P, _P, _I64, _I64, _P],
+    "lc_rmsnorm_f32": [_P, _P, _P, _P, _P, _I64, _I64, _P],
+    "lc_softmax_f32": [_P, _P, _I64, _I64, _P],
+    "lc_l2norm_f32": [_P, _P, _I64, _I64, _P],
+    "lc_gemm": [_INT, _INT, _INT, _INT, _P, _P, _P, _I64, _I64, _I64, _P],
+    "lc_sdpa_f16": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, ctypes.c_float, _P],
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+class LcError(RuntimeError):
+    """A non-zero status from a C-ABI entry point."""
+
+    def __init__(self, function: str, status: int, message: str):
+        super().__init__(f"{function} returned {STATUS.get(status, status)}: {message}")
+        self.function = function
+        self.status = status
+        self.message = message
+
+
+def library() -> ctypes.CDLL:
+    """Load ``liblazyb200.so`` once and bind every C-ABI signature.
+
+    Raises ``RuntimeError`` when the library has not been built: the kernels
+    are the only implementation.
+    """
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not LIBRARY_PATH.exists():
+                raise RuntimeError(
+                    f"{LIBRARY_PATH.name} is not built; run `python -m lazy_compiler_b200.build` "
+                    "(there is no CPU fallback)")
+            lib = ctypes.CDLL(str(LIBRARY_PATH))
+            for name, args in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = args
+                fn.restype = ctypes.c_int
+            _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(512)
+    library().lc_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def call(name: str, *args) -> None:
+    """Call one entry point and raise :class:`LcError` on a non-zero status."""
+    status = getattr(library(), name)(*args)
+    if status != 0:
+        raise LcError(name, status, last_error())
+
+
+def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
+    """Launch the kernel a ``compile.py`` plan names.
+
+    ``pointers`` maps meta.json argument names to device addresses (ints);
+    ``stream`` is a cudaStream_t handle (``torch.cuda.current_stream().cuda_stream``)
+    or ``None`` for the default stream.
+    """
+    b = plan["bind"]
+    p = plan["params"]
+    ptr = lambda role: ctypes.c_void_p(int(pointers[b[role]]))  # noqa: E731
+    s = ctypes.c_void_p(stream or 0)
+    op = plan["op"]
+    if op == "add_f32":
+        call("lc_add_f32", ptr("x0"), ptr("x1"), ptr("out"), p["n"], s)
+    elif op == "axpb_f32":
+        call("lc_axpb_f32", ptr("a"), ptr("b"), ptr("x"), ptr("out"), p["n"], s)
+    elif op == "relumul_f32":
+        call("lc_relumul_f32", ptr("x"), ptr("y"), ptr("out"), p["n"], s)
+    elif op == "gelu":
+        call("lc_gelu", DTYPE_CODES[plan["dtypes"]["io"]], 1 if p["approximate"] == "tanh" else 0,
+             ptr("x"), ptr("out"), p["n"], s)
+    elif op == "sum_f32":
+        call("lc_sum_f32", ptr("x"), ptr("out"), p["n"], s)
+    elif op == "mean_f32":
+        call("lc_mean_f32", ptr("x"), ptr("count"), ptr("out"), p["n"], s)
+    elif op == "rowsum_f32":
+        call("lc_rowsum_f32", ptr("x"), ptr("out"), p["rows"], p["cols"], s)
+    elif op == "rmsnorm_f32":
+        call("lc_rmsnorm_f32", ptr("count"), ptr("eps"), ptr("x"), ptr("w"), ptr("out"),
+             p["rows"], p["cols"], s)
+    elif op == "softmax_f32":
+        call("lc_softmax_f32", ptr("x"), ptr("out"), p["rows"], p["cols"], s)
+    elif op == "l2norm_f32":
+        call("lc_l2norm_f32", ptr("x"), ptr("out"), p["rows"], p["cols"], s)
+    elif op == "gemm":
+        d = plan["dtypes"]
+        call("lc_gemm", DTYPE_CODES[d["ab"]], DTYPE_CODES[d["c"]], B_LAYOUTS[p["b_layout"]],
+             EPILOGUES[p["epilogue"]], ptr("a"), ptr("b"), ptr("c"), p["m"], p["n"], p["k"], s)
+    elif op == "sdpa_f16":
+        call("lc_sdpa_f16", ptr("q"), ptr("k"), ptr("v"), ptr("o"), p["bh"], p["s_q"], p["s_kv"],
+             p["d"], ctypes.c_float(p["scale"]), s)
+    else:
+        raise ValueError(f"plan op {op!r} has no C-ABI entry point")

@@ -1,0 +1,148 @@
+"""The drop-in CLI boundary: ``python compile.py kernel.ir.json`` (reference compile.py:8-19)."""
+import json
+import shutil
+import subprocess
+import sys
+
+import pytest
+
+from conftest import ROOT, golden, golden_ir
+from lazy_compiler_b200.compiler import compile_file
+from lazy_compiler_b200.ir import CompileError, load_package, parse_body
+
+CLI = [sys.executable, str(ROOT / "compile.py")]
+
+EXPECTED = {
+    "p00_scalar_add": ("add_f32", {"n": 128}),
+    "p01_vector_add": ("add_f32", {"n": 1024}),
+    "p02_scale_shift": ("axpb_f32", {"n": 4096}),
+    "p03_relu_mul": ("relumul_f32", {"n": 2048}),
+    "r01_array_sum": ("sum_f32", {"n": 1024}),
+    "r02_big_sum": ("sum_f32", {"n": 65536}),
+    "r03_mean": ("mean_f32", {"n": 32768}),
+    "r04_row_sum": ("rowsum_f32", {"rows": 64, "cols": 512}),
+    "f01_rmsnorm": ("rmsnorm_f32", {"rows": 64, "cols": 1024}),
+    "f02_row_softmax": ("softmax_f32", {"rows": 64, "cols": 256}),
+    "f03_l2norm": ("l2norm_f32", {"rows": 64, "cols": 512}),
+    "phase9_gelu_erf_tail": ("gelu", {"n": 4099, "approximate": "none"}),
+    "phase9_gelu_tanh_matrix": ("gelu", {"n": 2603, "approximate": "tanh"}),
+    "phase9_gelu_erf_half": ("gelu", {"n": 1813, "approximate": "none"}),
+    "phase9_gelu_tanh_half": ("gelu", {"n": 1031, "approximate": "tanh"}),
+    "phase9_half_gelu_gemm": ("gemm", {"m": 17, "n": 21, "k": 33, "b_layout": "kn", "epilogue": "gelu_tanh"}),
+    "generated_tensor": ("gemm", {"m": 11, "n": 19, "k": 7, "b_layout": "kn", "epilogue": "none"}),
+}
+
+
+@pytest.mark.parametrize("name", sorted(EXPECTED))
+def test_cli_prints_plan(name):
+    result = subprocess.run(CLI + [str(golden_ir(name))], capture_output=True, text=True, cwd=ROOT)
+    assert result.returncode == 0, result.stderr
+    plan = json.loads(result.stdout)
+    op, params = EXPECTED[name]
+    assert plan["op"] == op
+    assert plan["params"] == params
+    assert plan["format"] == "lazyb200-plan/1"
+    meta = json.loads((golden(name) / "meta.json").read_text())
+    assert plan["arg_order"] == meta["kernels"][0]["arg_order"]
+    assert plan["entry"] == meta["kernels"][0]["entry"]
+    assert set(plan["bind"].values()) <= set(plan["arg_order"])
+
+
+def test_cli_usage_exit_2():
+    result = subprocess.run(CLI, capture_output=True, text=True, cwd=ROOT)
+    assert result.returncode == 2 and result.stdout == ""
+    assert "usage" in result.stderr
+
+
+def test_cli_missing_file_exit_1(tmp_path):
+    result = subprocess.run(CLI + [str(tmp_path / "nope.ir.json")], capture_output=True, text=True, cwd=ROOT)
+    assert result.returncode == 1 and result.stdout == ""
+    assert result.stderr.startswith("compile.py: ")
+
+
+@pytest.mark.parametrize("name", ["a01_attention", "m01_matmul_512", "activation_gelu_f32",
+                                  "fragment_attention_tile_f16"])
+def test_cli_rejects_unsupported_classes_without_output(name):
+    result = subprocess.run(CLI + [str(golden_ir(name))], capture_output=True, text=True, cwd=ROOT)
+    assert result.returncode == 1
+    assert result.stdout == ""
+    assert result.stderr.startswith("compile.py: ")
+
+
+def _copy(name, tmp_path):
+    dst = tmp_path / name
+    shutil.copytree(golden(name), dst)
+    return dst, next(dst.glob("*.ir.json"))
+
+
+def test_meta_entry_must_match_kernel_name(tmp_path):
+    folder, ir = _copy("p01_vector_add", tmp_path)
+    meta = json.loads((folder / "meta.json").read_text())
+    meta["kernels"][0]["entry"] = "k_other"
+    (folder / "meta.json").write_text(json.dumps(meta))
+    with pytest.raises(CompileError, match="no unique kernel entry"):
+        compile_file(ir)
+
+
+def test_arg_order_must_match_node_arguments(tmp_path):
+    folder, ir = _copy("p01_vector_add", tmp_path)
+    meta = json.loads((folder / "meta.json").read_text())
+    meta["kernels"][0]["arg_order"] = meta["kernels"][0]["arg_order"][:-1]
+    (folder / "meta.json").write_text(json.dumps(meta))
+    with pytest.raises(CompileError, match="arg_order"):
+        compile_file(ir)
+
+
+def test_arg_order_permutation_is_honoured(tmp_path):
+    folder, ir = _copy("p03_relu_mul", tmp_path)
+    meta = json.loads((folder / "meta.json").read_text())
+    meta["kernels"][0]["arg_order"] = list(reversed(meta["kernels"][0]["arg_order"]))
+    (folder / "meta.json").write_text(json.dumps(meta))
+    plan = compile_file(ir)
+    assert plan["arg_order"] == meta["kernels"][0]["arg_order"]
+    assert plan["bind"] == {"x": "x", "y": "y", "out": "mul"}
+
+
+def test_unknown_constructor_is_rejected():
+    with pytest.raises(CompileError, match="unsupported IR constructor"):
+        parse_body("Tile(axes=(), body=(Evil(x=1),))")
+    with pytest.raises(CompileError, match="plain name"):
+        parse_body("__import__('os').system('true')")
+    with pytest.raises(CompileError, match="unsupported IR syntax"):
+        parse_body("[x for x in ()]")
+    with pytest.raises(CompileError):
+        parse_body("Tile(axes=(), body=(Load(names=('a',), input=x.y),))")
+
+
+def test_corrupt_ir_is_a_compile_error(tmp_path):
+    folder, ir = _copy("r01_array_sum", tmp_path)
+    ir.write_text(ir.read_text()[:200])
+    with pytest.raises(CompileError, match="invalid JSON"):
+        compile_file(ir)
+
+
+def test_modified_semantics_are_not_misrecognised(tmp_path):
+    """A pointwise body whose op changes (add -> subtract) must be rejected, not run as add."""
+    folder, ir = _copy("p01_vector_add", tmp_path)
+    ir.write_text(ir.read_text().replace("ElementwiseImpl('add')", "ElementwiseImpl('subtract')"))
+    with pytest.raises(CompileError):
+        compile_file(ir)
+
+
+def test_gelu_constant_values_are_checked(tmp_path):
+    folder, ir = _copy("phase9_gelu_erf_tail", tmp_path)
+    meta = json.loads((folder / "meta.json").read_text())
+    for arg in meta["kernels"][0]["args"]:
+        if arg["name"] == "gelu_half":
+            arg["data"] = [0.25]
+    (folder / "meta.json").write_text(json.dumps(meta))
+    with pytest.raises(CompileError, match="GELU constant"):
+        compile_file(ir)
+
+
+def test_package_loader_reads_buffers():
+    pkg = load_package(golden_ir("f01_rmsnorm"))
+    assert pkg.entry == "k_mean_cbd1de"
+    assert pkg.buffers["x"].shape == (64, 1024)
+    assert pkg.buffers["mean_count"].role == "constant"
+    assert pkg.rtol == 1e-3

@@ -1,0 +1,282 @@
+"""GPU parity of the memory-bound kernels against the oracle and the reference's golden vectors.
+
+Everything here calls the CUDA kernels through the C ABI (``runtime.call`` /
+``runner.run_package``).  Tolerances: bit-exact for add / scale-shift /
+relu*mul (explicit-rounding f32 arithmetic, like numpy float32), relative
+1e-5 for reductions and norms against the float64 oracle, the package's own
+rtol/atol for golden packages.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import golden, golden_meta
+from lazy_compiler_b200 import runtime
+from lazy_compiler_b200.runner import run_package
+from oracle import expressions as O
+
+pytestmark = pytest.mark.gpu
+
+F32_RTOL = 1e-5
+
+PACKAGES = ["p00_scalar_add", "p01_vector_add", "p02_scale_shift", "p03_relu_mul",
+            "r01_array_sum", "r02_big_sum", "r03_mean", "r04_row_sum", "f01_rmsnorm",
+            "f02_row_softmax", "f03_l2norm", "phase9_gelu_erf_tail", "phase9_gelu_tanh_matrix",
+            "phase9_gelu_erf_half", "phase9_gelu_tanh_half"]
+
+
+def torch_():
+    import torch
+    return torch
+
+
+def dev(a, dtype=None):
+    torch = torch_()
+    t = torch.as_tensor(np.ascontiguousarray(a))
+    return t.to("cuda", dtype) if dtype is not None else t.to("cuda")
+
+
+def P(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def host(t):
+    torch = torch_()
+    torch.cuda.synchronize()
+    return (t.float() if t.dtype == torch.bfloat16 else t).cpu().numpy()
+
+
+def assert_close(actual, ref, rtol, atol=0.0):
+    row = O.compare(actual, ref, rtol, atol)
+    assert row["pass"], row
+
+
+# ---------------------------------------------------------------- golden packages
+
+@pytest.mark.parametrize("name", PACKAGES)
+def test_golden_package(name, cuda_device):
+    meta = golden_meta(name)
+    out = run_package(golden(name))
+    with np.load(golden(name) / "expected.npz") as z:
+        for key in z.files:
+            assert_close(out[key], z[key], meta["rtol"], meta["atol"])
+
+
+@pytest.mark.parametrize("name", PACKAGES)
+@pytest.mark.parametrize("offset", [1, 7])
+def test_package_alternate_seeds_against_oracle(name, offset, cuda_device):
+    """Alternate seeds (the reference harness's seed_offset), checked against the oracle."""
+    from lazy_compiler_b200.compiler import compile_file
+    from conftest import golden_ir
+    meta = golden_meta(name)
+    plan = compile_file(golden_ir(name))
+    args = {a["name"]: a for a in meta["kernels"][0]["args"] if not a.get("output")}
+    arrays = {n: O.input_array(a, offset) for n, a in args.items()}
+    ref = O.evaluate(plan, arrays)
+    out = run_package(golden(name), seed_offset=offset)
+    for key, value in ref.items():
+        assert_close(out[key], value, meta["rtol"], meta["atol"])
+
+
+# ---------------------------------------------------------------- pointwise edge cases
+
+SIZES = [1, 3, 4, 5, 255, 1023, 4099, (1 << 20) + 3]
+
+
+@pytest.mark.parametrize("n", SIZES + [0])
+@pytest.mark.parametrize("offset", [0, 1])
+def test_pointwise_exact(n, offset, cuda_device):
+    """add, scale-shift and relu*mul are bit-identical to numpy float32; offset 1 = unaligned."""
+    rng = np.random.default_rng(n + 11)
+    x = rng.standard_normal(n + offset).astype(np.float32)
+    y = rng.standard_normal(n + offset).astype(np.float32)
+    tx, ty = dev(x), dev(y)
+    xs, ys = tx[offset:], ty[offset:]
+    out = dev(np.full(n + offset, np.nan, np.float32))[offset:]
+    a, b = dev(np.float32([1.5])), dev(np.float32([-0.25]))
+    runtime.call("lc_add_f32", P(xs), P(ys), P(out), n, None)
+    np.testing.assert_array_equal(host(out), x[offset:] + y[offset:])
+    runtime.call("lc_axpb_f32", P(a), P(b), P(xs), P(out), n, None)
+    np.testing.assert_array_equal(host(out), O.axpb(1.5, -0.25, x[offset:])[0])
+    runtime.call("lc_relumul_f32", P(xs), P(ys), P(out), n, None)
+    np.testing.assert_array_equal(host(out), O.relumul(x[offset:], y[offset:])[0])
+
+
+@pytest.mark.parametrize("approx", ["none", "tanh"])
+@pytest.mark.parametrize("kind", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("n", [1, 7, 8, 9, 273, 4099])
+def test_gelu_sizes(approx, kind, n, cuda_device):
+    torch = torch_()
+    x = np.random.default_rng(n).uniform(-7, 7, n).astype(np.float32)
+    tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[kind]
+    tx = dev(x, tdt)
+    out = torch.full_like(tx, float("nan"))
+    code = runtime.DTYPE_CODES[kind]
+    runtime.call("lc_gelu", code, 1 if approx == "tanh" else 0, P(tx), P(out), n, None)
+    ref = O.gelu(x, approx, kind)
+    rtol = {"f32": 1e-5, "f16": 1e-3, "bf16": 8e-3}[kind]
+    assert_close(host(out), ref, rtol, 2e-6)
+
+
+def test_gelu_finite_sweep_matches_typed_fixtures(cuda_device):
+    """The reference's typed GELU fixtures (activation_gelu_*), checked through the C ABI."""
+    torch = torch_()
+    x = O.gelu_finite_inputs()
+    for approx in ("none", "tanh"):
+        for kind, rtol in (("f32", 1e-5), ("f16", 1e-3), ("bf16", 8e-3)):
+            name = f"activation_gelu{'_tanh' if approx == 'tanh' else ''}_{kind}"
+            meta = golden_meta(name)
+            tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[kind]
+            tx = dev(x, tdt)
+            out = torch.empty_like(tx)
+            runtime.call("lc_gelu", runtime.DTYPE_CODES[kind], int(approx == "tanh"), P(tx), P(out),
+                         x.size, None)
+            y = host(out)
+            with np.load(golden(name) / "expected.npz") as z:
+                for col in range(2):
+                    assert_close(y, z["out"][:, col], meta["rtol"], meta["atol"])
+
+
+@pytest.mark.parametrize("approx", ["none", "tanh"])
+def test_gelu_exceptional_values(approx, cuda_device):
+    """NaN/inf/-0/subnormal classification equals the reference's golden flags."""
+    torch = torch_()
+    x = O.exceptional_inputs()
+    name = f"activation_gelu{'_tanh' if approx == 'tanh' else ''}_special"
+    flags = []
+    for kind in ("f32", "f16", "bf16"):
+        tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[kind]
+        tx = dev(x, tdt) if kind == "f32" else dev(x).to(tdt)
+        out = torch.empty_like(tx)
+        runtime.call("lc_gelu", runtime.DTYPE_CODES[kind], int(approx == "tanh"), P(tx), P(out),
+                     x.size, None)
+        flags.append(O.classify(host(out)))
+    got = np.concatenate(flags, axis=1)
+    with np.load(golden(name) / "expected.npz") as z:
+        np.testing.assert_array_equal(got, z["out"])
+
+
+# ---------------------------------------------------------------- reductions
+
+@pytest.mark.parametrize("n", [0, 1, 7, 1024, 65536, 1000003, 1 << 24])
+def test_sum_and_mean(n, cuda_device):
+    x = O.uniform(n, seed=0)
+    tx = dev(x)
+    out = dev(np.float32([np.nan]))
+    runtime.call("lc_sum_f32", P(tx), P(out), n, None)
+    ref = O.sum_(x)[0]
+    assert_close(host(out)[0], ref, F32_RTOL, 1e-30)
+    if n:
+        count = dev(np.float32([n]))
+        runtime.call("lc_mean_f32", P(tx), P(count), P(out), n, None)
+        assert_close(host(out)[0], O.mean(x)[0], F32_RTOL, 1e-30)
+
+
+def test_sum_config_is_deterministic_and_offset_safe(cuda_device):
+    n = 1 << 24
+    x = O.uniform(n + 1, seed=3)
+    tx = dev(x)
+    out = dev(np.zeros(4, np.float32))
+    values = set()
+    for _ in range(3):
+        runtime.call("lc_sum_f32", P(tx), P(out), n, None)
+        values.add(host(out)[0].tobytes())
+    assert len(values) == 1
+    # unaligned start (scalar path) agrees with the oracle as well
+    runtime.call("lc_sum_f32", P(tx[1:]), P(out), n, None)
+    assert_close(host(out)[0], O.sum_(x[1:])[0], F32_RTOL, 1e-30)
+
+
+def test_sum_partial_and_finalize(cuda_device):
+    torch = torch_()
+    x = O.uniform(100003, seed=5)
+    tx = dev(x)
+    parts = torch.zeros(2, dtype=torch.float64, device="cuda")
+    runtime.call("lc_sum_partial_f32", P(tx), 60000, P(parts[0:]), None)
+    runtime.call("lc_sum_partial_f32", P(tx[60000:]), 100003 - 60000, P(parts[1:]), None)
+    total = parts.sum().reshape(1)
+    out = torch.zeros(1, dtype=torch.float32, device="cuda")
+    runtime.call("lc_sum_finalize", P(total), ctypes.c_void_p(0), P(out), None)
+    assert_close(host(out)[0], O.sum_(x)[0], F32_RTOL, 1e-30)
+    count = dev(np.float32([100003]))
+    runtime.call("lc_sum_finalize", P(total), P(count), P(out), None)
+    assert_close(host(out)[0], O.mean(x)[0], F32_RTOL, 1e-30)
+
+
+# ---------------------------------------------------------------- rows
+
+ROW_SHAPES = [(1, 1), (3, 5), (2, 4), (64, 256), (64, 1024), (7, 4100), (5, 4096), (3, 32768),
+              (2, 40000), (1, 33)]
+
+
+@pytest.mark.parametrize("rows,cols", ROW_SHAPES)
+def test_row_ops(rows, cols, cuda_device):
+    torch = torch_()
+    x = O.normal((rows, cols), seed=rows * 7 + cols)
+    w = O.normal((cols,), seed=1, mean=1.0, std=0.1)
+    tx, tw = dev(x), dev(w)
+    out = torch.full_like(tx, float("nan"))
+    rs = torch.full((rows,), float("nan"), device="cuda")
+    count, eps = dev(np.float32([cols])), dev(np.float32([1e-6]))
+    runtime.call("lc_rowsum_f32", P(tx), P(rs), rows, cols, None)
+    assert_close(host(rs), O.rowsum(x)[0], F32_RTOL, 1e-30)
+    runtime.call("lc_rmsnorm_f32", P(count), P(eps), P(tx), P(tw), P(out), rows, cols, None)
+    assert_close(host(out), O.rmsnorm(x, w, 1e-6)[0], F32_RTOL, 1e-30)
+    runtime.call("lc_softmax_f32", P(tx), P(out), rows, cols, None)
+    assert_close(host(out), O.softmax(x)[0], F32_RTOL, 1e-30)
+    runtime.call("lc_l2norm_f32", P(tx), P(out), rows, cols, None)
+    assert_close(host(out), O.l2norm(x)[0], F32_RTOL, 1e-30)
+
+
+def test_row_ops_config_size(cuda_device):
+    """X[16384, 4096] N(0,1), w ~ N(1, 0.1), eps 1e-6: the rows configuration, full size."""
+    torch = torch_()
+    rows, cols = 16384, 4096
+    x = O.normal((rows, cols), seed=0)
+    w = O.normal((cols,), seed=1, mean=1.0, std=0.1)
+    tx, tw = dev(x), dev(w)
+    out = torch.empty_like(tx)
+    rs = torch.empty(rows, device="cuda")
+    count, eps = dev(np.float32([cols])), dev(np.float32([1e-6]))
+    runtime.call("lc_rowsum_f32", P(tx), P(rs), rows, cols, None)
+    assert_close(host(rs), O.rowsum(x)[0], F32_RTOL, 1e-30)
+    runtime.call("lc_rmsnorm_f32", P(count), P(eps), P(tx), P(tw), P(out), rows, cols, None)
+    assert_close(host(out), O.rmsnorm(x, w, 1e-6)[0], F32_RTOL, 1e-30)
+    runtime.call("lc_softmax_f32", P(tx), P(out), rows, cols, None)
+    assert_close(host(out), O.softmax(x)[0], F32_RTOL, 1e-30)
+    runtime.call("lc_l2norm_f32", P(tx), P(out), rows, cols, None)
+    assert_close(host(out), O.l2norm(x)[0], F32_RTOL, 1e-30)
+
+
+def test_row_offset_rows_use_scalar_path(cuda_device):
+    torch = torch_()
+    x = O.normal((9, 257), seed=2)
+    tx = dev(x)
+    out = torch.empty_like(tx)
+    runtime.call("lc_softmax_f32", P(tx), P(out), 9, 257, None)
+    assert_close(host(out), O.softmax(x)[0], F32_RTOL, 1e-30)
+
+
+# ---------------------------------------------------------------- full-size elementwise
+
+def test_elementwise_config_size_sampled(cuda_device):
+    """2^28 elements: exact ops checked in full, GELU on a seeded sample of 2^20 positions."""
+    torch = torch_()
+    n = 1 << 28
+    g = torch.Generator(device="cuda").manual_seed(0)
+    tx = torch.randn(n, device="cuda", generator=g)
+    ty = torch.randn(n, device="cuda", generator=g)
+    out = torch.empty_like(tx)
+    runtime.call("lc_add_f32", P(tx), P(ty), P(out), n, None)
+    assert torch.equal(out, tx + ty)
+    a, b = dev(np.float32([1.5])), dev(np.float32([-0.25]))
+    runtime.call("lc_axpb_f32", P(a), P(b), P(tx), P(out), n, None)
+    assert torch.equal(out, (tx * 1.5) + (-0.25))
+    runtime.call("lc_relumul_f32", P(tx), P(ty), P(out), n, None)
+    assert torch.equal(out, ty * torch.relu(tx))
+    idx = torch.randint(0, n, (1 << 20,), device="cuda", generator=g)
+    xs = host(tx[idx])
+    for approx in ("none", "tanh"):
+        runtime.call("lc_gelu", 0, int(approx == "tanh"), P(tx), P(out), n, None)
+        assert_close(host(out[idx]), O.gelu(xs, approx, "f32"), 1e-5, 2e-6)
