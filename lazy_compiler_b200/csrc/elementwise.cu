@@ -182,9 +182,9 @@ template <class Op>
 int launch_f32(const char *name, const float *x0, const float *x1, float *out, int64_t n,
                void *stream, Op op) {
   if (n < 0) return fail(LC_ERR_INVALID, "%s: negative length %lld", name, (long long)n);
+  if (n == 0) return LC_OK;  // nothing to touch; empty buffers may be null
   if (!x0 || !out || (Op::kInputs == 2 && !x1))
     return fail(LC_ERR_INVALID, "%s: null buffer", name);
-  if (n == 0) return LC_OK;
   cudaStream_t s = as_stream(stream);
   const bool vec = aligned(x0, 16) && aligned(out, 16) && (Op::kInputs == 1 || aligned(x1, 16));
   if (vec) {
@@ -223,7 +223,7 @@ extern "C" int lc_add_f32(const float *x0, const float *x1, float *out, int64_t 
 
 extern "C" int lc_axpb_f32(const float *a, const float *b, const float *x, float *out,
                            int64_t n, void *stream) {
-  if (!a || !b) return lc::fail(LC_ERR_INVALID, "lc_axpb_f32: null scalar");
+  if (n > 0 && (!a || !b)) return lc::fail(LC_ERR_INVALID, "lc_axpb_f32: null scalar");
   lc::AxpbOp op{a, b, 0.0f, 0.0f};
   return lc::launch_f32("lc_axpb_f32", x, nullptr, out, n, stream, op);
 }
@@ -238,8 +238,8 @@ extern "C" int lc_gelu(int dtype, int approximate, const void *x, void *out, int
   if (approximate != 0 && approximate != 1)
     return lc::fail(LC_ERR_INVALID, "lc_gelu: approximate must be 0 (erf) or 1 (tanh)");
   if (n < 0) return lc::fail(LC_ERR_INVALID, "lc_gelu: negative length");
-  if (!x || !out) return lc::fail(LC_ERR_INVALID, "lc_gelu: null buffer");
   if (n == 0) return LC_OK;
+  if (!x || !out) return lc::fail(LC_ERR_INVALID, "lc_gelu: null buffer");
   switch (dtype) {
     case LC_F32: {
       if (approximate)

@@ -98,7 +98,7 @@ __global__ void finalize_kernel(const double *__restrict__ total, const float *_
 
 int launch_sum(const char *name, const float *x, int64_t n, int mode, const float *count,
                float *out, double *partial_out, void *stream) {
-  if (!x || n < 0) return fail(LC_ERR_INVALID, "%s: null input or negative length", name);
+  if (n < 0 || (!x && n > 0)) return fail(LC_ERR_INVALID, "%s: null input or negative length", name);
   if (mode < 2 && !out) return fail(LC_ERR_INVALID, "%s: null output", name);
   if (mode == 1 && !count) return fail(LC_ERR_INVALID, "%s: null count", name);
   if (mode == 2 && !partial_out) return fail(LC_ERR_INVALID, "%s: null partial", name);
