@@ -49,7 +49,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["elementwise", "reduce", "rows"], default="elementwise")
+    ap.add_argument("--config", choices=["elementwise", "reduce", "rows", "gemm_f16", "gemm_bf16"],
+                    default="elementwise")
     ap.add_argument("--no-suite", action="store_true", help="skip the secondary configurations")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
@@ -60,12 +61,27 @@ def parse_args():
 
 # ---------------------------------------------------------------- environment
 
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
 def peaks():
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         data = json.loads(path.read_text())
         return float(data["hbm_gbs"]), "measured"
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def tensor_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["bf16_tflops"]), float(data.get("bf16_tflops_sustained", 0)) or None, "measured"
+    return FALLBACK_BF16_TFLOPS, 1400.0, "fallback"
+
+
+SUITE = ("reduce", "rows", "elementwise")
+GEMM_SHAPES = {"gemm_f16": ("f16", 8192, 8192, 8192), "gemm_bf16": ("bf16", 4096, 16384, 2048)}
 
 
 def traffic_table():
@@ -233,6 +249,14 @@ def timed_steps(dist, ops, steps, warmup, flush=None):
 
 def roofline(ops, per_op_ms, peak, peak_kind, traffic):
     name, nbytes, _ = max(ops, key=lambda o: per_op_ms[o[0]])
+    if name.startswith("gemm") or name.startswith("sdpa"):
+        tpeak, sustained, kind = tensor_peak()
+        achieved = nbytes / (per_op_ms[name] / 1e3) / 1e12
+        return {"bound": "tensor", "kernel": name, "achieved": round(achieved, 1), "peak": tpeak,
+                "peak_kind": f"bf16_tflops burst of {kind}", "unit": "TFLOP/s",
+                "frac": round(achieved / tpeak, 4),
+                "frac_of_sustained": round(achieved / sustained, 4) if sustained else None,
+                "traffic": traffic.get(name), "algorithmic_flops": nbytes}
     achieved = nbytes / (per_op_ms[name] / 1e3) / 1e9
     return {"bound": "hbm", "kernel": name, "achieved": round(achieved, 1), "peak": peak,
             "peak_kind": f"hbm_gbs of {peak_kind}", "unit": "GB/s", "frac": round(achieved / peak, 4),
@@ -305,6 +329,19 @@ def run_ours(args):
             cfg = {"workload": "RMSNorm, softmax, L2 norm, row sums of X[16384,4096] fp32 per GPU",
                    "rows": ROWS, "cols": COLS, "l2": "inputs larger than L2 (256 MiB)"}
             return ops, cfg, None, ((x, w), out, rs, count, eps)
+        if config in GEMM_SHAPES:
+            ab, m, n, k = GEMM_SHAPES[config]
+            dt = torch.float16 if ab == "f16" else torch.bfloat16
+            a = (torch.randn(m, k, device=dist.device, generator=g) / k ** 0.5).to(dt)
+            b = (torch.randn(k, n, device=dist.device, generator=g) / k ** 0.5).to(dt)
+            c = torch.empty(m, n, device=dist.device)
+            s = ctypes.c_void_p(stream)
+            code = 1 if ab == "f16" else 2
+            flops = 2 * m * n * k
+            ops = [(f"gemm_{ab}", flops, lambda: runtime.call("lc_gemm", code, 0, 0, 0, P(a), P(b), P(c), m, n, k, s))]
+            cfg = {"workload": f"{ab} GEMM M{m} N{n} K{k}, B row-major [K,N], f32 out, A,B ~ N(0,1/sqrt(K))",
+                   "m": m, "n": n, "k": k, "l2": f"inputs larger than L2 ({(m * k + k * n) * 2 >> 20} MiB)"}
+            return ops, cfg, None, ((a, b), c)
         raise ValueError(config)
 
     def one(config, steps, warmup, with_clocks):
@@ -316,16 +353,19 @@ def run_ours(args):
             clocks = c.summary()
         else:
             seconds, per_op, launches = timed_steps(dist, ops, steps, warmup, flush)
-        total_bytes = sum(o[1] for o in ops) * steps * dist.world
+        total = sum(o[1] for o in ops) * steps * dist.world
+        scale = 1e12 if config in GEMM_SHAPES else 1e9
         return {"ops": ops, "cfg": cfg, "seconds": seconds, "per_op": per_op, "launches": launches,
-                "value": total_bytes / seconds / 1e9, "clocks": clocks, "keep": keep}
+                "value": total / seconds / scale, "unit": "TFLOP/s" if config in GEMM_SHAPES else "GB/s",
+                "clocks": clocks, "keep": keep}
 
     main = one(args.config, args.steps, args.warmup, True)
     line = {
-        "metric": METRIC, "value": round(main["value"], 1), "unit": "GB/s", "n_gpus": dist.world,
+        "metric": METRIC, "value": round(main["value"], 1), "unit": main["unit"], "n_gpus": dist.world,
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(main["seconds"] * 1e3 / args.steps, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": {"gemm_f16": "f16", "gemm_bf16": "bf16"}.get(args.config, "f32"),
         "data": "synthetic (seeded torch generator on device, N(0,1) / U[-1,1] as configured)",
         "config": {**main["cfg"], "parallelism": f"range shards x{dist.world}" if dist.world > 1 else "1 GPU"},
         "roofline": roofline(main["ops"], main["per_op"], peak, peak_kind, traffic),
@@ -338,11 +378,11 @@ def run_ours(args):
     torch.cuda.empty_cache()
     if not args.no_suite:
         suite = {}
-        for config in ("reduce", "rows", "elementwise"):
+        for config in SUITE:
             if config == args.config:
                 continue
             r = one(config, max(5, min(args.steps, 20)), args.warmup, False)
-            suite[config] = {"value": round(r["value"], 1), "unit": "GB/s",
+            suite[config] = {"value": round(r["value"], 1), "unit": r["unit"],
                              "kernels_ms": {k: round(v, 4) for k, v in r["per_op"].items()},
                              "roofline": roofline(r["ops"], r["per_op"], peak, peak_kind, traffic),
                              "config": r["cfg"]}
@@ -383,10 +423,11 @@ def e2e(args, dist, main):
     end.record()
     torch.cuda.synchronize()
     seconds = dist.max(start.elapsed_time(end) / 1e3)
-    nbytes = sum(o[1] for o in ops) * steps * dist.world
+    work = sum(o[1] for o in ops) * steps * dist.world
     h2d = sum(h.numel() * h.element_size() for h in host_in)
     d2h = host_out.numel() * host_out.element_size() * len(ops)
-    return {"value": round(nbytes / seconds / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+    scale = 1e12 if main["unit"] == "TFLOP/s" else 1e9
+    return {"value": round(work / seconds / scale, 3), "unit": main["unit"], "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": steps,
             "path": "ctypes C-ABI calls (lc_*) with pinned host inputs copied in and every result copied out"}
 

@@ -65,6 +65,13 @@ int lc_version(void);
  * truncated to len) and returns its last status code. */
 int lc_last_error(char *buf, size_t len);
 
+/* Synchronises `stream` and reports whether a kernel with bounded device waits
+ * (the tcgen05 GEMM and attention) gave up on a wait since the last call:
+ * LC_OK, or LC_ERR_TIMEOUT (the device error word is then cleared).  No
+ * reference counterpart: the reference's launcher isolates a faulting kernel
+ * in a child process instead (tools/check_compiler.py:425-445). */
+int lc_device_status(void *stream);
+
 /* ---------------------------------------------------------------- pointwise
  * Replace the Tile/Load/Assign/Write lowering of ptx_backend.py:1409-1427,
  * 1574-1642 and `operation` :894-1177 for the pointwise problems. */
@@ -130,6 +137,13 @@ int lc_l2norm_f32(const float *x, float *out, int64_t rows, int64_t cols, void *
  * RegStore m16n8k16 mma.sync lowering with its fused epilogue). */
 int lc_gemm(int ab_dtype, int c_dtype, int b_layout, int epilogue, const void *a,
             const void *b, void *c, int64_t m, int64_t n, int64_t k, void *stream);
+
+/* Which kernel lc_gemm would run for these operands: 1 = tcgen05 (TMA needs
+ * K and, for LC_B_KN, N to be multiples of 8 and 16-byte aligned bases; the
+ * problem must have at least 2^24 multiply-adds), 0 = the SIMT kernel.  Host
+ * only; no reference counterpart. */
+int lc_gemm_path(int ab_dtype, int b_layout, const void *a, const void *b, int64_t m, int64_t n,
+                 int64_t k);
 
 /* O = softmax(scale * Q K^T) V per (batch*head); Q,K,V,O f16 [bh, s, d]
  * row-major, softmax statistics in f32, non-causal.  Replaces the

@@ -15,6 +15,7 @@ thread_local int g_status = LC_OK;
 
 std::mutex g_mutex;
 std::map<std::pair<int, cudaStream_t>, lc::ReduceWorkspace> g_workspaces;
+int *g_error_words[64] = {nullptr};
 int g_sms[64] = {0};
 }  // namespace
 
@@ -78,7 +79,45 @@ int reduce_workspace(cudaStream_t stream, ReduceWorkspace *out) {
   return LC_OK;
 }
 
+int device_error_word(int **out) {
+  int dev = 0;
+  if (int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
+  if (dev < 0 || dev >= 64) return fail(LC_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (!g_error_words[dev]) {
+    void *mem = nullptr;
+    if (cudaMalloc(&mem, 256) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(LC_ERR_NOMEM, "device error word: cudaMalloc failed");
+    }
+    if (int rc = check_cuda(cudaMemset(mem, 0, 256), "error word memset")) {
+      cudaFree(mem);
+      return rc;
+    }
+    g_error_words[dev] = static_cast<int *>(mem);
+  }
+  *out = g_error_words[dev];
+  return LC_OK;
+}
+
 }  // namespace lc
+
+extern "C" int lc_device_status(void *stream) {
+  int *word = nullptr;
+  if (int rc = lc::device_error_word(&word)) return rc;
+  cudaStream_t s = lc::as_stream(stream);
+  if (int rc = lc::check_cuda(cudaStreamSynchronize(s), "lc_device_status: stream")) return rc;
+  int value = 0;
+  if (int rc = lc::check_cuda(cudaMemcpy(&value, word, sizeof(int), cudaMemcpyDeviceToHost),
+                              "lc_device_status: read"))
+    return rc;
+  if (value == 0) return LC_OK;
+  cudaMemset(word, 0, sizeof(int));
+  return lc::fail(LC_ERR_TIMEOUT,
+                  "a bounded device wait gave up (code %d: 1 producer, 2 mma, 3 epilogue, "
+                  "4 softmax, 5 correction)",
+                  value);
+}
 
 extern "C" int lc_version(void) { return 1 * 10000 + 0 * 100 + 0; }
 

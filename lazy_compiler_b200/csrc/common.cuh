@@ -35,6 +35,10 @@ struct ReduceWorkspace {
 constexpr int kMaxPartials = 4096;
 int reduce_workspace(cudaStream_t stream, ReduceWorkspace *out);
 
+// Per-device error word that kernels with bounded waits write when a wait
+// gives up (zero-initialised; read and cleared by lc_device_status).
+int device_error_word(int **out);
+
 // ---------------------------------------------------------------- device side
 
 // 128-bit streaming load that bypasses L1 allocation (read-only data).

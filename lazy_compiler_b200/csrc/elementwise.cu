@@ -13,6 +13,7 @@
 // gelu = (0.5x)(1 + erf(x/sqrt2)), gelu_tanh = (0.5x)(1 + tanh(sqrt(2/pi)(x + 0.044715 x^3)))
 // with CUDA's erff / tanhf; f16/bf16 storage computes in f32 and rounds once.
 #include "common.cuh"
+#include "epilogue.cuh"
 
 namespace lc {
 namespace {
@@ -44,15 +45,6 @@ struct ReluMulOp {  // y * relu(x); argument order (x, y)
   __device__ float operator()(float x, float y) const { return __fmul_rn(y, fmaxf(x, 0.0f)); }
 };
 
-__device__ __forceinline__ float gelu_erf(float x) {
-  const float gate = erff(__fmul_rn(x, 0.70710678118654752440f));
-  return __fmul_rn(__fadd_rn(1.0f, gate), __fmul_rn(0.5f, x));
-}
-__device__ __forceinline__ float gelu_tanh(float x) {
-  const float cube = __fmul_rn(x, __fmul_rn(x, x));
-  const float inner = __fmul_rn(0.79788456080286535588f, __fadd_rn(x, __fmul_rn(0.044715f, cube)));
-  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
-}
 
 template <int TANH>
 struct GeluFixedOp {

@@ -45,6 +45,8 @@ SIGNATURES = {
     "lc_softmax_f32": [_P, _P, _I64, _I64, _P],
     "lc_l2norm_f32": [_P, _P, _I64, _I64, _P],
     "lc_gemm": [_INT, _INT, _INT, _INT, _P, _P, _P, _I64, _I64, _I64, _P],
+    "lc_gemm_path": [_INT, _INT, _P, _P, _I64, _I64, _I64],
+    "lc_device_status": [_P],
     "lc_sdpa_f16": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, ctypes.c_float, _P],
 }
 
