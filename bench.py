@@ -442,13 +442,27 @@ def oracle_lib():
 
 
 def cpu_run(config, sample_scale):
-    """One bounded CPU sample of the configuration; returns (ops list, sample description)."""
+    """One bounded CPU sample of the configuration.
+
+    Returns (ops [(work, fn)], description, threads, unit, keep-alive arrays).
+    """
     import numpy as np
+    rng = np.random.default_rng(0)
+    if config in GEMM_SHAPES:
+        ab, m, n, k = GEMM_SHAPES[config]
+        rows = max(1, m // sample_scale)
+        a = (rng.standard_normal((rows, k)) / np.sqrt(k)).astype(np.float32)
+        b = (rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32)
+        a64, b64 = a.astype(np.float64), b.astype(np.float64)
+        ops = [(2 * rows * n * k, lambda: a64 @ b64)]
+        threads = blas_threads()
+        desc = (f"{rows} of {m} rows of the {ab} GEMM (1/{sample_scale} of a step) in float64 "
+                f"numpy/BLAS, {threads} threads")
+        return ops, desc, threads, "TFLOP/s", (a64, b64)
     lib = oracle_lib()
     threads = lib.oc_threads()
     i64 = ctypes.c_int64
     ptr = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
-    rng = np.random.default_rng(0)
     if config == "elementwise":
         n = N_ELEMENTWISE // sample_scale
         x = rng.standard_normal(n, dtype=np.float32)
@@ -460,11 +474,13 @@ def cpu_run(config, sample_scale):
                (2 * 4 * n, lambda: lib.oc_gelu(0, ptr(x), ptr(out), i64(n))),
                (2 * 4 * n, lambda: lib.oc_gelu(1, ptr(x), ptr(out), i64(n)))]
         desc = f"5 elementwise ops over 2^{(n).bit_length() - 1} fp32 elements each (1/{sample_scale} of a step)"
+        keep = (x, y, out)
     elif config == "reduce":
         n = N_REDUCE
         x = rng.uniform(-1, 1, n).astype(np.float32)
         ops = [(4 * n, lambda: lib.oc_sum(ptr(x), i64(n))), (4 * n, lambda: lib.oc_sum(ptr(x), i64(n)))]
         desc = "sum and mean of 2^24 fp32 (a full step)"
+        keep = (x,)
     else:
         r = ROWS // sample_scale
         x = rng.standard_normal((r, COLS), dtype=np.float32)
@@ -478,7 +494,19 @@ def cpu_run(config, sample_scale):
                (2 * xb, lambda: lib.oc_l2norm(ptr(x), ptr(out), i64(r), i64(COLS))),
                (xb, lambda: lib.oc_rowsum(ptr(x), ptr(rs), i64(r), i64(COLS)))]
         desc = f"4 row ops over {r} x {COLS} fp32 rows (1/{sample_scale} of a step)"
-    return ops, desc, threads, (locals().get("x"), locals().get("y"), locals().get("out"))
+        keep = (x, w, out, rs)
+    return ops, desc, threads, "GB/s", keep
+
+
+def blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        counts = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
+        if counts:
+            return max(counts)
+    except Exception:
+        pass
+    return os.cpu_count() or 1
 
 
 def cpu_time(ops, repeats):
@@ -492,14 +520,18 @@ def cpu_time(ops, repeats):
 
 
 def cpu_baseline(config, sample_scale):
-    ops, desc, threads, keep = cpu_run(config, sample_scale)
+    if config in GEMM_SHAPES:
+        sample_scale = 64
+    ops, desc, threads, unit, keep = cpu_run(config, sample_scale)
     cpu_time(ops, 1)
     times = cpu_time(ops, 3)
-    nbytes = sum(o[0] for o in ops)
-    return {"value": round(nbytes / statistics.median(times) / 1e9, 3), "unit": "GB/s",
+    work = sum(o[0] for o in ops)
+    scale = 1e12 if unit == "TFLOP/s" else 1e9
+    how = ("the reference's float64 numpy matmul oracle" if config in GEMM_SHAPES else
+           f"C restatement of the reference's numpy formula oracle, {threads} POSIX threads")
+    return {"value": round(work / statistics.median(times) / scale, 4), "unit": unit,
             "cores": threads, "kind": "port",
-            "sample": desc + "; C restatement of the reference's numpy formula oracle, "
-                             f"{threads} POSIX threads, median of 3 after 1 warm-up"}
+            "sample": desc + f"; {how}, median of 3 after 1 warm-up"}
 
 
 def run_reference(args):
@@ -507,22 +539,22 @@ def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    scale = 16 if args.config == "elementwise" else (1 if args.config == "reduce" else 4)
-    ops, desc, threads, keep = cpu_run(args.config, scale)
+    scale = {"elementwise": 16, "reduce": 1, "rows": 4}.get(args.config, 64)
+    ops, desc, threads, unit, keep = cpu_run(args.config, scale)
     cpu_time(ops, args.warmup)
     times = cpu_time(ops, args.steps)
-    nbytes = sum(o[0] for o in ops)
-    value = nbytes * args.steps / sum(times) / 1e9
+    work = sum(o[0] for o in ops)
+    value = work * args.steps / sum(times) / (1e12 if unit == "TFLOP/s" else 1e9)
     line = {
-        "metric": METRIC, "impl": "reference", "value": round(value, 3), "unit": "GB/s",
+        "metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(sum(times) * 1e3 / args.steps, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded numpy)",
+        "scaling": "weak", "vs_baseline": None, "data": "synthetic (seeded numpy)",
+        "dtype": {"gemm_f16": "f64 (f16 inputs)", "gemm_bf16": "f64 (bf16 inputs)"}.get(args.config, "f32"),
         "config": {"workload": args.config, "sample": desc},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": desc + "; the reference's numpy formula oracle restated in C, "
-                                          f"{threads} POSIX threads"},
-        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": threads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 

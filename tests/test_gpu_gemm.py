@@ -128,16 +128,6 @@ def test_tcgen05_repeated_calls_are_identical(cuda_device):
     assert torch_().equal(c1, c2)
 
 
-def _sampled_oracle(a64, b64, c, layout, rng, samples=256):
-    m, n = c.shape
-    rows = rng.integers(0, m, samples)
-    cols = rng.integers(0, n, samples)
-    bm = b64 if layout == "kn" else b64.T
-    ref = np.einsum("sk,ks->s", a64[rows], bm[:, cols])
-    got = c[rows, cols].double().cpu().numpy()
-    np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-4 * np.sqrt(np.mean(ref ** 2)))
-
-
 @pytest.mark.parametrize("cfg", [("f16", 8192, 8192, 8192), ("bf16", 4096, 16384, 2048)])
 def test_config_size_against_torch_fp32_and_sampled_oracle(cfg, cuda_device):
     """The GEMM configurations at full size: A,B ~ N(0, 1/sqrt(K)), f32 output."""
@@ -160,8 +150,6 @@ def test_config_size_against_torch_fp32_and_sampled_oracle(cfg, cuda_device):
     rng = np.random.default_rng(0)
     rows = rng.integers(0, m, 64)
     a64 = ta[torch.from_numpy(rows).cuda()].double().cpu().numpy()
-    full_a = np.zeros((m, k))
-    full_a[rows] = a64
     b64 = tb.double().cpu().numpy()
     ref_rows = a64 @ b64
     got = c[torch.from_numpy(rows).cuda()].double().cpu().numpy()
