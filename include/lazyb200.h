@@ -110,6 +110,25 @@ int lc_mean_f32(const float *x, const float *count, float *out, int64_t n, void 
 int lc_sum_partial_f32(const float *x, int64_t n, double *partial, void *stream);
 int lc_sum_finalize(const double *total, const float *count, float *out, void *stream);
 
+/* lc_sum_f32 without any allocation, for callers that cannot let a library
+ * call cudaMalloc: applications whose device memory is owned entirely by
+ * their own allocator (a framework's caching pool, or a service that reserves
+ * the GPU's memory at start-up), and launch paths that must not pay
+ * cudaMalloc's implicit device-wide synchronisation.  No counterpart in the
+ * reference; it is the same kernel as lc_sum_f32 with its per-CTA partials in
+ * a fixed device array of LC_SUM_NOALLOC_SCRATCH_BYTES inside the library
+ * (held on every GPU that loads the library until the process exits).
+ *  - n may be at most LC_SUM_NOALLOC_MAX_N; larger n returns LC_ERR_UNSUPPORTED.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture.
+ *  - All calls share the array: calls that overlap on the GPU (other streams,
+ *    other threads) race and must be serialised by the caller. */
+#define LC_SUM_NOALLOC_MAX_BLOCKS 1024
+#define LC_SUM_NOALLOC_MAX_N (((int64_t)1) << 32)
+#define LC_SUM_NOALLOC_SCRATCH_BYTES (LC_SUM_NOALLOC_MAX_BLOCKS * 8 + 256)
+int lc_sum_f32_noalloc(const float *x, float *out, int64_t n, void *stream);
+
 /* ---------------------------------------------------------------- rows
  * X is [rows, cols] row-major f32.  Replace the Tile[a0, a1_co] two-pass
  * lowering of r04/f01/f02/f03 (one 128-thread CTA per row, re-reading the row

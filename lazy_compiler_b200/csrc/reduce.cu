@@ -15,6 +15,8 @@
 // writes the fp32 result.  The order of every addition is fixed by the grid,
 // so the result is deterministic; the f64 combine makes it the correctly
 // rounded fp32 value of the exact sum in all but tie cases.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace lc {
@@ -123,6 +125,83 @@ int launch_sum(const char *name, const float *x, int64_t n, int mode, const floa
 
 }  // namespace
 }  // namespace lc
+
+// ---------------------------------------------------------------- no-allocation variant
+//
+// lc_sum_f32 keeps its per-CTA partials in a workspace the library creates
+// with cudaMalloc on the first call per (device, stream).  Some callers cannot
+// let a library allocate: applications whose device memory is entirely owned
+// by their own allocator (a framework's caching pool, or a service that
+// reserves the GPU's memory at start-up), and launch paths that must not pay
+// cudaMalloc's implicit device-wide synchronisation.  lc_sum_f32_noalloc runs
+// the same kernel with its scratch in this fixed-size device array instead.
+// Every GPU that loads the library holds the array (LC_SUM_NOALLOC_SCRATCH_BYTES)
+// until the process exits; all calls share it, so calls that overlap on the
+// GPU (different streams, or other threads) race on it.
+namespace {
+static __device__ __align__(256) unsigned char
+    g_sum_noalloc_scratch[LC_SUM_NOALLOC_MAX_BLOCKS * sizeof(double) + 256];
+
+std::mutex g_noalloc_mutex;
+unsigned char *g_noalloc_address[64] = {nullptr};
+
+// Device address of g_sum_noalloc_scratch on the current device.  Host code
+// only sees a host-side stand-in under that name, so the address is looked up
+// once per device (with that device current) and cached.
+int noalloc_scratch(unsigned char **out) {
+  int dev = 0;
+  if (int rc = lc::check_cuda(cudaGetDevice(&dev), "lc_sum_f32_noalloc: cudaGetDevice")) return rc;
+  if (dev < 0 || dev >= 64)
+    return lc::fail(LC_ERR_UNSUPPORTED, "lc_sum_f32_noalloc: device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_address[dev]) {
+    void *ptr = nullptr;
+    if (int rc = lc::check_cuda(cudaGetSymbolAddress(&ptr, g_sum_noalloc_scratch),
+                                "lc_sum_f32_noalloc: cudaGetSymbolAddress"))
+      return rc;
+    g_noalloc_address[dev] = static_cast<unsigned char *>(ptr);
+  }
+  *out = g_noalloc_address[dev];
+  return LC_OK;
+}
+}  // namespace
+
+extern "C" int lc_sum_f32_noalloc(const float *x, float *out, int64_t n, void *stream) {
+  using namespace lc;
+  if (n < 0 || (!x && n > 0) || !out)
+    return fail(LC_ERR_INVALID, "lc_sum_f32_noalloc: null buffer or negative length");
+  if (n > LC_SUM_NOALLOC_MAX_N)
+    return fail(LC_ERR_UNSUPPORTED,
+                "lc_sum_f32_noalloc: n = %lld exceeds the maximum of %lld elements; use lc_sum_f32",
+                (long long)n, (long long)LC_SUM_NOALLOC_MAX_N);
+  unsigned char *scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  double *partials = reinterpret_cast<double *>(scratch);
+  unsigned int *counter =
+      reinterpret_cast<unsigned int *>(scratch + LC_SUM_NOALLOC_MAX_BLOCKS * sizeof(double));
+  cudaStream_t s = as_stream(stream);
+  const bool vec = aligned(x, 16);
+  const int64_t per_block = vec ? (int64_t)kThreads * kUnroll * 4 : (int64_t)kThreads;
+  int64_t blocks = (n + per_block - 1) / per_block;
+  const int64_t cap = (int64_t)sm_count() * kBlocksPerSm;
+  if (blocks > cap) blocks = cap;
+  if (blocks > LC_SUM_NOALLOC_MAX_BLOCKS)
+    return fail(LC_ERR_UNSUPPORTED,
+                "lc_sum_f32_noalloc: this device needs %lld partials, the scratch holds %d",
+                (long long)blocks, LC_SUM_NOALLOC_MAX_BLOCKS);
+  if (blocks < 1) blocks = 1;
+  // the CTA ticket counter must start at zero; the array keeps the last call's contents
+  if (int rc = check_cuda(cudaMemsetAsync(counter, 0, sizeof(unsigned int), s),
+                          "lc_sum_f32_noalloc: clear counter"))
+    return rc;
+  if (vec)
+    sum_kernel<true><<<(int)blocks, kThreads, 0, s>>>(x, n, partials, counter, 0, nullptr, out,
+                                                      nullptr);
+  else
+    sum_kernel<false><<<(int)blocks, kThreads, 0, s>>>(x, n, partials, counter, 0, nullptr, out,
+                                                       nullptr);
+  return check_launch("lc_sum_f32_noalloc");
+}
 
 extern "C" int lc_sum_f32(const float *x, float *out, int64_t n, void *stream) {
   return lc::launch_sum("lc_sum_f32", x, n, 0, nullptr, out, nullptr, stream);

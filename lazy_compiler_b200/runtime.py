@@ -38,6 +38,7 @@ SIGNATURES = {
     "lc_gelu": [_INT, _INT, _P, _P, _I64, _P],
     "lc_sum_f32": [_P, _P, _I64, _P],
     "lc_mean_f32": [_P, _P, _P, _I64, _P],
+    "lc_sum_f32_noalloc": [_P, _P, _I64, _P],
     "lc_sum_partial_f32": [_P, _I64, _P, _P],
     "lc_sum_finalize": [_P, _P, _P, _P],
     "lc_rowsum_f32": [_P, _P, _I64, _I64, _P],
