@@ -49,7 +49,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["elementwise", "reduce", "rows", "gemm_f16", "gemm_bf16"],
+    ap.add_argument("--config", choices=["elementwise", "reduce", "rows", "gemm_f16", "gemm_bf16", "sdpa"],
                     default="elementwise")
     ap.add_argument("--no-suite", action="store_true", help="skip the secondary configurations")
     ap.add_argument("--no-e2e", action="store_true")
@@ -81,6 +81,7 @@ def tensor_peak():
 
 
 SUITE = ("reduce", "rows", "elementwise")
+SDPA_SHAPE = (8 * 16, 4096, 128)
 GEMM_SHAPES = {"gemm_f16": ("f16", 8192, 8192, 8192), "gemm_bf16": ("bf16", 4096, 16384, 2048)}
 
 
@@ -342,6 +343,20 @@ def run_ours(args):
             cfg = {"workload": f"{ab} GEMM M{m} N{n} K{k}, B row-major [K,N], f32 out, A,B ~ N(0,1/sqrt(K))",
                    "m": m, "n": n, "k": k, "l2": f"inputs larger than L2 ({(m * k + k * n) * 2 >> 20} MiB)"}
             return ops, cfg, None, ((a, b), c)
+        if config == "sdpa":
+            bh, sq, d = SDPA_SHAPE
+            q = torch.randn(bh, sq, d, device=dist.device, generator=g).half()
+            k = torch.randn(bh, sq, d, device=dist.device, generator=g).half()
+            v = torch.randn(bh, sq, d, device=dist.device, generator=g).half()
+            o = torch.empty_like(q)
+            s = ctypes.c_void_p(stream)
+            flops = 4 * bh * sq * sq * d
+            scale = ctypes.c_float(d ** -0.5)
+            ops = [("sdpa_f16", flops, lambda: runtime.call("lc_sdpa_f16", P(q), P(k), P(v), P(o), bh, sq, sq, d, scale, s))]
+            cfg = {"workload": "SDPA f16 B8 H16 S4096 D128, scale 1/sqrt(D), non-causal, f32 softmax statistics",
+                   "batch_heads": bh, "seq": sq, "head_dim": d,
+                   "l2": f"inputs larger than L2 ({3 * bh * sq * d * 2 >> 20} MiB)"}
+            return ops, cfg, None, ((q, k, v), o)
         raise ValueError(config)
 
     def one(config, steps, warmup, with_clocks):
@@ -354,9 +369,10 @@ def run_ours(args):
         else:
             seconds, per_op, launches = timed_steps(dist, ops, steps, warmup, flush)
         total = sum(o[1] for o in ops) * steps * dist.world
-        scale = 1e12 if config in GEMM_SHAPES else 1e9
+        tensor = config in GEMM_SHAPES or config == "sdpa"
+        scale = 1e12 if tensor else 1e9
         return {"ops": ops, "cfg": cfg, "seconds": seconds, "per_op": per_op, "launches": launches,
-                "value": total / seconds / scale, "unit": "TFLOP/s" if config in GEMM_SHAPES else "GB/s",
+                "value": total / seconds / scale, "unit": "TFLOP/s" if tensor else "GB/s",
                 "clocks": clocks, "keep": keep}
 
     main = one(args.config, args.steps, args.warmup, True)
@@ -365,7 +381,7 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(main["seconds"] * 1e3 / args.steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": {"gemm_f16": "f16", "gemm_bf16": "bf16"}.get(args.config, "f32"),
+        "dtype": {"gemm_f16": "f16", "gemm_bf16": "bf16", "sdpa": "f16"}.get(args.config, "f32"),
         "data": "synthetic (seeded torch generator on device, N(0,1) / U[-1,1] as configured)",
         "config": {**main["cfg"], "parallelism": f"range shards x{dist.world}" if dist.world > 1 else "1 GPU"},
         "roofline": roofline(main["ops"], main["per_op"], peak, peak_kind, traffic),

@@ -172,6 +172,12 @@ int lc_gemm_path(int ab_dtype, int b_layout, const void *a, const void *b, int64
 int lc_sdpa_f16(const void *q, const void *k, const void *v, void *o, int64_t bh,
                 int64_t s_q, int64_t s_kv, int64_t d, float scale, void *stream);
 
+/* Which kernel lc_sdpa_f16 would run: 1 = tcgen05 (head size 128, 16-byte
+ * aligned bases, at least 128 x 128 scores per head), 0 = the SIMT kernel
+ * (head sizes up to 256).  Host only; no reference counterpart. */
+int lc_sdpa_path(const void *q, const void *k, const void *v, const void *o, int64_t s_q,
+                 int64_t s_kv, int64_t d);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,6 +1,445 @@
-// Fused scaled-dot-product attention (tcgen05) — entry point placeholder.
+// Fused scaled-dot-product attention, f16 in/out, f32 softmax statistics.
+//
+// Replaces the reference's attention lowerings: the scalar per-output-element
+// online softmax of a01/a02 (every thread recomputes a full QK dot per key),
+// and the single 16x16 fragment tile of ptx_tensor.py:459-618 (QK mma.sync,
+// FragmentRowReduce, FragmentApply exp/div, FragmentRepack to f16, PV mma.sync).
+//
+// Here, per CTA, one 128-row query tile of one (batch, head), FlashAttention
+// style on tcgen05:
+//   warp 0     TMA: Q once, then K and V tiles of 128 keys through a 2-stage
+//              ring (3-D tensor maps [bh, s, d] so a ragged tail zero-fills
+//              inside its own head; 128-byte swizzle; no multicast);
+//   warp 1     allocates 512 TMEM columns (two 128x128 f32 S buffers, one
+//              128x128 f32 O accumulator) and one thread issues the MMAs:
+//              S(j+1) = Q K(j+1)^T is issued before O += P(j) V(j), so the
+//              tensor core works on the next scores while the softmax runs;
+//   warps 2-5  softmax: each thread owns one query row (its TMEM lane), loads
+//              the 128 scores, keeps the running max m and sum l in f32,
+//              writes P = 2^(s*scale*log2e - m) as f16 back into TMEM over the
+//              scores (the A operand of the PV MMA is read from TMEM), and
+//              rescales O only when a row max grows by more than 2^8 (the
+//              stale max is exact math: it cancels in O / l); finally O / l is
+//              stored as f16.
+// P is rounded to f16 before the PV product, as the reference's f16 attention
+// tile rounds its normalised weights (FragmentRepack).  Every mbarrier wait is
+// bounded; a wait that gives up writes the device error word.
+// Other head sizes, unaligned bases or tiny problems use a SIMT kernel.
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
-extern "C" int lc_sdpa_f16(const void *, const void *, const void *, void *, int64_t, int64_t,
-                           int64_t, int64_t, float, void *) {
-  return lc::fail(LC_ERR_UNSUPPORTED, "lc_sdpa_f16: not available in this build");
+#include "sm100.cuh"
+
+namespace lc {
+namespace {
+
+using namespace sm100;
+
+constexpr int BQ = 128;
+constexpr int BKV = 128;
+constexpr int HEAD = 128;
+constexpr int CHUNK_BYTES = 128 * 64 * 2;     // 128 rows x 64 columns of f16 (one swizzle span)
+constexpr int TILE_BYTES = 2 * CHUNK_BYTES;   // 128 rows x 128 columns
+constexpr int KV_STAGES = 2;
+constexpr int SMEM_BYTES = TILE_BYTES + KV_STAGES * 2 * TILE_BYTES + 1024;
+constexpr int THREADS = 192;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t O_COL = 256;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct SdpaParams {
+  int s_q, s_kv, n_kv;
+  float scale_log2;
+  __half *o;
+  int *err;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void raise_error(const SdpaParams &p, volatile int *abort, int code) {
+  *abort = 1;
+  atomicCAS(p.err, 0, code);
+}
+
+// One lane waits, the warp agrees on the outcome.
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                          const SdpaParams &p, int code) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) {
+    ok = mbar_wait(bar, parity, abort);
+    if (!ok) raise_error(p, abort, code);
+  }
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    sdpa_tc_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constant__ CUtensorMap tma_k,
+                   const __grid_constant__ CUtensorMap tma_v, SdpaParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *q_s = smem;
+  __shared__ __align__(8) uint64_t q_full;
+  __shared__ __align__(8) uint64_t k_full[KV_STAGES];
+  __shared__ __align__(8) uint64_t v_full[KV_STAGES];
+  __shared__ __align__(8) uint64_t kv_empty[KV_STAGES];
+  __shared__ __align__(8) uint64_t s_full[2];
+  __shared__ __align__(8) uint64_t p_full[2];
+  __shared__ __align__(8) uint64_t o_done;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  volatile int *abort = &abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int q_tile = blockIdx.x;
+  const int bh = blockIdx.y;
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 1);
+    for (int s = 0; s < KV_STAGES; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 4);
+    }
+    mbar_init(&o_done, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tma_q);
+    prefetch_tmap(&tma_k);
+    prefetch_tmap(&tma_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  const int n = p.n_kv;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_expect_tx(&q_full, TILE_BYTES);
+      tma_load_3d(q_s, &tma_q, &q_full, 0, q_tile * BQ, bh);
+      tma_load_3d(q_s + CHUNK_BYTES, &tma_q, &q_full, 64, q_tile * BQ, bh);
+      for (int j = 0; j < n; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&kv_empty[st], ph ^ 1, abort)) {
+          raise_error(p, abort, kErrTimeoutProducer);
+          break;
+        }
+        uint8_t *k_s = smem + TILE_BYTES + st * 2 * TILE_BYTES;
+        uint8_t *v_s = k_s + TILE_BYTES;
+        mbar_expect_tx(&k_full[st], TILE_BYTES);
+        tma_load_3d(k_s, &tma_k, &k_full[st], 0, j * BKV, bh);
+        tma_load_3d(k_s + CHUNK_BYTES, &tma_k, &k_full[st], 64, j * BKV, bh);
+        mbar_expect_tx(&v_full[st], TILE_BYTES);
+        tma_load_3d(v_s, &tma_v, &v_full[st], 0, j * BKV, bh);
+        tma_load_3d(v_s + CHUNK_BYTES, &tma_v, &v_full[st], 64, j * BKV, bh);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_f16(false, false, false, BQ, BKV);
+      constexpr uint32_t idesc_o = idesc_f16(false, false, true, BQ, HEAD);
+      const uint32_t q_addr = smem_u32(q_s);
+      bool ok = mbar_wait(&q_full, 0, abort);
+      if (!ok) raise_error(p, abort, kErrTimeoutMma);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1, abort)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + TILE_BYTES + st * 2 * TILE_BYTES);
+#pragma unroll
+        for (int k = 0; k < HEAD / 16; ++k) {
+          const uint32_t off = (k >> 2) * CHUNK_BYTES + (k & 3) * 32;
+          mma_f16(tmem + (j & 1) * BKV, smem_desc_sw128(q_addr + off, 16, 1024),
+                  smem_desc_sw128(k_addr + off, 16, 1024), idesc_s, k > 0);
+        }
+        mma_commit(&s_full[j & 1]);
+        return true;
+      };
+      if (ok && !issue_s(0)) {
+        raise_error(p, abort, kErrTimeoutMma);
+        ok = false;
+      }
+      for (int j = 0; ok && j < n; ++j) {
+        if (j + 1 < n && !issue_s(j + 1)) {
+          raise_error(p, abort, kErrTimeoutMma);
+          break;
+        }
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&p_full[st], ph, abort) || !mbar_wait(&v_full[st], ph, abort)) {
+          raise_error(p, abort, kErrTimeoutMma);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem + TILE_BYTES + st * 2 * TILE_BYTES + TILE_BYTES);
+#pragma unroll
+        for (int k = 0; k < BKV / 16; ++k)
+          mma_f16_tmem_a(tmem + O_COL, tmem + st * BKV + k * 8,
+                         smem_desc_sw128(v_addr + k * 2048, CHUNK_BYTES, 1024), idesc_o,
+                         (j | k) != 0);
+        mma_commit(&kv_empty[st]);
+        mma_commit(&o_done);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      const int b = j & 1;
+      if (!warp_wait(&s_full[b], (j >> 1) & 1, abort, p, kErrTimeoutSoftmax)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_base + b * BKV + c * 32, sr[c]);
+      tmem_wait_ld();
+      const int valid = p.s_kv - j * BKV;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float v = __uint_as_float(sr[c][i]) * p.scale_log2;
+          if (c * 32 + i >= valid) v = -INFINITY;
+          sr[c][i] = __float_as_uint(v);
+          mx = fmaxf(mx, v);
+        }
+      const float m_new = fmaxf(m, mx);
+      const bool need = m_new > m + kRescaleThreshold;
+      if (__any_sync(0xffffffffu, need)) {
+        const float alpha = need ? ex2(m - m_new) : 1.0f;
+        if (need) {
+          l *= alpha;
+          m = m_new;
+        }
+        if (j > 0) {
+          if (!warp_wait(&o_done, (j - 1) & 1, abort, p, kErrTimeoutCorrection)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < HEAD / 16; ++c) {
+            uint32_t o[16];
+            tmem_ld16(tmem + lane_base + O_COL + c * 16, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st16(tmem + lane_base + O_COL + c * 16, o);
+          }
+          tmem_wait_st();
+        }
+      }
+      float rowsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = ex2(__uint_as_float(sr[c][2 * i]) - m);
+          const float p1 = ex2(__uint_as_float(sr[c][2 * i + 1]) - m);
+          rowsum += p0 + p1;
+          __half2 h = __floats2half2_rn(p0, p1);
+          packed[i] = *reinterpret_cast<uint32_t *>(&h);
+        }
+        tmem_st16(tmem + lane_base + b * BKV + c * 16, packed);
+      }
+      tmem_wait_st();
+      l += rowsum;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
+    }
+    if (ok && n > 0 && warp_wait(&o_done, (n - 1) & 1, abort, p, kErrTimeoutSoftmax)) {
+      tc_fence_after();
+      const float inv = 1.0f / l;
+      const int q = q_tile * BQ + row;
+      __half *out = p.o + ((int64_t)bh * p.s_q + q) * HEAD;
+#pragma unroll 1
+      for (int c = 0; c < HEAD / 16; ++c) {
+        uint32_t o[16];
+        tmem_ld16(tmem + lane_base + O_COL + c * 16, o);
+        tmem_wait_ld();
+        if (q < p.s_q) {
+          uint4 pack[2];
+          __half *h = reinterpret_cast<__half *>(pack);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) h[i] = __float2half_rn(__uint_as_float(o[i]) * inv);
+          reinterpret_cast<uint4 *>(out + c * 16)[0] = pack[0];
+          reinterpret_cast<uint4 *>(out + c * 16)[1] = pack[1];
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (abort_flag) drain_delay();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- SIMT path
+// One warp per query row, online softmax in f32, any head size up to 256.
+__global__ void __launch_bounds__(256) sdpa_simt_kernel(const __half *__restrict__ q,
+                                                        const __half *__restrict__ k,
+                                                        const __half *__restrict__ v,
+                                                        __half *__restrict__ o, int s_q, int s_kv,
+                                                        int d, float scale) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  const int64_t bh = blockIdx.y;
+  if (row >= s_q) return;
+  constexpr int kMaxPerLane = 8;
+  float qv[kMaxPerLane], acc[kMaxPerLane];
+  const __half *qr = q + (bh * s_q + row) * d;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const int c = lane + 32 * i;
+    qv[i] = c < d ? __half2float(qr[c]) : 0.f;
+    acc[i] = 0.f;
+  }
+  float m = -INFINITY, l = 0.f;
+  for (int key = 0; key < s_kv; ++key) {
+    const __half *kr = k + (bh * s_kv + key) * d;
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) {
+      const int c = lane + 32 * i;
+      if (c < d) dot = fmaf(qv[i], __half2float(kr[c]), dot);
+    }
+    dot = warp_sum(dot) * scale;
+    const float m_new = fmaxf(m, dot);
+    const float alpha = expf(m - m_new);
+    const float pw = expf(dot - m_new);
+    l = l * alpha + pw;
+    const float ph = __half2float(__float2half_rn(pw));
+    const __half *vr = v + (bh * s_kv + key) * d;
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) {
+      const int c = lane + 32 * i;
+      acc[i] = acc[i] * alpha + (c < d ? ph * __half2float(vr[c]) : 0.f);
+    }
+    m = m_new;
+  }
+  __half *orow = o + (bh * s_q + row) * d;
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const int c = lane + 32 * i;
+    if (c < d) orow[c] = __float2half_rn(acc[i] / l);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void *ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// [bh, s, 128] f16 viewed as a 3-D tensor, box 64 x 128 x 1, 128-byte swizzle.
+int make_map_3d(CUtensorMap *map, const void *base, int64_t bh, int64_t s) {
+  auto fn = encode_fn();
+  if (!fn) return fail(LC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)HEAD, (cuuint64_t)s, (cuuint64_t)bh};
+  cuuint64_t strides[2] = {(cuuint64_t)HEAD * 2, (cuuint64_t)s * HEAD * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return LC_OK;
+}
+
+}  // namespace
+
+int sdpa_path(const void *q, const void *k, const void *v, const void *o, int64_t s_q,
+              int64_t s_kv, int64_t d) {
+  const bool tc = d == HEAD && aligned(q, 16) && aligned(k, 16) && aligned(v, 16) &&
+                  aligned(o, 16) && s_q >= 1 && s_kv >= 1 && s_q * s_kv >= 128 * 128;
+  return tc ? 1 : 0;
+}
+
+}  // namespace lc
+
+extern "C" int lc_sdpa_f16(const void *q, const void *k, const void *v, void *o, int64_t bh,
+                           int64_t s_q, int64_t s_kv, int64_t d, float scale, void *stream) {
+  using namespace lc;
+  if (bh < 0 || s_q < 0 || s_kv < 0 || d < 0) return fail(LC_ERR_INVALID, "lc_sdpa_f16: negative shape");
+  if (bh == 0 || s_q == 0) return LC_OK;
+  if (s_kv == 0) return fail(LC_ERR_INVALID, "lc_sdpa_f16: softmax over zero keys is undefined");
+  if (d == 0 || d > 256) return fail(LC_ERR_UNSUPPORTED, "lc_sdpa_f16: head size %lld", (long long)d);
+  if (!q || !k || !v || !o) return fail(LC_ERR_INVALID, "lc_sdpa_f16: null buffer");
+  if (bh > 65535 || s_q > 0x7fffffff / 2 || s_kv > 0x7fffffff / 2)
+    return fail(LC_ERR_UNSUPPORTED, "lc_sdpa_f16: shape too large");
+  if (!(scale > 0.f)) return fail(LC_ERR_INVALID, "lc_sdpa_f16: scale must be positive");
+  cudaStream_t s = as_stream(stream);
+  if (!sdpa_path(q, k, v, o, s_q, s_kv, d)) {
+    dim3 grid((unsigned)((s_q + 7) / 8), (unsigned)bh);
+    sdpa_simt_kernel<<<grid, 256, 0, s>>>(static_cast<const __half *>(q), static_cast<const __half *>(k),
+                                          static_cast<const __half *>(v), static_cast<__half *>(o),
+                                          (int)s_q, (int)s_kv, (int)d, scale);
+    return check_launch("lc_sdpa_f16 (simt)");
+  }
+  CUtensorMap tq, tk, tv;
+  if (int rc = make_map_3d(&tq, q, bh, s_q)) return rc;
+  if (int rc = make_map_3d(&tk, k, bh, s_kv)) return rc;
+  if (int rc = make_map_3d(&tv, v, bh, s_kv)) return rc;
+  SdpaParams p;
+  p.s_q = (int)s_q;
+  p.s_kv = (int)s_kv;
+  p.n_kv = (int)((s_kv + BKV - 1) / BKV);
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.o = static_cast<__half *>(o);
+  if (int rc = device_error_word(&p.err)) return rc;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (int rc = check_cuda(cudaFuncSetAttribute(sdpa_tc_kernel,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 SMEM_BYTES),
+                            "sdpa smem attribute"))
+      return rc;
+    configured[dev] = true;
+  }
+  dim3 grid((unsigned)((s_q + BQ - 1) / BQ), (unsigned)bh);
+  sdpa_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(tq, tk, tv, p);
+  return check_launch("lc_sdpa_f16");
+}
+
+extern "C" int lc_sdpa_path(const void *q, const void *k, const void *v, const void *o,
+                            int64_t s_q, int64_t s_kv, int64_t d) {
+  return lc::sdpa_path(q, k, v, o, s_q, s_kv, d);
 }

@@ -151,6 +151,17 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]: the A operand (M x 16, 16-bit elements packed two
+// per 32-bit column, row m in lane m) is read from tensor memory.
+__device__ __forceinline__ void mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrives once on `bar` when every tcgen05 operation this thread issued so far completes.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
   asm volatile(

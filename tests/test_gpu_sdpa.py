@@ -1,0 +1,107 @@
+"""GPU parity of lc_sdpa_f16 (tcgen05 path and SIMT path) against the oracle.
+
+Stated tolerance for f16 attention: isclose(rtol=2e-2, atol=2e-2 * rms(ref))
+elementwise and a normwise relative error below 5e-3 (f16 output rounding
+is 2^-11; P is rounded to f16 before the PV product like the reference's f16
+attention tile).
+"""
+import ctypes
+import math
+
+import numpy as np
+import pytest
+
+from lazy_compiler_b200 import runtime
+from oracle import expressions as O
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 2e-2
+
+
+def P(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def run_sdpa(q, k, v, scale):
+    import torch
+    bh, s_q, d = q.shape
+    s_kv = k.shape[1]
+    o = torch.full((bh, s_q, d), float("nan"), dtype=torch.float16, device="cuda")
+    runtime.call("lc_sdpa_f16", P(q), P(k), P(v), P(o), bh, s_q, s_kv, d, ctypes.c_float(scale), None)
+    runtime.call("lc_device_status", None)
+    return o
+
+
+def check(got, ref):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    assert np.isfinite(got).all()
+    rms = float(np.sqrt(np.mean(ref ** 2)))
+    close = np.isclose(got, ref, rtol=RTOL, atol=RTOL * rms)
+    assert close.all(), (np.argwhere(~close)[:5], got[~close][:5], ref[~close][:5])
+    norm = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    assert norm < 5e-3, norm
+
+
+def inputs(bh, s_q, s_kv, d, seed=0, spread=1.0):
+    import torch
+    rng = np.random.default_rng(seed)
+    q = (rng.standard_normal((bh, s_q, d)) * spread).astype(np.float16)
+    k = (rng.standard_normal((bh, s_kv, d)) * spread).astype(np.float16)
+    v = rng.standard_normal((bh, s_kv, d)).astype(np.float16)
+    return q, k, v, *(torch.from_numpy(a).cuda() for a in (q, k, v))
+
+
+@pytest.mark.parametrize("bh,s_q,s_kv,d", [(1, 1, 1, 16), (2, 16, 16, 16), (3, 37, 53, 64),
+                                           (2, 64, 200, 128), (1, 8, 33, 256)])
+def test_simt_path(bh, s_q, s_kv, d, cuda_device):
+    q, k, v, tq, tk, tv = inputs(bh, s_q, s_kv, d)
+    o = run_sdpa(tq, tk, tv, 1 / math.sqrt(d))
+    ref = O.sdpa_f16(q.astype(np.float32), k.astype(np.float32), v.astype(np.float32), 1 / math.sqrt(d))[0]
+    check(o.float().cpu().numpy(), ref)
+
+
+TC = [(1, 128, 128), (2, 256, 256), (3, 300, 300), (2, 128, 1000), (1, 1000, 130), (4, 1024, 1024)]
+
+
+@pytest.mark.parametrize("bh,s_q,s_kv", TC)
+@pytest.mark.parametrize("spread", [1.0, 3.0])
+def test_tcgen05_path(bh, s_q, s_kv, spread, cuda_device):
+    d = 128
+    q, k, v, tq, tk, tv = inputs(bh, s_q, s_kv, d, seed=s_q + s_kv, spread=spread)
+    assert runtime.library().lc_sdpa_path(P(tq), P(tk), P(tv), P(tq), s_q, s_kv, d) == 1
+    scale = 1 / math.sqrt(d)
+    o = run_sdpa(tq, tk, tv, scale)
+    ref = O.sdpa_f16(q.astype(np.float32), k.astype(np.float32), v.astype(np.float32), scale)[0]
+    check(o.float().cpu().numpy(), ref)
+
+
+def test_tcgen05_repeated_calls_are_identical(cuda_device):
+    import torch
+    _, _, _, tq, tk, tv = inputs(8, 512, 512, 128, seed=4)
+    o1 = run_sdpa(tq, tk, tv, 0.1)
+    o2 = run_sdpa(tq, tk, tv, 0.1)
+    assert torch.equal(o1, o2)
+
+
+def test_config_size_against_torch_fp32(cuda_device):
+    """B8 H16 S4096 D128 fp16, scale 1/sqrt(128): all heads run, 6 heads checked in fp32."""
+    import torch
+    bh, s, d = 8 * 16, 4096, 128
+    g = torch.Generator(device="cuda").manual_seed(7)
+    q = torch.randn(bh, s, d, device="cuda", generator=g).half()
+    k = torch.randn(bh, s, d, device="cuda", generator=g).half()
+    v = torch.randn(bh, s, d, device="cuda", generator=g).half()
+    scale = 1 / math.sqrt(d)
+    o = run_sdpa(q, k, v, scale)
+    assert torch.isfinite(o).all()
+    for h in (0, 1, 37, 64, 100, 127):
+        sc = (q[h].float() @ k[h].float().T) * scale
+        ref = torch.softmax(sc, dim=-1) @ v[h].float()
+        check(o[h].float().cpu().numpy(), ref.cpu().numpy())
+    rows = np.random.default_rng(0).integers(0, s, 8)
+    h = 90
+    ref64 = O.sdpa(q[h, rows].double().cpu().numpy(), k[h].double().cpu().numpy(),
+                   v[h].double().cpu().numpy(), scale)[0]
+    check(o[h, rows].float().cpu().numpy(), ref64)
