@@ -80,7 +80,7 @@ def tensor_peak():
     return FALLBACK_BF16_TFLOPS, 1400.0, "fallback"
 
 
-SUITE = ("reduce", "rows", "elementwise")
+SUITE = ("reduce", "rows", "elementwise", "gemm_f16", "gemm_bf16", "sdpa")
 SDPA_SHAPE = (8 * 16, 4096, 128)
 GEMM_SHAPES = {"gemm_f16": ("f16", 8192, 8192, 8192), "gemm_bf16": ("bf16", 4096, 16384, 2048)}
 
@@ -464,6 +464,24 @@ def cpu_run(config, sample_scale):
     """
     import numpy as np
     rng = np.random.default_rng(0)
+    if config == "sdpa":
+        bh, sq, d = SDPA_SHAPE
+        rows = max(1, sq // sample_scale)
+        q = rng.standard_normal((rows, d)).astype(np.float16).astype(np.float64)
+        k = rng.standard_normal((sq, d)).astype(np.float16).astype(np.float64)
+        v = rng.standard_normal((sq, d)).astype(np.float16).astype(np.float64)
+        scale = d ** -0.5
+
+        def attn():
+            sc = (q @ k.T) * scale
+            sc -= sc.max(-1, keepdims=True)
+            p = np.exp(sc)
+            p /= p.sum(-1, keepdims=True)
+            return p @ v
+        threads = blas_threads()
+        desc = (f"{rows} query rows of one head against 4096 keys (1/{bh * sample_scale} of a step), "
+                f"float64 numpy/BLAS softmax attention, {threads} threads")
+        return [(4 * rows * sq * d, attn)], desc, threads, "TFLOP/s", (q, k, v)
     if config in GEMM_SHAPES:
         ab, m, n, k = GEMM_SHAPES[config]
         rows = max(1, m // sample_scale)
@@ -538,12 +556,14 @@ def cpu_time(ops, repeats):
 def cpu_baseline(config, sample_scale):
     if config in GEMM_SHAPES:
         sample_scale = 64
+    if config == "sdpa":
+        sample_scale = 8
     ops, desc, threads, unit, keep = cpu_run(config, sample_scale)
     cpu_time(ops, 1)
     times = cpu_time(ops, 3)
     work = sum(o[0] for o in ops)
     scale = 1e12 if unit == "TFLOP/s" else 1e9
-    how = ("the reference's float64 numpy matmul oracle" if config in GEMM_SHAPES else
+    how = ("the reference's float64 numpy oracle" if config in GEMM_SHAPES or config == "sdpa" else
            f"C restatement of the reference's numpy formula oracle, {threads} POSIX threads")
     return {"value": round(work / statistics.median(times) / scale, 4), "unit": unit,
             "cores": threads, "kind": "port",
@@ -555,7 +575,7 @@ def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    scale = {"elementwise": 16, "reduce": 1, "rows": 4}.get(args.config, 64)
+    scale = {"elementwise": 16, "reduce": 1, "rows": 4, "sdpa": 8}.get(args.config, 64)
     ops, desc, threads, unit, keep = cpu_run(args.config, scale)
     cpu_time(ops, args.warmup)
     times = cpu_time(ops, args.steps)
@@ -566,7 +586,8 @@ def run_reference(args):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(sum(times) * 1e3 / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "data": "synthetic (seeded numpy)",
-        "dtype": {"gemm_f16": "f64 (f16 inputs)", "gemm_bf16": "f64 (bf16 inputs)"}.get(args.config, "f32"),
+        "dtype": {"gemm_f16": "f64 (f16 inputs)", "gemm_bf16": "f64 (bf16 inputs)",
+                  "sdpa": "f64 (f16 inputs)"}.get(args.config, "f32"),
         "config": {"workload": args.config, "sample": desc},
         "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": threads, "kind": "port",
                          "sample": desc},
