@@ -129,63 +129,96 @@ class Dist:
 
 
 class Clocks:
-    """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
+    """SM clock and throttle reasons sampled during the timed region.
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    Polls NVML (read-only queries) every millisecond from a background thread,
+    so even a 20 ms timed region yields tens of samples; falls back to
+    ``nvidia-smi -lms 100`` when NVML is unavailable.
+    """
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
     def __init__(self, device):
         import torch
+        self.samples = []
+        self.max_mhz = None
+        self.stop = False
+        self.thread = None
         self.proc = None
-        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
-            ident = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+            self.uuid = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
         except Exception:
-            ident = str(device.index or 0)
-        self.ident = ident
+            self.uuid = None
+        self.index = device.index or 0
+
+    def _poll(self, nvml, handle):
+        get_reasons = getattr(nvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop:
+            try:
+                self.samples.append((nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM),
+                                     int(get_reasons(handle))))
+            except Exception:
+                pass
+            time.sleep(0.001)
 
     def __enter__(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", self.ident, f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=self.file, stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
-        time.sleep(0.3)
+            import pynvml as nvml
+            nvml.nvmlInit()
+            handle = (nvml.nvmlDeviceGetHandleByUUID(self.uuid) if self.uuid
+                      else nvml.nvmlDeviceGetHandleByIndex(self.index))
+            self.max_mhz = nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM)
+            self.thread = threading.Thread(target=self._poll, args=(nvml, handle), daemon=True)
+            self.thread.start()
+        except Exception:
+            self.thread = None
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", "-i", self.uuid or str(self.index),
+                     "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                     "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                     "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "100"],
+                    stdout=self.file, stderr=subprocess.DEVNULL)
+            except OSError:
+                self.proc = None
+        time.sleep(0.01)
         return self
 
     def __exit__(self, *exc):
+        self.stop = True
+        if self.thread is not None:
+            self.thread.join(timeout=2)
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+            self.file.flush()
+            self.file.seek(0)
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            bits = [0x8, 0x40, 0x20, 0x4]
+            for line in self.file.read().splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                try:
+                    mask = sum(b for b, f in zip(bits, parts[2:6]) if f.lower().startswith("active"))
+                    self.samples.append((float(parts[0]), mask))
+                    self.max_mhz = float(parts[1])
+                except (ValueError, IndexError):
+                    continue
+            os.unlink(self.file.name)
 
     def summary(self) -> dict:
-        self.file.flush()
-        self.file.seek(0)
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.file.read().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 8:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx.append(float(parts[1]))
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[4:8]):
-                if flag.lower().startswith("active"):
-                    reasons.add(name)
-        os.unlink(self.file.name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0}
+        reasons = sorted({name for _, mask in self.samples for bit, name in self.REASONS.items() if mask & bit})
+        return {"sm_mhz": statistics.median(c for c, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "sm_mhz_min": min(c for c, _ in self.samples), "reasons": reasons,
+                "samples": len(self.samples), "source": "nvml" if self.proc is None else "nvidia-smi"}
 
 
 # ---------------------------------------------------------------- our kernels
@@ -300,14 +333,9 @@ def run_ours(args):
                 ops = [("sum", 4 * n, lambda: runtime.call("lc_sum_f32", P(x), P(out), n, s)),
                        ("mean", 4 * n, lambda: runtime.call("lc_mean_f32", P(x), P(count), P(out[1:]), n, s))]
             else:
-                import torch.distributed as tdist
-
-                def sharded(mean):
-                    runtime.call("lc_sum_partial_f32", P(x), n, P(part), s)
-                    tdist.all_reduce(part)
-                    runtime.call("lc_sum_finalize", P(part), P(count) if mean else ctypes.c_void_p(0),
-                                 P(out), s)
-                ops = [("sum", 4 * n, lambda: sharded(False)), ("mean", 4 * n, lambda: sharded(True))]
+                from lazy_compiler_b200.dist import sharded_sum
+                ops = [("sum", 4 * n, lambda: sharded_sum(x, n, out[:1], None, stream=stream)),
+                       ("mean", 4 * n, lambda: sharded_sum(x, n, out[1:], count, stream=stream))]
             scratch = torch.empty(L2_FLUSH_BYTES // 4, device=dist.device)
             cfg = {"workload": "whole-array sum and mean of 2^24 fp32 U[-1,1] per GPU"
                                + (", f64 partials all-reduced over NCCL" if dist.world > 1 else ""),

@@ -72,6 +72,14 @@ int lc_last_error(char *buf, size_t len);
  * in a child process instead (tools/check_compiler.py:425-445). */
 int lc_device_status(void *stream);
 
+/* Failure-detection self-test: launches a kernel whose mbarrier wait (the
+ * bounded-wait routine of the GEMM and attention kernels) can never complete
+ * and gives up after limit_ns (at most 2 s); the following lc_device_status
+ * returns LC_ERR_TIMEOUT and the context stays usable.  No reference
+ * counterpart (the reference isolates faulting kernels in a child process,
+ * tools/check_compiler.py:425-445). */
+int lc_selftest_bounded_wait(int64_t limit_ns, void *stream);
+
 /* ---------------------------------------------------------------- pointwise
  * Replace the Tile/Load/Assign/Write lowering of ptx_backend.py:1409-1427,
  * 1574-1642 and `operation` :894-1177 for the pointwise problems. */

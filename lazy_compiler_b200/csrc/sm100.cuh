@@ -30,6 +30,7 @@ enum DeviceError : int {
   kErrTimeoutEpilogue = 3,
   kErrTimeoutSoftmax = 4,
   kErrTimeoutCorrection = 5,
+  kErrTimeoutSelftest = 6,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -72,8 +73,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete.  Gives up (returns
-// false) after kWaitLimitNs or as soon as *abort is set by another role.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort) {
+// false) after limit_ns or as soon as *abort is set by another role.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t *bar, uint32_t parity,
+                                                volatile int *abort, uint64_t limit_ns) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t start = globaltimer();
@@ -81,9 +83,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     if (mbar_try_wait(addr, parity)) return true;
     if ((i & 63) == 0) {
       if (*abort) return false;
-      if (globaltimer() - start > kWaitLimitNs) return false;
+      if (globaltimer() - start > limit_ns) return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort) {
+  return mbar_wait_limit(bar, parity, abort, kWaitLimitNs);
 }
 
 // Lets in-flight asynchronous copies and MMAs land before a CTA that aborted

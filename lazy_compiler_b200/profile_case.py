@@ -1,0 +1,107 @@
+"""Runs one kernel of the library on a chosen size, for profiling and timing.
+
+    python -m lazy_compiler_b200.profile_case OP [--n N] [--rows R --cols C]
+           [--m M --n N --k K] [--bh B --seq S] [--warmup W] [--repeat R]
+
+OP is one of add, axpb, relumul, gelu_erf, gelu_tanh, sum, mean, rowsum,
+rmsnorm, softmax, l2norm, gemm_f16, gemm_bf16, sdpa.  Inputs are seeded
+device tensors; every launch goes through the C ABI.  The mean CUDA-event
+time of the repeated launches is printed (``--repeat`` launches after
+``--warmup``), so the same command line serves an ncu capture (``-k`` the
+kernel, ``-s`` the warm-up launches, ``-c`` one to three launches).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+
+from . import runtime
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("op")
+    ap.add_argument("--n", type=int, default=None)
+    ap.add_argument("--rows", type=int, default=16384)
+    ap.add_argument("--cols", type=int, default=4096)
+    ap.add_argument("--m", type=int, default=8192)
+    ap.add_argument("--k", type=int, default=8192)
+    ap.add_argument("--bh", type=int, default=128)
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--warmup", type=int, default=1)
+    ap.add_argument("--repeat", type=int, default=1)
+    a = ap.parse_args()
+
+    import torch
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    op = a.op
+    if op in ("add", "axpb", "relumul", "gelu_erf", "gelu_tanh", "sum", "mean"):
+        n = a.n or (1 << 28 if op not in ("sum", "mean") else 1 << 24)
+        x = torch.randn(n, device="cuda", generator=g)
+        y = torch.randn(n, device="cuda", generator=g) if op in ("add", "relumul") else x
+        out = torch.empty(n if op not in ("sum", "mean") else 1, device="cuda")
+        c1, c2 = torch.tensor([1.5], device="cuda"), torch.tensor([float(n)], device="cuda")
+        fn = {
+            "add": lambda: runtime.call("lc_add_f32", P(x), P(y), P(out), n, s),
+            "axpb": lambda: runtime.call("lc_axpb_f32", P(c1), P(c1), P(x), P(out), n, s),
+            "relumul": lambda: runtime.call("lc_relumul_f32", P(x), P(y), P(out), n, s),
+            "gelu_erf": lambda: runtime.call("lc_gelu", 0, 0, P(x), P(out), n, s),
+            "gelu_tanh": lambda: runtime.call("lc_gelu", 0, 1, P(x), P(out), n, s),
+            "sum": lambda: runtime.call("lc_sum_f32", P(x), P(out), n, s),
+            "mean": lambda: runtime.call("lc_mean_f32", P(x), P(c2), P(out), n, s),
+        }[op]
+        work, unit = (3 if op in ("add", "relumul") else (1 if op in ("sum", "mean") else 2)) * 4 * n, "GB/s"
+    elif op in ("rowsum", "rmsnorm", "softmax", "l2norm"):
+        r, c = a.rows, a.cols
+        x = torch.randn(r, c, device="cuda", generator=g)
+        w = torch.randn(c, device="cuda", generator=g) * 0.1 + 1
+        out = torch.empty_like(x)
+        cnt, eps = torch.tensor([float(c)], device="cuda"), torch.tensor([1e-6], device="cuda")
+        fn = {
+            "rowsum": lambda: runtime.call("lc_rowsum_f32", P(x), P(out), r, c, s),
+            "rmsnorm": lambda: runtime.call("lc_rmsnorm_f32", P(cnt), P(eps), P(x), P(w), P(out), r, c, s),
+            "softmax": lambda: runtime.call("lc_softmax_f32", P(x), P(out), r, c, s),
+            "l2norm": lambda: runtime.call("lc_l2norm_f32", P(x), P(out), r, c, s),
+        }[op]
+        work, unit = (1 if op == "rowsum" else 2) * 4 * r * c, "GB/s"
+    elif op in ("gemm_f16", "gemm_bf16"):
+        m, n, k = a.m, a.n or 8192, a.k
+        dt = torch.float16 if op == "gemm_f16" else torch.bfloat16
+        A = (torch.randn(m, k, device="cuda", generator=g) / k ** 0.5).to(dt)
+        B = (torch.randn(k, n, device="cuda", generator=g) / k ** 0.5).to(dt)
+        C = torch.empty(m, n, device="cuda")
+        code = 1 if op == "gemm_f16" else 2
+        fn = lambda: runtime.call("lc_gemm", code, 0, 0, 0, P(A), P(B), P(C), m, n, k, s)  # noqa: E731
+        work, unit = 2 * m * n * k, "TFLOP/s"
+    elif op == "sdpa":
+        bh, sq, d = a.bh, a.seq, 128
+        q = torch.randn(bh, sq, d, device="cuda", generator=g).half()
+        k_ = torch.randn(bh, sq, d, device="cuda", generator=g).half()
+        v = torch.randn(bh, sq, d, device="cuda", generator=g).half()
+        o = torch.empty_like(q)
+        scale = ctypes.c_float(d ** -0.5)
+        fn = lambda: runtime.call("lc_sdpa_f16", P(q), P(k_), P(v), P(o), bh, sq, sq, d, scale, s)  # noqa: E731
+        work, unit = 4 * bh * sq * sq * d, "TFLOP/s"
+    else:
+        raise SystemExit(f"unknown op {op}")
+    for _ in range(a.warmup):
+        fn()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(a.repeat):
+        fn()
+    end.record()
+    torch.cuda.synchronize()
+    runtime.call("lc_device_status", s)
+    ms = start.elapsed_time(end) / a.repeat
+    rate = work / (ms / 1e3) / (1e12 if unit == "TFLOP/s" else 1e9)
+    print(json.dumps({"op": op, "ms": round(ms, 4), "rate": round(rate, 1), "unit": unit}))
+
+
+if __name__ == "__main__":
+    main()

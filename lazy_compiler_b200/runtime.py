@@ -48,6 +48,7 @@ SIGNATURES = {
     "lc_gemm": [_INT, _INT, _INT, _INT, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_path": [_INT, _INT, _P, _P, _I64, _I64, _I64],
     "lc_device_status": [_P],
+    "lc_selftest_bounded_wait": [_I64, _P],
     "lc_sdpa_f16": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, ctypes.c_float, _P],
     "lc_sdpa_path": [_P, _P, _P, _P, _I64, _I64, _I64],
 }
