@@ -436,7 +436,7 @@ def run_ours(args):
     if dist.rank == 0 and dist.world == 1:
         line["cpu_baseline"] = cpu_baseline(args.config, sample_scale=16)
     if dist.rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     dist.close()
 
 
@@ -621,11 +621,29 @@ def run_reference(args):
                          "sample": desc},
         "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+_RESULT_FD = None
+
+
+def emit(line: dict) -> None:
+    """Writes the one JSON result line to the real stdout."""
+    data = (json.dumps(line) + "\n").encode()
+    if _RESULT_FD is not None:
+        os.write(_RESULT_FD, data)
+    else:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
 
 
 def main():
+    global _RESULT_FD
     args = parse_args()
+    # Libraries (NCCL, torch) may print to fd 1; keep stdout for the result line only.
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
     if args.impl == "reference":
         run_reference(args)
     else:
