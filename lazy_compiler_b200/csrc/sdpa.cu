@@ -5,22 +5,22 @@
 // and the single 16x16 fragment tile of ptx_tensor.py:459-618 (QK mma.sync,
 // FragmentRowReduce, FragmentApply exp/div, FragmentRepack to f16, PV mma.sync).
 //
-// Here, per CTA, one 128-row query tile of one (batch, head), FlashAttention
-// style on tcgen05:
-//   warp 0     TMA: Q once, then K and V tiles of 128 keys through a 2-stage
-//              ring (3-D tensor maps [bh, s, d] so a ragged tail zero-fills
-//              inside its own head; 128-byte swizzle; no multicast);
-//   warp 1     allocates 512 TMEM columns (two 128x128 f32 S buffers, one
-//              128x128 f32 O accumulator) and one thread issues the MMAs:
-//              S(j+1) = Q K(j+1)^T is issued before O += P(j) V(j), so the
-//              tensor core works on the next scores while the softmax runs;
-//   warps 2-5  softmax: each thread owns one query row (its TMEM lane), loads
-//              the 128 scores, keeps the running max m and sum l in f32,
-//              writes P = 2^(s*scale*log2e - m) as f16 back into TMEM over the
-//              scores (the A operand of the PV MMA is read from TMEM), and
-//              rescales O only when a row max grows by more than 2^8 (the
-//              stale max is exact math: it cancels in O / l); finally O / l is
-//              stored as f16.
+// Here, per CTA, two 128-row query tiles of one (batch, head), FlashAttention
+// style on tcgen05 (the Blackwell "ping-pong" schedule):
+//   warp 0     TMA: both Q tiles once, then K and V tiles of 128 keys through
+//              a 2-stage ring (3-D tensor maps [bh, s, d] so a ragged tail
+//              zero-fills inside its own head; 128-byte swizzle; no multicast);
+//   warp 1     allocates all 512 TMEM columns (S0, S1, O0, O1: 128 columns of
+//              f32 each) and one thread issues the MMAs in the order
+//              PV0(j), S0(j+1), PV1(j), S1(j+1), so the tensor core computes one
+//              tile's products while the other tile's softmax runs;
+//   warps 2-9  two softmax warpgroups, one per query tile: each thread owns one
+//              query row (its TMEM lane), loads the 128 scores, keeps the
+//              running max m and sum l in f32, writes P = 2^(s*scale*log2e - m)
+//              as f16 back into TMEM over the scores (the A operand of the PV
+//              MMA is read from TMEM), and rescales O only when a row max grows
+//              by more than 2^8 (the stale max is exact math: it cancels in
+//              O / l); finally O / l is stored as f16.
 // P is rounded to f16 before the PV product, as the reference's f16 attention
 // tile rounds its normalised weights (FragmentRepack).  Every mbarrier wait is
 // bounded; a wait that gives up writes the device error word.
@@ -35,17 +35,19 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BQ = 128;
+constexpr int BQ = 128;       // rows of one query tile
+constexpr int QT = 2;         // query tiles per CTA (one softmax warpgroup each)
 constexpr int BKV = 128;
 constexpr int HEAD = 128;
 constexpr int CHUNK_BYTES = 128 * 64 * 2;     // 128 rows x 64 columns of f16 (one swizzle span)
 constexpr int TILE_BYTES = 2 * CHUNK_BYTES;   // 128 rows x 128 columns
 constexpr int KV_STAGES = 2;
-constexpr int SMEM_BYTES = TILE_BYTES + KV_STAGES * 2 * TILE_BYTES + 1024;
-constexpr int THREADS = 192;
+constexpr int Q_BYTES = QT * TILE_BYTES;
+constexpr int SMEM_BYTES = Q_BYTES + KV_STAGES * 2 * TILE_BYTES + 1024;
+constexpr int THREADS = 64 + QT * 128;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t O_COL = 256;
-constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr uint32_t O_COL = 256;               // O tile t at O_COL + t * 128; S tile t at t * 128
+constexpr float kRescaleThreshold = 8.0f;     // log2 units
 
 struct SdpaParams {
   int s_q, s_kv, n_kv;
@@ -83,20 +85,20 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t *q_s = smem;
+  uint8_t *kv_s = smem + Q_BYTES;
   __shared__ __align__(8) uint64_t q_full;
   __shared__ __align__(8) uint64_t k_full[KV_STAGES];
   __shared__ __align__(8) uint64_t v_full[KV_STAGES];
   __shared__ __align__(8) uint64_t kv_empty[KV_STAGES];
-  __shared__ __align__(8) uint64_t s_full[2];
-  __shared__ __align__(8) uint64_t p_full[2];
-  __shared__ __align__(8) uint64_t o_done;
+  __shared__ __align__(8) uint64_t s_full[QT];
+  __shared__ __align__(8) uint64_t p_full[QT];
+  __shared__ __align__(8) uint64_t o_done[QT];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   volatile int *abort = &abort_flag;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int q_tile = blockIdx.x;
   const int bh = blockIdx.y;
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 1);
@@ -105,11 +107,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], 4);
+    for (int t = 0; t < QT; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_done[t], 1);
     }
-    mbar_init(&o_done, 1);
     abort_flag = 0;
     fence_barrier_init();
   }
@@ -130,9 +132,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_expect_tx(&q_full, TILE_BYTES);
-      tma_load_3d(q_s, &tma_q, &q_full, 0, q_tile * BQ, bh);
-      tma_load_3d(q_s + CHUNK_BYTES, &tma_q, &q_full, 64, q_tile * BQ, bh);
+      mbar_expect_tx(&q_full, Q_BYTES);
+      for (int t = 0; t < QT; ++t) {
+        const int row0 = (blockIdx.x * QT + t) * BQ;
+        tma_load_3d(q_s + t * TILE_BYTES, &tma_q, &q_full, 0, row0, bh);
+        tma_load_3d(q_s + t * TILE_BYTES + CHUNK_BYTES, &tma_q, &q_full, 64, row0, bh);
+      }
       for (int j = 0; j < n; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
@@ -140,7 +145,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           raise_error(p, abort, kErrTimeoutProducer);
           break;
         }
-        uint8_t *k_s = smem + TILE_BYTES + st * 2 * TILE_BYTES;
+        uint8_t *k_s = kv_s + st * 2 * TILE_BYTES;
         uint8_t *v_s = k_s + TILE_BYTES;
         mbar_expect_tx(&k_full[st], TILE_BYTES);
         tma_load_3d(k_s, &tma_k, &k_full[st], 0, j * BKV, bh);
@@ -155,64 +160,75 @@ __global__ void __launch_bounds__(THREADS, 1)
       constexpr uint32_t idesc_s = idesc_f16(false, false, false, BQ, BKV);
       constexpr uint32_t idesc_o = idesc_f16(false, false, true, BQ, HEAD);
       const uint32_t q_addr = smem_u32(q_s);
-      bool ok = mbar_wait(&q_full, 0, abort);
-      if (!ok) raise_error(p, abort, kErrTimeoutMma);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait(&k_full[st], (j >> 1) & 1, abort)) return false;
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(smem + TILE_BYTES + st * 2 * TILE_BYTES);
+      const uint32_t kv_addr = smem_u32(kv_s);
+      // S_t(j) = Q_t K(j)^T into TMEM columns [t*128, t*128+128)
+      auto issue_s = [&](int t, int j) {
+        const uint32_t k_addr = kv_addr + (j & 1) * 2 * TILE_BYTES;
 #pragma unroll
         for (int k = 0; k < HEAD / 16; ++k) {
           const uint32_t off = (k >> 2) * CHUNK_BYTES + (k & 3) * 32;
-          mma_f16(tmem + (j & 1) * BKV, smem_desc_sw128(q_addr + off, 16, 1024),
+          mma_f16(tmem + t * BKV, smem_desc_sw128(q_addr + t * TILE_BYTES + off, 16, 1024),
                   smem_desc_sw128(k_addr + off, 16, 1024), idesc_s, k > 0);
         }
-        mma_commit(&s_full[j & 1]);
-        return true;
+        mma_commit(&s_full[t]);
       };
-      if (ok && !issue_s(0)) {
-        raise_error(p, abort, kErrTimeoutMma);
-        ok = false;
-      }
-      for (int j = 0; ok && j < n; ++j) {
-        if (j + 1 < n && !issue_s(j + 1)) {
-          raise_error(p, abort, kErrTimeoutMma);
-          break;
-        }
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&p_full[st], ph, abort) || !mbar_wait(&v_full[st], ph, abort)) {
-          raise_error(p, abort, kErrTimeoutMma);
-          break;
-        }
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(smem + TILE_BYTES + st * 2 * TILE_BYTES + TILE_BYTES);
+      // O_t += P_t(j) V(j), P_t read from TMEM over S_t
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t v_addr = kv_addr + (j & 1) * 2 * TILE_BYTES + TILE_BYTES;
 #pragma unroll
         for (int k = 0; k < BKV / 16; ++k)
-          mma_f16_tmem_a(tmem + O_COL, tmem + st * BKV + k * 8,
+          mma_f16_tmem_a(tmem + O_COL + t * HEAD, tmem + t * BKV + k * 8,
                          smem_desc_sw128(v_addr + k * 2048, CHUNK_BYTES, 1024), idesc_o,
                          (j | k) != 0);
-        mma_commit(&kv_empty[st]);
-        mma_commit(&o_done);
+        mma_commit(&o_done[t]);
+      };
+      bool ok = mbar_wait(&q_full, 0, abort) && mbar_wait(&k_full[0], 0, abort);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < QT; ++t) issue_s(t, 0);
       }
+      for (int j = 0; ok && j < n; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        const bool next = j + 1 < n;
+        for (int t = 0; t < QT; ++t) {
+          if (!mbar_wait(&p_full[t], j & 1, abort) || (t == 0 && !mbar_wait(&v_full[st], ph, abort))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(t, j);
+          if (t == QT - 1) mma_commit(&kv_empty[st]);
+          if (next) {
+            if (t == 0 && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(t, j + 1);
+          }
+        }
+      }
+      if (!ok) raise_error(p, abort, kErrTimeoutMma);
     }
   } else {
+    const int t = (warp - 2) >> 2;  // query tile of this softmax warpgroup
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t s_col = t * BKV;
+    const uint32_t o_col = O_COL + t * HEAD;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n; ++j) {
-      const int b = j & 1;
-      if (!warp_wait(&s_full[b], (j >> 1) & 1, abort, p, kErrTimeoutSoftmax)) {
+      if (!warp_wait(&s_full[t], j & 1, abort, p, kErrTimeoutSoftmax)) {
         ok = false;
         break;
       }
       tc_fence_after();
       uint32_t sr[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_base + b * BKV + c * 32, sr[c]);
+      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_base + s_col + c * 32, sr[c]);
       tmem_wait_ld();
       const int valid = p.s_kv - j * BKV;
       float mx = -INFINITY;
@@ -234,7 +250,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           m = m_new;
         }
         if (j > 0) {
-          if (!warp_wait(&o_done, (j - 1) & 1, abort, p, kErrTimeoutCorrection)) {
+          if (!warp_wait(&o_done[t], (j - 1) & 1, abort, p, kErrTimeoutCorrection)) {
             ok = false;
             break;
           }
@@ -242,11 +258,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
           for (int c = 0; c < HEAD / 16; ++c) {
             uint32_t o[16];
-            tmem_ld16(tmem + lane_base + O_COL + c * 16, o);
+            tmem_ld16(tmem + lane_base + o_col + c * 16, o);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st16(tmem + lane_base + O_COL + c * 16, o);
+            tmem_st16(tmem + lane_base + o_col + c * 16, o);
           }
           tmem_wait_st();
         }
@@ -263,23 +279,23 @@ __global__ void __launch_bounds__(THREADS, 1)
           __half2 h = __floats2half2_rn(p0, p1);
           packed[i] = *reinterpret_cast<uint32_t *>(&h);
         }
-        tmem_st16(tmem + lane_base + b * BKV + c * 16, packed);
+        tmem_st16(tmem + lane_base + s_col + c * 16, packed);
       }
       tmem_wait_st();
       l += rowsum;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[b]);
+      if (lane == 0) mbar_arrive(&p_full[t]);
     }
-    if (ok && n > 0 && warp_wait(&o_done, (n - 1) & 1, abort, p, kErrTimeoutSoftmax)) {
+    if (ok && n > 0 && warp_wait(&o_done[t], (n - 1) & 1, abort, p, kErrTimeoutSoftmax)) {
       tc_fence_after();
       const float inv = 1.0f / l;
-      const int q = q_tile * BQ + row;
+      const int q = (blockIdx.x * QT + t) * BQ + row;
       __half *out = p.o + ((int64_t)bh * p.s_q + q) * HEAD;
 #pragma unroll 1
       for (int c = 0; c < HEAD / 16; ++c) {
         uint32_t o[16];
-        tmem_ld16(tmem + lane_base + O_COL + c * 16, o);
+        tmem_ld16(tmem + lane_base + o_col + c * 16, o);
         tmem_wait_ld();
         if (q < p.s_q) {
           uint4 pack[2];
@@ -434,7 +450,7 @@ extern "C" int lc_sdpa_f16(const void *q, const void *k, const void *v, void *o,
       return rc;
     configured[dev] = true;
   }
-  dim3 grid((unsigned)((s_q + BQ - 1) / BQ), (unsigned)bh);
+  dim3 grid((unsigned)((s_q + QT * BQ - 1) / (QT * BQ)), (unsigned)bh);
   sdpa_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(tq, tk, tv, p);
   return check_launch("lc_sdpa_f16");
 }
