@@ -254,11 +254,17 @@ __global__ void __maxnreg__(200)
           for (int i = 0; i < 32; ++i)
             if (c * 32 + i >= valid) sr[c][i] = __float_as_uint(-INFINITY);
       }
-      float mx = -INFINITY;  // max of the raw scores; the positive scale commutes with max
+      // max of the raw scores (the positive scale commutes with max), as 8
+      // independent chains so the reduction is not one 128-deep dependency
+      float mx8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sr[c][i]));
+        for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[c][i]));
+      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       mx *= p.scale_log2;
       const float m_new = fmaxf(m, mx);
       const bool need = m_new > m + kRescaleThreshold;
@@ -286,7 +292,7 @@ __global__ void __maxnreg__(200)
           tmem_wait_st();
         }
       }
-      float rowsum = 0.f;
+      float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent row-sum chains
       const float neg_m = -m;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -298,14 +304,14 @@ __global__ void __maxnreg__(200)
           const float x1 = fmaf(__uint_as_float(sr[c][2 * i + 1]), p.scale_log2, neg_m);
           const float p0 = (i & 3) == 3 ? ex2_poly(x0) : ex2(x0);
           const float p1 = (i & 3) == 3 ? ex2_poly(x1) : ex2(x1);
-          rowsum += p0 + p1;
+          part[i & 7] += p0 + p1;
           __half2 h = __floats2half2_rn(p0, p1);
           packed[i] = *reinterpret_cast<uint32_t *>(&h);
         }
         tmem_st16(tmem + lane_base + s_col + c * 16, packed);
       }
       tmem_wait_st();
-      l += rowsum;
+      l += ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
