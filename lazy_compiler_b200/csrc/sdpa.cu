@@ -94,7 +94,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volati
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(THREADS, 1)
     sdpa_tc_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constant__ CUtensorMap tma_k,
                    const __grid_constant__ CUtensorMap tma_v, SdpaParams p) {
   extern __shared__ uint8_t smem_raw[];
