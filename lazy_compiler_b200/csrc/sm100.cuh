@@ -61,13 +61,18 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
                : "memory");
 }
 
+// One probe of the phase; the thread may sleep in hardware for up to
+// kSuspendHintNs while the phase is incomplete (it wakes when the phase
+// completes), so waiting warps do not spin on the issue slots.
+constexpr uint32_t kSuspendHintNs = 200000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
       " selp.u32 %0, 1, 0, p;\n}"
       : "=r"(done)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return done != 0;
 }
@@ -81,7 +86,7 @@ __device__ __forceinline__ bool mbar_wait_limit(uint64_t *bar, uint32_t parity,
   const uint64_t start = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(addr, parity)) return true;
-    if ((i & 63) == 0) {
+    if ((i & 7) == 0) {
       if (*abort) return false;
       if (globaltimer() - start > limit_ns) return false;
     }
