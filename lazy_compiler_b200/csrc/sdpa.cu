@@ -105,7 +105,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   __shared__ __align__(8) uint64_t q_full;
   __shared__ __align__(8) uint64_t k_full[KV_STAGES];
   __shared__ __align__(8) uint64_t v_full[KV_STAGES];
-  __shared__ __align__(8) uint64_t kv_empty[KV_STAGES];
+  __shared__ __align__(8) uint64_t k_empty[KV_STAGES];
+  __shared__ __align__(8) uint64_t v_empty[KV_STAGES];
   __shared__ __align__(8) uint64_t s_full[QT];
   __shared__ __align__(8) uint64_t p_full[QT];
   __shared__ __align__(8) uint64_t o_done[QT];
@@ -121,7 +122,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int s = 0; s < KV_STAGES; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int t = 0; t < QT; ++t) {
       mbar_init(&s_full[t], 1);
@@ -154,18 +156,24 @@ __global__ void __launch_bounds__(THREADS, 1)
         tma_load_3d(q_s + t * TILE_BYTES, &tma_q, &q_full, 0, row0, bh);
         tma_load_3d(q_s + t * TILE_BYTES + CHUNK_BYTES, &tma_q, &q_full, 64, row0, bh);
       }
+      // K(j) is released once both S(j) products completed, V(j) once both PV(j)
+      // products completed, so K(j+2) loads while V(j) is still in use.
       for (int j = 0; j < n; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1, abort)) {
+        uint8_t *k_s = kv_s + st * 2 * TILE_BYTES;
+        uint8_t *v_s = k_s + TILE_BYTES;
+        if (!mbar_wait(&k_empty[st], ph ^ 1, abort)) {
           raise_error(p, abort, kErrTimeoutProducer);
           break;
         }
-        uint8_t *k_s = kv_s + st * 2 * TILE_BYTES;
-        uint8_t *v_s = k_s + TILE_BYTES;
         mbar_expect_tx(&k_full[st], TILE_BYTES);
         tma_load_3d(k_s, &tma_k, &k_full[st], 0, j * BKV, bh);
         tma_load_3d(k_s + CHUNK_BYTES, &tma_k, &k_full[st], 64, j * BKV, bh);
+        if (!mbar_wait(&v_empty[st], ph ^ 1, abort)) {
+          raise_error(p, abort, kErrTimeoutProducer);
+          break;
+        }
         mbar_expect_tx(&v_full[st], TILE_BYTES);
         tma_load_3d(v_s, &tma_v, &v_full[st], 0, j * BKV, bh);
         tma_load_3d(v_s + CHUNK_BYTES, &tma_v, &v_full[st], 64, j * BKV, bh);
@@ -202,6 +210,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (ok) {
         tc_fence_after();
         for (int t = 0; t < QT; ++t) issue_s(t, 0);
+        mma_commit(&k_empty[0]);
       }
       for (int j = 0; ok && j < n; ++j) {
         const int st = j & 1;
@@ -214,7 +223,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           tc_fence_after();
           issue_pv(t, j);
-          if (t == QT - 1) mma_commit(&kv_empty[st]);
+          if (t == QT - 1) mma_commit(&v_empty[st]);
           if (next) {
             if (t == 0 && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort)) {
               ok = false;
@@ -222,6 +231,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             tc_fence_after();
             issue_s(t, j + 1);
+            if (t == QT - 1) mma_commit(&k_empty[(j + 1) & 1]);
           }
         }
       }
