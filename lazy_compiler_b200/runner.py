@@ -62,7 +62,8 @@ def run_package(folder: str | Path, seed_offset: int = 0, device: str = "cuda",
                 inputs: dict | None = None) -> dict:
     """Compile and run every kernel of a package; returns graph outputs as numpy arrays.
 
-    ``inputs`` optionally overrides argument values by name (host arrays).
+    ``inputs`` optionally overrides argument values by name (host arrays or
+    tensors, which are used in place when already on the device).
     """
     import torch
 
@@ -86,8 +87,12 @@ def run_package(folder: str | Path, seed_offset: int = 0, device: str = "cuda",
             elif arg.get("intermediate"):
                 raise CompileError(f"intermediate {name} is used before it is produced")
             else:
-                host = inputs[name] if inputs and name in inputs else seeded_input(arg, seed_offset)
-                t = torch.as_tensor(np.ascontiguousarray(host)).to(dev, _torch_dtype(kind))
+                given = inputs.get(name) if inputs else None
+                if isinstance(given, torch.Tensor):
+                    t = given.to(dev, _torch_dtype(kind)).contiguous()
+                else:
+                    host = given if given is not None else seeded_input(arg, seed_offset)
+                    t = torch.as_tensor(np.ascontiguousarray(host)).to(dev, _torch_dtype(kind))
             buffers[name] = t
         for name in kernel.get("zero_outputs", []):
             buffers[name].zero_()

@@ -1,0 +1,111 @@
+"""Rescaled copies of the reference's public IR packages at the BASELINE sizes — TEST INFRASTRUCTURE.
+
+    python oracle/rescale.py REFERENCE_CHECKOUT
+
+Emmy (absent here) would schedule new IR for new shapes; instead each public
+package is copied with only its extents changed — the Tile / loop axis
+extents in the KernelOp body, the tensor shapes of the graph and meta.json,
+the meta grid (same block size, so the same per-thread schedule), and the
+count constants that depend on the size.  The rescaled packages go to
+``oracle/_ref/rescaled/<name>/`` and the reference's own compiler (unchanged,
+through ``oracle/emmy_shim``) emits their PTX to
+``oracle/_ref/ptx_rescaled/<name>.ptx``; ``manifest_rescaled.json`` records
+hashes and meta.  These are labelled "rescaled" wherever they are used.
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import re
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+OUT = HERE / "_ref"
+N28, N24 = 1 << 28, 1 << 24
+ROWS, COLS = 16384, 4096
+
+# name: (source package, {axis name: new extent}, {buffer: new shape}, grid x, {constant: value})
+PLAN = {
+    "r02_big_sum": ("problems/r02_big_sum", {"a0": N24}, {"x": [N24]}, 1, {}),
+    "r03_mean": ("problems/r03_mean", {"a0": N24}, {"x": [N24]}, 1, {"mean_keepdim_count": float(N24)}),
+    "p01_vector_add": ("problems/p01_vector_add", {"a0": N28 // 2}, {"x0": [N28], "x1": [N28], "add": [N28]},
+                       N28 // 2 // 256, {}),
+    "p02_scale_shift": ("problems/p02_scale_shift", {"a0": N28 // 4}, {"x": [N28], "add": [N28]},
+                        N28 // 4 // 256, {"mul_c1": 1.5, "add_c1": -0.25}),
+    "p03_relu_mul": ("problems/p03_relu_mul", {"a0": N28 // 4}, {"x": [N28], "y": [N28], "mul": [N28]},
+                     N28 // 4 // 256, {}),
+    "phase9_gelu_erf_tail": ("examples/phase9/generated/phase9_gelu_erf_tail", {"a0": N28},
+                             {"x": [N28], "gelu": [N28]}, N28 // 256, {}),
+    "r04_row_sum": ("problems/r04_row_sum", {"a0": ROWS, "a1": COLS}, {"x": [ROWS, COLS], "sum_1": [ROWS]},
+                    ROWS, {}),
+    "f01_rmsnorm": ("problems/f01_rmsnorm", {"a0": ROWS, "a1": COLS, "a2": COLS},
+                    {"x": [ROWS, COLS], "w": [COLS], "mul_1": [ROWS, COLS]}, ROWS,
+                    {"mean_count": float(COLS), "add_c1": 1e-6}),
+    "f02_row_softmax": ("problems/f02_row_softmax", {"a0": ROWS, "a1": COLS, "a3": COLS},
+                        {"x": [ROWS, COLS], "softmax": [ROWS, COLS]}, ROWS, {}),
+    "f03_l2norm": ("problems/f03_l2norm", {"a0": ROWS, "a1": COLS, "a2": COLS},
+                   {"x": [ROWS, COLS], "div": [ROWS, COLS]}, ROWS, {}),
+}
+
+
+def rescale_body(text: str, axes: dict) -> str:
+    for axis, extent in axes.items():
+        text, count = re.subn(rf"Axis\(name='{axis}', extent=Dim\(\d+\)", f"Axis(name='{axis}', extent=Dim({extent})", text)
+        if count == 0:
+            raise ValueError(f"axis {axis} not found")
+    return text
+
+
+def make(reference: Path, name: str) -> Path:
+    src_rel, axes, shapes, grid_x, constants = PLAN[name]
+    src = reference / src_rel
+    (ir_path,) = sorted(src.glob("*.ir.json"))
+    graph = json.loads(ir_path.read_text())
+    for node in graph["nodes"].values():
+        if node["op"] == "KernelOp":
+            node["op_fields"]["body"] = [rescale_body(b, axes) for b in node["op_fields"]["body"]]
+        for out in node.get("outputs", []):
+            if out["name"] in shapes:
+                out["shape"] = shapes[out["name"]]
+        if node["op"] == "ConstantOp" and node["op_fields"].get("name") in constants:
+            node["op_fields"]["value"] = constants[node["op_fields"]["name"]]
+    meta = json.loads((src / "meta.json").read_text())
+    meta["id"] = f"{meta['id']}_rescaled"
+    for kernel in meta["kernels"]:
+        kernel["grid"] = [grid_x, 1, 1]
+        for arg in kernel["args"]:
+            if arg["name"] in shapes:
+                arg["shape"] = shapes[arg["name"]]
+            if arg["name"] in constants:
+                arg["data"] = [constants[arg["name"]]]
+    dst = OUT / "rescaled" / name
+    dst.mkdir(parents=True, exist_ok=True)
+    (dst / ir_path.name).write_text(json.dumps(graph))
+    (dst / "meta.json").write_text(json.dumps(meta, indent=1))
+    return dst / ir_path.name
+
+
+def main(reference: Path) -> int:
+    sys.path.insert(0, str(HERE / "emmy_shim"))
+    sys.path.insert(0, str(reference))
+    import ptx_backend  # the reference compiler, unchanged
+
+    (OUT / "ptx_rescaled").mkdir(parents=True, exist_ok=True)
+    manifest = {}
+    for name in PLAN:
+        ir = make(reference, name)
+        ptx = ptx_backend.compile_file(ir)
+        (OUT / "ptx_rescaled" / f"{name}.ptx").write_text(ptx)
+        manifest[name] = {"package": str(ir.parent.relative_to(HERE.parent)),
+                          "sha256": hashlib.sha256(ptx.encode("ascii")).hexdigest(),
+                          "meta": json.loads((ir.parent / "meta.json").read_text())}
+        print(f"{name}: rescaled and compiled by the reference")
+    (OUT / "manifest_rescaled.json").write_text(json.dumps(manifest, indent=1, sort_keys=True) + "\n")
+    return 0
+
+
+if __name__ == "__main__":
+    if len(sys.argv) != 2:
+        sys.exit("usage: python oracle/rescale.py REFERENCE_CHECKOUT")
+    sys.exit(main(Path(sys.argv[1]).resolve()))

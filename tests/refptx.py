@@ -45,17 +45,23 @@ def manifest() -> dict:
     return json.loads(path.read_text()) if path.exists() else {}
 
 
+def manifest_rescaled() -> dict:
+    path = REF / "manifest_rescaled.json"
+    return json.loads(path.read_text()) if path.exists() else {}
+
+
 class RefKernel:
     """One reference-compiled PTX module, JIT-loaded on the current device."""
 
-    def __init__(self, name: str):
+    def __init__(self, name: str, rescaled: bool = False):
         import torch
         torch.cuda.init()
         torch.cuda.current_stream()  # make the primary context current
-        row = manifest()[name]
+        row = (manifest_rescaled() if rescaled else manifest())[name]
         self.meta = row["meta"]
         self.kernel_meta = self.meta["kernels"][0]
-        image = (REF / "ptx" / f"{name}.ptx").read_bytes() + b"\0"
+        folder = "ptx_rescaled" if rescaled else "ptx"
+        image = (REF / folder / f"{name}.ptx").read_bytes() + b"\0"
         cu = driver()
         self.module = ctypes.c_void_p()
         check(cu.cuModuleLoadData(ctypes.byref(self.module), ctypes.c_char_p(image)), "cuModuleLoadData")
@@ -76,8 +82,8 @@ class RefKernel:
                                       ctypes.c_uint(int(km.get("smem_bytes", 0))), ctypes.c_void_p(stream),
                                       params, None), "cuLaunchKernel")
 
-    def run(self, inputs: dict | None = None, seed_offset: int = 0) -> dict:
-        """Allocate, launch once, return graph outputs (numpy) and the device buffers."""
+    def run(self, inputs: dict | None = None, seed_offset: int = 0, keep: bool = False):
+        """Allocate, launch once, return graph outputs (numpy; with ``keep`` also the buffers)."""
         import torch
         from lazy_compiler_b200.runner import _torch_dtype, seeded_input
         km = self.kernel_meta
@@ -90,8 +96,12 @@ class RefKernel:
                 t = torch.empty(shape, dtype=_torch_dtype(arg["dtype"]), device="cuda")
                 t.fill_(-1 if arg["dtype"].startswith("i") else math.nan)
             else:
-                host = inputs[name] if inputs and name in inputs else seeded_input(arg, seed_offset)
-                t = torch.as_tensor(np.ascontiguousarray(host)).to("cuda", _torch_dtype(arg["dtype"]))
+                given = inputs.get(name) if inputs else None
+                if isinstance(given, torch.Tensor):
+                    t = given.to("cuda", _torch_dtype(arg["dtype"])).contiguous()
+                else:
+                    host = given if given is not None else seeded_input(arg, seed_offset)
+                    t = torch.as_tensor(np.ascontiguousarray(host)).to("cuda", _torch_dtype(arg["dtype"]))
             buffers[name] = t
         for name in km.get("zero_outputs", []):
             buffers[name].zero_()
@@ -102,4 +112,4 @@ class RefKernel:
         for name in self.meta["graph_outputs"]:
             t = buffers[name]
             out[name] = (t.float() if t.dtype == torch.bfloat16 else t).cpu().numpy()
-        return out
+        return (out, buffers) if keep else out
