@@ -66,6 +66,17 @@ def test_ours_match_reference_ptx(name, offset, cuda_device):
     inputs = {n: seeded_input(a, offset) for n, a in args.items()}
     ref = kernel.run(inputs)
     ours = run_package(GOLDEN / name, inputs=inputs)
+    if name in REFERENCE_KNOWN_FAILURES:
+        # the reference rounds every f16 node; against the oracle ours must pass
+        # and be at least as close as the reference PTX
+        plan = compile_file(next((GOLDEN / name).glob("*.ir.json")))
+        oracle = O.evaluate(plan, inputs)
+        for key, value in oracle.items():
+            mine = O.compare(ours[key], value, meta["rtol"], meta["atol"])
+            theirs = O.compare(ref[key], value, meta["rtol"], meta["atol"])
+            assert mine["pass"], (key, mine)
+            assert mine["mismatches"] <= theirs["mismatches"], (mine, theirs)
+        return
     for key, value in ref.items():
         row = O.compare(ours[key], value, meta["rtol"], meta["atol"])
         assert row["pass"], (key, row)

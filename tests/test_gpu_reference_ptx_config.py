@@ -58,6 +58,6 @@ def test_config_size_ours_match_reference_ptx(name, cuda_device):
         x = inputs["x"].double().cpu().numpy()
         exact = x.sum() / (x.size if name == "r03_mean" else 1)
         key = next(iter(ours))
-        ours_rel = abs(float(ours[key]) - exact) / abs(exact)
-        ref_rel = abs(float(ref[key]) - exact) / abs(exact)
+        ours_rel = abs(float(np.asarray(ours[key]).ravel()[0]) - exact) / abs(exact)
+        ref_rel = abs(float(np.asarray(ref[key]).ravel()[0]) - exact) / abs(exact)
         assert ours_rel < 1e-5, f"ours {ours_rel:.3e} (reference PTX {ref_rel:.3e})"
