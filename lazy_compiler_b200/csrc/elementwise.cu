@@ -5,8 +5,7 @@
 // per-element scalar ld.global and a v2/v4 store, grid = ceil(cells/256).
 // Here every pointwise op is one HBM pass with 128-bit streaming loads
 // (ld.global.nc.L1::no_allocate) and evict-first 128-bit stores, four vectors
-// in flight per thread, and a grid capped at 8 CTAs of 256 threads per SM
-// (full occupancy) that strides over the array.  The arithmetic uses the
+// in flight per thread, one 4096-element tile per 256-thread CTA.  The arithmetic uses the
 // reference's explicit-rounding form (mul.rn / add.rn, no FMA contraction,
 // ptx_backend.py:777-781) so add, scale-shift and relu*mul are bit-identical
 // to numpy float32.  GELU follows ptx_backend.py:1122-1140:
@@ -20,7 +19,6 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;
-constexpr int kBlocksPerSm = 8;
 
 struct AddOp {
   static constexpr int kInputs = 2;
@@ -163,11 +161,15 @@ __global__ void __launch_bounds__(kThreads) gelu16_scalar(const T *__restrict__ 
     out[i] = from_f<T>(op(to_f<T>(x[i]), 0.0f));
 }
 
+// One tile of work per CTA (no persistent cap): measured on B200, a grid that
+// covers the array outright keeps more loads in flight than a grid-stride loop
+// over 8 CTAs per SM (6.8-7.0 vs 5.4-6.5 TB/s on 2^28 elements).  The loop in
+// the kernels only strides when n exceeds what one launch grid can cover.
 int grid_for(int64_t work_items, int64_t per_block) {
-  const int64_t cap = (int64_t)sm_count() * kBlocksPerSm;
+  constexpr int64_t kMaxGrid = 0x7fffffff;
   int64_t blocks = (work_items + per_block - 1) / per_block;
   if (blocks < 1) blocks = 1;
-  return (int)(blocks < cap ? blocks : cap);
+  return (int)(blocks < kMaxGrid ? blocks : kMaxGrid);
 }
 
 template <class Op>
