@@ -264,6 +264,192 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+// ---------------------------------------------------------------- 2-SM path
+//
+// A cluster of two CTAs (one per SM of a pair) computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M=256, N=256, K=16): each CTA stages its 128 rows
+// of A and its 128 columns of B per k-block (32 KB per stage, 6 stages), so
+// each SM's shared memory carries half the B traffic of the 1-SM kernel.
+// The even CTA issues the MMAs; both CTAs' TMA loads complete on the even
+// CTA's `full` barrier; the even CTA forwards "stage free" and "accumulator
+// ready" to the odd CTA with remote mbarrier arrives, and the odd CTA's
+// epilogue arrives remotely on the even CTA's `tmem_empty`.  No multicast.
+constexpr int PBM = 128;   // rows of A per CTA (256 per pair)
+constexpr int PBN = 128;   // columns of B per CTA (256 per pair, all 256 accumulated per CTA)
+constexpr int PSTAGES = 6;
+constexpr int PA_BYTES = PBM * BK * 2;
+constexpr int PB_BYTES = BK * PBN * 2;
+constexpr int PSTAGE_BYTES = PA_BYTES + PB_BYTES;
+constexpr int PSMEM_BYTES = PSTAGES * PSTAGE_BYTES + 1024;
+constexpr int PTILE = 256;
+
+template <bool BF16, bool B_MN, int OUT, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tma_a,
+                    const __grid_constant__ CUtensorMap tma_b, GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  __shared__ __align__(8) uint64_t full_bar[PSTAGES];
+  __shared__ __align__(8) uint64_t empty_bar[PSTAGES];
+  __shared__ __align__(8) uint64_t tfull_bar[2];
+  __shared__ __align__(8) uint64_t tempty_bar[2];
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  volatile int *abort = &abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PSTAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tma_a);
+    prefetch_tmap(&tma_b);
+  }
+  cluster_sync();  // every barrier of the pair is initialised before any remote use
+  if (warp == 1) {
+    tmem_alloc_pair(&tmem_base, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  const int tiles_m = (p.m + PTILE - 1) / PTILE;
+  const int tiles_n = (p.n + PTILE - 1) / PTILE;
+  const int num_tiles = tiles_m * tiles_n;
+  const int num_kb = (p.k + BK - 1) / BK;
+  const int cluster = blockIdx.x >> 1;
+  const int clusters = gridDim.x >> 1;
+  GemmParams tp = p;
+  tp.tiles_m = tiles_m;
+  tp.tiles_n = tiles_n;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = cluster; ok && tile < num_tiles; tile += clusters) {
+        int tm, tn;
+        tile_coords(tile, tp, tm, tn);
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int stage = it % PSTAGES;
+          const uint32_t phase = (it / PSTAGES) & 1;
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort)) {
+            raise_error(p, abort, kErrTimeoutProducer);
+            ok = false;
+            break;
+          }
+          // the even CTA's MMA freed this stage: tell the odd CTA (its own wait is on its barrier)
+          if (leader && it >= PSTAGES) mbar_arrive_cluster(mapa(smem_u32(&empty_bar[stage]), 1));
+          uint8_t *a_s = smem + stage * PSTAGE_BYTES;
+          uint8_t *b_s = a_s + PA_BYTES;
+          const uint32_t full = mapa(smem_u32(&full_bar[stage]), 0);
+          if (leader) mbar_expect_tx(&full_bar[stage], 2 * PSTAGE_BYTES);
+          tma_load_2d_pair(a_s, &tma_a, full, kb * BK, tm * PTILE + rank * PBM);
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int c = 0; c < PBN / 64; ++c)
+              tma_load_2d_pair(b_s + c * (BK * 128), &tma_b, full, tn * PTILE + rank * PBN + c * 64,
+                               kb * BK);
+          } else {
+            tma_load_2d_pair(b_s, &tma_b, full, kb * BK, tn * PTILE + rank * PBN);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(BF16, false, B_MN, 2 * PBM, PTILE);
+      int it = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = cluster; ok && tile < num_tiles; tile += clusters, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, abort)) {
+          raise_error(p, abort, kErrTimeoutMma);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + acc * PTILE;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int stage = it % PSTAGES;
+          const uint32_t phase = (it / PSTAGES) & 1;
+          if (!mbar_wait(&full_bar[stage], phase, abort)) {
+            raise_error(p, abort, kErrTimeoutMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * PSTAGE_BYTES);
+          const uint32_t b_addr = a_addr + PA_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? smem_desc_sw128(b_addr + k * 2048, BK * 128, 1024)
+                                        : smem_desc_sw128(b_addr + k * 32, 16, 1024);
+            mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0);
+          }
+          mma_commit_pair(&empty_bar[stage]);
+        }
+        if (ok) mma_commit_pair(&tfull_bar[acc]);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    int local = 0;
+    for (int tile = cluster; tile < num_tiles; tile += clusters, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      int ok = 0;
+      if (lane == 0) {
+        ok = mbar_wait(&tfull_bar[acc], acc_phase, abort);
+        if (!ok) raise_error(p, abort, kErrTimeoutEpilogue);
+        // the even CTA forwards "accumulator ready" to the odd CTA once
+        else if (leader && warp == 2) mbar_arrive_cluster(mapa(smem_u32(&tfull_bar[acc]), 1));
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(tile, tp, tm, tn);
+      const int gm = tm * PTILE + rank * PBM + row;
+#pragma unroll 1
+      for (int c = 0; c < PTILE / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + acc * PTILE + c * 32, r);
+        tmem_wait_ld();
+        store_chunk<OUT, EPI>(p, gm, tn * PTILE + c * 32, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa(smem_u32(&tempty_bar[acc]), 0));
+    }
+  }
+
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the pair's MMAs may touch its memory
+  if (abort_flag) drain_delay();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, TMEM_COLS);
+  }
+}
+
 // ---------------------------------------------------------------- SIMT path
 
 template <typename TI, int OUT, int EPI>
@@ -364,11 +550,67 @@ int launch_tc(const void *a, const void *b, void *c, int m, int n, int k, cudaSt
   return check_launch("lc_gemm");
 }
 
+template <bool BF16, bool B_MN, int OUT, int EPI>
+int launch_tc2(const void *a, const void *b, void *c, int m, int n, int k, cudaStream_t s) {
+  CUtensorMap ta, tb;
+  if (int rc = make_map_2d(&ta, BF16, a, k, m, (uint64_t)k * 2, BK, PBM)) return rc;
+  if (B_MN) {
+    if (int rc = make_map_2d(&tb, BF16, b, n, k, (uint64_t)n * 2, 64, BK)) return rc;
+  } else {
+    if (int rc = make_map_2d(&tb, BF16, b, k, n, (uint64_t)k * 2, BK, PBN)) return rc;
+  }
+  GemmParams p;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.c = c;
+  p.ldc = n;
+  p.tiles_m = (m + PTILE - 1) / PTILE;
+  p.tiles_n = (n + PTILE - 1) / PTILE;
+  const int elem = OUT == LC_F32 ? 4 : 2;
+  p.vec_store = aligned(c, 16) && ((int64_t)n * elem) % 16 == 0;
+  if (int rc = device_error_word(&p.err)) return rc;
+  auto kernel = gemm_tc2_kernel<BF16, B_MN, OUT, EPI>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (int rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 PSMEM_BYTES),
+                            "gemm (2-SM) smem attribute"))
+      return rc;
+    configured[dev] = true;
+  }
+  const int tiles = p.tiles_m * p.tiles_n;
+  // persistent: as many pairs as can be resident at once (GPC boundaries may
+  // leave fewer than SMs / 2)
+  static int resident[64] = {0};
+  if (dev >= 0 && dev < 64 && resident[dev] == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sm_count(), 1, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = PSMEM_BYTES;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters < 1) {
+      cudaGetLastError();
+      clusters = sm_count() / 2;
+    }
+    resident[dev] = clusters;
+  }
+  int clusters = (dev >= 0 && dev < 64) ? resident[dev] : sm_count() / 2;
+  if (clusters > tiles) clusters = tiles;
+  if (clusters < 1) clusters = 1;
+  kernel<<<2 * clusters, THREADS, PSMEM_BYTES, s>>>(ta, tb, p);
+  return check_launch("lc_gemm (2-SM)");
+}
+
 template <bool BF16, bool B_MN>
 int dispatch_tc(int out, int epi, const void *a, const void *b, void *c, int m, int n, int k,
-                cudaStream_t s) {
-#define LC_TC(O, E) \
-  if (out == O && epi == E) return launch_tc<BF16, B_MN, O, E>(a, b, c, m, n, k, s);
+                cudaStream_t s, bool pair) {
+#define LC_TC(O, E)                                                              \
+  if (out == O && epi == E)                                                      \
+    return pair ? launch_tc2<BF16, B_MN, O, E>(a, b, c, m, n, k, s)              \
+                : launch_tc<BF16, B_MN, O, E>(a, b, c, m, n, k, s);
   LC_TC(LC_F32, LC_EPI_NONE) LC_TC(LC_F32, LC_EPI_GELU_ERF) LC_TC(LC_F32, LC_EPI_GELU_TANH)
   LC_TC(LC_F16, LC_EPI_NONE) LC_TC(LC_F16, LC_EPI_GELU_ERF) LC_TC(LC_F16, LC_EPI_GELU_TANH)
   LC_TC(LC_BF16, LC_EPI_NONE) LC_TC(LC_BF16, LC_EPI_GELU_ERF) LC_TC(LC_BF16, LC_EPI_GELU_TANH)
@@ -396,13 +638,16 @@ int dispatch_simt(int out, int epi, const void *a, const void *b, void *c, int m
 
 }  // namespace
 
-// Chooses the path of one GEMM: 1 = tcgen05, 0 = SIMT.  Exposed for tests through lc_gemm_path.
+// Chooses the path of one GEMM: 2 = tcgen05 on SM pairs, 1 = tcgen05 on one SM,
+// 0 = SIMT.  Exposed for tests through lc_gemm_path.
 int gemm_path(int ab, int b_layout, const void *a, const void *b, int64_t m, int64_t n, int64_t k) {
   (void)ab;
   const bool tma_ok = k % 8 == 0 && aligned(a, 16) && aligned(b, 16) &&
                       (b_layout == LC_B_NK || n % 8 == 0) && k >= 16;
   const bool big = m * n * k >= ((int64_t)1 << 24);
-  return tma_ok && big ? 1 : 0;
+  if (!(tma_ok && big)) return 0;
+  const int64_t pair_tiles = ((m + PTILE - 1) / PTILE) * ((n + PTILE - 1) / PTILE);
+  return m >= PTILE && n >= PTILE && pair_tiles >= 16 ? 2 : 1;
 }
 
 }  // namespace lc
@@ -426,11 +671,12 @@ extern "C" int lc_gemm(int ab_dtype, int c_dtype, int b_layout, int epilogue, co
   cudaStream_t s = as_stream(stream);
   const bool bf16 = ab_dtype == LC_BF16;
   const bool b_mn = b_layout == LC_B_KN;
-  if (gemm_path(ab_dtype, b_layout, a, b, m, n, k)) {
-    if (bf16) return b_mn ? dispatch_tc<true, true>(c_dtype, epilogue, a, b, c, m, n, k, s)
-                          : dispatch_tc<true, false>(c_dtype, epilogue, a, b, c, m, n, k, s);
-    return b_mn ? dispatch_tc<false, true>(c_dtype, epilogue, a, b, c, m, n, k, s)
-                : dispatch_tc<false, false>(c_dtype, epilogue, a, b, c, m, n, k, s);
+  if (const int path = gemm_path(ab_dtype, b_layout, a, b, m, n, k)) {
+    const bool pair = path == 2;
+    if (bf16) return b_mn ? dispatch_tc<true, true>(c_dtype, epilogue, a, b, c, m, n, k, s, pair)
+                          : dispatch_tc<true, false>(c_dtype, epilogue, a, b, c, m, n, k, s, pair);
+    return b_mn ? dispatch_tc<false, true>(c_dtype, epilogue, a, b, c, m, n, k, s, pair)
+                : dispatch_tc<false, false>(c_dtype, epilogue, a, b, c, m, n, k, s, pair);
   }
   if (bf16)
     return dispatch_simt<__nv_bfloat16>(c_dtype, epilogue, a, b, c, m, n, k, !b_mn, s);

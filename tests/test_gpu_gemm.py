@@ -87,7 +87,14 @@ def test_simt_path(m, n, k, layout, cuda_device):
 
 
 TC = [(256, 256, 256), (128, 256, 512), (333, 520, 200), (1024, 1024, 1024), (640, 1280, 4096),
-      (2000, 264, 136)]
+      (2000, 264, 136), (1024, 1024, 64), (1100, 1300, 520), (2048, 1536, 2048)]
+
+
+@pytest.mark.parametrize("m,n,k,path", [(256, 256, 256, 1), (1024, 1024, 256, 2), (4096, 4096, 64, 2),
+                                        (128, 8192, 1024, 1)])
+def test_path_selection(m, n, k, path, cuda_device):
+    _, _, ta, tb = operands(8, 8, 16, "f16", "kn")
+    assert runtime.library().lc_gemm_path(1, 0, P(ta), P(tb), m, n, k) == path
 
 
 @pytest.mark.parametrize("m,n,k", TC)
@@ -96,7 +103,7 @@ TC = [(256, 256, 256), (128, 256, 512), (333, 520, 200), (1024, 1024, 1024), (64
 def test_tcgen05_path(m, n, k, layout, ab, cuda_device):
     a, b, ta, tb = operands(m, n, k, ab, layout, seed=m + n + k)
     assert runtime.library().lc_gemm_path(runtime.DTYPE_CODES[ab], runtime.B_LAYOUTS[layout],
-                                          P(ta), P(tb), m, n, k) == 1
+                                          P(ta), P(tb), m, n, k) >= 1
     c = run_gemm(ta, tb, ab, "f32", layout, "none", m, n, k)
     ref = O.gemm(a, b, layout, "none", ab, "f32")[0]
     check(c.cpu().numpy(), ref, "f32")
