@@ -271,9 +271,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 // of A and its 128 columns of B per k-block (32 KB per stage, 6 stages), so
 // each SM's shared memory carries half the B traffic of the 1-SM kernel.
 // The even CTA issues the MMAs; both CTAs' TMA loads complete on the even
-// CTA's `full` barrier; the even CTA forwards "stage free" and "accumulator
-// ready" to the odd CTA with remote mbarrier arrives, and the odd CTA's
-// epilogue arrives remotely on the even CTA's `tmem_empty`.  No multicast.
+// CTA's `full` barrier; the MMA commits arrive on the `empty` and
+// `tmem_full` barriers of both CTAs (the commit's CTA-mask form), and the odd
+// CTA's epilogue arrives remotely on the even CTA's `tmem_empty`.  No TMA
+// load multicasts.
 constexpr int PBM = 128;   // rows of A per CTA (256 per pair)
 constexpr int PBN = 128;   // columns of B per CTA (256 per pair, all 256 accumulated per CTA)
 constexpr int PSTAGES = 6;
@@ -352,8 +353,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             ok = false;
             break;
           }
-          // the even CTA's MMA freed this stage: tell the odd CTA (its own wait is on its barrier)
-          if (leader && it >= PSTAGES) mbar_arrive_cluster(mapa(smem_u32(&empty_bar[stage]), 1));
           uint8_t *a_s = smem + stage * PSTAGE_BYTES;
           uint8_t *b_s = a_s + PA_BYTES;
           const uint32_t full = mapa(smem_u32(&full_bar[stage]), 0);
@@ -403,9 +402,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                                         : smem_desc_sw128(b_addr + k * 32, 16, 1024);
             mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0);
           }
-          mma_commit_pair(&empty_bar[stage]);
+          mma_commit_pair_both(&empty_bar[stage]);
         }
-        if (ok) mma_commit_pair(&tfull_bar[acc]);
+        if (ok) mma_commit_pair_both(&tfull_bar[acc]);
       }
     }
   } else {
@@ -419,8 +418,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       if (lane == 0) {
         ok = mbar_wait(&tfull_bar[acc], acc_phase, abort);
         if (!ok) raise_error(p, abort, kErrTimeoutEpilogue);
-        // the even CTA forwards "accumulator ready" to the odd CTA once
-        else if (leader && warp == 2) mbar_arrive_cluster(mapa(smem_u32(&tfull_bar[acc]), 1));
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;

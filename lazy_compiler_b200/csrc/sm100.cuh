@@ -151,10 +151,9 @@ __device__ __forceinline__ uint32_t mapa(uint32_t local_smem_addr, uint32_t rank
   return r;
 }
 
-// Arrive (release, cluster scope) on an mbarrier given by a shared::cluster address.
+// Arrive on an mbarrier given by a shared::cluster address (possibly another CTA's).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // 2-D TMA load issued by either CTA of a 2-SM pair into its own shared memory,
@@ -219,6 +218,17 @@ __device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
   asm volatile(
       "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
           smem_u32(bar))
+      : "memory");
+}
+// Arrives once on `bar` in both CTAs of the pair (same shared offset; CTA mask
+// 0b11) when the pair MMAs complete.  This is the commit's own signalling
+// form; it moves no data (the TMA loads of this library never multicast).
+__device__ __forceinline__ void mma_commit_pair_both(uint64_t *bar) {
+  const uint16_t mask = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(mask)
       : "memory");
 }
 
