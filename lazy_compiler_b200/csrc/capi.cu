@@ -5,6 +5,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <utility>
 
 #include "common.cuh"
@@ -15,6 +16,11 @@ thread_local int g_status = LC_OK;
 
 std::mutex g_mutex;
 std::map<std::pair<int, cudaStream_t>, lc::ReduceWorkspace> g_workspaces;
+struct Scratch {
+  void *ptr = nullptr;
+  size_t bytes = 0;
+};
+std::map<std::tuple<int, cudaStream_t, int>, Scratch> g_scratch;
 int *g_error_words[64] = {nullptr};
 int g_sms[64] = {0};
 }  // namespace
@@ -76,6 +82,31 @@ int reduce_workspace(cudaStream_t stream, ReduceWorkspace *out) {
                                                 kMaxPartials * sizeof(double));
   g_workspaces.emplace(key, ws);
   *out = ws;
+  return LC_OK;
+}
+
+int scratch_buffer(cudaStream_t stream, int slot, size_t bytes, void **out) {
+  int dev = 0;
+  if (int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  Scratch &sc = g_scratch[std::make_tuple(dev, stream, slot)];
+  if (sc.bytes < bytes) {
+    if (sc.ptr) {
+      // the stream may still read the old buffer
+      if (int rc = check_cuda(cudaStreamSynchronize(stream), "scratch: stream")) return rc;
+      cudaFree(sc.ptr);
+      sc.ptr = nullptr;
+      sc.bytes = 0;
+    }
+    void *mem = nullptr;
+    if (cudaMalloc(&mem, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(LC_ERR_NOMEM, "scratch: cudaMalloc(%zu) failed", bytes);
+    }
+    sc.ptr = mem;
+    sc.bytes = bytes;
+  }
+  *out = sc.ptr;
   return LC_OK;
 }
 

@@ -35,6 +35,21 @@ struct ReduceWorkspace {
 constexpr int kMaxPartials = 4096;
 int reduce_workspace(cudaStream_t stream, ReduceWorkspace *out);
 
+// GEMM paths shared between the 16-bit (gemm.cu) and f32 (gemm_f32.cu) entry
+// points.  gemm_path16/32 return 2 (tcgen05 on SM pairs), 1 (tcgen05 on one
+// SM) or 0 (SIMT); gemm_tc_launch runs the tcgen05 kernel on 16-bit operands.
+int gemm_path16(int b_layout, const void *a, const void *b, int64_t m, int64_t n, int64_t k);
+int gemm_path32(int b_layout, const void *a, const void *b, int64_t m, int64_t n, int64_t k);
+int gemm_tc_launch(bool bf16, bool b_mn, int out, int epi, const void *a, const void *b,
+                   const float *bias, void *c, int m, int n, int k, cudaStream_t s, bool pair);
+int gemm_f32(int out, int b_layout, int epi, const void *a, const void *b, const float *bias,
+             void *c, int m, int n, int k, cudaStream_t s);
+
+// Library-owned scratch of at least `bytes`, one per (device, stream, slot),
+// grown (never shrunk) on demand with cudaMalloc.  Growing synchronises the
+// device, so it must not happen inside stream capture.
+int scratch_buffer(cudaStream_t stream, int slot, size_t bytes, void **out);
+
 // Per-device error word that kernels with bounded waits write when a wait
 // gives up (zero-initialised; read and cleared by lc_device_status).
 int device_error_word(int **out);

@@ -51,6 +51,7 @@ constexpr int GROUP_M = 8;
 struct GemmParams {
   int m, n, k;
   void *c;
+  const float *bias;  // f32 [N] added before the activation, or null
   int64_t ldc;
   int tiles_m, tiles_n;
   int vec_store;
@@ -78,7 +79,12 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int gm, int gn0
                                             const uint32_t (&r)[32]) {
   float v[32];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = apply_epilogue<EPI>(__uint_as_float(r[j]));
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  if (p.bias) {
+    for (int j = 0; j < 32 && gn0 + j < p.n; ++j) v[j] = __fadd_rn(v[j], p.bias[gn0 + j]);
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = apply_epilogue<EPI>(v[j]);
   if (gm >= p.m) return;
   const bool full = p.vec_store && gn0 + 32 <= p.n;
   if constexpr (OUT == LC_F32) {
@@ -451,8 +457,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 
 template <typename TI, int OUT, int EPI>
 __global__ void __launch_bounds__(256) gemm_simt_kernel(const TI *__restrict__ a,
-                                                        const TI *__restrict__ b, void *c, int m,
-                                                        int n, int k, int b_nk) {
+                                                        const TI *__restrict__ b,
+                                                        const float *__restrict__ bias, void *c,
+                                                        int m, int n, int k, int b_nk) {
   __shared__ float as[16][17];
   __shared__ float bs[16][17];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -470,6 +477,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const TI *__restrict__ a
     __syncthreads();
   }
   if (row < m && col < n) {
+    if (bias) acc = __fadd_rn(acc, bias[col]);
     const float v = apply_epilogue<EPI>(acc);
     if constexpr (OUT == LC_F32) static_cast<float *>(c)[(int64_t)row * n + col] = v;
     else {
@@ -511,7 +519,8 @@ int make_map_2d(CUtensorMap *map, bool bf16, const void *base, uint64_t inner, u
 }
 
 template <bool BF16, bool B_MN, int OUT, int EPI>
-int launch_tc(const void *a, const void *b, void *c, int m, int n, int k, cudaStream_t s) {
+int launch_tc(const void *a, const void *b, const float *bias, void *c, int m, int n, int k,
+              cudaStream_t s) {
   CUtensorMap ta, tb;
   if (int rc = make_map_2d(&ta, BF16, a, k, m, (uint64_t)k * 2, BK, BM)) return rc;
   if (B_MN) {
@@ -524,6 +533,7 @@ int launch_tc(const void *a, const void *b, void *c, int m, int n, int k, cudaSt
   p.n = n;
   p.k = k;
   p.c = c;
+  p.bias = bias;
   p.ldc = n;
   p.tiles_m = (m + BM - 1) / BM;
   p.tiles_n = (n + BN - 1) / BN;
@@ -548,7 +558,8 @@ int launch_tc(const void *a, const void *b, void *c, int m, int n, int k, cudaSt
 }
 
 template <bool BF16, bool B_MN, int OUT, int EPI>
-int launch_tc2(const void *a, const void *b, void *c, int m, int n, int k, cudaStream_t s) {
+int launch_tc2(const void *a, const void *b, const float *bias, void *c, int m, int n, int k,
+               cudaStream_t s) {
   CUtensorMap ta, tb;
   if (int rc = make_map_2d(&ta, BF16, a, k, m, (uint64_t)k * 2, BK, PBM)) return rc;
   if (B_MN) {
@@ -561,6 +572,7 @@ int launch_tc2(const void *a, const void *b, void *c, int m, int n, int k, cudaS
   p.n = n;
   p.k = k;
   p.c = c;
+  p.bias = bias;
   p.ldc = n;
   p.tiles_m = (m + PTILE - 1) / PTILE;
   p.tiles_n = (n + PTILE - 1) / PTILE;
@@ -602,12 +614,12 @@ int launch_tc2(const void *a, const void *b, void *c, int m, int n, int k, cudaS
 }
 
 template <bool BF16, bool B_MN>
-int dispatch_tc(int out, int epi, const void *a, const void *b, void *c, int m, int n, int k,
-                cudaStream_t s, bool pair) {
+int dispatch_tc(int out, int epi, const void *a, const void *b, const float *bias, void *c, int m,
+                int n, int k, cudaStream_t s, bool pair) {
 #define LC_TC(O, E)                                                              \
   if (out == O && epi == E)                                                      \
-    return pair ? launch_tc2<BF16, B_MN, O, E>(a, b, c, m, n, k, s)              \
-                : launch_tc<BF16, B_MN, O, E>(a, b, c, m, n, k, s);
+    return pair ? launch_tc2<BF16, B_MN, O, E>(a, b, bias, c, m, n, k, s)        \
+                : launch_tc<BF16, B_MN, O, E>(a, b, bias, c, m, n, k, s);
   LC_TC(LC_F32, LC_EPI_NONE) LC_TC(LC_F32, LC_EPI_GELU_ERF) LC_TC(LC_F32, LC_EPI_GELU_TANH)
   LC_TC(LC_F16, LC_EPI_NONE) LC_TC(LC_F16, LC_EPI_GELU_ERF) LC_TC(LC_F16, LC_EPI_GELU_TANH)
   LC_TC(LC_BF16, LC_EPI_NONE) LC_TC(LC_BF16, LC_EPI_GELU_ERF) LC_TC(LC_BF16, LC_EPI_GELU_TANH)
@@ -616,14 +628,14 @@ int dispatch_tc(int out, int epi, const void *a, const void *b, void *c, int m, 
 }
 
 template <typename TI>
-int dispatch_simt(int out, int epi, const void *a, const void *b, void *c, int m, int n, int k,
-                  int b_nk, cudaStream_t s) {
+int dispatch_simt(int out, int epi, const void *a, const void *b, const float *bias, void *c, int m,
+                  int n, int k, int b_nk, cudaStream_t s) {
   dim3 grid((n + 15) / 16, (m + 15) / 16);
   const TI *ai = static_cast<const TI *>(a);
   const TI *bi = static_cast<const TI *>(b);
 #define LC_SIMT(O, E)                                                       \
   if (out == O && epi == E) {                                               \
-    gemm_simt_kernel<TI, O, E><<<grid, 256, 0, s>>>(ai, bi, c, m, n, k, b_nk); \
+    gemm_simt_kernel<TI, O, E><<<grid, 256, 0, s>>>(ai, bi, bias, c, m, n, k, b_nk); \
     return check_launch("lc_gemm (simt)");                                  \
   }
   LC_SIMT(LC_F32, LC_EPI_NONE) LC_SIMT(LC_F32, LC_EPI_GELU_ERF) LC_SIMT(LC_F32, LC_EPI_GELU_TANH)
@@ -635,10 +647,9 @@ int dispatch_simt(int out, int epi, const void *a, const void *b, void *c, int m
 
 }  // namespace
 
-// Chooses the path of one GEMM: 2 = tcgen05 on SM pairs, 1 = tcgen05 on one SM,
-// 0 = SIMT.  Exposed for tests through lc_gemm_path.
-int gemm_path(int ab, int b_layout, const void *a, const void *b, int64_t m, int64_t n, int64_t k) {
-  (void)ab;
+// Chooses the path of one 16-bit GEMM: 2 = tcgen05 on SM pairs, 1 = tcgen05 on
+// one SM, 0 = SIMT.
+int gemm_path16(int b_layout, const void *a, const void *b, int64_t m, int64_t n, int64_t k) {
   const bool tma_ok = k % 8 == 0 && aligned(a, 16) && aligned(b, 16) &&
                       (b_layout == LC_B_NK || n % 8 == 0) && k >= 16;
   const bool big = m * n * k >= ((int64_t)1 << 24);
@@ -647,13 +658,22 @@ int gemm_path(int ab, int b_layout, const void *a, const void *b, int64_t m, int
   return m >= PTILE && n >= PTILE && pair_tiles >= 16 ? 2 : 1;
 }
 
+int gemm_tc_launch(bool bf16, bool b_mn, int out, int epi, const void *a, const void *b,
+                   const float *bias, void *c, int m, int n, int k, cudaStream_t s, bool pair) {
+  if (bf16) return b_mn ? dispatch_tc<true, true>(out, epi, a, b, bias, c, m, n, k, s, pair)
+                        : dispatch_tc<true, false>(out, epi, a, b, bias, c, m, n, k, s, pair);
+  return b_mn ? dispatch_tc<false, true>(out, epi, a, b, bias, c, m, n, k, s, pair)
+              : dispatch_tc<false, false>(out, epi, a, b, bias, c, m, n, k, s, pair);
+}
+
 }  // namespace lc
 
-extern "C" int lc_gemm(int ab_dtype, int c_dtype, int b_layout, int epilogue, const void *a,
-                       const void *b, void *c, int64_t m, int64_t n, int64_t k, void *stream) {
+extern "C" int lc_gemm_ex(int ab_dtype, int c_dtype, int b_layout, int epilogue, const void *a,
+                          const void *b, const void *bias, void *c, int64_t m, int64_t n,
+                          int64_t k, void *stream) {
   using namespace lc;
-  if (ab_dtype != LC_F16 && ab_dtype != LC_BF16)
-    return fail(LC_ERR_INVALID, "lc_gemm: operands must be LC_F16 or LC_BF16");
+  if (ab_dtype != LC_F32 && ab_dtype != LC_F16 && ab_dtype != LC_BF16)
+    return fail(LC_ERR_INVALID, "lc_gemm: unknown operand type %d", ab_dtype);
   if (c_dtype != LC_F32 && c_dtype != LC_F16 && c_dtype != LC_BF16)
     return fail(LC_ERR_INVALID, "lc_gemm: unknown output type %d", c_dtype);
   if (b_layout != LC_B_KN && b_layout != LC_B_NK)
@@ -665,22 +685,27 @@ extern "C" int lc_gemm(int ab_dtype, int c_dtype, int b_layout, int epilogue, co
     return fail(LC_ERR_UNSUPPORTED, "lc_gemm: dimensions above 2^31-1");
   if (m == 0 || n == 0) return LC_OK;
   if (!c || (k > 0 && (!a || !b))) return fail(LC_ERR_INVALID, "lc_gemm: null buffer");
+  const float *bias_f = static_cast<const float *>(bias);
   cudaStream_t s = as_stream(stream);
+  if (ab_dtype == LC_F32)
+    return gemm_f32(c_dtype, b_layout, epilogue, a, b, bias_f, c, (int)m, (int)n, (int)k, s);
   const bool bf16 = ab_dtype == LC_BF16;
   const bool b_mn = b_layout == LC_B_KN;
-  if (const int path = gemm_path(ab_dtype, b_layout, a, b, m, n, k)) {
-    const bool pair = path == 2;
-    if (bf16) return b_mn ? dispatch_tc<true, true>(c_dtype, epilogue, a, b, c, m, n, k, s, pair)
-                          : dispatch_tc<true, false>(c_dtype, epilogue, a, b, c, m, n, k, s, pair);
-    return b_mn ? dispatch_tc<false, true>(c_dtype, epilogue, a, b, c, m, n, k, s, pair)
-                : dispatch_tc<false, false>(c_dtype, epilogue, a, b, c, m, n, k, s, pair);
-  }
+  if (const int path = gemm_path16(b_layout, a, b, m, n, k))
+    return gemm_tc_launch(bf16, b_mn, c_dtype, epilogue, a, b, bias_f, c, (int)m, (int)n, (int)k,
+                          s, path == 2);
   if (bf16)
-    return dispatch_simt<__nv_bfloat16>(c_dtype, epilogue, a, b, c, m, n, k, !b_mn, s);
-  return dispatch_simt<__half>(c_dtype, epilogue, a, b, c, m, n, k, !b_mn, s);
+    return dispatch_simt<__nv_bfloat16>(c_dtype, epilogue, a, b, bias_f, c, m, n, k, !b_mn, s);
+  return dispatch_simt<__half>(c_dtype, epilogue, a, b, bias_f, c, m, n, k, !b_mn, s);
+}
+
+extern "C" int lc_gemm(int ab_dtype, int c_dtype, int b_layout, int epilogue, const void *a,
+                       const void *b, void *c, int64_t m, int64_t n, int64_t k, void *stream) {
+  return lc_gemm_ex(ab_dtype, c_dtype, b_layout, epilogue, a, b, nullptr, c, m, n, k, stream);
 }
 
 extern "C" int lc_gemm_path(int ab_dtype, int b_layout, const void *a, const void *b, int64_t m,
                             int64_t n, int64_t k) {
-  return lc::gemm_path(ab_dtype, b_layout, a, b, m, n, k);
+  if (ab_dtype == LC_F32) return lc::gemm_path32(b_layout, a, b, m, n, k);
+  return lc::gemm_path16(b_layout, a, b, m, n, k);
 }
