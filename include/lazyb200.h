@@ -157,20 +157,54 @@ int lc_l2norm_f32(const float *x, float *out, int64_t rows, int64_t cols, void *
 
 /* ---------------------------------------------------------------- tensor cores */
 
-/* C[M,N] = epilogue(A[M,K] @ B), f32 accumulation on tcgen05 with TMEM
- * accumulators.  ab_dtype LC_F16 or LC_BF16; c_dtype LC_F32, LC_F16 or
- * LC_BF16; b_layout LC_B_KN or LC_B_NK; epilogue LC_EPI_*.
+/* C[M,N] = epilogue(A[M,K] @ B), f32 accumulation.  ab_dtype LC_F16 or
+ * LC_BF16 (tcgen05 with TMEM accumulators; c_dtype LC_F32, LC_F16 or LC_BF16)
+ * or LC_F32 (c_dtype LC_F32; FP32 accuracy without TF32: a SIMT FFMA kernel,
+ * or for large problems an exact three-way bf16 split of A and B summed by
+ * the tcgen05 GEMM, with a plain f32 recomputation when an operand is not
+ * finite).  b_layout LC_B_KN or LC_B_NK; epilogue LC_EPI_*.
  * Replaces ptx_tensor.py:160-473 (RegFragment / LdmatrixLoad / MmaSyncPtx /
- * RegStore m16n8k16 mma.sync lowering with its fused epilogue). */
+ * RegStore m16n8k16 mma.sync lowering with its fused epilogue) and, for f32
+ * operands, the scalar matmul schedules (cp.async staging ptx_backend.py:1457-1492,
+ * Dot2 ptx_backend.py:571-593, split-K red.global.add ptx_backend.py:1307-1318). */
 int lc_gemm(int ab_dtype, int c_dtype, int b_layout, int epilogue, const void *a,
             const void *b, void *c, int64_t m, int64_t n, int64_t k, void *stream);
 
-/* Which kernel lc_gemm would run for these operands: 1 = tcgen05 (TMA needs
- * K and, for LC_B_KN, N to be multiples of 8 and 16-byte aligned bases; the
- * problem must have at least 2^24 multiply-adds), 0 = the SIMT kernel.  Host
- * only; no reference counterpart. */
+/* lc_gemm with a bias: C = epilogue(A @ B + bias[col]); bias is f32 [N] (or
+ * NULL) and is added, rounded once, before the activation.  Replaces the
+ * RegStore epilogue lambdas with a bias load (ptx_tensor.py:431-457) and the
+ * scalar bias-GELU matmul (examples/phase9/generated/phase9_bias_gelu_gemm). */
+int lc_gemm_ex(int ab_dtype, int c_dtype, int b_layout, int epilogue, const void *a,
+               const void *b, const void *bias, void *c, int64_t m, int64_t n, int64_t k,
+               void *stream);
+
+/* Which kernel lc_gemm would run for these operands.  16-bit operands:
+ * 2 = tcgen05 on SM pairs (M, N >= 256 and >= 16 pair tiles), 1 = tcgen05 on
+ * one SM (TMA needs K and, for LC_B_KN, N to be multiples of 8 and 16-byte
+ * aligned bases; at least 2^24 multiply-adds), 0 = the SIMT kernel.  LC_F32
+ * operands: 1 or 2 = bf16 split on tcgen05 (K a multiple of 4, at least 2^30
+ * multiply-adds), 0 = the SIMT FFMA kernel.  Host only; no reference
+ * counterpart. */
 int lc_gemm_path(int ab_dtype, int b_layout, const void *a, const void *b, int64_t m, int64_t n,
                  int64_t k);
+
+/* Score forms of the FP32 attention IR: s = dot * c, dot * (1/c) with 1/c
+ * rounded once (the IR's reciprocal-then-multiply), or dot / c. */
+#define LC_SCALE_MUL 0
+#define LC_SCALE_MUL_RECIP 1
+#define LC_SCALE_DIV 2
+
+/* O[bh, s_q, dv] = epilogue(softmax(score(Q Kt)) V) in f32 with Q [bh, s_q, d],
+ * Kt [bh, d, s_kv] (keys pre-transposed, as the reference's attention IR
+ * takes them), V [bh, s_kv, dv]; `scale` is a 1-element f32 device buffer.
+ * exp is ex2.approx(x * log2 e), the running max starts at -1e30 and the
+ * output is acc * (1/sum), as in the IR.  Replaces the scalar online-softmax
+ * attention kernels (problems/a01_attention, problems/a02_attention_128,
+ * examples/phase9/generated/phase9_gelu_attention; ptx_backend.py:1062-1068
+ * exp, :1047-1048 reciprocal). */
+int lc_attention_f32(int scale_mode, int epilogue, const void *scale, const void *q,
+                     const void *kt, const void *v, void *o, int64_t bh, int64_t s_q,
+                     int64_t s_kv, int64_t d, int64_t dv, void *stream);
 
 /* O = softmax(scale * Q K^T) V per (batch*head); Q,K,V,O f16 [bh, s, d]
  * row-major, softmax statistics in f32, non-causal.  Replaces the

@@ -1,0 +1,276 @@
+// FP32 attention, O = epilogue(softmax(score(Q Kt)) V), the reference's scalar
+// attention class.
+//
+// Replaces the per-output online-softmax kernels Emmy schedules for FP32
+// attention (problems/a01_attention, problems/a02_attention_128,
+// examples/phase9/generated/phase9_gelu_attention): every thread of those
+// kernels walks all keys for its (query row, value column) pairs, recomputing
+// each q.kt dot product, with exp(x) = ex2.approx(x * log2 e)
+// (ptx_backend.py:1062-1068), reciprocal = 1 / x correctly rounded
+// (ptx_backend.py:1047-1048) and the coupled (max, sum, acc) accumulators of
+// the IR (running max seeded with -1e30).
+//
+// Here one CTA of 256 threads owns 64 query rows of one (batch, head): Q is
+// staged once in shared memory (transposed), then per 64-key block Kt and V
+// are staged, each thread computes a 4 x 4 block of scores with FFMA, the row
+// max and sum are combined across the 16 threads sharing a row by shuffles,
+// P goes through shared memory and each thread accumulates a 4 x 4 (head
+// size <= 64) or 4 x 8 (<= 128) block of O in registers.  The score is
+// dot * c, dot * (1/c) or dot / c for the 1-element scale buffer c, matching
+// the three forms the IR can take.  Head sizes above 128 take a direct kernel
+// with one thread per output element.
+#include "common.cuh"
+#include "epilogue.cuh"
+
+namespace lc {
+namespace {
+
+constexpr int BQ = 64;
+constexpr int BKV = 64;
+constexpr int kThreads = 256;
+constexpr int kMaxTiled = 128;
+constexpr int QS = BQ + 4;  // padded row of the transposed Q tile
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kMaxIdentity = -1e30f;  // the IR's identity of `maximum`
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// exp as the reference lowers it
+__device__ __forceinline__ float exp_ref(float x) { return ex2_approx(__fmul_rn(x, kLog2e)); }
+
+__device__ __forceinline__ float apply_scale(float dot, float c, float rc, int mode) {
+  if (mode == LC_SCALE_MUL) return __fmul_rn(dot, c);
+  if (mode == LC_SCALE_MUL_RECIP) return __fmul_rn(dot, rc);
+  return __fdiv_rn(dot, c);
+}
+
+template <int DVH, int EPI>
+__global__ void __launch_bounds__(kThreads) attention_f32_kernel(
+    const float *__restrict__ q, const float *__restrict__ kt, const float *__restrict__ v,
+    float *__restrict__ o, int s_q, int s_kv, int d, int dv, const float *__restrict__ scale,
+    int scale_mode) {
+  constexpr int DVW = 64 * DVH;  // value columns staged per key
+  extern __shared__ float4 smem4[];
+  float *Qs = reinterpret_cast<float *>(smem4);  // [d][QS]   Q transposed
+  float *Ks = Qs + d * QS;                        // [d][BKV]  Kt block
+  float *Vs = Ks + d * BKV;                       // [BKV][DVW]
+  float *Ps = Vs + BKV * DVW;                     // [BKV][BQ]  P transposed
+
+  const int t = threadIdx.x, tx = t & 15, ty = t >> 4;
+  const int bh = blockIdx.y;
+  const int q0 = blockIdx.x * BQ;
+  const float *qb = q + (int64_t)bh * s_q * d;
+  const float *kb = kt + (int64_t)bh * d * s_kv;
+  const float *vb = v + (int64_t)bh * s_kv * dv;
+  const float c = scale[0];
+  const float rc = __frcp_rn(c);
+
+  for (int idx = t; idx < BQ * d; idx += kThreads) {
+    const int row = idx / d, dd = idx - row * d;
+    Qs[dd * QS + row] = q0 + row < s_q ? qb[(int64_t)(q0 + row) * d + dd] : 0.f;
+  }
+
+  float m[4], l[4], acc[4][4 * DVH];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = kMaxIdentity;
+    l[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4 * DVH; ++j) acc[i][j] = 0.f;
+  }
+
+  for (int k0 = 0; k0 < s_kv; k0 += BKV) {
+    for (int idx = t; idx < d * BKV; idx += kThreads) {
+      const int dd = idx / BKV, key = idx - dd * BKV;
+      Ks[idx] = k0 + key < s_kv ? kb[(int64_t)dd * s_kv + k0 + key] : 0.f;
+    }
+    for (int idx = t; idx < BKV * DVW; idx += kThreads) {
+      const int key = idx / DVW, col = idx - key * DVW;
+      Vs[idx] = (k0 + key < s_kv && col < dv) ? vb[(int64_t)(k0 + key) * dv + col] : 0.f;
+    }
+    __syncthreads();
+
+    float s[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
+    for (int dd = 0; dd < d; ++dd) {
+      const float4 a = *reinterpret_cast<const float4 *>(&Qs[dd * QS + ty * 4]);
+      const float4 b = *reinterpret_cast<const float4 *>(&Ks[dd * BKV + tx * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s[i][j] = fmaf(av[i], bv[j], s[i][j]);
+    }
+
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float x = apply_scale(s[i][j], c, rc, scale_mode);
+        s[i][j] = k0 + tx * 4 + j < s_kv ? x : -INFINITY;
+        mx = fmaxf(mx, s[i][j]);
+      }
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_new = fmaxf(m[i], mx);
+      const float alpha = exp_ref(__fsub_rn(m[i], m_new));
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        s[i][j] = exp_ref(__fsub_rn(s[i][j], m_new));
+        sum = __fadd_rn(sum, s[i][j]);
+      }
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, off));
+      l[i] = __fadd_rn(__fmul_rn(l[i], alpha), sum);
+      m[i] = m_new;
+#pragma unroll
+      for (int j = 0; j < 4 * DVH; ++j) acc[i][j] = __fmul_rn(acc[i][j], alpha);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<float4 *>(&Ps[(tx * 4 + j) * BQ + ty * 4]) =
+          make_float4(s[0][j], s[1][j], s[2][j], s[3][j]);
+    __syncthreads();
+
+    const int keys = s_kv - k0 < BKV ? s_kv - k0 : BKV;
+    for (int key = 0; key < keys; ++key) {
+      const float4 pr = *reinterpret_cast<const float4 *>(&Ps[key * BQ + ty * 4]);
+      const float pv[4] = {pr.x, pr.y, pr.z, pr.w};
+#pragma unroll
+      for (int h = 0; h < DVH; ++h) {
+        const float4 w = *reinterpret_cast<const float4 *>(&Vs[key * DVW + h * 64 + tx * 4]);
+        const float wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][h * 4 + j] = fmaf(pv[i], wv[j], acc[i][h * 4 + j]);
+      }
+    }
+    __syncthreads();  // the next block overwrites Ks, Vs and Ps
+  }
+
+  float *ob = o + (int64_t)bh * s_q * dv;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int row = q0 + ty * 4 + i;
+    if (row >= s_q) continue;
+    const float inv = __frcp_rn(l[i]);
+#pragma unroll
+    for (int h = 0; h < DVH; ++h)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int col = h * 64 + tx * 4 + j;
+        if (col < dv) ob[(int64_t)row * dv + col] = apply_epilogue<EPI>(__fmul_rn(acc[i][h * 4 + j], inv));
+      }
+  }
+}
+
+// Any head size: one thread per output element, online softmax over the keys
+// in order, the arithmetic of the tiled kernel.
+template <int EPI>
+__global__ void __launch_bounds__(256) attention_f32_direct_kernel(
+    const float *__restrict__ q, const float *__restrict__ kt, const float *__restrict__ v,
+    float *__restrict__ o, int64_t bh, int s_q, int s_kv, int d, int dv,
+    const float *__restrict__ scale, int scale_mode) {
+  const int64_t total = bh * s_q * dv;
+  const float c = scale[0];
+  const float rc = __frcp_rn(c);
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int col = (int)(e % dv);
+    const int64_t r = e / dv;
+    const int row = (int)(r % s_q);
+    const int64_t b = r / s_q;
+    const float *qr = q + (b * s_q + row) * d;
+    const float *kb = kt + b * d * s_kv;
+    const float *vb = v + b * s_kv * dv;
+    float m = kMaxIdentity, l = 0.f, acc = 0.f;
+    for (int key = 0; key < s_kv; ++key) {
+      float dot = 0.f;
+      for (int dd = 0; dd < d; ++dd) dot = fmaf(qr[dd], kb[(int64_t)dd * s_kv + key], dot);
+      const float x = apply_scale(dot, c, rc, scale_mode);
+      const float m_new = fmaxf(m, x);
+      const float alpha = exp_ref(__fsub_rn(m, m_new));
+      const float p = exp_ref(__fsub_rn(x, m_new));
+      l = __fadd_rn(__fmul_rn(l, alpha), p);
+      acc = __fadd_rn(__fmul_rn(acc, alpha), __fmul_rn(vb[(int64_t)key * dv + col], p));
+      m = m_new;
+    }
+    o[e] = apply_epilogue<EPI>(__fmul_rn(acc, __frcp_rn(l)));
+  }
+}
+
+size_t tiled_smem(int d, int dvh) {
+  return (size_t)(d * QS + d * BKV + BKV * 64 * dvh + BKV * BQ) * sizeof(float);
+}
+
+template <int DVH, int EPI>
+int launch_tiled(const float *q, const float *kt, const float *v, float *o, int64_t bh, int s_q,
+                 int s_kv, int d, int dv, const float *scale, int mode, cudaStream_t s) {
+  auto kernel = attention_f32_kernel<DVH, EPI>;
+  const size_t smem = tiled_smem(d, DVH);
+  if (smem > 48 * 1024) {
+    if (int rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)tiled_smem(kMaxTiled, DVH)),
+                            "attention smem attribute"))
+      return rc;
+  }
+  dim3 grid((s_q + BQ - 1) / BQ, (unsigned)bh);
+  kernel<<<grid, kThreads, smem, s>>>(q, kt, v, o, s_q, s_kv, d, dv, scale, mode);
+  return check_launch("lc_attention_f32");
+}
+
+template <int EPI>
+int launch(const float *q, const float *kt, const float *v, float *o, int64_t bh, int s_q,
+           int s_kv, int d, int dv, const float *scale, int mode, cudaStream_t s) {
+  if (d <= kMaxTiled && dv <= kMaxTiled) {
+    if (dv <= 64) return launch_tiled<1, EPI>(q, kt, v, o, bh, s_q, s_kv, d, dv, scale, mode, s);
+    return launch_tiled<2, EPI>(q, kt, v, o, bh, s_q, s_kv, d, dv, scale, mode, s);
+  }
+  const int64_t total = bh * s_q * dv;
+  const int64_t blocks = (total + 255) / 256;
+  const int64_t cap = 16LL * sm_count();
+  attention_f32_direct_kernel<EPI><<<(int)(blocks < cap ? blocks : cap), 256, 0, s>>>(
+      q, kt, v, o, bh, s_q, s_kv, d, dv, scale, mode);
+  return check_launch("lc_attention_f32 (direct)");
+}
+
+}  // namespace
+}  // namespace lc
+
+extern "C" int lc_attention_f32(int scale_mode, int epilogue, const void *scale, const void *q,
+                                const void *kt, const void *v, void *o, int64_t bh, int64_t s_q,
+                                int64_t s_kv, int64_t d, int64_t dv, void *stream) {
+  using namespace lc;
+  if (scale_mode != LC_SCALE_MUL && scale_mode != LC_SCALE_MUL_RECIP && scale_mode != LC_SCALE_DIV)
+    return fail(LC_ERR_INVALID, "lc_attention_f32: unknown scale mode %d", scale_mode);
+  if (epilogue < LC_EPI_NONE || epilogue > LC_EPI_GELU_TANH)
+    return fail(LC_ERR_INVALID, "lc_attention_f32: unknown epilogue %d", epilogue);
+  if (bh < 0 || s_q < 0 || s_kv < 0 || d < 0 || dv < 0)
+    return fail(LC_ERR_INVALID, "lc_attention_f32: negative shape");
+  if (bh > 65535 || s_q > 0x7fffffff || s_kv > 0x7fffffff || d > 0x7fffffff || dv > 0x7fffffff)
+    return fail(LC_ERR_UNSUPPORTED, "lc_attention_f32: shape beyond the supported range");
+  if (bh == 0 || s_q == 0 || dv == 0) return LC_OK;
+  if (!o || !scale || !q || !v || (d > 0 && !kt))
+    return fail(LC_ERR_INVALID, "lc_attention_f32: null buffer");
+  auto *qf = static_cast<const float *>(q);
+  auto *kf = static_cast<const float *>(kt);
+  auto *vf = static_cast<const float *>(v);
+  auto *of = static_cast<float *>(o);
+  auto *sc = static_cast<const float *>(scale);
+  cudaStream_t s = as_stream(stream);
+#define LC_ATT(E)                                                                          \
+  if (epilogue == E)                                                                       \
+    return launch<E>(qf, kf, vf, of, bh, (int)s_q, (int)s_kv, (int)d, (int)dv, sc, scale_mode, s);
+  LC_ATT(LC_EPI_NONE) LC_ATT(LC_EPI_GELU_ERF) LC_ATT(LC_EPI_GELU_TANH)
+#undef LC_ATT
+  return fail(LC_ERR_INVALID, "lc_attention_f32: bad epilogue");
+}

@@ -81,7 +81,9 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int gm, int gn0
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
   if (p.bias) {
-    for (int j = 0; j < 32 && gn0 + j < p.n; ++j) v[j] = __fadd_rn(v[j], p.bias[gn0 + j]);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (gn0 + j < p.n) v[j] = __fadd_rn(v[j], p.bias[gn0 + j]);
   }
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = apply_epilogue<EPI>(v[j]);
@@ -94,7 +96,9 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int gm, int gn0
       for (int j = 0; j < 32; j += 4)
         *reinterpret_cast<float4 *>(row + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
     } else {
-      for (int j = 0; j < 32 && gn0 + j < p.n; ++j) row[j] = v[j];
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (gn0 + j < p.n) row[j] = v[j];
     }
   } else {
     using T = typename OutType<OUT>::type;
@@ -109,7 +113,9 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int gm, int gn0
         *reinterpret_cast<uint4 *>(row + j) = pack;
       }
     } else {
-      for (int j = 0; j < 32 && gn0 + j < p.n; ++j) row[j] = to_out<T>(v[j]);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (gn0 + j < p.n) row[j] = to_out<T>(v[j]);
     }
   }
 }

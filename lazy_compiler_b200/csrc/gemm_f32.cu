@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(kThreads) split3_kernel(const float *__restric
 // of a thread (likewise columns); TM = 4: 64x64 tiles.  `flag`, when given,
 // makes the kernel a guard: it returns unless *flag is non-zero.
 template <int TM, int EPI, bool B_NK>
-__global__ void __launch_bounds__(kThreads) gemm_f32_simt_kernel(
+__global__ void __launch_bounds__(kThreads, 2) gemm_f32_simt_kernel(
     const float *__restrict__ a, const float *__restrict__ b, const float *__restrict__ bias,
     float *__restrict__ c, int m, int n, int k, const int *flag) {
   if (flag && *reinterpret_cast<const volatile int *>(flag) == 0) return;

@@ -22,6 +22,7 @@ LC_F32, LC_F16, LC_BF16 = 0, 1, 2
 DTYPE_CODES = {"f32": LC_F32, "f16": LC_F16, "bf16": LC_BF16}
 EPILOGUES = {"none": 0, "gelu_erf": 1, "gelu_tanh": 2}
 B_LAYOUTS = {"kn": 0, "nk": 1}
+SCALE_MODES = {"mul": 0, "mul_recip": 1, "div": 2}
 STATUS = {0: "LC_OK", -1: "LC_ERR_INVALID", -2: "LC_ERR_ALIGN", -3: "LC_ERR_CUDA",
           -4: "LC_ERR_TIMEOUT", -5: "LC_ERR_UNSUPPORTED", -6: "LC_ERR_NOMEM"}
 
@@ -46,7 +47,9 @@ SIGNATURES = {
     "lc_softmax_f32": [_P, _P, _I64, _I64, _P],
     "lc_l2norm_f32": [_P, _P, _I64, _I64, _P],
     "lc_gemm": [_INT, _INT, _INT, _INT, _P, _P, _P, _I64, _I64, _I64, _P],
+    "lc_gemm_ex": [_INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_path": [_INT, _INT, _P, _P, _I64, _I64, _I64],
+    "lc_attention_f32": [_INT, _INT, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
     "lc_device_status": [_P],
     "lc_selftest_bounded_wait": [_I64, _P],
     "lc_sdpa_f16": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, ctypes.c_float, _P],
@@ -138,8 +141,13 @@ def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
         call("lc_l2norm_f32", ptr("x"), ptr("out"), p["rows"], p["cols"], s)
     elif op == "gemm":
         d = plan["dtypes"]
-        call("lc_gemm", DTYPE_CODES[d["ab"]], DTYPE_CODES[d["c"]], B_LAYOUTS[p["b_layout"]],
-             EPILOGUES[p["epilogue"]], ptr("a"), ptr("b"), ptr("c"), p["m"], p["n"], p["k"], s)
+        bias = ptr("bias") if "bias" in b else ctypes.c_void_p(0)
+        call("lc_gemm_ex", DTYPE_CODES[d["ab"]], DTYPE_CODES[d["c"]], B_LAYOUTS[p["b_layout"]],
+             EPILOGUES[p["epilogue"]], ptr("a"), ptr("b"), bias, ptr("c"), p["m"], p["n"], p["k"], s)
+    elif op == "attention_f32":
+        call("lc_attention_f32", SCALE_MODES[p["scale_mode"]], EPILOGUES[p["epilogue"]],
+             ptr("scale"), ptr("q"), ptr("kt"), ptr("v"), ptr("o"), p["bh"], p["s_q"], p["s_kv"],
+             p["d"], p["dv"], s)
     elif op == "sdpa_f16":
         call("lc_sdpa_f16", ptr("q"), ptr("k"), ptr("v"), ptr("o"), p["bh"], p["s_q"], p["s_kv"],
              p["d"], ctypes.c_float(p["scale"]), s)

@@ -207,18 +207,24 @@ def l2norm(x):
 
 # ---------------------------------------------------------------- tensor cores
 
-def gemm(a, b, b_layout: str = "kn", epilogue: str = "none", ab: str = "f16", out: str = "f32"):
-    """float64 matmul of the quantised operands, optional GELU, quantised output.
+def gemm(a, b, b_layout: str = "kn", epilogue: str = "none", ab: str = "f16", out: str = "f32",
+         bias=None):
+    """float64 matmul of the quantised operands, optional bias and GELU, quantised output.
 
-    Operands are quantised to ``ab`` (tests/test_tensor_cores.py:38-44); the
-    product is float64 (expressions_open.py:66-73); the epilogue is the GELU
-    formula of tests/test_gelu.py:51-66 applied to the f32 accumulator.
+    Operands are quantised to ``ab`` (tests/test_tensor_cores.py:38-44; a no-op
+    for f32); the product is float64 (expressions_open.py:66-73), rounded to
+    f32 as the accumulator; a bias is added in f32 (the IR's
+    ``add(acc, bias[col])``, examples/phase9/generated/phase9_bias_gelu_gemm);
+    the epilogue is the GELU formula of tests/test_gelu.py:51-66.
     """
     a = quantize(a, ab).astype(np.float64)
     b = quantize(b, ab).astype(np.float64)
     if b_layout == "nk":
-        b = b.T
-    c = (a @ b).astype(np.float32)
+        b = np.swapaxes(b, -1, -2)
+    with np.errstate(all="ignore"):
+        c = (a @ b).astype(np.float32)
+        if bias is not None:
+            c = (c + np.asarray(bias, np.float32)).astype(np.float32)
     if epilogue == "gelu_erf":
         c = gelu(c, "none", "f32")
     elif epilogue == "gelu_tanh":
@@ -242,6 +248,39 @@ def attention_kt(q, kt, v, divisor: float):
     """Reference attention with K pre-transposed (expressions_open a01/a02)."""
     s = (q.astype(np.float64) @ kt.astype(np.float64)) / divisor
     return [(softmax(s)[0].astype(np.float64) @ v.astype(np.float64)).astype(np.float32)]
+
+
+def attention_f32(q, kt, v, scale: float, mode: str = "div", epilogue: str = "none"):
+    """FP32 attention of the IR class: softmax(score(q @ kt)) @ v, then GELU.
+
+    q [..., s_q, d], kt [..., d, s_kv], v [..., s_kv, dv] (expressions_open.py:92-104
+    takes kt pre-transposed).  The score is dot * c ("mul"), dot * f32(1/c)
+    ("mul_recip", the IR's reciprocal-then-multiply) or dot / c ("div"), in
+    float64 after the f32 reciprocal; the result is rounded to f32 before the
+    GELU of tests/test_gelu.py:51-66.
+    """
+    q64, kt64, v64 = (np.asarray(t, np.float64) for t in (q, kt, v))
+    dot = q64 @ kt64
+    c = np.float32(scale)
+    if mode == "mul":
+        s = dot * np.float64(c)
+    elif mode == "mul_recip":
+        s = dot * np.float64(np.float32(1.0) / c)
+    elif mode == "div":
+        s = dot / np.float64(c)
+    else:
+        raise ValueError(mode)
+    s = s - s.max(-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(-1, keepdims=True)
+    out = (p @ v64).astype(np.float32)
+    if epilogue == "gelu_erf":
+        out = gelu(out, "none", "f32").reshape(out.shape)
+    elif epilogue == "gelu_tanh":
+        out = gelu(out, "tanh", "f32").reshape(out.shape)
+    elif epilogue != "none":
+        raise ValueError(epilogue)
+    return [out]
 
 
 # ---------------------------------------------------------------- plans
@@ -275,10 +314,18 @@ def evaluate(plan: dict, arrays: dict) -> dict:
     elif op == "l2norm_f32":
         out = l2norm(g("x"))
     elif op == "gemm":
-        out = gemm(g("a"), g("b"), p["b_layout"], p["epilogue"], plan["dtypes"]["ab"], plan["dtypes"]["c"])
+        bias = g("bias") if "bias" in bind else None
+        out = gemm(g("a"), g("b"), p["b_layout"], p["epilogue"], plan["dtypes"]["ab"], plan["dtypes"]["c"],
+                   bias)
+    elif op == "attention_f32":
+        shape = lambda a, tail: np.asarray(a).reshape((p["bh"],) + tail)  # noqa: E731
+        out = attention_f32(shape(g("q"), (p["s_q"], p["d"])), shape(g("kt"), (p["d"], p["s_kv"])),
+                            shape(g("v"), (p["s_kv"], p["dv"])), s("scale"), p["scale_mode"], p["epilogue"])
+        out = [out[0].reshape((p["s_q"], p["dv"])) if p["bh"] == 1 else out[0]]
     else:
         raise ValueError(f"no oracle for {op}")
-    return {bind["out"] if "out" in bind else bind["c"]: out[0]}
+    key = next(bind[r] for r in ("out", "c", "o") if r in bind)
+    return {key: out[0]}
 
 
 def compare(actual, reference, rtol: float, atol: float) -> dict:
