@@ -185,12 +185,16 @@ class _Eval:
     def stmt(self, s: Node) -> None:
         k = s.kind
         if k == "Load":
-            if len(s.names) != 1:
-                raise CompileError("vector Load is not supported")
             buf = self.pkg.buffers.get(s.input)
             if buf is None and s.input not in self.smem:
                 raise CompileError(f"Load from unknown buffer {s.input}")
-            self.env[s.names[0]] = ("ld", s.input, tuple(self.index(i) for i in s.index))
+            index = tuple(self.index(i) for i in s.index)
+            if len(s.names) > 1 and not index:
+                raise CompileError("vector Load of a scalar")
+            for lane, name in enumerate(s.names):
+                # a vector load reads consecutive elements along the last dimension
+                lane_index = index if lane == 0 else index[:-1] + (_aff_add(index[-1], _aff({1: lane})),)
+                self.env[name] = ("ld", s.input, lane_index)
         elif k == "Assign":
             op = s.op.name if isinstance(s.op, Node) else str(s.op)
             args = tuple(self.value(a) for a in s.args)
@@ -266,6 +270,7 @@ class _Eval:
             "axis": name, "extent": extent, "accums": [],
             "start": self.index(start) if start is not None else _aff({}),
             "step": _aff_const(self.index(step)) if step is not None else 1,
+            "parent": self.loop_stack[-1]["axis"] if self.loop_stack else None,
         }
         if s.get("end") is not None:
             info["end"] = s.end
@@ -453,6 +458,16 @@ _GELU_ERF_B = op("multiply", op("multiply", op("add", V("one", _iss), op("erf", 
 _GELU_TANH = op("multiply", op("multiply", V("half", _iss), V("x", _isin)),
                 op("add", V("one", _iss), op("tanh", op("multiply", V("c0", _iss), op(
                     "add", V("x"), op("multiply", V("c1", _iss), op("multiply", V("x"), op("multiply", V("x"), V("x")))))))))
+
+
+# the same chains around an arbitrary operand (activation epilogues)
+_GELU_ERF_ANY = op("multiply", op("add", V("one", _iss), op("erf", op("multiply", V("r2", _iss), V("x")))),
+                   op("multiply", V("half", _iss), V("x")))
+_GELU_ERF_B_ANY = op("multiply", op("multiply", op("add", V("one", _iss), op("erf", op("multiply", V("r2", _iss), V("x")))),
+                                    V("half", _iss)), V("x"))
+_GELU_TANH_ANY = op("multiply", op("multiply", V("half", _iss), V("x")),
+                    op("add", V("one", _iss), op("tanh", op("multiply", V("c0", _iss), op(
+                        "add", V("x"), op("multiply", V("c1", _iss), op("multiply", V("x"), op("multiply", V("x"), V("x")))))))))
 
 
 def _pointwise_class(pkg: KernelPackage, expr: Any) -> tuple[str, dict, dict]:
@@ -803,12 +818,19 @@ def recognise(pkg: KernelPackage) -> Plan:
     kinds = {s.kind for s in _walk(tile.body)}
     if "MmaSyncPtx" in kinds:
         return _recognise_gemm(pkg, tile)
+    from . import recognize_f32 as f32
+    if "CpAsyncCopy" in kinds:
+        return f32.recognise_staged_gemm(pkg, tile)
     ev = _Eval(pkg)
     ev.smem = set()
     for axis in tile.axes:
         ev.axes[axis.name] = static_extent(axis.extent)
     ev.run(tile.body)
     if ev.loops and ev.reductions:
+        if f32.looks_like_attention(ev):
+            return f32.recognise_attention(pkg, tile, ev)
+        if f32.looks_like_dot(ev):
+            return f32.recognise_dot_gemm(pkg, tile, ev)
         return _recognise_reduction(pkg, tile, ev)
     if ev.loops:
         raise CompileError("loops without a reduction are not a supported operation class")

@@ -30,6 +30,16 @@ EXPECTED = {
     "phase9_gelu_tanh_half": ("gelu", {"n": 1031, "approximate": "tanh"}),
     "phase9_half_gelu_gemm": ("gemm", {"m": 17, "n": 21, "k": 33, "b_layout": "kn", "epilogue": "gelu_tanh"}),
     "generated_tensor": ("gemm", {"m": 11, "n": 19, "k": 7, "b_layout": "kn", "epilogue": "none"}),
+    # FP32 contraction classes: staged (cp.async, split-K), serial and block-cooperative schedules
+    "m01_matmul_512": ("gemm", {"m": 512, "n": 512, "k": 512, "b_layout": "kn", "epilogue": "none"}),
+    "m02_matmul_rect": ("gemm", {"m": 128, "n": 64, "k": 256, "b_layout": "kn", "epilogue": "none"}),
+    "phase9_bias_gelu_gemm": ("gemm", {"m": 33, "n": 47, "k": 65, "b_layout": "kn", "epilogue": "gelu_erf"}),
+    "a01_attention": ("attention_f32", {"bh": 1, "s_q": 64, "s_kv": 64, "d": 64, "dv": 64,
+                                        "scale_mode": "mul_recip", "epilogue": "none"}),
+    "a02_attention_128": ("attention_f32", {"bh": 1, "s_q": 128, "s_kv": 128, "d": 32, "dv": 32,
+                                            "scale_mode": "mul_recip", "epilogue": "none"}),
+    "phase9_gelu_attention": ("attention_f32", {"bh": 1, "s_q": 11, "s_kv": 37, "d": 17, "dv": 13,
+                                                "scale_mode": "mul", "epilogue": "gelu_erf"}),
 }
 
 
@@ -60,8 +70,7 @@ def test_cli_missing_file_exit_1(tmp_path):
     assert result.stderr.startswith("compile.py: ")
 
 
-@pytest.mark.parametrize("name", ["a01_attention", "m01_matmul_512", "activation_gelu_f32",
-                                  "fragment_attention_tile_f16"])
+@pytest.mark.parametrize("name", ["activation_gelu_f32", "fragment_attention_tile_f16"])
 def test_cli_rejects_unsupported_classes_without_output(name):
     result = subprocess.run(CLI + [str(golden_ir(name))], capture_output=True, text=True, cwd=ROOT)
     assert result.returncode == 1
@@ -146,3 +155,56 @@ def test_package_loader_reads_buffers():
     assert pkg.buffers["x"].shape == (64, 1024)
     assert pkg.buffers["mean_count"].role == "constant"
     assert pkg.rtol == 1e-3
+
+
+def test_f32_plans_bind_bias_and_dtypes():
+    plan = compile_file(golden_ir("phase9_bias_gelu_gemm"))
+    assert plan["bind"] == {"a": "a", "b": "b", "bias": "bias", "c": "gelu"}
+    assert plan["dtypes"] == {"ab": "f32", "c": "f32"}
+    plan = compile_file(golden_ir("m02_matmul_rect"))
+    assert plan["zero_outputs"] == ["matmul"]
+
+
+def _mutate(name, tmp_path, old, new, count=None):
+    folder, ir = _copy(name, tmp_path)
+    text = ir.read_text()
+    assert old in text
+    ir.write_text(text.replace(old, new) if count is None else text.replace(old, new, count))
+    return folder, ir
+
+
+def test_staged_gemm_with_wrong_prefetch_distance_is_rejected(tmp_path):
+    """Prefetching 64 instead of 128 columns ahead pairs stale shared-memory tiles."""
+    _, ir = _mutate("m01_matmul_512", tmp_path, "Literal(value=128, dtype='int')",
+                    "Literal(value=64, dtype='int')")
+    with pytest.raises(CompileError, match="cover the contraction"):
+        compile_file(ir)
+
+
+def test_split_k_without_zeroed_output_is_rejected(tmp_path):
+    folder, ir = _copy("m02_matmul_rect", tmp_path)
+    meta = json.loads((folder / "meta.json").read_text())
+    meta["kernels"][0]["zero_outputs"] = []
+    (folder / "meta.json").write_text(json.dumps(meta))
+    with pytest.raises(CompileError, match="zero_outputs"):
+        compile_file(ir)
+
+
+def test_attention_with_transposed_keys_is_rejected(tmp_path):
+    _, ir = _mutate("a02_attention_128", tmp_path, "input='kt', index=(Var(name='a2'), Var(name='a1'))",
+                    "input='kt', index=(Var(name='a1'), Var(name='a2'))")
+    with pytest.raises(CompileError):
+        compile_file(ir)
+
+
+def test_attention_with_min_instead_of_max_is_rejected(tmp_path):
+    _, ir = _mutate("phase9_gelu_attention", tmp_path, "ElementwiseImpl('maximum')", "ElementwiseImpl('minimum')")
+    with pytest.raises(CompileError):
+        compile_file(ir)
+
+
+def test_gemm_bias_on_the_wrong_axis_is_rejected(tmp_path):
+    _, ir = _mutate("phase9_bias_gelu_gemm", tmp_path, "input='bias', index=(Var(name='a1'),)",
+                    "input='bias', index=(Var(name='a0'),)")
+    with pytest.raises(CompileError):
+        compile_file(ir)

@@ -162,8 +162,9 @@ def attention(q, kt, v, scale, mode, epi="none"):
     s_kv, dv = v.shape[1], v.shape[2]
     o = torch.full((bh, s_q, dv), float("nan"), dtype=torch.float32, device="cuda")
     c = dev(np.array([scale], np.float32))
+    tq, tkt, tv = dev(q), dev(kt), dev(v)  # kept alive across the launch
     runtime.call("lc_attention_f32", runtime.SCALE_MODES[mode], runtime.EPILOGUES[epi], P(c),
-                 P(dev(q)), P(dev(kt)), P(dev(v)), P(o), bh, s_q, s_kv, d, dv, None)
+                 P(tq), P(tkt), P(tv), P(o), bh, s_q, s_kv, d, dv, None)
     runtime.call("lc_device_status", None)
     return o.cpu().numpy()
 

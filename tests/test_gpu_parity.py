@@ -23,7 +23,10 @@ F32_RTOL = 1e-5
 PACKAGES = ["p00_scalar_add", "p01_vector_add", "p02_scale_shift", "p03_relu_mul",
             "r01_array_sum", "r02_big_sum", "r03_mean", "r04_row_sum", "f01_rmsnorm",
             "f02_row_softmax", "f03_l2norm", "phase9_gelu_erf_tail", "phase9_gelu_tanh_matrix",
-            "phase9_gelu_erf_half", "phase9_gelu_tanh_half"]
+            "phase9_gelu_erf_half", "phase9_gelu_tanh_half",
+            # FP32 GEMM and attention (staged, split-K, serial and block-cooperative schedules)
+            "m01_matmul_512", "m02_matmul_rect", "phase9_bias_gelu_gemm", "a01_attention",
+            "a02_attention_128", "phase9_gelu_attention"]
 
 
 def torch_():

@@ -100,6 +100,14 @@ def test_oracle_sdpa_matches_attention_tile_rounding():
     np.testing.assert_allclose(sd, tile, rtol=2e-3, atol=2e-3)
 
 
+@pytest.mark.parametrize("name", ["m01_matmul_512", "m02_matmul_rect", "phase9_bias_gelu_gemm",
+                                  "a01_attention", "a02_attention_128", "phase9_gelu_attention"])
+def test_oracle_evaluates_fp32_plans(name):
+    """The oracle run on the recognised plan (bias, score form, epilogue) reproduces the golden outputs."""
+    plan = compile_file(golden_ir(name))
+    check(name, O.evaluate(plan, inputs(name)))
+
+
 def test_oracle_bias_gelu_gemm_formula():
     name = "phase9_bias_gelu_gemm"
     a = inputs(name)
