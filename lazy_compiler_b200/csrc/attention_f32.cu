@@ -259,7 +259,8 @@ extern "C" int lc_attention_f32(int scale_mode, int epilogue, const void *scale,
   if (bh > 65535 || s_q > 0x7fffffff || s_kv > 0x7fffffff || d > 0x7fffffff || dv > 0x7fffffff)
     return fail(LC_ERR_UNSUPPORTED, "lc_attention_f32: shape beyond the supported range");
   if (bh == 0 || s_q == 0 || dv == 0) return LC_OK;
-  if (!o || !scale || !q || !v || (d > 0 && !kt))
+  // empty operands may be null: Q when d = 0, V when s_kv = 0, Kt when either is
+  if (!o || !scale || (d > 0 && !q) || (s_kv > 0 && !v) || (d > 0 && s_kv > 0 && !kt))
     return fail(LC_ERR_INVALID, "lc_attention_f32: null buffer");
   auto *qf = static_cast<const float *>(q);
   auto *kf = static_cast<const float *>(kt);
