@@ -62,20 +62,58 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe, for a share of the exponentials so the MUFU unit is not
-// the limiter.  Range reduction: x = n + f with n = round(x) taken from the
-// low mantissa bits of x + 1.5*2^23 and f in [-0.5, 0.5]; 2^f from a degree-3
-// polynomial fitted here by the Remez exchange algorithm for minimax relative
-// error on [-0.5, 0.5] (max relative error 7.5e-5, below half an f16 ulp); 2^n
-// is added to the exponent field.  x is clamped at -125 so the exponent stays
-// normal; the caller's x never exceeds 8.
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -125.0f);
-  const float t = __fadd_rn(x, 12582912.0f);
-  const float f = __fsub_rn(x, __fsub_rn(t, 12582912.0f));
-  const float p = fmaf(fmaf(fmaf(0.0551716685f, f, 0.242611125f), f, 0.693260968f), f,
-                       0.999928057f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+// Packed pairs of f32 (Blackwell's f32x2 ALU forms: one instruction for two
+// lanes of FMA, ADD or SUB).
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 unpack2(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair on the FMA pipe, for a share of the exponentials so the MUFU
+// unit is not the limiter.  Range reduction: x = n + f with n = round(x) taken
+// from the low mantissa bits of x + 1.5*2^23 and f in [-0.5, 0.5]; 2^f from a
+// degree-3 polynomial fitted here by the Remez exchange algorithm for minimax
+// relative error on [-0.5, 0.5] (max relative error 7.5e-5, below half an f16
+// ulp); 2^n is added to the exponent field.  x is clamped at -125 so the
+// exponent stays normal; the caller's x never exceeds 8.
+__device__ __forceinline__ uint64_t ex2_poly2(uint64_t x2) {
+  const float2 x = unpack2(x2);
+  const uint64_t xc = pack2(fmaxf(x.x, -125.0f), fmaxf(x.y, -125.0f));
+  const uint64_t magic = pack2(12582912.0f, 12582912.0f);
+  const uint64_t t = fadd2(xc, magic);
+  const uint64_t f = fsub2(xc, fsub2(t, magic));
+  uint64_t q = ffma2(pack2(0.0551716685f, 0.0551716685f), f, pack2(0.242611125f, 0.242611125f));
+  q = ffma2(q, f, pack2(0.693260968f, 0.693260968f));
+  q = ffma2(q, f, pack2(0.999928057f, 0.999928057f));
+  const float2 qq = unpack2(q), tt = unpack2(t);
+  return pack2(__int_as_float(__float_as_int(qq.x) + (__float_as_int(tt.x) << 23)),
+               __int_as_float(__float_as_int(qq.y) + (__float_as_int(tt.y) << 23)));
 }
 
 __device__ __forceinline__ void raise_error(const SdpaParams &p, volatile int *abort, int code) {
@@ -272,9 +310,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[c][i]));
-      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        for (int i = 0; i < 32; i += 2)
+          mx8[(i >> 1) & 7] = max3(mx8[(i >> 1) & 7], __uint_as_float(sr[c][i]),
+                                   __uint_as_float(sr[c][i + 1]));
+      float mx = max3(max3(mx8[0], mx8[1], mx8[2]), max3(mx8[3], mx8[4], mx8[5]),
+                      fmaxf(mx8[6], mx8[7]));
       mx *= p.scale_log2;
       const float m_new = fmaxf(m, mx);
       const bool need = m_new > m + kRescaleThreshold;
@@ -302,26 +342,36 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_wait_st();
         }
       }
-      float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent row-sum chains
-      const float neg_m = -m;
+      // independent row-sum chains, each a pair of f32 lanes
+      uint64_t part2[4] = {0ull, 0ull, 0ull, 0ull};
+      const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
+      const uint64_t neg_m2 = pack2(-m, -m);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t packed[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          // p = 2^(s * scale * log2 e - m): one FFMA, then MUFU ex2 or (1 pair in 4) the polynomial
-          const float x0 = fmaf(__uint_as_float(sr[c][2 * i]), p.scale_log2, neg_m);
-          const float x1 = fmaf(__uint_as_float(sr[c][2 * i + 1]), p.scale_log2, neg_m);
-          const float p0 = (i & 3) == 3 ? ex2_poly(x0) : ex2(x0);
-          const float p1 = (i & 3) == 3 ? ex2_poly(x1) : ex2(x1);
-          part[i & 7] += p0 + p1;
-          __half2 h = __floats2half2_rn(p0, p1);
+          // p = 2^(s * scale * log2 e - m): one paired FMA, then MUFU ex2 or
+          // (one pair in four) the paired polynomial
+          const uint64_t x2 = ffma2(pack2(__uint_as_float(sr[c][2 * i]), __uint_as_float(sr[c][2 * i + 1])),
+                                    scale2, neg_m2);
+          uint64_t p2;
+          if ((i & 3) == 3) {
+            p2 = ex2_poly2(x2);
+          } else {
+            const float2 x = unpack2(x2);
+            p2 = pack2(ex2(x.x), ex2(x.y));
+          }
+          part2[i & 3] = fadd2(part2[i & 3], p2);
+          const float2 pp = unpack2(p2);
+          __half2 h = __floats2half2_rn(pp.x, pp.y);
           packed[i] = *reinterpret_cast<uint32_t *>(&h);
         }
         tmem_st16(tmem + lane_base + s_col + c * 16, packed);
       }
       tmem_wait_st();
-      l += ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
+      const float2 s01 = unpack2(fadd2(fadd2(part2[0], part2[1]), fadd2(part2[2], part2[3])));
+      l += s01.x + s01.y;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
