@@ -220,6 +220,14 @@ int lc_sdpa_f16(const void *q, const void *k, const void *v, void *o, int64_t bh
 int lc_sdpa_path(const void *q, const void *k, const void *v, const void *o, int64_t s_q,
                  int64_t s_kv, int64_t d);
 
+/* Diagnostic: one CTA per SM issues `groups` groups of 8 back-to-back
+ * tcgen05.mma (M128 N128 K16) of form `variant` (0 A and B from shared
+ * memory, B K-major; 1 A from tensor memory, B MN-major; 2 shared memory with
+ * B MN-major; 3 and 4 alternate form 0 with form 1 or 2 every 2 groups; 5-9
+ * vary the accumulator reuse, see probe_mma.cu) on zeroed operands.  Timing it measures the tensor pipe's rate for each form
+ * and the cost of switching forms.  No reference counterpart. */
+int lc_probe_mma(int variant, int groups, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -4,7 +4,9 @@
            [--m M --n N --k K] [--bh B --seq S] [--warmup W] [--repeat R]
 
 OP is one of add, axpb, relumul, gelu_erf, gelu_tanh, sum, mean, rowsum,
-rmsnorm, softmax, l2norm, gemm_f16, gemm_bf16, sdpa.  Inputs are seeded
+rmsnorm, softmax, l2norm, gemm_f16, gemm_bf16, gemm_f32, attention_f32, sdpa,
+or mma_probe (``--variant V --groups G``: the tcgen05 issue-pattern probe,
+reported per MMA).  Inputs are seeded
 device tensors; every launch goes through the C ABI.  The mean CUDA-event
 time of the repeated launches is printed (``--repeat`` launches after
 ``--warmup``), so the same command line serves an ncu capture (``-k`` the
@@ -29,6 +31,8 @@ def main() -> None:
     ap.add_argument("--k", type=int, default=8192)
     ap.add_argument("--bh", type=int, default=128)
     ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--variant", type=int, default=0)
+    ap.add_argument("--groups", type=int, default=512)
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--repeat", type=int, default=1)
     a = ap.parse_args()
@@ -77,6 +81,27 @@ def main() -> None:
         code = 1 if op == "gemm_f16" else 2
         fn = lambda: runtime.call("lc_gemm", code, 0, 0, 0, P(A), P(B), P(C), m, n, k, s)  # noqa: E731
         work, unit = 2 * m * n * k, "TFLOP/s"
+    elif op == "gemm_f32":
+        m, n, k = a.m, a.n or 8192, a.k
+        A = torch.randn(m, k, device="cuda", generator=g)
+        B = torch.randn(k, n, device="cuda", generator=g)
+        C = torch.empty(m, n, device="cuda")
+        fn = lambda: runtime.call("lc_gemm", 0, 0, 0, 0, P(A), P(B), P(C), m, n, k, s)  # noqa: E731
+        work, unit = 2 * m * n * k, "TFLOP/s"
+    elif op == "attention_f32":
+        bh, sq, d = a.bh, a.seq, 128
+        q = torch.randn(bh, sq, d, device="cuda", generator=g)
+        kt = torch.randn(bh, d, sq, device="cuda", generator=g)
+        v = torch.randn(bh, sq, d, device="cuda", generator=g)
+        o = torch.empty_like(q)
+        c = torch.tensor([d ** -0.5], device="cuda")
+        fn = lambda: runtime.call("lc_attention_f32", 0, 0, P(c), P(q), P(kt), P(v), P(o),  # noqa: E731
+                                  bh, sq, sq, d, d, s)
+        work, unit = 4 * bh * sq * sq * d, "TFLOP/s"
+    elif op == "mma_probe":
+        fn = lambda: runtime.call("lc_probe_mma", a.variant, a.groups, s)  # noqa: E731
+        sms = torch.cuda.get_device_properties(0).multi_processor_count
+        work, unit = 2 * 128 * 128 * 16 * 8 * a.groups * sms, "TFLOP/s"
     elif op == "sdpa":
         bh, sq, d = a.bh, a.seq, 128
         q = torch.randn(bh, sq, d, device="cuda", generator=g).half()
