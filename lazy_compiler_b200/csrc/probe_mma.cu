@@ -25,7 +25,9 @@ using namespace sm100;
 
 constexpr int kProbeSmem = 120 * 1024;  // > half the SM's shared memory: one CTA per SM
 
-__global__ void __launch_bounds__(128, 1) mma_probe_kernel(int variant, int groups, int *err) {
+template <int VARIANT>
+__global__ void __launch_bounds__(128, 1) mma_probe_kernel(int groups, int *err) {
+  constexpr int variant = VARIANT;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -63,26 +65,36 @@ __global__ void __launch_bounds__(128, 1) mma_probe_kernel(int variant, int grou
     for (int g = 0; g < groups; ++g) {
       // form: 0 SS/K, 1 TS/MN, 2 SS/MN, 3 TS/K; the accumulator is column 0 or
       // 384, alternating with 128 per group when `alt`
-      int form = variant;
-      bool alt = variant == 0 || variant == 6 || variant == 7 || variant == 9;
-      if (variant == 3) form = (g >> 1) & 1 ? 1 : 0;
-      if (variant == 4) form = (g >> 1) & 1 ? 2 : 0;
-      if (variant == 5) form = 0;
-      if (variant == 6) form = 1;
-      if (variant == 7) form = 2;
-      if (variant == 8 || variant == 9) form = 3;
-      const uint32_t d_base = form == 0 ? 0u : 384u;
+      constexpr bool alt = variant == 0 || variant == 6 || variant == 7 || variant == 9;
+      constexpr int fixed_form = variant == 5 ? 0 : variant == 6 ? 1 : variant == 7 ? 2
+                               : (variant == 8 || variant == 9) ? 3 : variant;
+      constexpr bool mixed = variant == 3 || variant == 4;
+      if (mixed && ((g >> 1) & 1)) {
+        // second form of the alternating variants, accumulator at column 384
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if constexpr (variant == 3)
+            mma_f16_tmem_a(tmem + 384, tmem + 256 + k * 8, smem_desc_sw128(v + k * 2048, 16384, 1024),
+                           idesc_mn, 1);
+          else
+            mma_f16(tmem + 384, smem_desc_sw128(a + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024),
+                    smem_desc_sw128(v + k * 2048, 16384, 1024), idesc_mn, 1);
+        }
+        continue;
+      }
+      constexpr int form = mixed ? 0 : fixed_form;
+      constexpr uint32_t d_base = form == 0 ? 0u : 384u;
       const uint32_t d = alt && (g & 1) ? 128u : d_base;
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-        if (form == 0)
+        if constexpr (form == 0)
           mma_f16(tmem + d, smem_desc_sw128(a + off, 16, 1024), smem_desc_sw128(b + off, 16, 1024),
                   idesc_k, 1);
-        else if (form == 1)
+        else if constexpr (form == 1)
           mma_f16_tmem_a(tmem + d, tmem + 256 + k * 8, smem_desc_sw128(v + k * 2048, 16384, 1024),
                          idesc_mn, 1);
-        else if (form == 2)
+        else if constexpr (form == 2)
           mma_f16(tmem + d, smem_desc_sw128(a + off, 16, 1024),
                   smem_desc_sw128(v + k * 2048, 16384, 1024), idesc_mn, 1);
         else
@@ -107,11 +119,15 @@ extern "C" int lc_probe_mma(int variant, int groups, void *stream) {
     return fail(LC_ERR_INVALID, "lc_probe_mma: bad variant or group count");
   int *err = nullptr;
   if (int rc = device_error_word(&err)) return rc;
-  if (int rc = check_cuda(cudaFuncSetAttribute(mma_probe_kernel,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+  void (*kernels[10])(int, int *) = {mma_probe_kernel<0>, mma_probe_kernel<1>, mma_probe_kernel<2>,
+                                     mma_probe_kernel<3>, mma_probe_kernel<4>, mma_probe_kernel<5>,
+                                     mma_probe_kernel<6>, mma_probe_kernel<7>, mma_probe_kernel<8>,
+                                     mma_probe_kernel<9>};
+  auto kernel = kernels[variant];
+  if (int rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                kProbeSmem),
                           "probe smem attribute"))
     return rc;
-  mma_probe_kernel<<<sm_count(), 128, kProbeSmem, as_stream(stream)>>>(variant, groups, err);
+  kernel<<<sm_count(), 128, kProbeSmem, as_stream(stream)>>>(groups, err);
   return check_launch("lc_probe_mma");
 }

@@ -221,26 +221,33 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16(false, false, false, BQ, BKV);
       constexpr uint32_t idesc_o = idesc_f16(false, false, true, BQ, HEAD);
-      const uint32_t q_addr = smem_u32(q_s);
-      const uint32_t kv_addr = smem_u32(kv_s);
+      // Shared-memory descriptors are built once; an MMA adds its operand's
+      // byte offset / 16 to the 14-bit start-address field (no carry: every
+      // address is below 256 KB), so issuing one costs a single integer add.
+      const uint64_t q_desc = smem_desc_sw128(smem_u32(q_s), 16, 1024);
+      const uint64_t k_desc = smem_desc_sw128(smem_u32(kv_s), 16, 1024);
+      const uint64_t v_desc = smem_desc_sw128(smem_u32(kv_s) + TILE_BYTES, CHUNK_BYTES, 1024);
+      constexpr uint32_t kStageStep = 2 * TILE_BYTES / 16;
       // S_t(j) = Q_t K(j)^T into TMEM columns [t*128, t*128+128)
       auto issue_s = [&](int t, int j) {
-        const uint32_t k_addr = kv_addr + (j & 1) * 2 * TILE_BYTES;
+        const uint64_t qd = q_desc + (uint64_t)(t * TILE_BYTES / 16);
+        const uint64_t kd = k_desc + (uint64_t)((j & 1) * kStageStep);
+        const uint32_t d_tmem = tmem + t * BKV;
 #pragma unroll
         for (int k = 0; k < HEAD / 16; ++k) {
-          const uint32_t off = (k >> 2) * CHUNK_BYTES + (k & 3) * 32;
-          mma_f16(tmem + t * BKV, smem_desc_sw128(q_addr + t * TILE_BYTES + off, 16, 1024),
-                  smem_desc_sw128(k_addr + off, 16, 1024), idesc_s, k > 0);
+          const uint32_t off = ((k >> 2) * CHUNK_BYTES + (k & 3) * 32) / 16;
+          mma_f16(d_tmem, qd + off, kd + off, idesc_s, k > 0);
         }
         mma_commit(&s_full[t]);
       };
       // O_t += P_t(j) V(j), P_t read from TMEM over S_t
       auto issue_pv = [&](int t, int j) {
-        const uint32_t v_addr = kv_addr + (j & 1) * 2 * TILE_BYTES + TILE_BYTES;
+        const uint64_t vd = v_desc + (uint64_t)((j & 1) * kStageStep);
+        const uint32_t d_tmem = tmem + O_COL + t * HEAD;
+        const uint32_t a_tmem = tmem + t * BKV;
 #pragma unroll
         for (int k = 0; k < BKV / 16; ++k)
-          mma_f16_tmem_a(tmem + O_COL + t * HEAD, tmem + t * BKV + k * 8,
-                         smem_desc_sw128(v_addr + k * 2048, CHUNK_BYTES, 1024), idesc_o,
+          mma_f16_tmem_a(d_tmem, a_tmem + k * 8, vd + (uint64_t)(k * 2048 / 16), idesc_o,
                          (j | k) != 0);
         mma_commit(&o_done[t]);
       };
