@@ -199,6 +199,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16(BF16, false, B_MN, BM, BN);
+      const uint64_t a_desc0 = smem_desc_sw128(smem_u32(smem), 16, 1024);
+      const uint64_t b_desc0 = B_MN ? smem_desc_sw128(smem_u32(smem) + A_BYTES, BK * 128, 1024)
+                                    : smem_desc_sw128(smem_u32(smem) + A_BYTES, 16, 1024);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -219,15 +222,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
-          const uint32_t b_addr = a_addr + A_BYTES;
+          // descriptors of stage 0 plus the stage's offset / 16 (start-address field)
+          const uint64_t ad = a_desc0 + (uint64_t)(stage * (STAGE_BYTES / 16));
+          const uint64_t bd = b_desc0 + (uint64_t)(stage * (STAGE_BYTES / 16));
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
-            const uint64_t bdesc = B_MN ? smem_desc_sw128(b_addr + k * 2048, BK * 128, 1024)
-                                        : smem_desc_sw128(b_addr + k * 32, 16, 1024);
-            mma_f16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0);
-          }
+          for (int k = 0; k < BK / 16; ++k)
+            mma_f16(d_tmem, ad + (uint64_t)(k * 2), bd + (uint64_t)(B_MN ? k * 128 : k * 2), idesc,
+                    (kb | k) != 0);
           mma_commit(&empty_bar[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -384,6 +385,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     if (leader && lane == 0) {
       constexpr uint32_t idesc = idesc_f16(BF16, false, B_MN, 2 * PBM, PTILE);
+      const uint64_t a_desc0 = smem_desc_sw128(smem_u32(smem), 16, 1024);
+      const uint64_t b_desc0 = B_MN ? smem_desc_sw128(smem_u32(smem) + PA_BYTES, BK * 128, 1024)
+                                    : smem_desc_sw128(smem_u32(smem) + PA_BYTES, 16, 1024);
       int it = 0;
       int local = 0;
       bool ok = true;
@@ -405,15 +409,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * PSTAGE_BYTES);
-          const uint32_t b_addr = a_addr + PA_BYTES;
+          const uint64_t ad = a_desc0 + (uint64_t)(stage * (PSTAGE_BYTES / 16));
+          const uint64_t bd = b_desc0 + (uint64_t)(stage * (PSTAGE_BYTES / 16));
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
-            const uint64_t bdesc = B_MN ? smem_desc_sw128(b_addr + k * 2048, BK * 128, 1024)
-                                        : smem_desc_sw128(b_addr + k * 32, 16, 1024);
-            mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0);
-          }
+          for (int k = 0; k < BK / 16; ++k)
+            mma_f16_pair(d_tmem, ad + (uint64_t)(k * 2), bd + (uint64_t)(B_MN ? k * 128 : k * 2), idesc,
+                         (kb | k) != 0);
           mma_commit_pair_both(&empty_bar[stage]);
         }
         if (ok) mma_commit_pair_both(&tfull_bar[acc]);
