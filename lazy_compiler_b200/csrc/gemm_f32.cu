@@ -12,7 +12,10 @@
 //  * SIMT (path 0): a persistent FFMA kernel over 128x128 (or, when there are
 //    fewer such tiles than SMs, 64x64) output tiles, 8x8 (4x4) outputs per
 //    thread, k-slices of 8 double-buffered in shared memory.  Small problems and
-//    shapes TMA cannot describe take it.
+//    shapes TMA cannot describe take it.  When even 64x64 tiles leave SMs idle,
+//    the contraction is split into up to 16 chunks whose partial products a
+//    second kernel adds in a fixed order (deterministic), with the bias and
+//    activation.
 //  * Tensor cores (paths 1, 2): every f32 value x is split exactly into three
 //    bf16 pieces, hi = bf16(x), mid = bf16(x - hi), lo = bf16(x - hi - mid)
 //    (both subtractions are exact; |x - hi - mid - lo| <= 2^-24 |x|).  The six
@@ -37,7 +40,10 @@ namespace {
 constexpr int SK = 8;                   // k-slice of the SIMT kernel
 constexpr int kThreads = 256;
 constexpr int64_t kSplitMacs = (int64_t)1 << 30;  // tensor-core path from here up
-constexpr int kScratchSlot = 0;
+constexpr int kScratchSlot = 0;      // bf16 split operands of the tensor-core path
+constexpr int kSplitSlot = 1;        // split-K partial products of the SIMT path
+constexpr int kMinChunk = 64;        // smallest contraction chunk of a split
+constexpr int kMaxSplits = 16;
 
 // Piece orders of A' and B' slots: 0 = hi, 1 = mid, 2 = lo (two bits a slot).
 constexpr int pack_order(int s0, int s1, int s2, int s3, int s4, int s5) {
@@ -94,11 +100,15 @@ __global__ void __launch_bounds__(kThreads) split3_kernel(const float *__restric
 
 // SIMT FP32 GEMM.  TM = 8: 128x128 tiles, rows ty*4+{0..3} and 64+ty*4+{0..3}
 // of a thread (likewise columns); TM = 4: 64x64 tiles.  `flag`, when given,
-// makes the kernel a guard: it returns unless *flag is non-zero.
+// makes the kernel a guard: it returns unless *flag is non-zero.  With
+// `partial`, blockIdx.y picks the k range [y * k_chunk, (y + 1) * k_chunk) and
+// the raw sums go to partial[y][M][N] (no bias, no activation) for
+// split_k_reduce_kernel.
 template <int TM, int EPI, bool B_NK>
 __global__ void __launch_bounds__(kThreads, 2) gemm_f32_simt_kernel(
     const float *__restrict__ a, const float *__restrict__ b, const float *__restrict__ bias,
-    float *__restrict__ c, int m, int n, int k, const int *flag) {
+    float *__restrict__ c, int m, int n, int k, const int *flag, int k_chunk,
+    float *__restrict__ partial) {
   if (flag && *reinterpret_cast<const volatile int *>(flag) == 0) return;
   constexpr int ST = 16 * TM;         // tile edge
   constexpr int LPT = TM / 2;         // elements of each operand a thread loads per slice
@@ -110,7 +120,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemm_f32_simt_kernel(
   const int tiles = ((m + ST - 1) / ST) * tiles_n;
   const int a_row = t / KT, a_k = (t % KT) * LPT;     // A and [N,K] B
   const int b_k = t / (ST / LPT), b_col = (t % (ST / LPT)) * LPT;  // [K,N] B
-  const bool vec_out = (n & 3) == 0 && (reinterpret_cast<uintptr_t>(c) & 15) == 0;
+  const int k_lo = partial ? blockIdx.y * k_chunk : 0;
+  const int k_hi = partial ? min(k, k_lo + k_chunk) : k;
+  float *out = partial ? partial + (int64_t)blockIdx.y * m * n : c;
+  const bool vec_out = (n & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
 
   for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
     const int m0 = (tile / tiles_n) * ST, n0 = (tile % tiles_n) * ST;
@@ -120,21 +133,21 @@ __global__ void __launch_bounds__(kThreads, 2) gemm_f32_simt_kernel(
 #pragma unroll
       for (int q = 0; q < LPT; ++q) {
         const int kk = k0 + a_k + q;
-        ra[q] = (gr < m && kk < k) ? a[(int64_t)gr * k + kk] : 0.f;
+        ra[q] = (gr < m && kk < k_hi) ? a[(int64_t)gr * k + kk] : 0.f;
       }
       if constexpr (B_NK) {
         const int gc = n0 + a_row;
 #pragma unroll
         for (int q = 0; q < LPT; ++q) {
           const int kk = k0 + a_k + q;
-          rb[q] = (gc < n && kk < k) ? b[(int64_t)gc * k + kk] : 0.f;
+          rb[q] = (gc < n && kk < k_hi) ? b[(int64_t)gc * k + kk] : 0.f;
         }
       } else {
         const int kk = k0 + b_k;
 #pragma unroll
         for (int q = 0; q < LPT; ++q) {
           const int gc = n0 + b_col + q;
-          rb[q] = (kk < k && gc < n) ? b[(int64_t)kk * n + gc] : 0.f;
+          rb[q] = (kk < k_hi && gc < n) ? b[(int64_t)kk * n + gc] : 0.f;
         }
       }
     };
@@ -156,12 +169,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemm_f32_simt_kernel(
 #pragma unroll
       for (int j = 0; j < TM; ++j) acc[i][j] = 0.f;
 
-    load(0);
+    load(k_lo);
     store(0);
     __syncthreads();
     int buf = 0;
-    for (int k0 = 0; k0 < k; k0 += SK) {
-      const bool more = k0 + SK < k;
+    for (int k0 = k_lo; k0 < k_hi; k0 += SK) {
+      const bool more = k0 + SK < k_hi;
       if (more) load(k0 + SK);
 #pragma unroll
       for (int kk = 0; kk < SK; ++kk) {
@@ -194,10 +207,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemm_f32_simt_kernel(
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           float x = acc[i][h * 4 + j];
-          if (bias && col + j < n) x = __fadd_rn(x, bias[col + j]);
-          v[j] = apply_epilogue<EPI>(x);
+          if (!partial) {
+            if (bias && col + j < n) x = __fadd_rn(x, bias[col + j]);
+            x = apply_epilogue<EPI>(x);
+          }
+          v[j] = x;
         }
-        float *dst = c + (int64_t)row * n + col;
+        float *dst = out + (int64_t)row * n + col;
         if (vec_out && col + 3 < n) {
           *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
         } else {
@@ -211,6 +227,23 @@ __global__ void __launch_bounds__(kThreads, 2) gemm_f32_simt_kernel(
   }
 }
 
+// Sums the split-K partial products in a fixed order, adds the bias and
+// applies the activation: deterministic for a given shape.
+template <int EPI>
+__global__ void __launch_bounds__(kThreads) split_k_reduce_kernel(const float *__restrict__ partial,
+                                                                  const float *__restrict__ bias,
+                                                                  float *__restrict__ c, int m, int n,
+                                                                  int splits) {
+  const int64_t total = (int64_t)m * n;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float x = partial[i];
+    for (int sp = 1; sp < splits; ++sp) x = __fadd_rn(x, partial[sp * total + i]);
+    if (bias) x = __fadd_rn(x, bias[i % n]);
+    c[i] = apply_epilogue<EPI>(x);
+  }
+}
+
 template <int TM, int EPI>
 int launch_simt_tm(bool b_nk, const float *a, const float *b, const float *bias, float *c, int m,
                    int n, int k, const int *flag, cudaStream_t s) {
@@ -218,10 +251,37 @@ int launch_simt_tm(bool b_nk, const float *a, const float *b, const float *bias,
   const int64_t tiles = (int64_t)((m + ST - 1) / ST) * ((n + ST - 1) / ST);
   const int64_t cap = 2LL * sm_count();
   const int grid = (int)(tiles < cap ? tiles : cap);
+  // Too few output tiles to fill the GPU: split the contraction into chunks
+  // of at least kMinChunk and reduce the partial products in a second pass.
+  int splits = 1;
+  if (!flag && tiles < sm_count() && k >= 2 * kMinChunk) {
+    const int64_t want = (2LL * sm_count() + tiles - 1) / tiles;
+    const int64_t most = k / kMinChunk;
+    splits = (int)(want < most ? want : most);
+    if (splits > kMaxSplits) splits = kMaxSplits;
+  }
+  if (splits > 1) {
+    const int k_chunk = ((k + splits - 1) / splits + SK - 1) / SK * SK;
+    splits = (k + k_chunk - 1) / k_chunk;
+    void *ws = nullptr;
+    if (int rc = scratch_buffer(s, kSplitSlot, (size_t)splits * m * n * sizeof(float), &ws)) return rc;
+    float *part = static_cast<float *>(ws);
+    dim3 g2((unsigned)grid, (unsigned)splits);
+    if (b_nk)
+      gemm_f32_simt_kernel<TM, EPI, true><<<g2, kThreads, 0, s>>>(a, b, bias, c, m, n, k, flag, k_chunk, part);
+    else
+      gemm_f32_simt_kernel<TM, EPI, false><<<g2, kThreads, 0, s>>>(a, b, bias, c, m, n, k, flag, k_chunk, part);
+    if (int rc = check_launch("lc_gemm (f32 simt, split k)")) return rc;
+    const int64_t total = (int64_t)m * n;
+    const int64_t blocks = (total + kThreads - 1) / kThreads;
+    const int rgrid = (int)(blocks < 4LL * sm_count() ? blocks : 4LL * sm_count());
+    split_k_reduce_kernel<EPI><<<rgrid, kThreads, 0, s>>>(part, bias, c, m, n, splits);
+    return check_launch("lc_gemm (f32 split-k reduce)");
+  }
   if (b_nk)
-    gemm_f32_simt_kernel<TM, EPI, true><<<grid, kThreads, 0, s>>>(a, b, bias, c, m, n, k, flag);
+    gemm_f32_simt_kernel<TM, EPI, true><<<grid, kThreads, 0, s>>>(a, b, bias, c, m, n, k, flag, 0, nullptr);
   else
-    gemm_f32_simt_kernel<TM, EPI, false><<<grid, kThreads, 0, s>>>(a, b, bias, c, m, n, k, flag);
+    gemm_f32_simt_kernel<TM, EPI, false><<<grid, kThreads, 0, s>>>(a, b, bias, c, m, n, k, flag, 0, nullptr);
   return check_launch("lc_gemm (f32 simt)");
 }
 

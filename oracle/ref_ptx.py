@@ -41,6 +41,9 @@ PACKAGES = [
     "examples/phase9/generated/phase9_gelu_erf_half",
     "examples/phase9/generated/phase9_gelu_tanh_half",
     "examples/phase9/generated/phase9_half_gelu_gemm",
+    "examples/phase9/generated/phase9_bias_gelu_gemm",
+    "examples/phase9/generated/phase9_gelu_attention",
+    "examples/phase9/generated/phase9_gelu_row_dot",
     "examples/generated_tensor",
     "examples/phase9/gelu/activation_gelu_f32", "examples/phase9/gelu/activation_gelu_f16",
     "examples/phase9/gelu/activation_gelu_bf16", "examples/phase9/gelu/activation_gelu_tanh_f32",
