@@ -337,10 +337,20 @@ def run_ours(args):
                 ops = [("sum", 4 * n, lambda: sharded_sum(x, n, out[:1], None, stream=stream)),
                        ("mean", 4 * n, lambda: sharded_sum(x, n, out[1:], count, stream=stream))]
             scratch = torch.empty(L2_FLUSH_BYTES // 4, device=dist.device)
+            clean = torch.zeros(L2_FLUSH_BYTES // 8, device=dist.device)
+            sink = torch.empty(1, device=dist.device)
+
+            def flush():
+                # write more than L2 holds, then read an unrelated buffer larger than
+                # L2 so the lines the timed reduction evicts are clean (no
+                # write-back of the flush's dirty lines inside the timed kernels)
+                scratch.zero_()
+                torch.sum(clean, dim=0, keepdim=True, out=sink)
             cfg = {"workload": "whole-array sum and mean of 2^24 fp32 U[-1,1] per GPU"
                                + (", f64 partials all-reduced over NCCL" if dist.world > 1 else ""),
-                   "elements_per_gpu": n, "l2": "flushed between steps (512 MiB write, not timed)"}
-            return ops, cfg, (lambda: scratch.zero_()), ((x,), out, part, count, scratch)
+                   "elements_per_gpu": n,
+                   "l2": "flushed between steps (512 MiB write, then a 256 MiB read; not timed)"}
+            return ops, cfg, flush, ((x,), out, part, count, scratch, clean, sink)
         if config == "rows":
             x = torch.randn(ROWS, COLS, device=dist.device, generator=g)
             w = torch.randn(COLS, device=dist.device, generator=g) * 0.1 + 1.0
