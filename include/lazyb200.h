@@ -155,6 +155,15 @@ int lc_softmax_f32(const float *x, float *out, int64_t rows, int64_t cols, void 
 /* out[r,c] = X[r,c] * 1/sqrt(sum_c X[r,c]^2)   (f03_l2norm) */
 int lc_l2norm_f32(const float *x, float *out, int64_t rows, int64_t cols, void *stream);
 
+/* out[r] = sum_c Y[r,c] * f(X[r,c]) with f the identity (LC_EPI_NONE) or GELU
+ * (LC_EPI_GELU_ERF / LC_EPI_GELU_TANH); each product rounded once, sums
+ * compensated like the row sum.  Replaces the row reductions of fused
+ * pointwise products (examples/phase9/generated/phase9_gelu_row_dot:
+ * acc += g * gelu(x) in a strided loop, warp butterfly and block tree,
+ * ptx_backend.py:1496-1554, 1668-1744). */
+int lc_rowdot_f32(int activation, const float *x, const float *y, float *out, int64_t rows,
+                  int64_t cols, void *stream);
+
 /* ---------------------------------------------------------------- tensor cores */
 
 /* C[M,N] = epilogue(A[M,K] @ B), f32 accumulation.  ab_dtype LC_F16 or

@@ -1,4 +1,5 @@
-// Row operations on X[rows, cols] f32: row sum, RMSNorm, softmax, L2 norm.
+// Row operations on X[rows, cols] f32: row sum, RMSNorm, softmax, L2 norm,
+// and row dot products sum_c Y[r,c] * f(X[r,c]) with f the identity or GELU.
 //
 // The reference lowers r04/f01/f02/f03 to one 128-thread CTA per row with a
 // strided first pass (sum, sum of squares or the coupled online-softmax
@@ -17,18 +18,32 @@
 // arithmetic follows the IR's own order (f01: w * (x * 1/sqrt(eps + ss/count)),
 // f03: x * 1/sqrt(ss), f02: 1/sum * exp(x - max)) with correctly rounded
 // sqrt and reciprocal (ptx_backend.py:1047-1050 div.rn / sqrt.rn).
+// Row dot products (phase9_gelu_row_dot: acc += g * gelu(x)) round each
+// product once and sum like the row sum.
 // Rows that are not 16-byte aligned, not a multiple of 4 wide or wider than
 // 32,768 take a scalar kernel that streams the row from global (L2) per pass.
 #include "common.cuh"
+#include "epilogue.cuh"
 
 namespace lc {
 namespace {
 
-enum RowOp { kRowSum = 0, kRmsNorm = 1, kSoftmax = 2, kL2 = 3 };
+enum RowOp { kRowSum = 0, kRmsNorm = 1, kSoftmax = 2, kL2 = 3, kRowDot = 4, kRowDotGeluErf = 5,
+             kRowDotGeluTanh = 6 };
+
+constexpr bool is_dot(int op) { return op >= kRowDot; }
+
+// y * f(x) of the row dot products, rounded once
+template <int OP>
+__device__ __forceinline__ float dot_term(float x, float y) {
+  if constexpr (OP == kRowDotGeluErf) return __fmul_rn(y, gelu_erf(x));
+  else if constexpr (OP == kRowDotGeluTanh) return __fmul_rn(y, gelu_tanh(x));
+  else return __fmul_rn(y, x);
+}
 
 struct RowArgs {
   const float *x;
-  const float *w;
+  const float *w;  // RMSNorm weight, or Y of the row dot products
   const float *count;
   const float *eps;
   float *out;
@@ -69,6 +84,22 @@ __global__ void __launch_bounds__(1024) row_vec_kernel(RowArgs args) {
         acc.add(v[j].y);
         acc.add(v[j].z);
         acc.add(v[j].w);
+      }
+      const double total = block_sum<double>(acc.value(), dscratch);
+      if (threadIdx.x == 0) args.out[row] = (float)total;
+    } else if constexpr (is_dot(OP)) {
+      const float4 *yr = reinterpret_cast<const float4 *>(args.w + row * args.cols);
+      CompSum acc;
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        const int64_t idx = threadIdx.x + (int64_t)j * T;
+        if (idx < c4) {
+          const float4 y = ld_stream(yr + idx);
+          acc.add(dot_term<OP>(v[j].x, y.x));
+          acc.add(dot_term<OP>(v[j].y, y.y));
+          acc.add(dot_term<OP>(v[j].z, y.z));
+          acc.add(dot_term<OP>(v[j].w, y.w));
+        }
       }
       const double total = block_sum<double>(acc.value(), dscratch);
       if (threadIdx.x == 0) args.out[row] = (float)total;
@@ -142,6 +173,12 @@ __global__ void __launch_bounds__(256) row_scalar_kernel(RowArgs args) {
       for (int64_t c = threadIdx.x; c < args.cols; c += blockDim.x) acc.add(xr[c]);
       const double total = block_sum<double>(acc.value(), dscratch);
       if (threadIdx.x == 0) args.out[row] = (float)total;
+    } else if constexpr (is_dot(OP)) {
+      const float *yr = args.w + row * args.cols;
+      CompSum acc;
+      for (int64_t c = threadIdx.x; c < args.cols; c += blockDim.x) acc.add(dot_term<OP>(xr[c], yr[c]));
+      const double total = block_sum<double>(acc.value(), dscratch);
+      if (threadIdx.x == 0) args.out[row] = (float)total;
     } else if constexpr (OP == kSoftmax) {
       float m = -INFINITY;
       for (int64_t c = threadIdx.x; c < args.cols; c += blockDim.x) m = fmaxf(m, xr[c]);
@@ -170,10 +207,11 @@ int launch_rows(const char *name, const RowArgs &a, void *stream) {
   if (!a.x || !a.out) return fail(LC_ERR_INVALID, "%s: null buffer", name);
   if (OP == kRmsNorm && (!a.w || !a.count || !a.eps))
     return fail(LC_ERR_INVALID, "%s: null weight, count or eps", name);
+  if (is_dot(OP) && !a.w) return fail(LC_ERR_INVALID, "%s: null y", name);
   if (a.rows < 0 || a.cols < 0) return fail(LC_ERR_INVALID, "%s: negative shape", name);
   if (a.rows == 0) return LC_OK;
   if (a.cols == 0) {
-    if (OP == kRowSum) return check_cuda(cudaMemsetAsync(a.out, 0, a.rows * sizeof(float),
+    if (OP == kRowSum || is_dot(OP)) return check_cuda(cudaMemsetAsync(a.out, 0, a.rows * sizeof(float),
                                                          as_stream(stream)), name);
     return LC_OK;
   }
@@ -181,7 +219,7 @@ int launch_rows(const char *name, const RowArgs &a, void *stream) {
   const int64_t grid = a.rows < 0x7fffffff ? a.rows : 0x7fffffff;
   const int64_t c4 = a.cols >> 2;
   const bool vec = (a.cols & 3) == 0 && aligned(a.x, 16) && aligned(a.out, 16) &&
-                   (OP != kRmsNorm || aligned(a.w, 16)) && c4 <= 8 * 1024;
+                   ((OP != kRmsNorm && !is_dot(OP)) || aligned(a.w, 16)) && c4 <= 8 * 1024;
   if (!vec) {
     row_scalar_kernel<OP><<<(int)grid, 256, 0, s>>>(a);
     return check_launch(name);
@@ -226,4 +264,15 @@ extern "C" int lc_l2norm_f32(const float *x, float *out, int64_t rows, int64_t c
                              void *stream) {
   lc::RowArgs a{x, nullptr, nullptr, nullptr, out, rows, cols};
   return lc::launch_rows<lc::kL2>("lc_l2norm_f32", a, stream);
+}
+
+extern "C" int lc_rowdot_f32(int activation, const float *x, const float *y, float *out,
+                             int64_t rows, int64_t cols, void *stream) {
+  lc::RowArgs a{x, y, nullptr, nullptr, out, rows, cols};
+  if (activation == LC_EPI_NONE) return lc::launch_rows<lc::kRowDot>("lc_rowdot_f32", a, stream);
+  if (activation == LC_EPI_GELU_ERF)
+    return lc::launch_rows<lc::kRowDotGeluErf>("lc_rowdot_f32", a, stream);
+  if (activation == LC_EPI_GELU_TANH)
+    return lc::launch_rows<lc::kRowDotGeluTanh>("lc_rowdot_f32", a, stream);
+  return lc::fail(LC_ERR_INVALID, "lc_rowdot_f32: unknown activation %d", activation);
 }

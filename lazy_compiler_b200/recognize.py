@@ -563,6 +563,21 @@ def _is_load(buf=None, index=None):
     return pred
 
 
+def _rowdot_terms(pkg: KernelPackage, value: Any, x_index: tuple):
+    """y[r,c] * f(x[r,c]) with f the identity or a GELU -> (x, y, activation), else None."""
+    from .recognize_f32 import strip_epilogue
+    if not (isinstance(value, tuple) and value[:2] == ("op", "multiply") and len(value) == 4):
+        return None
+    at = _is_load(index=x_index)
+    for ya, fx in ((value[2], value[3]), (value[3], value[2])):
+        if not at(ya):
+            continue
+        act, inner = strip_epilogue(pkg, fx)
+        if at(inner):
+            return inner[1], ya[1], act
+    return None
+
+
 def _recognise_reduction(pkg: KernelPackage, tile: Node, ev: _Eval) -> Plan:
     axes = [(a.name, static_extent(a.extent)) for a in tile.axes]
     block = tile.get("block_threads") or axes[-1][1]
@@ -608,6 +623,23 @@ def _recognise_reduction(pkg: KernelPackage, tile: Node, ev: _Eval) -> Plan:
         out = w["buffer"]
         square = _match(op("multiply", V("x", _is_load(index=x_index)), V("x")), red["value"], {})
         plain = _is_load(index=x_index)(red["value"])
+        if two_d and not plain:
+            dot = _rowdot_terms(pkg, red["value"], x_index)
+            if dot is not None:
+                xb, yb, act = dot
+                if len(ev.writes) != 1 or not cond_ok(ev.writes[0]):
+                    raise CompileError("row dot product must be written once by thread 0")
+                w = ev.writes[0]
+                if w["values"][0] != ("red", acc) or w["index"] != (_aff({row_name: 1}),):
+                    raise CompileError("row dot product must write acc[row]")
+                for b_ in (xb, yb, w["buffer"]):
+                    if pkg.buffers[b_].dtype != "f32":
+                        raise CompileError("row dot products are f32")
+                for b_ in (xb, yb):
+                    if pkg.buffers[b_].shape != (rows, cols):
+                        raise CompileError("row dot operand shape does not match the loop extent")
+                return _plan(pkg, "rowdot_f32", "lc_rowdot_f32", {"x": xb, "y": yb, "out": w["buffer"]},
+                             {"rows": rows, "cols": cols, "activation": act}, {"io": "f32"})
         if not plain or square:
             raise CompileError("reduction accumulates an unsupported expression")
         x = red["value"][1]

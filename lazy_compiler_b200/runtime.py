@@ -46,6 +46,7 @@ SIGNATURES = {
     "lc_rmsnorm_f32": [_P, _P, _P, _P, _P, _I64, _I64, _P],
     "lc_softmax_f32": [_P, _P, _I64, _I64, _P],
     "lc_l2norm_f32": [_P, _P, _I64, _I64, _P],
+    "lc_rowdot_f32": [_INT, _P, _P, _P, _I64, _I64, _P],
     "lc_gemm": [_INT, _INT, _INT, _INT, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_ex": [_INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_path": [_INT, _INT, _P, _P, _I64, _I64, _I64],
@@ -140,6 +141,9 @@ def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
         call("lc_softmax_f32", ptr("x"), ptr("out"), p["rows"], p["cols"], s)
     elif op == "l2norm_f32":
         call("lc_l2norm_f32", ptr("x"), ptr("out"), p["rows"], p["cols"], s)
+    elif op == "rowdot_f32":
+        call("lc_rowdot_f32", EPILOGUES[p["activation"]], ptr("x"), ptr("y"), ptr("out"), p["rows"],
+             p["cols"], s)
     elif op == "gemm":
         d = plan["dtypes"]
         bias = ptr("bias") if "bias" in b else ctypes.c_void_p(0)

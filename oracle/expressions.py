@@ -313,6 +313,11 @@ def evaluate(plan: dict, arrays: dict) -> dict:
         out = softmax(g("x"))
     elif op == "l2norm_f32":
         out = l2norm(g("x"))
+    elif op == "rowdot_f32":
+        x = np.asarray(g("x"), np.float32)
+        fx = x if p["activation"] == "none" else gelu(x, "none" if p["activation"] == "gelu_erf" else "tanh",
+                                                      "f32").reshape(x.shape)
+        out = [(np.asarray(g("y"), np.float64) * fx.astype(np.float64)).sum(-1).astype(np.float32)]
     elif op == "gemm":
         bias = g("bias") if "bias" in bind else None
         out = gemm(g("a"), g("b"), p["b_layout"], p["epilogue"], plan["dtypes"]["ab"], plan["dtypes"]["c"],

@@ -40,6 +40,7 @@ EXPECTED = {
                                             "scale_mode": "mul_recip", "epilogue": "none"}),
     "phase9_gelu_attention": ("attention_f32", {"bh": 1, "s_q": 11, "s_kv": 37, "d": 17, "dv": 13,
                                                 "scale_mode": "mul", "epilogue": "gelu_erf"}),
+    "phase9_gelu_row_dot": ("rowdot_f32", {"rows": 19, "cols": 131, "activation": "gelu_erf"}),
 }
 
 
@@ -207,4 +208,15 @@ def test_gemm_bias_on_the_wrong_axis_is_rejected(tmp_path):
     _, ir = _mutate("phase9_bias_gelu_gemm", tmp_path, "input='bias', index=(Var(name='a1'),)",
                     "input='bias', index=(Var(name='a0'),)")
     with pytest.raises(CompileError):
+        compile_file(ir)
+
+
+def test_row_dot_with_changed_gelu_constant_is_rejected(tmp_path):
+    folder, ir = _copy("phase9_gelu_row_dot", tmp_path)
+    meta = json.loads((folder / "meta.json").read_text())
+    for arg in meta["kernels"][0]["args"]:
+        if arg["name"] == "gelu_inv_sqrt2":
+            arg["data"] = [0.5]
+    (folder / "meta.json").write_text(json.dumps(meta))
+    with pytest.raises(CompileError, match="GELU constant"):
         compile_file(ir)

@@ -26,7 +26,7 @@ PACKAGES = ["p00_scalar_add", "p01_vector_add", "p02_scale_shift", "p03_relu_mul
             "phase9_gelu_erf_half", "phase9_gelu_tanh_half",
             # FP32 GEMM and attention (staged, split-K, serial and block-cooperative schedules)
             "m01_matmul_512", "m02_matmul_rect", "phase9_bias_gelu_gemm", "a01_attention",
-            "a02_attention_128", "phase9_gelu_attention"]
+            "a02_attention_128", "phase9_gelu_attention", "phase9_gelu_row_dot"]
 
 
 def torch_():
@@ -283,3 +283,26 @@ def test_elementwise_config_size_sampled(cuda_device):
     for approx in ("none", "tanh"):
         runtime.call("lc_gelu", 0, int(approx == "tanh"), P(tx), P(out), n, None)
         assert_close(host(out[idx]), O.gelu(xs, approx, "f32"), 1e-5, 2e-6)
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (19, 131), (64, 4096), (3, 40000), (16384, 4096)])
+@pytest.mark.parametrize("act", ["none", "gelu_erf", "gelu_tanh"])
+def test_row_dot(rows, cols, act, cuda_device):
+    """sum_c y * f(x) per row (phase9_gelu_row_dot class): relative 1e-5 against float64."""
+    torch = torch_()
+    rng = np.random.default_rng(rows + cols)
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    y = rng.standard_normal((rows, cols)).astype(np.float32)
+    tx, ty = dev(x), dev(y)
+    out = torch.full((rows,), float("nan"), device="cuda")
+    runtime.call("lc_rowdot_f32", runtime.EPILOGUES[act], P(tx), P(ty), P(out), rows, cols, None)
+    plan = {"op": "rowdot_f32", "bind": {"x": "x", "y": "y", "out": "out"},
+            "params": {"rows": rows, "cols": cols, "activation": act}, "dtypes": {"io": "f32"}}
+    ref = O.evaluate(plan, {"x": x, "y": y})["out"]
+    # each product is rounded once and CUDA erff/tanhf differ from the formula by
+    # a few ulp; the compensated sum adds
+    # almost nothing: bound by the row's sum of |terms|
+    fx = x if act == "none" else O.gelu(x, "none" if act == "gelu_erf" else "tanh", "f32").reshape(x.shape)
+    mag = np.abs(y.astype(np.float64) * fx.astype(np.float64)).sum(-1)
+    got = host(out)
+    assert np.all(np.abs(got - ref) <= 1e-5 * np.abs(ref) + 2.0 ** -21 * mag), float(np.abs(got - ref).max())
