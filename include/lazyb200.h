@@ -164,6 +164,17 @@ int lc_l2norm_f32(const float *x, float *out, int64_t rows, int64_t cols, void *
 int lc_rowdot_f32(int activation, const float *x, const float *y, float *out, int64_t rows,
                   int64_t cols, void *stream);
 
+/* The fragment attention tile class: O[bh, s_q, dv] = f16(softmax(f16(Q) f16(Kt))) f16(V)
+ * with f32 buffers Q [bh, s_q, d], Kt [bh, d, s_kv], V [bh, s_kv, dv], O f32:
+ * operands rounded to f16, scores accumulated in f32, each row normalised
+ * (max, exp = ex2.approx(x log2 e), sum, correctly rounded division) and the
+ * weights rounded to f16 before O = P V accumulates in f32; s_kv <= 4096.
+ * Replaces the RegFragment / LdmatrixLoad / MmaSyncPtx / FragmentRowReduce /
+ * FragmentApply / FragmentRepack / RegStore chain of
+ * examples/phase9/fragments/fragment_attention_tile_f16 (ptx_tensor.py:459-618). */
+int lc_attention_tile_f16q(const void *q, const void *kt, const void *v, void *o, int64_t bh,
+                           int64_t s_q, int64_t s_kv, int64_t d, int64_t dv, void *stream);
+
 /* ---------------------------------------------------------------- tensor cores */
 
 /* C[M,N] = epilogue(A[M,K] @ B), f32 accumulation.  ab_dtype LC_F16 or

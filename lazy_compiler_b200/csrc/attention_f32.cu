@@ -208,6 +208,54 @@ __global__ void __launch_bounds__(256) attention_f32_direct_kernel(
   }
 }
 
+// The fragment attention tile (examples/phase9/fragments/fragment_attention_tile_f16):
+// Q, Kt and V are read as f16 (round to nearest), S = Q Kt accumulates their
+// exact products in f32, each row is normalised before the PV product
+// (max, exp(s - max) = ex2.approx((s - max) log2 e), row sum, correctly rounded
+// division) and the weights are rounded to f16 — the reference's
+// FragmentRowReduce / FragmentApply / FragmentRepack chain
+// (ptx_tensor.py:459-618) — and O = P V accumulates in f32.  One warp per
+// query row: lanes stride over keys for the statistics and over output columns
+// for O; the row's f16 weights live in shared memory.
+constexpr int kTileWarps = 4;
+constexpr int kTileMaxKeys = 4096;
+
+__device__ __forceinline__ float f16r(float x) { return __half2float(__float2half_rn(x)); }
+
+__global__ void __launch_bounds__(32 * kTileWarps) attention_tile_f16q_kernel(
+    const float *__restrict__ q, const float *__restrict__ kt, const float *__restrict__ v,
+    float *__restrict__ o, int s_q, int s_kv, int d, int dv) {
+  __shared__ __half pw[kTileWarps][kTileMaxKeys];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kTileWarps + warp;
+  const int64_t bh = blockIdx.y;
+  if (row >= s_q) return;
+  const float *qr = q + (bh * s_q + row) * d;
+  const float *kb = kt + bh * d * s_kv;
+  const float *vb = v + bh * s_kv * dv;
+  auto score = [&](int key) {
+    float acc = 0.f;
+    for (int dd = 0; dd < d; ++dd) acc = fmaf(f16r(qr[dd]), f16r(kb[(int64_t)dd * s_kv + key]), acc);
+    return acc;
+  };
+  float mx = -INFINITY;
+  for (int key = lane; key < s_kv; key += 32) mx = fmaxf(mx, score(key));
+  mx = warp_max(mx);
+  float sum = 0.f;
+  for (int key = lane; key < s_kv; key += 32) sum += exp_ref(__fsub_rn(score(key), mx));
+  sum = warp_sum(sum);
+  for (int key = lane; key < s_kv; key += 32)
+    pw[warp][key] = __float2half_rn(__fdiv_rn(exp_ref(__fsub_rn(score(key), mx)), sum));
+  __syncwarp();
+  float *orow = o + (bh * s_q + row) * dv;
+  for (int c = lane; c < dv; c += 32) {
+    float acc = 0.f;
+    for (int key = 0; key < s_kv; ++key)
+      acc = fmaf(__half2float(pw[warp][key]), f16r(vb[(int64_t)key * dv + c]), acc);
+    orow[c] = acc;
+  }
+}
+
 size_t tiled_smem(int d, int dvh) {
   return (size_t)(d * QS + d * BKV + BKV * 64 * dvh + BKV * BQ) * sizeof(float);
 }
@@ -274,4 +322,22 @@ extern "C" int lc_attention_f32(int scale_mode, int epilogue, const void *scale,
   LC_ATT(LC_EPI_NONE) LC_ATT(LC_EPI_GELU_ERF) LC_ATT(LC_EPI_GELU_TANH)
 #undef LC_ATT
   return fail(LC_ERR_INVALID, "lc_attention_f32: bad epilogue");
+}
+
+extern "C" int lc_attention_tile_f16q(const void *q, const void *kt, const void *v, void *o,
+                                      int64_t bh, int64_t s_q, int64_t s_kv, int64_t d, int64_t dv,
+                                      void *stream) {
+  using namespace lc;
+  if (bh < 0 || s_q < 0 || s_kv < 0 || d < 0 || dv < 0)
+    return fail(LC_ERR_INVALID, "lc_attention_tile_f16q: negative shape");
+  if (s_kv > kTileMaxKeys || bh > 65535 || s_q > 0x7fffffff || d > 0x7fffffff || dv > 0x7fffffff)
+    return fail(LC_ERR_UNSUPPORTED, "lc_attention_tile_f16q: more than %d keys or too large", kTileMaxKeys);
+  if (bh == 0 || s_q == 0 || dv == 0) return LC_OK;
+  if (s_kv == 0) return fail(LC_ERR_INVALID, "lc_attention_tile_f16q: softmax over zero keys");
+  if (!o || !v || (d > 0 && (!q || !kt))) return fail(LC_ERR_INVALID, "lc_attention_tile_f16q: null buffer");
+  dim3 grid((unsigned)((s_q + kTileWarps - 1) / kTileWarps), (unsigned)bh);
+  attention_tile_f16q_kernel<<<grid, 32 * kTileWarps, 0, as_stream(stream)>>>(
+      static_cast<const float *>(q), static_cast<const float *>(kt), static_cast<const float *>(v),
+      static_cast<float *>(o), (int)s_q, (int)s_kv, (int)d, (int)dv);
+  return check_launch("lc_attention_tile_f16q");
 }

@@ -848,9 +848,11 @@ def recognise(pkg: KernelPackage) -> Plan:
         raise CompileError("KernelOp body must be a single Tile")
     tile = pkg.body[0]
     kinds = {s.kind for s in _walk(tile.body)}
+    from . import recognize_f32 as f32
+    if "FragmentRowReduce" in kinds:
+        return f32.recognise_fragment_attention(pkg, tile)
     if "MmaSyncPtx" in kinds:
         return _recognise_gemm(pkg, tile)
-    from . import recognize_f32 as f32
     if "CpAsyncCopy" in kinds:
         return f32.recognise_staged_gemm(pkg, tile)
     ev = _Eval(pkg)

@@ -670,3 +670,91 @@ def recognise_staged_gemm(pkg: KernelPackage, tile: Node) -> Plan:
     check_cover(pkg, [(n, e) for n, e in ev.tile_axes if n not in dict(split)], ev.writes, out,
                 repeat=1)
     return _gemm_plan(pkg, a, b, bias, out, layout, epi, k)
+
+
+# ----------------------------------------------------------------------------
+# the fragment attention tile (m16n8k16 fragment algebra)
+# ----------------------------------------------------------------------------
+
+def _op_name(x) -> str:
+    return x.name if isinstance(x, Node) else str(x)
+
+
+def recognise_fragment_attention(pkg: KernelPackage, tile: Node) -> Plan:
+    """The FragmentRowReduce / FragmentApply / FragmentRepack attention chain.
+
+    Matches, statement by statement, the chain of
+    examples/phase9/fragments/fragment_attention_tile_f16 (ptx_tensor.py:459-618):
+    A <- Q; B_i <- Kt[:, 8i:8i+8]; S_i = A B_i; pivot = rowmax(S);
+    S_i = exp(S_i - pivot); denom = rowsum(S); S_i = S_i / denom; A <- f16(S);
+    B <- V; O = A B; store O.  One m16 tile of queries, K = 16 (one k step),
+    n_frag * 8 keys, 8 value columns.
+    """
+    body = [s for s in tile.body if s.kind != "RegFragment"]
+    kinds = [s.kind for s in body]
+    it = iter(body)
+
+    def take(kind):
+        s = next(it, None)
+        if s is None or s.kind != kind:
+            raise CompileError(f"fragment attention chain: expected {kind}, found {getattr(s, 'kind', None)}")
+        return s
+
+    def origin(s):
+        return tuple(_aff_const(_Eval(pkg).index(i)) for i in s.src_index)
+
+    qa = take("LdmatrixLoad")
+    if qa.role != "a" or origin(qa) != (0, 0) or qa.get("b_trans"):
+        raise CompileError("fragment attention: A must be Q at (0, 0)")
+    n_frag = kinds.count("MmaSyncPtx") - 1
+    scores = []
+    for i in range(n_frag):
+        kb = take("LdmatrixLoad")
+        mma = take("MmaSyncPtx")
+        if kb.role != "b" or kb.get("b_trans") or origin(kb) != (0, 8 * i) or mma.a_frag != qa.frag \
+                or mma.b_frag != kb.frag or tuple(mma.shape) != (16, 8, 16) or mma.ab_dtype != "f16" \
+                or mma.c_dtype != "f32":
+            raise CompileError("fragment attention: S_i = Q Kt[:, 8i:8i+8] expected")
+        if i and kb.src_buffer != kt:
+            raise CompileError("fragment attention: all B fragments must come from one Kt")
+        kt = kb.src_buffer
+        scores.append(mma.c_frag)
+    red = take("FragmentRowReduce")
+    if _op_name(red.op) != "maximum" or tuple(red.frags) != tuple(scores):
+        raise CompileError("fragment attention: row max of the scores expected")
+    for f in scores:
+        ap = take("FragmentApply")
+        post = tuple(_op_name(x) for x in ap.get("post", ()))
+        if ap.out != f or _op_name(ap.op) != "subtract" or ap.args[0] != f or \
+                tuple(ap.args[1]) != (red.top, red.bot) or post != ("exp",):
+            raise CompileError("fragment attention: exp(S - rowmax) expected")
+    den = take("FragmentRowReduce")
+    if _op_name(den.op) != "add" or tuple(den.frags) != tuple(scores):
+        raise CompileError("fragment attention: row sum expected")
+    for f in scores:
+        ap = take("FragmentApply")
+        if ap.out != f or _op_name(ap.op) != "divide" or ap.args[0] != f or \
+                tuple(ap.args[1]) != (den.top, den.bot) or tuple(ap.get("post", ())):
+            raise CompileError("fragment attention: division by the row sum expected")
+    rp = take("FragmentRepack")
+    if rp.frag != qa.frag or tuple(rp.srcs) != tuple(scores) or rp.ab_dtype != "f16":
+        raise CompileError("fragment attention: P must be repacked to f16 into the A fragment")
+    vb = take("LdmatrixLoad")
+    mma = take("MmaSyncPtx")
+    st = take("RegStore")
+    if next(it, None) is not None:
+        raise CompileError("fragment attention: statements after the store")
+    if vb.role != "b" or vb.get("b_trans") or origin(vb) != (0, 0) or mma.a_frag != qa.frag \
+            or mma.b_frag != vb.frag or tuple(mma.shape) != (16, 8, 16):
+        raise CompileError("fragment attention: O = P V expected")
+    if st.frag != mma.c_frag or st.get("epilogue") is not None or st.get("atomic") or \
+            tuple(_aff_const(_Eval(pkg).index(i)) for i in st.dst_index) != (0, 0):
+        raise CompileError("fragment attention: O stored at (0, 0) without an epilogue expected")
+    q, v, out = qa.src_buffer, vb.src_buffer, st.dst_buffer
+    sq, sk, sv, so = (pkg.buffers[b].shape for b in (q, kt, v, out))
+    if tuple(sq) != (16, 16) or tuple(sk) != (16, 8 * n_frag) or tuple(sv) != (8 * n_frag, 8) or \
+            tuple(so) != (16, 8):
+        raise CompileError(f"fragment attention shapes {sq} {sk} {sv} -> {so} unsupported")
+    _f32(pkg, q, kt, v, out)
+    return _plan(pkg, "attention_tile_f16q", "lc_attention_tile_f16q", {"q": q, "kt": kt, "v": v, "o": out},
+                 {"bh": 1, "s_q": 16, "s_kv": 8 * n_frag, "d": 16, "dv": 8}, {"io": "f32", "compute": "f16"})

@@ -51,6 +51,7 @@ SIGNATURES = {
     "lc_gemm_ex": [_INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_path": [_INT, _INT, _P, _P, _I64, _I64, _I64],
     "lc_attention_f32": [_INT, _INT, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
+    "lc_attention_tile_f16q": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
     "lc_device_status": [_P],
     "lc_selftest_bounded_wait": [_I64, _P],
     "lc_probe_mma": [_INT, _INT, _P],
@@ -152,6 +153,9 @@ def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
     elif op == "attention_f32":
         call("lc_attention_f32", SCALE_MODES[p["scale_mode"]], EPILOGUES[p["epilogue"]],
              ptr("scale"), ptr("q"), ptr("kt"), ptr("v"), ptr("o"), p["bh"], p["s_q"], p["s_kv"],
+             p["d"], p["dv"], s)
+    elif op == "attention_tile_f16q":
+        call("lc_attention_tile_f16q", ptr("q"), ptr("kt"), ptr("v"), ptr("o"), p["bh"], p["s_q"], p["s_kv"],
              p["d"], p["dv"], s)
     elif op == "sdpa_f16":
         call("lc_sdpa_f16", ptr("q"), ptr("k"), ptr("v"), ptr("o"), p["bh"], p["s_q"], p["s_kv"],

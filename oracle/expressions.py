@@ -313,6 +313,8 @@ def evaluate(plan: dict, arrays: dict) -> dict:
         out = softmax(g("x"))
     elif op == "l2norm_f32":
         out = l2norm(g("x"))
+    elif op == "attention_tile_f16q":
+        out = attention_tile_f16(g("q"), g("kt"), g("v"))
     elif op == "rowdot_f32":
         x = np.asarray(g("x"), np.float32)
         fx = x if p["activation"] == "none" else gelu(x, "none" if p["activation"] == "gelu_erf" else "tanh",

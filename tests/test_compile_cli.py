@@ -41,6 +41,8 @@ EXPECTED = {
     "phase9_gelu_attention": ("attention_f32", {"bh": 1, "s_q": 11, "s_kv": 37, "d": 17, "dv": 13,
                                                 "scale_mode": "mul", "epilogue": "gelu_erf"}),
     "phase9_gelu_row_dot": ("rowdot_f32", {"rows": 19, "cols": 131, "activation": "gelu_erf"}),
+    "fragment_attention_tile_f16": ("attention_tile_f16q", {"bh": 1, "s_q": 16, "s_kv": 16, "d": 16,
+                                                            "dv": 8}),
 }
 
 
@@ -71,7 +73,7 @@ def test_cli_missing_file_exit_1(tmp_path):
     assert result.stderr.startswith("compile.py: ")
 
 
-@pytest.mark.parametrize("name", ["activation_gelu_f32", "fragment_attention_tile_f16"])
+@pytest.mark.parametrize("name", ["activation_gelu_f32", "activation_gelu_special"])
 def test_cli_rejects_unsupported_classes_without_output(name):
     result = subprocess.run(CLI + [str(golden_ir(name))], capture_output=True, text=True, cwd=ROOT)
     assert result.returncode == 1
@@ -219,4 +221,20 @@ def test_row_dot_with_changed_gelu_constant_is_rejected(tmp_path):
             arg["data"] = [0.5]
     (folder / "meta.json").write_text(json.dumps(meta))
     with pytest.raises(CompileError, match="GELU constant"):
+        compile_file(ir)
+
+
+def test_fragment_attention_without_exp_is_rejected(tmp_path):
+    _, ir = _mutate("fragment_attention_tile_f16", tmp_path, "post=(ElementwiseImpl('exp'),)", "post=()")
+    with pytest.raises(CompileError, match="exp"):
+        compile_file(ir)
+
+
+def test_fragment_attention_with_row_min_is_rejected(tmp_path):
+    _, ir = _mutate("fragment_attention_tile_f16", tmp_path,
+                    "FragmentRowReduce(top='pivot0', bot='pivot1', frags=('scores[0]', 'scores[1]'), "
+                    "op=ElementwiseImpl('maximum')",
+                    "FragmentRowReduce(top='pivot0', bot='pivot1', frags=('scores[0]', 'scores[1]'), "
+                    "op=ElementwiseImpl('minimum')")
+    with pytest.raises(CompileError, match="row max"):
         compile_file(ir)

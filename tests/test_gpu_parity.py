@@ -26,7 +26,8 @@ PACKAGES = ["p00_scalar_add", "p01_vector_add", "p02_scale_shift", "p03_relu_mul
             "phase9_gelu_erf_half", "phase9_gelu_tanh_half",
             # FP32 GEMM and attention (staged, split-K, serial and block-cooperative schedules)
             "m01_matmul_512", "m02_matmul_rect", "phase9_bias_gelu_gemm", "a01_attention",
-            "a02_attention_128", "phase9_gelu_attention", "phase9_gelu_row_dot"]
+            "a02_attention_128", "phase9_gelu_attention", "phase9_gelu_row_dot",
+            "fragment_attention_tile_f16"]
 
 
 def torch_():
@@ -306,3 +307,20 @@ def test_row_dot(rows, cols, act, cuda_device):
     mag = np.abs(y.astype(np.float64) * fx.astype(np.float64)).sum(-1)
     got = host(out)
     assert np.all(np.abs(got - ref) <= 1e-5 * np.abs(ref) + 2.0 ** -21 * mag), float(np.abs(got - ref).max())
+
+
+@pytest.mark.parametrize("bh,s_q,s_kv,d,dv", [(1, 16, 16, 16, 8), (2, 37, 100, 24, 40), (1, 5, 4096, 8, 3)])
+def test_attention_tile_f16q(bh, s_q, s_kv, d, dv, cuda_device):
+    """The fragment attention tile class at other shapes: f16 operands and weights (rtol 2e-4)."""
+    torch = torch_()
+    rng = np.random.default_rng(s_q + s_kv)
+    q = rng.standard_normal((bh, s_q, d)).astype(np.float32)
+    kt = rng.standard_normal((bh, d, s_kv)).astype(np.float32)
+    v = rng.standard_normal((bh, s_kv, dv)).astype(np.float32)
+    tq, tk, tv = dev(q), dev(kt), dev(v)
+    out = torch.full((bh, s_q, dv), float("nan"), device="cuda")
+    runtime.call("lc_attention_tile_f16q", P(tq), P(tk), P(tv), P(out), bh, s_q, s_kv, d, dv, None)
+    got = host(out)
+    for b in range(bh):
+        ref = O.attention_tile_f16(q[b], kt[b], v[b])[0]
+        assert_close(got[b], ref, 2e-4, 2e-5)

@@ -102,7 +102,7 @@ def test_oracle_sdpa_matches_attention_tile_rounding():
 
 @pytest.mark.parametrize("name", ["m01_matmul_512", "m02_matmul_rect", "phase9_bias_gelu_gemm",
                                   "a01_attention", "a02_attention_128", "phase9_gelu_attention",
-                                  "phase9_gelu_row_dot"])
+                                  "phase9_gelu_row_dot", "fragment_attention_tile_f16"])
 def test_oracle_evaluates_fp32_plans(name):
     """The oracle run on the recognised plan (bias, score form, epilogue) reproduces the golden outputs."""
     plan = compile_file(golden_ir(name))
