@@ -51,6 +51,7 @@ constexpr float kRescaleThreshold = 8.0f;     // log2 units
 
 struct SdpaParams {
   int s_q, s_kv, n_kv;
+  int q_blocks, items;  // QT-tile query blocks per head; work items = heads x q_blocks
   float scale_log2;
   __half *o;
   int *err;
@@ -141,6 +142,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t *q_s = smem;
   uint8_t *kv_s = smem + Q_BYTES;
   __shared__ __align__(8) uint64_t q_full;
+  __shared__ __align__(8) uint64_t q_empty;
   __shared__ __align__(8) uint64_t k_full[KV_STAGES];
   __shared__ __align__(8) uint64_t v_full[KV_STAGES];
   __shared__ __align__(8) uint64_t k_empty[KV_STAGES];
@@ -148,15 +150,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   __shared__ __align__(8) uint64_t s_full[QT];
   __shared__ __align__(8) uint64_t p_full[QT];
   __shared__ __align__(8) uint64_t o_done[QT];
+  __shared__ __align__(8) uint64_t o_empty[QT];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   volatile int *abort = &abort_flag;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int bh = blockIdx.y;
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 1);
+    mbar_init(&q_empty, 1);
     for (int s = 0; s < KV_STAGES; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
@@ -167,6 +170,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&s_full[t], 1);
       mbar_init(&p_full[t], 4);
       mbar_init(&o_done[t], 1);
+      mbar_init(&o_empty[t], 4);
     }
     abort_flag = 0;
     fence_barrier_init();
@@ -185,36 +189,52 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_base;
   const int n = p.n_kv;
+  // Persistent: work item w is query block w % q_blocks of head w / q_blocks;
+  // CTA c takes items c, c + gridDim.x, ...  Every barrier phase counts over
+  // all items of the CTA: KV block g (g = local item * n + j) uses K/V stage
+  // g & 1, and s_full / p_full / o_done complete once per block.
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_expect_tx(&q_full, Q_BYTES);
-      for (int t = 0; t < QT; ++t) {
-        const int row0 = (blockIdx.x * QT + t) * BQ;
-        tma_load_3d(q_s + t * TILE_BYTES, &tma_q, &q_full, 0, row0, bh);
-        tma_load_3d(q_s + t * TILE_BYTES + CHUNK_BYTES, &tma_q, &q_full, 64, row0, bh);
-      }
-      // K(j) is released once both S(j) products completed, V(j) once both PV(j)
-      // products completed, so K(j+2) loads while V(j) is still in use.
-      for (int j = 0; j < n; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        uint8_t *k_s = kv_s + st * 2 * TILE_BYTES;
-        uint8_t *v_s = k_s + TILE_BYTES;
-        if (!mbar_wait(&k_empty[st], ph ^ 1, abort)) {
+      int g = 0, local = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < p.items; item += gridDim.x, ++local) {
+        const int bh = item / p.q_blocks, qb = item - bh * p.q_blocks;
+        // Q of the previous item is free once its last S products completed
+        if (local > 0 && !mbar_wait(&q_empty, (local - 1) & 1, abort)) {
           raise_error(p, abort, kErrTimeoutProducer);
           break;
         }
-        mbar_expect_tx(&k_full[st], TILE_BYTES);
-        tma_load_3d(k_s, &tma_k, &k_full[st], 0, j * BKV, bh);
-        tma_load_3d(k_s + CHUNK_BYTES, &tma_k, &k_full[st], 64, j * BKV, bh);
-        if (!mbar_wait(&v_empty[st], ph ^ 1, abort)) {
-          raise_error(p, abort, kErrTimeoutProducer);
-          break;
+        mbar_expect_tx(&q_full, Q_BYTES);
+        for (int t = 0; t < QT; ++t) {
+          const int row0 = (qb * QT + t) * BQ;
+          tma_load_3d(q_s + t * TILE_BYTES, &tma_q, &q_full, 0, row0, bh);
+          tma_load_3d(q_s + t * TILE_BYTES + CHUNK_BYTES, &tma_q, &q_full, 64, row0, bh);
         }
-        mbar_expect_tx(&v_full[st], TILE_BYTES);
-        tma_load_3d(v_s, &tma_v, &v_full[st], 0, j * BKV, bh);
-        tma_load_3d(v_s + CHUNK_BYTES, &tma_v, &v_full[st], 64, j * BKV, bh);
+        // K(j) is released once both S(j) products completed, V(j) once both PV(j)
+        // products completed, so K(j+2) loads while V(j) is still in use.
+        for (int j = 0; j < n; ++j, ++g) {
+          const int st = g & 1;
+          const uint32_t ph = (g >> 1) & 1;
+          uint8_t *k_s = kv_s + st * 2 * TILE_BYTES;
+          uint8_t *v_s = k_s + TILE_BYTES;
+          if (!mbar_wait(&k_empty[st], ph ^ 1, abort)) {
+            raise_error(p, abort, kErrTimeoutProducer);
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&k_full[st], TILE_BYTES);
+          tma_load_3d(k_s, &tma_k, &k_full[st], 0, j * BKV, bh);
+          tma_load_3d(k_s + CHUNK_BYTES, &tma_k, &k_full[st], 64, j * BKV, bh);
+          if (!mbar_wait(&v_empty[st], ph ^ 1, abort)) {
+            raise_error(p, abort, kErrTimeoutProducer);
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&v_full[st], TILE_BYTES);
+          tma_load_3d(v_s, &tma_v, &v_full[st], 0, j * BKV, bh);
+          tma_load_3d(v_s + CHUNK_BYTES, &tma_v, &v_full[st], 64, j * BKV, bh);
+        }
       }
     }
   } else if (warp == 1) {
@@ -228,10 +248,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint64_t k_desc = smem_desc_sw128(smem_u32(kv_s), 16, 1024);
       const uint64_t v_desc = smem_desc_sw128(smem_u32(kv_s) + TILE_BYTES, CHUNK_BYTES, 1024);
       constexpr uint32_t kStageStep = 2 * TILE_BYTES / 16;
-      // S_t(j) = Q_t K(j)^T into TMEM columns [t*128, t*128+128)
-      auto issue_s = [&](int t, int j) {
+      // S_t = Q_t K(block g)^T into TMEM columns [t*128, t*128+128)
+      auto issue_s = [&](int t, int g) {
         const uint64_t qd = q_desc + (uint64_t)(t * TILE_BYTES / 16);
-        const uint64_t kd = k_desc + (uint64_t)((j & 1) * kStageStep);
+        const uint64_t kd = k_desc + (uint64_t)((g & 1) * kStageStep);
         const uint32_t d_tmem = tmem + t * BKV;
 #pragma unroll
         for (int k = 0; k < HEAD / 16; ++k) {
@@ -240,43 +260,54 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         mma_commit(&s_full[t]);
       };
-      // O_t += P_t(j) V(j), P_t read from TMEM over S_t
-      auto issue_pv = [&](int t, int j) {
-        const uint64_t vd = v_desc + (uint64_t)((j & 1) * kStageStep);
+      // O_t (+)= P_t V(block g), P_t read from TMEM over S_t; the item's first
+      // block overwrites O
+      auto issue_pv = [&](int t, int g, bool first) {
+        const uint64_t vd = v_desc + (uint64_t)((g & 1) * kStageStep);
         const uint32_t d_tmem = tmem + O_COL + t * HEAD;
         const uint32_t a_tmem = tmem + t * BKV;
 #pragma unroll
         for (int k = 0; k < BKV / 16; ++k)
           mma_f16_tmem_a(d_tmem, a_tmem + k * 8, vd + (uint64_t)(k * 2048 / 16), idesc_o,
-                         (j | k) != 0);
+                         !(first && k == 0));
         mma_commit(&o_done[t]);
       };
-      bool ok = mbar_wait(&q_full, 0, abort) && mbar_wait(&k_full[0], 0, abort);
-      if (ok) {
+      int g0 = 0, local = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < p.items; item += gridDim.x, ++local, g0 += n) {
+        ok = mbar_wait(&q_full, local & 1, abort) && mbar_wait(&k_full[g0 & 1], (g0 >> 1) & 1, abort);
+        if (!ok) break;
         tc_fence_after();
-        for (int t = 0; t < QT; ++t) issue_s(t, 0);
-        mma_commit(&k_empty[0]);
-      }
-      for (int j = 0; ok && j < n; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        const bool next = j + 1 < n;
-        for (int t = 0; t < QT; ++t) {
-          if (!mbar_wait(&p_full[t], j & 1, abort) || (t == 0 && !mbar_wait(&v_full[st], ph, abort))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_pv(t, j);
-          if (t == QT - 1) mma_commit(&v_empty[st]);
-          if (next) {
-            if (t == 0 && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort)) {
+        for (int t = 0; t < QT; ++t) issue_s(t, g0);
+        mma_commit(&k_empty[g0 & 1]);
+        if (n == 1) mma_commit(&q_empty);
+        for (int j = 0; ok && j < n; ++j) {
+          const int g = g0 + j;
+          const int st = g & 1;
+          const uint32_t ph = (g >> 1) & 1;
+          const bool next = j + 1 < n;
+          for (int t = 0; t < QT; ++t) {
+            if (!mbar_wait(&p_full[t], g & 1, abort) ||
+                (j == 0 && local > 0 && !mbar_wait(&o_empty[t], (local - 1) & 1, abort)) ||
+                (t == 0 && !mbar_wait(&v_full[st], ph, abort))) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_s(t, j + 1);
-            if (t == QT - 1) mma_commit(&k_empty[(j + 1) & 1]);
+            issue_pv(t, g, j == 0);
+            if (t == QT - 1) mma_commit(&v_empty[st]);
+            if (next) {
+              if (t == 0 && !mbar_wait(&k_full[(g + 1) & 1], ((g + 1) >> 1) & 1, abort)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_s(t, g + 1);
+              if (t == QT - 1) {
+                mma_commit(&k_empty[(g + 1) & 1]);
+                if (j + 2 == n) mma_commit(&q_empty);  // the item's last S products
+              }
+            }
           }
         }
       }
@@ -289,104 +320,109 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const uint32_t s_col = t * BKV;
     const uint32_t o_col = O_COL + t * HEAD;
-    float m = -INFINITY, l = 0.f;
+    int g0 = 0;
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
-      if (!warp_wait(&s_full[t], j & 1, abort, p, kErrTimeoutSoftmax)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t sr[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_base + s_col + c * 32, sr[c]);
-      tmem_wait_ld();
-      const int valid = p.s_kv - j * BKV;
-      if (valid < BKV) {  // ragged last KV tile (uniform across the CTA): mask absent keys
-#pragma unroll
+    for (int item = blockIdx.x; ok && item < p.items; item += gridDim.x, g0 += n) {
+      const int bh = item / p.q_blocks, qb = item - bh * p.q_blocks;
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < n; ++j) {
+        const int g = g0 + j;
+        if (!warp_wait(&s_full[t], g & 1, abort, p, kErrTimeoutSoftmax)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t sr[4][32];
+  #pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_base + s_col + c * 32, sr[c]);
+        tmem_wait_ld();
+        const int valid = p.s_kv - j * BKV;
+        if (valid < BKV) {  // ragged last KV tile (uniform across the CTA): mask absent keys
+  #pragma unroll
+          for (int c = 0; c < 4; ++c)
+  #pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c * 32 + i >= valid) sr[c][i] = __float_as_uint(-INFINITY);
+        }
+        // max of the raw scores (the positive scale commutes with max), as 8
+        // independent chains so the reduction is not one 128-deep dependency
+        float mx8[8];
+  #pragma unroll
+        for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
+  #pragma unroll
         for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c * 32 + i >= valid) sr[c][i] = __float_as_uint(-INFINITY);
-      }
-      // max of the raw scores (the positive scale commutes with max), as 8
-      // independent chains so the reduction is not one 128-deep dependency
-      float mx8[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int i = 0; i < 32; i += 2)
-          mx8[(i >> 1) & 7] = max3(mx8[(i >> 1) & 7], __uint_as_float(sr[c][i]),
-                                   __uint_as_float(sr[c][i + 1]));
-      float mx = max3(max3(mx8[0], mx8[1], mx8[2]), max3(mx8[3], mx8[4], mx8[5]),
-                      fmaxf(mx8[6], mx8[7]));
-      mx *= p.scale_log2;
-      const float m_new = fmaxf(m, mx);
-      const bool need = m_new > m + kRescaleThreshold;
-      if (__any_sync(0xffffffffu, need)) {
-        const float alpha = need ? ex2(m - m_new) : 1.0f;
-        if (need) {
-          l *= alpha;
-          m = m_new;
-        }
-        if (j > 0) {
-          if (!warp_wait(&o_done[t], (j - 1) & 1, abort, p, kErrTimeoutCorrection)) {
-            ok = false;
-            break;
+  #pragma unroll
+          for (int i = 0; i < 32; i += 2)
+            mx8[(i >> 1) & 7] = max3(mx8[(i >> 1) & 7], __uint_as_float(sr[c][i]),
+                                     __uint_as_float(sr[c][i + 1]));
+        float mx = max3(max3(mx8[0], mx8[1], mx8[2]), max3(mx8[3], mx8[4], mx8[5]),
+                        fmaxf(mx8[6], mx8[7]));
+        mx *= p.scale_log2;
+        const float m_new = fmaxf(m, mx);
+        const bool need = m_new > m + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          const float alpha = need ? ex2(m - m_new) : 1.0f;
+          if (need) {
+            l *= alpha;
+            m = m_new;
           }
-          tc_fence_after();
-#pragma unroll 1
-          for (int c = 0; c < HEAD / 16; ++c) {
-            uint32_t o[16];
-            tmem_ld16(tmem + lane_base + o_col + c * 16, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st16(tmem + lane_base + o_col + c * 16, o);
+          if (j > 0) {
+            if (!warp_wait(&o_done[t], (g - 1) & 1, abort, p, kErrTimeoutCorrection)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+  #pragma unroll 1
+            for (int c = 0; c < HEAD / 16; ++c) {
+              uint32_t o[16];
+              tmem_ld16(tmem + lane_base + o_col + c * 16, o);
+              tmem_wait_ld();
+  #pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+              tmem_st16(tmem + lane_base + o_col + c * 16, o);
+            }
+            tmem_wait_st();
           }
-          tmem_wait_st();
         }
-      }
-      // independent row-sum chains, each a pair of f32 lanes
-      uint64_t part2[4] = {0ull, 0ull, 0ull, 0ull};
-      const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
-      const uint64_t neg_m2 = pack2(-m, -m);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          // p = 2^(s * scale * log2 e - m): one paired FMA, then MUFU ex2 or
-          // (one pair in four) the paired polynomial
-          const uint64_t x2 = ffma2(pack2(__uint_as_float(sr[c][2 * i]), __uint_as_float(sr[c][2 * i + 1])),
-                                    scale2, neg_m2);
-          uint64_t p2;
-          if ((i & 3) == 3) {
-            p2 = ex2_poly2(x2);
-          } else {
-            const float2 x = unpack2(x2);
-            p2 = pack2(ex2(x.x), ex2(x.y));
+        // independent row-sum chains, each a pair of f32 lanes
+        uint64_t part2[4] = {0ull, 0ull, 0ull, 0ull};
+        const uint64_t scale2 = pack2(p.scale_log2, p.scale_log2);
+        const uint64_t neg_m2 = pack2(-m, -m);
+  #pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t packed[16];
+  #pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            // p = 2^(s * scale * log2 e - m): one paired FMA, then MUFU ex2 or
+            // (one pair in four) the paired polynomial
+            const uint64_t x2 = ffma2(pack2(__uint_as_float(sr[c][2 * i]), __uint_as_float(sr[c][2 * i + 1])),
+                                      scale2, neg_m2);
+            uint64_t p2;
+            if ((i & 3) == 3) {
+              p2 = ex2_poly2(x2);
+            } else {
+              const float2 x = unpack2(x2);
+              p2 = pack2(ex2(x.x), ex2(x.y));
+            }
+            part2[i & 3] = fadd2(part2[i & 3], p2);
+            const float2 pp = unpack2(p2);
+            __half2 h = __floats2half2_rn(pp.x, pp.y);
+            packed[i] = *reinterpret_cast<uint32_t *>(&h);
           }
-          part2[i & 3] = fadd2(part2[i & 3], p2);
-          const float2 pp = unpack2(p2);
-          __half2 h = __floats2half2_rn(pp.x, pp.y);
-          packed[i] = *reinterpret_cast<uint32_t *>(&h);
+          tmem_st16(tmem + lane_base + s_col + c * 16, packed);
         }
-        tmem_st16(tmem + lane_base + s_col + c * 16, packed);
+        tmem_wait_st();
+        const float2 s01 = unpack2(fadd2(fadd2(part2[0], part2[1]), fadd2(part2[2], part2[3])));
+        l += s01.x + s01.y;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
       }
-      tmem_wait_st();
-      const float2 s01 = unpack2(fadd2(fadd2(part2[0], part2[1]), fadd2(part2[2], part2[3])));
-      l += s01.x + s01.y;
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
-    }
-    if (ok && n > 0 && warp_wait(&o_done[t], (n - 1) & 1, abort, p, kErrTimeoutSoftmax)) {
+      if (!ok || n == 0) break;
+      if (!warp_wait(&o_done[t], (g0 + n - 1) & 1, abort, p, kErrTimeoutSoftmax)) break;
       tc_fence_after();
       const float inv = 1.0f / l;
-      const int q = (blockIdx.x * QT + t) * BQ + row;
+      const int q = (qb * QT + t) * BQ + row;
       __half *out = p.o + ((int64_t)bh * p.s_q + q) * HEAD;
 #pragma unroll 1
       for (int c = 0; c < HEAD / 16; ++c) {
@@ -402,6 +438,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           reinterpret_cast<uint4 *>(out + c * 16)[1] = pack[1];
         }
       }
+      // O of this tile may now be overwritten by the next item's first PV
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_empty[t]);
     }
   }
 
@@ -546,7 +586,10 @@ extern "C" int lc_sdpa_f16(const void *q, const void *k, const void *v, void *o,
       return rc;
     configured[dev] = true;
   }
-  dim3 grid((unsigned)((s_q + QT * BQ - 1) / (QT * BQ)), (unsigned)bh);
+  // persistent: one CTA per SM (shared memory and TMEM admit one)
+  p.q_blocks = (int)((s_q + QT * BQ - 1) / (QT * BQ));
+  p.items = (int)(bh * p.q_blocks);
+  const int grid = p.items < sm_count() ? p.items : sm_count();
   sdpa_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(tq, tk, tv, p);
   return check_launch("lc_sdpa_f16");
 }
