@@ -208,14 +208,16 @@ def l2norm(x):
 # ---------------------------------------------------------------- tensor cores
 
 def gemm(a, b, b_layout: str = "kn", epilogue: str = "none", ab: str = "f16", out: str = "f32",
-         bias=None):
+         bias=None, transpose_out: bool = False):
     """float64 matmul of the quantised operands, optional bias and GELU, quantised output.
 
     Operands are quantised to ``ab`` (tests/test_tensor_cores.py:38-44; a no-op
     for f32); the product is float64 (expressions_open.py:66-73), rounded to
     f32 as the accumulator; a bias is added in f32 (the IR's
     ``add(acc, bias[col])``, examples/phase9/generated/phase9_bias_gelu_gemm);
-    the epilogue is the GELU formula of tests/test_gelu.py:51-66.
+    the epilogue is the GELU formula of tests/test_gelu.py:51-66 or max(., 0)
+    (the tensor fixtures' bias + ReLU, tests/test_tensor_cores.py:129-135);
+    ``transpose_out`` stores C transposed.
     """
     a = quantize(a, ab).astype(np.float64)
     b = quantize(b, ab).astype(np.float64)
@@ -226,12 +228,23 @@ def gemm(a, b, b_layout: str = "kn", epilogue: str = "none", ab: str = "f16", ou
         if bias is not None:
             c = (c + np.asarray(bias, np.float32)).astype(np.float32)
     if epilogue == "gelu_erf":
-        c = gelu(c, "none", "f32")
+        c = gelu(c, "none", "f32").reshape(c.shape)
     elif epilogue == "gelu_tanh":
-        c = gelu(c, "tanh", "f32")
+        c = gelu(c, "tanh", "f32").reshape(c.shape)
+    elif epilogue == "relu":
+        c = np.maximum(c, np.float32(0))
     elif epilogue != "none":
         raise ValueError(epilogue)
+    if transpose_out:
+        c = np.ascontiguousarray(np.swapaxes(c, -1, -2))
     return [quantize(c, out) if out != "f32" else c]
+
+
+def gemm_chain_f16(x, y, z, ab: str = "f16"):
+    """(q(q(x) @ q(y)) @ q(z)): the C -> A fragment repack of two tensor-core
+    products (tests/test_tensor_cores.py:169-171)."""
+    xy = quantize(x, ab).astype(np.float64) @ quantize(y, ab).astype(np.float64)
+    return [(quantize(xy, ab).astype(np.float64) @ quantize(z, ab).astype(np.float64)).astype(np.float32)]
 
 
 def sdpa(q, k, v, scale: float):
@@ -323,7 +336,9 @@ def evaluate(plan: dict, arrays: dict) -> dict:
     elif op == "gemm":
         bias = g("bias") if "bias" in bind else None
         out = gemm(g("a"), g("b"), p["b_layout"], p["epilogue"], plan["dtypes"]["ab"], plan["dtypes"]["c"],
-                   bias)
+                   bias, p.get("transpose_out", False))
+    elif op == "gemm_chain":
+        out = gemm_chain_f16(g("x"), g("y"), g("z"), plan["dtypes"]["ab"])
     elif op == "attention_f32":
         shape = lambda a, tail: np.asarray(a).reshape((p["bh"],) + tail)  # noqa: E731
         out = attention_f32(shape(g("q"), (p["s_q"], p["d"])), shape(g("kt"), (p["d"], p["s_kv"])),

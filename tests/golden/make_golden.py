@@ -40,6 +40,13 @@ PACKAGES = [
     "examples/phase9/gelu/activation_gelu_special", "examples/phase9/gelu/activation_gelu_tanh_special",
     # fragment attention tile (tests/test_fragment_rows.py)
     "examples/phase9/fragments/fragment_attention_tile_f16",
+    # tensor-core lowering fixtures (tests/test_tensor_cores.py)
+    *[f"examples/tensor/packages/{name}" for name in (
+        "tensor_atomic_f32", "tensor_cp_async_shared", "tensor_family_live_index",
+        "tensor_fused_guarded_epilogue", "tensor_global_bf16", "tensor_global_bf16_trans_ragged",
+        "tensor_global_f16", "tensor_global_f16_ragged", "tensor_repack_f16", "tensor_shared_b128",
+        "tensor_shared_b32", "tensor_shared_b64", "tensor_shared_bf16_trans", "tensor_shared_f16",
+        "tensor_shared_paired", "tensor_shared_paired_trans", "tensor_transposed_output")],
 ]
 
 

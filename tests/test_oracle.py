@@ -129,3 +129,43 @@ def test_compare_semantics():
     assert not O.compare(np.float32([np.nan]), np.float32([np.nan]), 1, 1)["pass"]
     assert O.compare(np.float32([5.0]), np.float32(5.0), 0, 0)["pass"]
     assert not O.compare(np.int32([3]), np.int32([4]), 0, 0)["pass"]
+
+
+TENSOR_FIXTURES = {
+    # name: (operand kind, B layout, epilogue, transposed output)
+    "tensor_atomic_f32": ("f16", "kn", "none", False),
+    "tensor_cp_async_shared": ("f16", "kn", "none", False),
+    "tensor_family_live_index": ("f16", "kn", "none", False),
+    "tensor_fused_guarded_epilogue": ("f16", "kn", "relu", False),
+    "tensor_global_bf16": ("bf16", "kn", "none", False),
+    "tensor_global_bf16_trans_ragged": ("bf16", "nk", "none", False),
+    "tensor_global_f16": ("f16", "kn", "none", False),
+    "tensor_global_f16_ragged": ("f16", "kn", "none", False),
+    "tensor_shared_b128": ("f16", "kn", "none", False),
+    "tensor_shared_b32": ("f16", "kn", "none", False),
+    "tensor_shared_b64": ("f16", "kn", "none", False),
+    "tensor_shared_bf16_trans": ("bf16", "nk", "none", False),
+    "tensor_shared_f16": ("f16", "kn", "none", False),
+    "tensor_shared_paired": ("f16", "kn", "none", False),
+    "tensor_shared_paired_trans": ("f16", "nk", "none", False),
+    "tensor_transposed_output": ("f16", "kn", "none", True),
+}
+
+
+@pytest.mark.parametrize("name", sorted(TENSOR_FIXTURES))
+def test_oracle_tensor_fixtures(name):
+    """The tensor-core lowering fixtures: quantised operands, float64 product
+    rounded to f32, optional bias + ReLU, optional transposed store — exact."""
+    kind, layout, epi, trans = TENSOR_FIXTURES[name]
+    a = inputs(name)
+    bias = a.get("bias")
+    out = O.gemm(a["a"], a["b"], layout, epi, kind, "f32", bias, trans)[0]
+    with np.load(golden(name) / "expected.npz") as z:
+        np.testing.assert_array_equal(out, z["out"])
+
+
+def test_oracle_tensor_repack_chain():
+    a = inputs("tensor_repack_f16")
+    out = O.gemm_chain_f16(a["x"], a["y"], a["z"])[0]
+    with np.load(golden("tensor_repack_f16") / "expected.npz") as z:
+        np.testing.assert_array_equal(out, z["out"])
