@@ -52,6 +52,14 @@ extern "C" {
 #define LC_EPI_NONE 0
 #define LC_EPI_GELU_ERF 1
 #define LC_EPI_GELU_TANH 2
+#define LC_EPI_RELU 3 /* max(x, 0); lc_gemm_mixed only (ptx_backend.py:1058) */
+
+/* RegStore variants (ptx_tensor.py:359-428) taken by lc_gemm_mixed:
+ * TRANSPOSE_C stores C[i, j] at c[j * M + i] (row_dim = 1, col_dim = 0);
+ * ACCUMULATE adds into c (the `atomic` store into an output the launcher
+ * zeroed first; f32 outputs only). */
+#define LC_GEMM_TRANSPOSE_C 1
+#define LC_GEMM_ACCUMULATE 2
 
 /* GEMM B layouts: "kn" = B[K,N] row-major (LdmatrixLoad b_trans=False),
  * "nk" = B[N,K] row-major (b_trans=True), ptx_tensor.py:281-363. */
@@ -207,6 +215,32 @@ int lc_gemm_ex(int ab_dtype, int c_dtype, int b_layout, int epilogue, const void
  * counterpart. */
 int lc_gemm_path(int ab_dtype, int b_layout, const void *a, const void *b, int64_t m, int64_t n,
                  int64_t k);
+
+/* C = epilogue(Q(A) Q(B) + bias) for operands stored as f32, f16 or bf16
+ * (a_type, b_type) and read by an f16 or bf16 tensor-core MMA (mma_type):
+ * Q rounds each element to mma_type (round to nearest even), products
+ * accumulate in f32.  Replaces the m16n8k16 fragment program of
+ * ptx_tensor.py:253-428: LdmatrixLoad gathers from f32/f16/bf16 buffers
+ * (ptx_tensor.py:315-357), MmaSyncPtx (359-374), RegStore with an epilogue
+ * lambda, a transposed layout or an atomic store (376-457).  A is [M, K]
+ * row-major, B as b_layout says, C [M, N] (or [N, M] with
+ * LC_GEMM_TRANSPOSE_C) of c_type; bias: n floats or NULL; epilogue: an
+ * LC_EPI_* code including LC_EPI_RELU; flags: LC_GEMM_TRANSPOSE_C |
+ * LC_GEMM_ACCUMULATE.  Problems of at least 2^24 multiply-adds with K % 8 ==
+ * 0, K >= 16 (and N % 8 == 0 for "kn") run the tcgen05 GEMM on operands
+ * rounded once into library scratch; the rest run one fused SIMT kernel. */
+int lc_gemm_mixed(int mma_type, int a_type, int b_type, int c_type, int b_layout, int epilogue,
+                  int flags, const void *a, const void *b, const void *bias, void *c, int64_t m,
+                  int64_t n, int64_t k, void *stream);
+
+/* C = Q(Q(X) Q(Y)) Q(Z): two chained products whose f32 intermediate is
+ * rounded to mma_type before the second, the FragmentRepack of C fragments
+ * into an A fragment (ptx_tensor.py:459-477).  X [M, K] row-major; Y [K, N1]
+ * or [N1, K] (y_layout); Z [N1, N2] or [N2, N1] (z_layout); C [M, N2] of
+ * c_type.  The intermediate lives in library scratch. */
+int lc_gemm_chain(int mma_type, int x_type, int y_type, int z_type, int c_type, int y_layout,
+                  int z_layout, const void *x, const void *y, const void *z, void *c, int64_t m,
+                  int64_t k, int64_t n1, int64_t n2, void *stream);
 
 /* Score forms of the FP32 attention IR: s = dot * c, dot * (1/c) with 1/c
  * rounded once (the IR's reciprocal-then-multiply), or dot / c. */

@@ -39,11 +39,17 @@ int reduce_workspace(cudaStream_t stream, ReduceWorkspace *out);
 // points.  gemm_path16/32 return 2 (tcgen05 on SM pairs), 1 (tcgen05 on one
 // SM) or 0 (SIMT); gemm_tc_launch runs the tcgen05 kernel on 16-bit operands.
 int gemm_path16(int b_layout, const void *a, const void *b, int64_t m, int64_t n, int64_t k);
+// gemm_path16 from the operands' 16-byte alignment instead of their addresses
+int gemm_path16_shape(int b_layout, bool a_aligned, bool b_aligned, int64_t m, int64_t n, int64_t k);
 int gemm_path32(int b_layout, const void *a, const void *b, int64_t m, int64_t n, int64_t k);
 int gemm_tc_launch(bool bf16, bool b_mn, int out, int epi, const void *a, const void *b,
                    const float *bias, void *c, int m, int n, int k, cudaStream_t s, bool pair);
 int gemm_f32(int out, int b_layout, int epi, const void *a, const void *b, const float *bias,
              void *c, int m, int n, int k, cudaStream_t s);
+// lc_gemm_mixed after argument checks (gemm_mixed.cu)
+int gemm_mixed(int mma_type, int a_type, int b_type, int c_type, int b_layout, int epilogue,
+               int flags, const void *a, const void *b, const float *bias, void *c, int m, int n,
+               int k, cudaStream_t s);
 
 // Library-owned scratch of at least `bytes`, one per (device, stream, slot),
 // grown (never shrunk) on demand with cudaMalloc.  Growing synchronises the

@@ -657,8 +657,12 @@ int dispatch_simt(int out, int epi, const void *a, const void *b, const float *b
 // Chooses the path of one 16-bit GEMM: 2 = tcgen05 on SM pairs, 1 = tcgen05 on
 // one SM, 0 = SIMT.
 int gemm_path16(int b_layout, const void *a, const void *b, int64_t m, int64_t n, int64_t k) {
-  const bool tma_ok = k % 8 == 0 && aligned(a, 16) && aligned(b, 16) &&
-                      (b_layout == LC_B_NK || n % 8 == 0) && k >= 16;
+  return gemm_path16_shape(b_layout, aligned(a, 16), aligned(b, 16), m, n, k);
+}
+
+int gemm_path16_shape(int b_layout, bool a_aligned, bool b_aligned, int64_t m, int64_t n, int64_t k) {
+  const bool tma_ok = k % 8 == 0 && a_aligned && b_aligned && (b_layout == LC_B_NK || n % 8 == 0) &&
+                      k >= 16;
   const bool big = m * n * k >= ((int64_t)1 << 24);
   if (!(tma_ok && big)) return 0;
   const int64_t pair_tiles = ((m + PTILE - 1) / PTILE) * ((n + PTILE - 1) / PTILE);

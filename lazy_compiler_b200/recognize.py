@@ -852,6 +852,9 @@ def recognise(pkg: KernelPackage) -> Plan:
     if "FragmentRowReduce" in kinds:
         return f32.recognise_fragment_attention(pkg, tile)
     if "MmaSyncPtx" in kinds:
+        from . import recognize_frag
+        if recognize_frag.is_single_warp(pkg, tile):
+            return recognize_frag.recognise_fragment_tile(pkg, tile)
         return _recognise_gemm(pkg, tile)
     if "CpAsyncCopy" in kinds:
         return f32.recognise_staged_gemm(pkg, tile)

@@ -20,7 +20,8 @@ LIBRARY_PATH = Path(__file__).resolve().parent / "liblazyb200.so"
 
 LC_F32, LC_F16, LC_BF16 = 0, 1, 2
 DTYPE_CODES = {"f32": LC_F32, "f16": LC_F16, "bf16": LC_BF16}
-EPILOGUES = {"none": 0, "gelu_erf": 1, "gelu_tanh": 2}
+EPILOGUES = {"none": 0, "gelu_erf": 1, "gelu_tanh": 2, "relu": 3}
+LC_GEMM_TRANSPOSE_C, LC_GEMM_ACCUMULATE = 1, 2
 B_LAYOUTS = {"kn": 0, "nk": 1}
 SCALE_MODES = {"mul": 0, "mul_recip": 1, "div": 2}
 STATUS = {0: "LC_OK", -1: "LC_ERR_INVALID", -2: "LC_ERR_ALIGN", -3: "LC_ERR_CUDA",
@@ -50,6 +51,8 @@ SIGNATURES = {
     "lc_gemm": [_INT, _INT, _INT, _INT, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_ex": [_INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_path": [_INT, _INT, _P, _P, _I64, _I64, _I64],
+    "lc_gemm_mixed": [_INT, _INT, _INT, _INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _P],
+    "lc_gemm_chain": [_INT, _INT, _INT, _INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P],
     "lc_attention_f32": [_INT, _INT, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
     "lc_attention_tile_f16q": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
     "lc_device_status": [_P],
@@ -150,6 +153,18 @@ def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
         bias = ptr("bias") if "bias" in b else ctypes.c_void_p(0)
         call("lc_gemm_ex", DTYPE_CODES[d["ab"]], DTYPE_CODES[d["c"]], B_LAYOUTS[p["b_layout"]],
              EPILOGUES[p["epilogue"]], ptr("a"), ptr("b"), bias, ptr("c"), p["m"], p["n"], p["k"], s)
+    elif op == "gemm_mixed":
+        d = plan["dtypes"]
+        bias = ptr("bias") if "bias" in b else ctypes.c_void_p(0)
+        flags = (LC_GEMM_TRANSPOSE_C if p["transpose"] else 0) | (LC_GEMM_ACCUMULATE if p["accumulate"] else 0)
+        call("lc_gemm_mixed", DTYPE_CODES[d["mma"]], DTYPE_CODES[d["a"]], DTYPE_CODES[d["b"]],
+             DTYPE_CODES[d["c"]], B_LAYOUTS[p["b_layout"]], EPILOGUES[p["epilogue"]], flags, ptr("a"),
+             ptr("b"), bias, ptr("c"), p["m"], p["n"], p["k"], s)
+    elif op == "gemm_chain":
+        d = plan["dtypes"]
+        call("lc_gemm_chain", DTYPE_CODES[d["mma"]], DTYPE_CODES[d["x"]], DTYPE_CODES[d["y"]],
+             DTYPE_CODES[d["z"]], DTYPE_CODES[d["c"]], B_LAYOUTS[p["y_layout"]], B_LAYOUTS[p["z_layout"]],
+             ptr("x"), ptr("y"), ptr("z"), ptr("c"), p["m"], p["k"], p["n1"], p["n2"], s)
     elif op == "attention_f32":
         call("lc_attention_f32", SCALE_MODES[p["scale_mode"]], EPILOGUES[p["epilogue"]],
              ptr("scale"), ptr("q"), ptr("kt"), ptr("v"), ptr("o"), p["bh"], p["s_q"], p["s_kv"],

@@ -240,9 +240,12 @@ def gemm(a, b, b_layout: str = "kn", epilogue: str = "none", ab: str = "f16", ou
     return [quantize(c, out) if out != "f32" else c]
 
 
-def gemm_chain_f16(x, y, z, ab: str = "f16"):
+def gemm_chain_f16(x, y, z, ab: str = "f16", y_layout: str = "kn", z_layout: str = "kn"):
     """(q(q(x) @ q(y)) @ q(z)): the C -> A fragment repack of two tensor-core
-    products (tests/test_tensor_cores.py:169-171)."""
+    products (tests/test_tensor_cores.py:169-171); "nk" operands are stored
+    transposed."""
+    y = np.swapaxes(y, -1, -2) if y_layout == "nk" else y
+    z = np.swapaxes(z, -1, -2) if z_layout == "nk" else z
     xy = quantize(x, ab).astype(np.float64) @ quantize(y, ab).astype(np.float64)
     return [(quantize(xy, ab).astype(np.float64) @ quantize(z, ab).astype(np.float64)).astype(np.float32)]
 
@@ -337,8 +340,14 @@ def evaluate(plan: dict, arrays: dict) -> dict:
         bias = g("bias") if "bias" in bind else None
         out = gemm(g("a"), g("b"), p["b_layout"], p["epilogue"], plan["dtypes"]["ab"], plan["dtypes"]["c"],
                    bias, p.get("transpose_out", False))
+    elif op == "gemm_mixed":
+        bias = g("bias") if "bias" in bind else None
+        out = gemm(g("a"), g("b"), p["b_layout"], p["epilogue"], plan["dtypes"]["mma"], plan["dtypes"]["c"],
+                   bias, p["transpose"])
     elif op == "gemm_chain":
-        out = gemm_chain_f16(g("x"), g("y"), g("z"), plan["dtypes"]["ab"])
+        out = gemm_chain_f16(g("x"), g("y"), g("z"), plan["dtypes"]["mma"], p["y_layout"], p["z_layout"])
+        if plan["dtypes"]["c"] != "f32":
+            out = [quantize(out[0], plan["dtypes"]["c"])]
     elif op == "attention_f32":
         shape = lambda a, tail: np.asarray(a).reshape((p["bh"],) + tail)  # noqa: E731
         out = attention_f32(shape(g("q"), (p["s_q"], p["d"])), shape(g("kt"), (p["d"], p["s_kv"])),

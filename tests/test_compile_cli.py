@@ -43,6 +43,29 @@ EXPECTED = {
     "phase9_gelu_row_dot": ("rowdot_f32", {"rows": 19, "cols": 131, "activation": "gelu_erf"}),
     "fragment_attention_tile_f16": ("attention_tile_f16q", {"bh": 1, "s_q": 16, "s_kv": 16, "d": 16,
                                                             "dv": 8}),
+    # one-warp m16n8k16 fragment programs (tests/test_tensor_cores.py fixtures)
+    **{name: ("gemm_mixed", {"m": m, "n": n, "k": k, "b_layout": lay, "epilogue": epi, "transpose": tr,
+                             "accumulate": acc})
+       for name, (m, n, k, lay, epi, tr, acc) in {
+           "tensor_atomic_f32": (16, 8, 16, "kn", "none", False, True),
+           "tensor_cp_async_shared": (16, 8, 16, "kn", "none", False, False),
+           "tensor_family_live_index": (32, 8, 16, "kn", "none", False, False),
+           "tensor_fused_guarded_epilogue": (11, 7, 19, "kn", "relu", False, False),
+           "tensor_global_bf16": (16, 8, 16, "kn", "none", False, False),
+           "tensor_global_bf16_trans_ragged": (9, 7, 17, "nk", "none", False, False),
+           "tensor_global_f16": (16, 8, 16, "kn", "none", False, False),
+           "tensor_global_f16_ragged": (11, 7, 19, "kn", "none", False, False),
+           "tensor_shared_b128": (16, 8, 16, "kn", "none", False, False),
+           "tensor_shared_b32": (16, 8, 16, "kn", "none", False, False),
+           "tensor_shared_b64": (16, 8, 16, "kn", "none", False, False),
+           "tensor_shared_bf16_trans": (16, 8, 16, "nk", "none", False, False),
+           "tensor_shared_f16": (16, 8, 16, "kn", "none", False, False),
+           "tensor_shared_paired": (16, 16, 16, "kn", "none", False, False),
+           "tensor_shared_paired_trans": (16, 16, 16, "nk", "none", False, False),
+           "tensor_transposed_output": (16, 8, 16, "kn", "none", True, False),
+       }.items()},
+    "tensor_repack_f16": ("gemm_chain", {"m": 16, "k": 16, "n1": 16, "n2": 8, "y_layout": "kn",
+                                         "z_layout": "kn"}),
 }
 
 

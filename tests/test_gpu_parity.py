@@ -27,7 +27,13 @@ PACKAGES = ["p00_scalar_add", "p01_vector_add", "p02_scale_shift", "p03_relu_mul
             # FP32 GEMM and attention (staged, split-K, serial and block-cooperative schedules)
             "m01_matmul_512", "m02_matmul_rect", "phase9_bias_gelu_gemm", "a01_attention",
             "a02_attention_128", "phase9_gelu_attention", "phase9_gelu_row_dot",
-            "fragment_attention_tile_f16"]
+            "fragment_attention_tile_f16",
+            # one-warp tensor-fragment programs: quantised operands, staging, swizzles, store variants
+            "tensor_atomic_f32", "tensor_cp_async_shared", "tensor_family_live_index",
+            "tensor_fused_guarded_epilogue", "tensor_global_bf16", "tensor_global_bf16_trans_ragged",
+            "tensor_global_f16", "tensor_global_f16_ragged", "tensor_repack_f16", "tensor_shared_b128",
+            "tensor_shared_b32", "tensor_shared_b64", "tensor_shared_bf16_trans", "tensor_shared_f16",
+            "tensor_shared_paired", "tensor_shared_paired_trans", "tensor_transposed_output"]
 
 
 def torch_():
