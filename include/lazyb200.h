@@ -282,6 +282,126 @@ int lc_sdpa_path(const void *q, const void *k, const void *v, const void *o, int
  * and the cost of switching forms.  No reference counterpart. */
 int lc_probe_mma(int variant, int groups, void *stream);
 
+
+/* ---------------------------------------------------------------- pointwise programs
+ * A straight-line scalar Tile body (Load / Let / Assign / Select / Write with
+ * indices affine in the Tile axes) compiled to register operations, run once
+ * per tile point.  Each operation is the PTX instruction the reference's
+ * scalar lowering emits for that step (ptx_backend.py:406-1177): f32 add,
+ * sub, mul, div and sqrt with explicit round-to-nearest, fma.rn, max/min with
+ * PTX NaN rules, ex2/lg2/sin/cos.approx, copysign, cvt.rn to f16/bf16,
+ * cvt.rzi to s32, 32-bit integer arithmetic, ordered comparisons and an
+ * unordered float `!=`.  f16 and bf16 values are held widened in f32
+ * registers, predicates as 0/1 words.
+ *
+ * code[i] = { op | dst << 8 | a << 16 | b << 24, c | aux << 8 }: dst and
+ * sources a, b, c are registers (< n_regs); aux is a constant index for
+ * CONST and a form index for loads and stores.  A form addresses element
+ * base + sum_d coef[d] * x[d] of buffer slot `buffer`, x the point's
+ * coordinates over `extents` (row-major, last axis fastest); sizes[slot] is
+ * the slot's element count and every form must stay inside it over the
+ * whole tile (checked before launch). */
+#define LC_PW_MAX_CODE 384
+#define LC_PW_MAX_CONST 128
+#define LC_PW_MAX_FORMS 32
+#define LC_PW_MAX_BUFFERS 16
+#define LC_PW_MAX_AXES 4
+#define LC_PW_MAX_REGS 48
+
+enum lc_pw_op {
+  LC_PW_MOV = 0,
+  LC_PW_CONST = 1,
+  LC_PW_LD_F32 = 2,
+  LC_PW_LD_F16 = 3,
+  LC_PW_LD_BF16 = 4,
+  LC_PW_LD_S32 = 5,
+  LC_PW_ST_F32 = 6,
+  LC_PW_ST_F16 = 7,
+  LC_PW_ST_BF16 = 8,
+  LC_PW_ST_S32 = 9,
+  LC_PW_FADD = 10,
+  LC_PW_FSUB = 11,
+  LC_PW_FMUL = 12,
+  LC_PW_FDIV = 13,
+  LC_PW_FFMA = 14,
+  LC_PW_FNEG = 15,
+  LC_PW_FABS = 16,
+  LC_PW_FMAX = 17,
+  LC_PW_FMIN = 18,
+  LC_PW_FSQRT = 19,
+  LC_PW_FFLOOR = 20,
+  LC_PW_FCEIL = 21,
+  LC_PW_FTRUNC = 22,
+  LC_PW_FRINT = 23,
+  LC_PW_FEX2 = 24,
+  LC_PW_FLG2 = 25,
+  LC_PW_FSIN = 26,
+  LC_PW_FCOS = 27,
+  LC_PW_FCOPYSIGN = 28,
+  LC_PW_RND_F16 = 29,
+  LC_PW_RND_BF16 = 30,
+  LC_PW_F2I = 31,
+  LC_PW_I2F = 32,
+  LC_PW_I2H = 33,
+  LC_PW_I2BF = 34,
+  LC_PW_IADD = 35,
+  LC_PW_ISUB = 36,
+  LC_PW_IMUL = 37,
+  LC_PW_IDIV = 38,
+  LC_PW_IREM = 39,
+  LC_PW_ISHL = 40,
+  LC_PW_ISHR = 41,
+  LC_PW_IAND = 42,
+  LC_PW_IOR = 43,
+  LC_PW_IXOR = 44,
+  LC_PW_INOT = 45,
+  LC_PW_INEG = 46,
+  LC_PW_IABS = 47,
+  LC_PW_IMAX = 48,
+  LC_PW_IMIN = 49,
+  LC_PW_IPOPC = 50,
+  LC_PW_FEQ = 51,
+  LC_PW_FNE = 52,
+  LC_PW_FLT = 53,
+  LC_PW_FLE = 54,
+  LC_PW_FGT = 55,
+  LC_PW_FGE = 56,
+  LC_PW_IEQ = 57,
+  LC_PW_INE = 58,
+  LC_PW_ILT = 59,
+  LC_PW_ILE = 60,
+  LC_PW_IGT = 61,
+  LC_PW_IGE = 62,
+  LC_PW_PAND = 63,
+  LC_PW_POR = 64,
+  LC_PW_SEL = 65,
+  LC_PW_NUM_OPS
+};
+
+typedef struct {
+  int64_t base;
+  int64_t coef[LC_PW_MAX_AXES];
+  int32_t buffer;
+  int32_t dtype; /* LC_F32, LC_F16, LC_BF16 or LC_S32 */
+} lc_pw_form;
+
+#define LC_S32 3 /* storage code of int32 buffers in pointwise programs */
+
+typedef struct {
+  int32_t n_code, n_consts, n_forms, n_buffers, n_axes, n_regs;
+  int64_t extents[LC_PW_MAX_AXES];
+  int64_t sizes[LC_PW_MAX_BUFFERS];
+  uint32_t code[LC_PW_MAX_CODE][2];
+  uint32_t consts[LC_PW_MAX_CONST];
+  lc_pw_form forms[LC_PW_MAX_FORMS];
+} lc_pw_program;
+
+/* Runs `program` over every point of its tile with buffers[slot] the device
+ * pointer of each buffer slot.  Validates the program (opcodes, register,
+ * constant and form indices, each form's range against sizes[]) before the
+ * launch: LC_ERR_INVALID on any violation, nothing launched. */
+int lc_pointwise(const lc_pw_program *program, void *const *buffers, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,225 @@
+// Pointwise programs: one register program (lc_pw_program, built by the
+// plan compiler from a straight-line Tile body) run per tile point.
+//
+// Each thread walks tile points in a grid-stride loop, decodes the point's
+// coordinates and runs the program; every operation is one PTX instruction
+// of the reference's scalar lowering (ptx_backend.py:406-1177), so the
+// program computes what the reference's kernel computes, step for step.
+// The program itself lives in the kernel's parameter space (a
+// __grid_constant__ struct): every lane of a warp reads the same operation
+// at the same time, a broadcast from the constant bank.
+#include "common.cuh"
+
+namespace lc {
+namespace {
+
+struct PointwiseArgs {
+  lc_pw_program prog;
+  void *buffers[LC_PW_MAX_BUFFERS];
+  int64_t points;
+};
+
+__device__ __forceinline__ float f(uint32_t w) { return __uint_as_float(w); }
+__device__ __forceinline__ uint32_t w(float x) { return __float_as_uint(x); }
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float lg2_approx(float x) {
+  float y;
+  asm("lg2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float sin_approx(float x) {
+  float y;
+  asm("sin.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float cos_approx(float x) {
+  float y;
+  asm("cos.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float round_half(float x) { return __half2float(__float2half_rn(x)); }
+__device__ __forceinline__ float round_bf16(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+__global__ void __launch_bounds__(256) pointwise_kernel(const __grid_constant__ PointwiseArgs p) {
+  uint32_t r[LC_PW_MAX_REGS];
+  for (int i = 0; i < LC_PW_MAX_REGS; ++i) r[i] = 0u;
+  const lc_pw_program &g = p.prog;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gid < p.points; gid += stride) {
+    int64_t x[LC_PW_MAX_AXES] = {0, 0, 0, 0};
+    int64_t rest = gid;
+    for (int d = g.n_axes - 1; d >= 0; --d) {
+      x[d] = rest % g.extents[d];
+      rest /= g.extents[d];
+    }
+    for (int pc = 0; pc < g.n_code; ++pc) {
+      const uint32_t w0 = g.code[pc][0], w1 = g.code[pc][1];
+      const int op = w0 & 255, dst = (w0 >> 8) & 255;
+      const uint32_t A = r[(w0 >> 16) & 255], B = r[w0 >> 24], C = r[w1 & 255];
+      const int aux = (int)(w1 >> 8);
+      const int32_t ia = (int32_t)A, ib = (int32_t)B;
+      uint32_t out = 0;
+      if (op >= LC_PW_LD_F32 && op <= LC_PW_ST_S32) {
+        const lc_pw_form &fm = g.forms[aux];
+        int64_t at = fm.base;
+        for (int d = 0; d < g.n_axes; ++d) at += fm.coef[d] * x[d];
+        void *base = p.buffers[fm.buffer];
+        switch (op) {
+          case LC_PW_LD_F32: out = static_cast<const uint32_t *>(base)[at]; break;
+          case LC_PW_LD_F16: out = w(__half2float(static_cast<const __half *>(base)[at])); break;
+          case LC_PW_LD_BF16: out = w(__bfloat162float(static_cast<const __nv_bfloat16 *>(base)[at])); break;
+          case LC_PW_LD_S32: out = static_cast<const uint32_t *>(base)[at]; break;
+          case LC_PW_ST_F32: static_cast<uint32_t *>(base)[at] = A; continue;
+          case LC_PW_ST_F16: static_cast<__half *>(base)[at] = __float2half_rn(f(A)); continue;
+          case LC_PW_ST_BF16: static_cast<__nv_bfloat16 *>(base)[at] = __float2bfloat16_rn(f(A)); continue;
+          default: static_cast<uint32_t *>(base)[at] = A; continue;  // LC_PW_ST_S32
+        }
+        r[dst] = out;
+        continue;
+      }
+      switch (op) {
+        case LC_PW_MOV: out = A; break;
+        case LC_PW_CONST: out = g.consts[aux]; break;
+        case LC_PW_FADD: out = w(__fadd_rn(f(A), f(B))); break;
+        case LC_PW_FSUB: out = w(__fsub_rn(f(A), f(B))); break;
+        case LC_PW_FMUL: out = w(__fmul_rn(f(A), f(B))); break;
+        case LC_PW_FDIV: out = w(__fdiv_rn(f(A), f(B))); break;
+        case LC_PW_FFMA: out = w(__fmaf_rn(f(A), f(B), f(C))); break;
+        case LC_PW_FNEG: out = A ^ 0x80000000u; break;
+        case LC_PW_FABS: out = A & 0x7fffffffu; break;
+        case LC_PW_FMAX: out = w(fmaxf(f(A), f(B))); break;
+        case LC_PW_FMIN: out = w(fminf(f(A), f(B))); break;
+        case LC_PW_FSQRT: out = w(__fsqrt_rn(f(A))); break;
+        case LC_PW_FFLOOR: out = w(floorf(f(A))); break;
+        case LC_PW_FCEIL: out = w(ceilf(f(A))); break;
+        case LC_PW_FTRUNC: out = w(truncf(f(A))); break;
+        case LC_PW_FRINT: out = w(rintf(f(A))); break;
+        case LC_PW_FEX2: out = w(ex2_approx(f(A))); break;
+        case LC_PW_FLG2: out = w(lg2_approx(f(A))); break;
+        case LC_PW_FSIN: out = w(sin_approx(f(A))); break;
+        case LC_PW_FCOS: out = w(cos_approx(f(A))); break;
+        case LC_PW_FCOPYSIGN: out = (B & 0x7fffffffu) | (A & 0x80000000u); break;  // |b| with a's sign
+        case LC_PW_RND_F16: out = w(round_half(f(A))); break;
+        case LC_PW_RND_BF16: out = w(round_bf16(f(A))); break;
+        case LC_PW_F2I: out = (uint32_t)__float2int_rz(f(A)); break;
+        case LC_PW_I2F: out = w(__int2float_rn(ia)); break;
+        case LC_PW_I2H: out = w(__half2float(__int2half_rn(ia))); break;
+        case LC_PW_I2BF: out = w(__bfloat162float(__int2bfloat16_rn(ia))); break;
+        case LC_PW_IADD: out = A + B; break;
+        case LC_PW_ISUB: out = A - B; break;
+        case LC_PW_IMUL: out = A * B; break;
+        case LC_PW_IDIV:  // integer division by zero has no defined result; it yields 0 here
+          out = ib == 0 ? 0u : (ib == -1 ? 0u - A : (uint32_t)(ia / ib));
+          break;
+        case LC_PW_IREM: out = (ib == 0 || ib == -1) ? (ib == 0 ? A : 0u) : (uint32_t)(ia % ib); break;
+        case LC_PW_ISHL: out = B >= 32u ? 0u : A << B; break;  // shl.b32 clamps the count
+        case LC_PW_ISHR: out = (uint32_t)(ia >> (B >= 32u ? 31u : B)); break;
+        case LC_PW_IAND: out = A & B; break;
+        case LC_PW_IOR: out = A | B; break;
+        case LC_PW_IXOR: out = A ^ B; break;
+        case LC_PW_INOT: out = ~A; break;
+        case LC_PW_INEG: out = 0u - A; break;
+        case LC_PW_IABS: out = ia < 0 ? 0u - A : A; break;
+        case LC_PW_IMAX: out = (uint32_t)max(ia, ib); break;
+        case LC_PW_IMIN: out = (uint32_t)min(ia, ib); break;
+        case LC_PW_IPOPC: out = (uint32_t)__popc(A); break;
+        case LC_PW_FEQ: out = f(A) == f(B); break;
+        case LC_PW_FNE: out = !(f(A) == f(B)); break;  // unordered: true when either is NaN
+        case LC_PW_FLT: out = f(A) < f(B); break;
+        case LC_PW_FLE: out = f(A) <= f(B); break;
+        case LC_PW_FGT: out = f(A) > f(B); break;
+        case LC_PW_FGE: out = f(A) >= f(B); break;
+        case LC_PW_IEQ: out = ia == ib; break;
+        case LC_PW_INE: out = ia != ib; break;
+        case LC_PW_ILT: out = ia < ib; break;
+        case LC_PW_ILE: out = ia <= ib; break;
+        case LC_PW_IGT: out = ia > ib; break;
+        case LC_PW_IGE: out = ia >= ib; break;
+        case LC_PW_PAND: out = (A != 0u) & (B != 0u); break;
+        case LC_PW_POR: out = (A != 0u) | (B != 0u); break;
+        case LC_PW_SEL: out = A != 0u ? B : C; break;
+        default: out = 0u; break;  // the host admits no other opcode
+      }
+      r[dst] = out;
+    }
+  }
+}
+
+bool form_in_range(const lc_pw_program &g, const lc_pw_form &fm) {
+  int64_t lo = fm.base, hi = fm.base;
+  for (int d = 0; d < g.n_axes; ++d) {
+    const int64_t span = fm.coef[d] * (g.extents[d] - 1);
+    if (span < 0) lo += span;
+    else hi += span;
+  }
+  return lo >= 0 && hi < g.sizes[fm.buffer];
+}
+
+int storage_of(int op) {
+  switch (op) {
+    case LC_PW_LD_F32: case LC_PW_ST_F32: return LC_F32;
+    case LC_PW_LD_F16: case LC_PW_ST_F16: return LC_F16;
+    case LC_PW_LD_BF16: case LC_PW_ST_BF16: return LC_BF16;
+    default: return LC_S32;
+  }
+}
+
+}  // namespace
+}  // namespace lc
+
+extern "C" int lc_pointwise(const lc_pw_program *program, void *const *buffers, void *stream) {
+  using namespace lc;
+  if (!program || !buffers) return fail(LC_ERR_INVALID, "lc_pointwise: null program or buffers");
+  const lc_pw_program &g = *program;
+  if (g.n_code < 0 || g.n_code > LC_PW_MAX_CODE || g.n_consts < 0 || g.n_consts > LC_PW_MAX_CONST ||
+      g.n_forms < 0 || g.n_forms > LC_PW_MAX_FORMS || g.n_buffers < 1 || g.n_buffers > LC_PW_MAX_BUFFERS ||
+      g.n_axes < 1 || g.n_axes > LC_PW_MAX_AXES || g.n_regs < 1 || g.n_regs > LC_PW_MAX_REGS)
+    return fail(LC_ERR_INVALID, "lc_pointwise: program counts out of range");
+  int64_t points = 1;
+  for (int d = 0; d < g.n_axes; ++d) {
+    if (g.extents[d] < 1 || g.extents[d] > ((int64_t)1 << 40))
+      return fail(LC_ERR_INVALID, "lc_pointwise: bad extent");
+    points *= g.extents[d];
+    if (points > ((int64_t)1 << 40)) return fail(LC_ERR_INVALID, "lc_pointwise: tile too large");
+  }
+  for (int i = 0; i < g.n_buffers; ++i)
+    if (!buffers[i] || g.sizes[i] < 1) return fail(LC_ERR_INVALID, "lc_pointwise: buffer slot %d", i);
+  for (int i = 0; i < g.n_forms; ++i) {
+    const lc_pw_form &fm = g.forms[i];
+    bool sane = fm.base >= -((int64_t)1 << 50) && fm.base <= ((int64_t)1 << 50);
+    for (int d = 0; d < g.n_axes; ++d)
+      sane = sane && fm.coef[d] >= -((int64_t)1 << 40) && fm.coef[d] <= ((int64_t)1 << 40);
+    if (!sane || fm.buffer < 0 || fm.buffer >= g.n_buffers || !form_in_range(g, fm))
+      return fail(LC_ERR_INVALID, "lc_pointwise: form %d leaves its buffer", i);
+  }
+  for (int pc = 0; pc < g.n_code; ++pc) {
+    const uint32_t w0 = g.code[pc][0], w1 = g.code[pc][1];
+    const int op = w0 & 255;
+    const uint32_t dst = (w0 >> 8) & 255, a = (w0 >> 16) & 255, b = w0 >> 24, c = w1 & 255;
+    const int aux = (int)(w1 >> 8);
+    if (op >= LC_PW_NUM_OPS) return fail(LC_ERR_INVALID, "lc_pointwise: bad opcode at %d", pc);
+    if ((int)dst >= g.n_regs || (int)a >= g.n_regs || (int)b >= g.n_regs || (int)c >= g.n_regs)
+      return fail(LC_ERR_INVALID, "lc_pointwise: register out of range at %d", pc);
+    if (op == LC_PW_CONST && aux >= g.n_consts)
+      return fail(LC_ERR_INVALID, "lc_pointwise: constant out of range at %d", pc);
+    if (op >= LC_PW_LD_F32 && op <= LC_PW_ST_S32 &&
+        (aux >= g.n_forms || g.forms[aux].dtype != storage_of(op)))
+      return fail(LC_ERR_INVALID, "lc_pointwise: form or storage type mismatch at %d", pc);
+  }
+  PointwiseArgs args;
+  args.prog = g;
+  for (int i = 0; i < LC_PW_MAX_BUFFERS; ++i) args.buffers[i] = i < g.n_buffers ? buffers[i] : nullptr;
+  args.points = points;
+  int64_t blocks = (points + 255) / 256;
+  const int64_t cap = (int64_t)sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  pointwise_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(args);
+  return check_launch("lc_pointwise");
+}

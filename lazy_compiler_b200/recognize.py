@@ -862,7 +862,13 @@ def recognise(pkg: KernelPackage) -> Plan:
     ev.smem = set()
     for axis in tile.axes:
         ev.axes[axis.name] = static_extent(axis.extent)
-    ev.run(tile.body)
+    straight = not any(s.kind in ("StridedLoop", "Loop", "Cond") for s in _walk(tile.body))
+    try:
+        ev.run(tile.body)
+    except CompileError as err:
+        if straight:
+            return _pointwise_program(pkg, tile, err)
+        raise
     if ev.loops and ev.reductions:
         if f32.looks_like_attention(ev):
             return f32.recognise_attention(pkg, tile, ev)
@@ -871,4 +877,18 @@ def recognise(pkg: KernelPackage) -> Plan:
         return _recognise_reduction(pkg, tile, ev)
     if ev.loops:
         raise CompileError("loops without a reduction are not a supported operation class")
-    return _recognise_pointwise(pkg, tile, ev)
+    try:
+        return _recognise_pointwise(pkg, tile, ev)
+    except CompileError as err:
+        if straight:
+            return _pointwise_program(pkg, tile, err)
+        raise
+
+
+def _pointwise_program(pkg: KernelPackage, tile: Node, reason: CompileError) -> Plan:
+    """A straight-line body outside the fixed pointwise classes: compile it to a register program."""
+    from .pointwise import compile_pointwise
+    try:
+        return compile_pointwise(pkg, tile)
+    except CompileError as err:
+        raise CompileError(f"{err} (and not a fixed pointwise class: {reason})") from err

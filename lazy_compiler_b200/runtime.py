@@ -51,6 +51,7 @@ SIGNATURES = {
     "lc_gemm": [_INT, _INT, _INT, _INT, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_ex": [_INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_path": [_INT, _INT, _P, _P, _I64, _I64, _I64],
+    "lc_pointwise": [_P, _P, _P],
     "lc_gemm_mixed": [_INT, _INT, _INT, _INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_chain": [_INT, _INT, _INT, _INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P],
     "lc_attention_f32": [_INT, _INT, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
@@ -61,6 +62,46 @@ SIGNATURES = {
     "lc_sdpa_f16": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, ctypes.c_float, _P],
     "lc_sdpa_path": [_P, _P, _P, _P, _I64, _I64, _I64],
 }
+
+# pointwise programs (include/lazyb200.h lc_pw_program)
+LC_S32 = 3
+STORAGE_CODES = {"f32": LC_F32, "f16": LC_F16, "bf16": LC_BF16, "s32": LC_S32}
+PW_MAX_CODE, PW_MAX_CONST, PW_MAX_FORMS, PW_MAX_BUFFERS, PW_MAX_AXES = 384, 128, 32, 16, 4
+
+
+class PwForm(ctypes.Structure):
+    _fields_ = [("base", ctypes.c_int64), ("coef", ctypes.c_int64 * PW_MAX_AXES),
+                ("buffer", ctypes.c_int32), ("dtype", ctypes.c_int32)]
+
+
+class PwProgram(ctypes.Structure):
+    _fields_ = [("n_code", ctypes.c_int32), ("n_consts", ctypes.c_int32), ("n_forms", ctypes.c_int32),
+                ("n_buffers", ctypes.c_int32), ("n_axes", ctypes.c_int32), ("n_regs", ctypes.c_int32),
+                ("extents", ctypes.c_int64 * PW_MAX_AXES), ("sizes", ctypes.c_int64 * PW_MAX_BUFFERS),
+                ("code", (ctypes.c_uint32 * 2) * PW_MAX_CODE), ("consts", ctypes.c_uint32 * PW_MAX_CONST),
+                ("forms", PwForm * PW_MAX_FORMS)]
+
+
+def pw_program(prog: dict) -> PwProgram:
+    """The C struct of a compiled pointwise program (a plan's ``params["program"]``)."""
+    g = PwProgram()
+    g.n_code, g.n_consts, g.n_forms = len(prog["code"]), len(prog["consts"]), len(prog["forms"])
+    g.n_buffers, g.n_axes, g.n_regs = len(prog["buffers"]), len(prog["extents"]), max(1, prog["n_regs"])
+    for d, e in enumerate(prog["extents"]):
+        g.extents[d] = e
+    for i, size in enumerate(prog["sizes"]):
+        g.sizes[i] = size
+    for i, (op, dst, a, b, c, aux) in enumerate(prog["code"]):
+        g.code[i][0] = op | dst << 8 | a << 16 | b << 24
+        g.code[i][1] = c | aux << 8
+    for i, word in enumerate(prog["consts"]):
+        g.consts[i] = word
+    for i, f in enumerate(prog["forms"]):
+        g.forms[i].base, g.forms[i].buffer, g.forms[i].dtype = f["base"], f["buffer"], STORAGE_CODES[f["dtype"]]
+        for d, c in enumerate(f["coef"]):
+            g.forms[i].coef[d] = c
+    return g
+
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
@@ -153,6 +194,11 @@ def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
         bias = ptr("bias") if "bias" in b else ctypes.c_void_p(0)
         call("lc_gemm_ex", DTYPE_CODES[d["ab"]], DTYPE_CODES[d["c"]], B_LAYOUTS[p["b_layout"]],
              EPILOGUES[p["epilogue"]], ptr("a"), ptr("b"), bias, ptr("c"), p["m"], p["n"], p["k"], s)
+    elif op == "pointwise":
+        prog = p["program"]
+        ptrs = (ctypes.c_void_p * PW_MAX_BUFFERS)(*[int(pointers[b[f"buf{i}"]]) for i in range(len(prog["buffers"]))])
+        g = pw_program(prog)
+        call("lc_pointwise", ctypes.c_void_p(ctypes.addressof(g)), ptrs, s)
     elif op == "gemm_mixed":
         d = plan["dtypes"]
         bias = ptr("bias") if "bias" in b else ctypes.c_void_p(0)

@@ -301,9 +301,18 @@ def attention_f32(q, kt, v, scale: float, mode: str = "div", epilogue: str = "no
 
 # ---------------------------------------------------------------- plans
 
-def evaluate(plan: dict, arrays: dict) -> dict:
-    """Reference outputs of one launch plan from named input arrays."""
+def evaluate(plan: dict, arrays: dict, ir=None) -> dict:
+    """Reference outputs of one launch plan from named input arrays.
+
+    Pointwise-program plans are checked against their IR (``ir``: the
+    package's kernel.ir.json), which oracle/pointwise_ir.py evaluates.
+    """
     op = plan["op"]
+    if op == "pointwise":
+        if ir is None:
+            raise ValueError("pointwise plans are evaluated from their IR: pass ir=")
+        from oracle.pointwise_ir import evaluate as evaluate_ir
+        return evaluate_ir(ir, arrays)
     bind = plan["bind"]
     p = plan["params"]
     g = lambda role: arrays[bind[role]]  # noqa: E731

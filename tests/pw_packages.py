@@ -1,0 +1,178 @@
+"""Builders of small pointwise IR packages (kernel.ir.json + meta.json) —
+test infrastructure for the pointwise-program compiler.
+
+Statements are written as IR ``repr`` text, the form the reference's
+packages carry, with helpers for the common node spellings.
+"""
+import json
+from pathlib import Path
+
+_NP = {"f32": ("float32", 4), "f16": ("float16", 2), "bf16": ("uint16", 2), "i32": ("int32", 4)}
+
+
+def dt(name):
+    np_name, size = _NP[name]
+    return f"DataType(name='{name}', np=dtype('{np_name}'), nbytes={size})"
+
+
+def var(name):
+    return f"Var(name='{name}')"
+
+
+def lit(value, kind="int"):
+    if kind == "int":
+        return f"Literal(value={value}, dtype='int')"
+    return f"Literal(value={value!r}, dtype={dt(kind)})"
+
+
+def bin_(op, a, b):
+    return f"BinaryExpr(op='{op}', left={a}, right={b})"
+
+
+def load(name, buf, index, kind):
+    return f"Load(names=('{name}',), input='{buf}', index=({', '.join(index)},), dtype={dt(kind)})"
+
+
+def assign(name, op, args, kind=None):
+    d = dt(kind) if kind else "None"
+    return f"Assign(name='{name}', op=ElementwiseImpl('{op}'), args=({', '.join(repr(a) for a in args)},), dtype={d})"
+
+
+def let(name, value, kind=None):
+    d = dt(kind) if kind else "None"
+    return f"Let(name='{name}', value={value}, dtype={d})"
+
+
+def write(out, index, values, kind):
+    return (f"Write(output='{out}', index=({', '.join(index)},), values=({', '.join(repr(v) for v in values)},), "
+            f"value_dtype={dt(kind)}, atomic=False, swizzle='NONE')")
+
+
+def package(folder: Path, name: str, inputs: dict, output: tuple, axes: list, body: list, rtol=1e-5,
+            atol=1e-6, data: dict | None = None) -> Path:
+    """Write a one-kernel package; inputs {name: (shape, dtype)}, output (name, shape, dtype)."""
+    folder.mkdir(parents=True, exist_ok=True)
+    out_name, out_shape, out_dtype = output
+    axes_repr = ", ".join(f"Axis(name='{a}', extent=Dim({e}), window=None)" for a, e in axes)
+    tile = (f"Tile(axes=({axes_repr},), body=({', '.join(body)},), block_threads=None, aux_threads=0, "
+            f"raster_axes=None, raster_group=None, raster_orient='m')")
+    entry = f"k_{name}"
+    nodes = {n: {"op": "InputOp", "op_fields": {}, "inputs": [],
+                 "outputs": [{"name": n, "shape": list(s), "dtype": d}]} for n, (s, d) in inputs.items()}
+    nodes[out_name] = {"op": "KernelOp", "op_fields": {"body": [tile], "name": entry, "zero_delegated": [],
+                                                       "serial": []},
+                       "inputs": list(inputs), "outputs": [{"name": out_name, "shape": list(out_shape),
+                                                            "dtype": out_dtype}]}
+    graph = {"inputs": list(inputs), "outputs": [out_name], "nodes": nodes}
+    ir = folder / f"{entry}.ir.json"
+    ir.write_text(json.dumps(graph))
+    args = []
+    for i, (n, (s, d)) in enumerate(inputs.items()):
+        a = {"name": n, "dtype": d, "shape": list(s), "seed": i}
+        if data and n in data:
+            a["data"] = list(data[n])
+        args.append(a)
+    args.append({"name": out_name, "dtype": out_dtype, "shape": list(out_shape), "output": True})
+    meta = {"id": name, "rtol": rtol, "atol": atol, "graph_inputs": list(inputs), "graph_outputs": [out_name],
+            "kernels": [{"node": out_name, "entry": entry, "arg_order": list(inputs) + [out_name],
+                         "grid": [1, 1, 1], "block": [256, 1, 1], "smem_bytes": 0, "zero_outputs": [],
+                         "args": args, "final": True}]}
+    (folder / "meta.json").write_text(json.dumps(meta))
+    return ir
+
+
+# ---------------------------------------------------------------- synthetic programs
+# name -> (builder(folder) -> ir path, tolerance): op mixes beyond the fixed classes
+
+def _bias_rows(folder):
+    i, j = var("i"), var("j")
+    return package(folder, "bias_rows", {"x": ((64, 48), "f32"), "w": ((48,), "f32"), "b": ((48,), "f32")},
+                   ("out", (64, 48), "f32"), [("i", 64), ("j", 48)],
+                   [load("xv", "x", [i, j], "f32"), load("wv", "w", [j], "f32"), load("bv", "b", [j], "f32"),
+                    assign("p", "multiply", ["xv", "wv"], "f32"), assign("s", "add", ["p", "bv"], "f32"),
+                    assign("y", "sigmoid", ["s"], "f32"), write("out", [i, j], ["y"], "f32")])
+
+
+def _half_io(folder):
+    i = var("i")
+    return package(folder, "half_io", {"x": ((1000,), "f16"), "y": ((1000,), "f16")}, ("out", (1000,), "f16"),
+                   [("i", 1000)],
+                   [load("xv", "x", [i], "f16"), load("yv", "y", [i], "f16"),
+                    assign("sx", "silu", ["xv"], "f16"), let("half", lit(0.5, "f16"), "f16"),
+                    assign("hy", "multiply", ["yv", "half"], "f16"), assign("d", "subtract", ["sx", "hy"], "f16"),
+                    write("out", [i], ["d"], "f16")], rtol=2e-3, atol=2e-3)
+
+
+def _bf16_mix(folder):
+    i = var("i")
+    return package(folder, "bf16_mix", {"x": ((777,), "bf16")}, ("out", (777,), "f32"), [("i", 777)],
+                   [load("xv", "x", [i], "bf16"), assign("t", "tanh", ["xv"], "bf16"),
+                    let("k", lit(0.1, "f32"), "f32"), let("xf", var("xv"), "f32"),
+                    assign("sc", "multiply", ["xf", "k"], "f32"), assign("e", "exp", ["sc"], "f32"),
+                    let("tf", var("t"), "f32"), assign("r", "add", ["tf", "e"], "f32"),
+                    write("out", [i], ["r"], "f32")], rtol=1e-2, atol=1e-2)
+
+
+def _int_select(folder):
+    i = var("i")
+    return package(folder, "int_select", {"n": ((256,), "i32"), "x": ((256,), "f32")}, ("out", (256,), "f32"),
+                   [("i", 256)],
+                   [load("nv", "n", [i], "i32"), load("xv", "x", [i], "f32"),
+                    let("three", lit(3), None), assign("m", "remainder", ["nv", "three"], None),
+                    let("zero", lit(0), None), assign("c", "equal", ["m", "zero"], "i32"),
+                    assign("ax", "abs", ["xv"], "f32"), assign("sq", "sqrt", ["ax"], "f32"),
+                    assign("ng", "negative", ["xv"], "f32"), assign("r", "where", ["c", "sq", "ng"], "f32"),
+                    write("out", [i], ["r"], "f32")],
+                   data={"n": [(-1) ** k * (k * 7919 % 1000) for k in range(256)]})
+
+
+def _compare_flags(folder):
+    i = var("i")
+    rows = 300
+    body = [load("xv", "x", [i], "f32"), load("yv", "y", [i], "f32"), let("zero", lit(0.0, "f32"), "f32"),
+            assign("pos", "greater", ["xv", "zero"], "i32"), assign("eq", "equal", ["xv", "yv"], "i32"),
+            assign("nan", "not_equal", ["xv", "xv"], "i32"), assign("any", "logical_or", ["pos", "nan"], "i32")]
+    body += [write("out", [bin_("+", bin_("*", i, lit(4)), lit(c))], [v], "i32")
+             for c, v in enumerate(("pos", "eq", "nan", "any"))]
+    data_x = [float("nan") if k % 17 == 0 else (k % 7) - 3.0 for k in range(rows)]
+    data_y = [(k % 5) - 2.0 for k in range(rows)]
+    return package(folder, "compare_flags", {"x": ((rows,), "f32"), "y": ((rows,), "f32")},
+                   ("out", (rows * 4,), "i32"), [("i", rows)], body, rtol=0, atol=0,
+                   data={"x": data_x, "y": data_y})
+
+
+def _erf_log(folder):
+    i = var("i")
+    return package(folder, "erf_log", {"x": ((4099,), "f32"), "y": ((4099,), "f32")}, ("out", (4099,), "f32"),
+                   [("i", 4099)],
+                   [load("xv", "x", [i], "f32"), load("yv", "y", [i], "f32"), assign("e", "erf", ["xv"], "f32"),
+                    assign("x2", "square", ["xv"], "f32"), let("one", lit(1.0, "f32"), "f32"),
+                    assign("q", "add", ["x2", "one"], "f32"), assign("l", "log", ["q"], "f32"),
+                    assign("rs", "rsqrt", ["q"], "f32"), let("three", lit(3.0, "f32"), "f32"),
+                    assign("t3", "multiply", ["xv", "three"], "f32"), assign("fl", "floor", ["t3"], "f32"),
+                    assign("mx", "maximum", ["xv", "yv"], "f32"), assign("s1", "add", ["e", "l"], "f32"),
+                    assign("s2", "add", ["s1", "rs"], "f32"), assign("s3", "add", ["s2", "fl"], "f32"),
+                    assign("s4", "add", ["s3", "mx"], "f32"), write("out", [i], ["s4"], "f32")],
+                   rtol=1e-5, atol=2e-6)
+
+
+def _vector_rows(folder):
+    i = var("i")
+    idx = bin_("*", i, lit(4))
+    return package(folder, "vector_rows", {"x": ((128,), "f32")}, ("out", (128,), "f32"), [("i", 32)],
+                   [f"Load(names=('a', 'b', 'c', 'd'), input='x', index=({idx},), dtype={dt('f32')})"] +
+                   [assign(f"r{k}", "relu", [v], "f32") for k, v in enumerate("abcd")] +
+                   [write("out", [idx], ["r0", "r1", "r2", "r3"], "f32")], rtol=0, atol=0)
+
+
+def _transposed(folder):
+    i, j = var("i"), var("j")
+    return package(folder, "transposed", {"x": ((40, 24), "f32")}, ("out", (24, 40), "f32"), [("i", 40), ("j", 24)],
+                   [load("xv", "x", [i, j], "f32"), let("two", lit(2.0, "f32"), "f32"),
+                    assign("y", "multiply", ["xv", "two"], "f32"), write("out", [j, i], ["y"], "f32")],
+                   rtol=0, atol=0)
+
+
+SYNTHETIC = {"bias_rows": _bias_rows, "half_io": _half_io, "bf16_mix": _bf16_mix, "int_select": _int_select,
+             "compare_flags": _compare_flags, "erf_log": _erf_log, "vector_rows": _vector_rows,
+             "transposed": _transposed}

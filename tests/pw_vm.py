@@ -1,0 +1,139 @@
+"""A numpy interpreter of compiled pointwise programs — test infrastructure.
+
+Runs the register program of a ``pointwise`` plan on the CPU, one numpy
+array per register over all tile points, so the CPU suite can check the
+program compiler's typing and lowering against the IR oracle without a GPU.
+The approximate PTX instructions (ex2/lg2/sin/cos.approx) are replaced by
+accurate numpy functions; everything else is bit-exact IEEE arithmetic.
+"""
+import math
+
+import numpy as np
+
+from lazy_compiler_b200.pointwise import OPCODES
+
+_NP = {"f32": np.float32, "f16": np.float16, "bf16": np.float32, "s32": np.int32}
+
+
+def _f(w):
+    return w.view(np.float32)
+
+
+def _w(x):
+    return np.asarray(x, np.float32).view(np.uint32)
+
+
+def _bf16(x):
+    bits = np.asarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    rounded = ((bits + 0x7FFF + ((bits >> 16) & 1)) >> 16) << 16
+    out = rounded.astype(np.uint32).view(np.float32)
+    return np.where(np.isnan(x), np.float32(np.nan), out)
+
+
+def run(prog: dict, arrays: dict) -> dict:
+    ext = prog["extents"]
+    grids = np.meshgrid(*[np.arange(e, dtype=np.int64) for e in ext], indexing="ij")
+    coords = [g.ravel() for g in grids]
+    n = coords[0].size
+    bufs = []
+    for name, size in zip(prog["buffers"], prog["sizes"]):
+        if name in arrays:
+            a = np.asarray(arrays[name]).ravel()
+            bufs.append(a.astype(np.float32) if a.dtype == np.float16 else a.copy())
+        else:
+            bufs.append(None)
+    outs = {}
+    r = {}
+    consts = np.asarray(prog["consts"], np.uint64).astype(np.uint32)
+    with np.errstate(all="ignore"):
+        for op, dst, a, b, c, aux in prog["code"]:
+            name = OPCODES[op]
+            A, B, C = r.get(a), r.get(b), r.get(c)
+            if name.startswith(("LD_", "ST_")):
+                f = prog["forms"][aux]
+                at = f["base"] + sum(k * x for k, x in zip(f["coef"], coords))
+                slot = f["buffer"]
+                if name.startswith("LD_"):
+                    v = bufs[slot][at]
+                    r[dst] = v.astype(np.int32).view(np.uint32) if name == "LD_S32" else _w(v.astype(np.float32))
+                else:
+                    bname = prog["buffers"][slot]
+                    if bname not in outs:
+                        outs[bname] = np.full(prog["sizes"][slot], np.nan if name != "ST_S32" else 0,
+                                              np.float32 if name != "ST_S32" else np.int32)
+                    val = A.view(np.int32) if name == "ST_S32" else _f(A)
+                    if name == "ST_F16":
+                        val = val.astype(np.float16).astype(np.float32)
+                    elif name == "ST_BF16":
+                        val = _bf16(val)
+                    outs[bname][at] = val
+                continue
+            fa, fb, fc = (_f(x) if x is not None else None for x in (A, B, C))
+            ia, ib = (x.view(np.int32).astype(np.int64) if x is not None else None for x in (A, B))
+            if name == "MOV":
+                out = A
+            elif name == "CONST":
+                out = np.full(n, consts[aux], np.uint32)
+            elif name in ("FADD", "FSUB", "FMUL", "FDIV"):
+                out = _w({"FADD": fa + fb, "FSUB": fa - fb, "FMUL": fa * fb, "FDIV": fa / fb}[name])
+            elif name == "FFMA":
+                out = _w((fa.astype(np.float64) * fb + fc.astype(np.float64)).astype(np.float32))
+            elif name == "FNEG":
+                out = A ^ np.uint32(0x80000000)
+            elif name == "FABS":
+                out = A & np.uint32(0x7FFFFFFF)
+            elif name in ("FMAX", "FMIN"):
+                out = _w(np.fmax(fa, fb) if name == "FMAX" else np.fmin(fa, fb))
+            elif name in ("FSQRT", "FFLOOR", "FCEIL", "FTRUNC", "FRINT"):
+                fn = {"FSQRT": np.sqrt, "FFLOOR": np.floor, "FCEIL": np.ceil, "FTRUNC": np.trunc,
+                      "FRINT": np.rint}[name]
+                out = _w(fn(fa))
+            elif name in ("FEX2", "FLG2", "FSIN", "FCOS"):
+                fn = {"FEX2": np.exp2, "FLG2": np.log2, "FSIN": np.sin, "FCOS": np.cos}[name]
+                out = _w(fn(fa.astype(np.float64)).astype(np.float32))
+            elif name == "FCOPYSIGN":
+                out = (B & np.uint32(0x7FFFFFFF)) | (A & np.uint32(0x80000000))
+            elif name == "RND_F16":
+                out = _w(fa.astype(np.float16).astype(np.float32))
+            elif name == "RND_BF16":
+                out = _w(_bf16(fa))
+            elif name == "F2I":
+                x = np.nan_to_num(np.trunc(fa.astype(np.float64)), nan=0.0, posinf=2.0 ** 31, neginf=-2.0 ** 31)
+                out = np.clip(x, -2 ** 31, 2 ** 31 - 1).astype(np.int32).view(np.uint32)
+            elif name in ("I2F", "I2H", "I2BF"):
+                x = ia.astype(np.float64)
+                if name == "I2F":
+                    out = _w(x.astype(np.float32))
+                elif name == "I2H":
+                    out = _w(x.astype(np.float16).astype(np.float32))
+                else:
+                    m, e = np.frexp(x)
+                    out = _w(np.ldexp(np.rint(np.ldexp(m, 8)), e - 8).astype(np.float32))
+            elif name.startswith("I") and name not in ("IEQ", "INE", "ILT", "ILE", "IGT", "IGE"):
+                safe = np.where(ib == 0, 1, ib) if ib is not None else None
+                q = np.where(ib == 0, 0, np.trunc(ia / safe)).astype(np.int64) if ib is not None else None
+                res = {"IADD": lambda: ia + ib, "ISUB": lambda: ia - ib, "IMUL": lambda: ia * ib,
+                       "IDIV": lambda: q, "IREM": lambda: np.where(ib == 0, ia, ia - safe * q),
+                       "ISHL": lambda: np.where((ib & 0xFFFFFFFF) >= 32, 0, ia << np.clip(ib, 0, 31)),
+                       "ISHR": lambda: ia >> np.clip(ib & 0xFFFFFFFF, 0, 31), "IAND": lambda: ia & ib,
+                       "IOR": lambda: ia | ib, "IXOR": lambda: ia ^ ib, "INOT": lambda: ~ia, "INEG": lambda: -ia,
+                       "IABS": lambda: np.abs(ia), "IMAX": lambda: np.maximum(ia, ib),
+                       "IMIN": lambda: np.minimum(ia, ib),
+                       "IPOPC": lambda: np.asarray([bin(int(v) & 0xFFFFFFFF).count("1") for v in ia])}[name]()
+                out = (np.asarray(res, np.int64) % (1 << 32)).astype(np.uint32)
+            elif name in ("FEQ", "FNE", "FLT", "FLE", "FGT", "FGE"):
+                res = {"FEQ": fa == fb, "FNE": ~(fa == fb), "FLT": fa < fb, "FLE": fa <= fb, "FGT": fa > fb,
+                       "FGE": fa >= fb}[name]
+                out = res.astype(np.uint32)
+            elif name in ("IEQ", "INE", "ILT", "ILE", "IGT", "IGE"):
+                res = {"IEQ": ia == ib, "INE": ia != ib, "ILT": ia < ib, "ILE": ia <= ib, "IGT": ia > ib,
+                       "IGE": ia >= ib}[name]
+                out = res.astype(np.uint32)
+            elif name in ("PAND", "POR"):
+                out = (((A != 0) & (B != 0)) if name == "PAND" else ((A != 0) | (B != 0))).astype(np.uint32)
+            elif name == "SEL":
+                out = np.where(A != 0, B, C)
+            else:
+                raise ValueError(name)
+            r[dst] = np.asarray(out, np.uint32)
+    return outs

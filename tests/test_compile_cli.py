@@ -66,6 +66,9 @@ EXPECTED = {
        }.items()},
     "tensor_repack_f16": ("gemm_chain", {"m": 16, "k": 16, "n1": 16, "n2": 8, "y_layout": "kn",
                                          "z_layout": "kn"}),
+    # GELU regression packages (examples/phase9/gelu): several typed results per element
+    **{f"activation_gelu{t}_{k}": ("pointwise", {"out": "out", "points": 37 if k == "special" else 273})
+       for t in ("", "_tanh") for k in ("f32", "f16", "bf16", "special")},
 }
 
 
@@ -76,7 +79,10 @@ def test_cli_prints_plan(name):
     plan = json.loads(result.stdout)
     op, params = EXPECTED[name]
     assert plan["op"] == op
-    assert plan["params"] == params
+    if op == "pointwise":   # the register program itself is checked in test_pointwise_programs.py
+        assert {k: plan["params"][k] for k in params} == params
+    else:
+        assert plan["params"] == params
     assert plan["format"] == "lazyb200-plan/1"
     meta = json.loads((golden(name) / "meta.json").read_text())
     assert plan["arg_order"] == meta["kernels"][0]["arg_order"]
@@ -96,9 +102,13 @@ def test_cli_missing_file_exit_1(tmp_path):
     assert result.stderr.startswith("compile.py: ")
 
 
-@pytest.mark.parametrize("name", ["activation_gelu_f32", "activation_gelu_special"])
-def test_cli_rejects_unsupported_classes_without_output(name):
-    result = subprocess.run(CLI + [str(golden_ir(name))], capture_output=True, text=True, cwd=ROOT)
+def test_cli_rejects_unsupported_classes_without_output(tmp_path):
+    import pw_packages as W
+    i = W.var("i")
+    ir = W.package(tmp_path / "pow", "pow", {"x": ((64,), "f32")}, ("out", (64,), "f32"), [("i", 64)],
+                   [W.load("v", "x", [i], "f32"), W.assign("p", "power", ["v", "v"], "f32"),
+                    W.write("out", [i], ["p"], "f32")])
+    result = subprocess.run(CLI + [str(ir)], capture_output=True, text=True, cwd=ROOT)
     assert result.returncode == 1
     assert result.stdout == ""
     assert result.stderr.startswith("compile.py: ")
@@ -157,22 +167,41 @@ def test_corrupt_ir_is_a_compile_error(tmp_path):
 
 
 def test_modified_semantics_are_not_misrecognised(tmp_path):
-    """A pointwise body whose op changes (add -> subtract) must be rejected, not run as add."""
+    """A pointwise body whose op changes (add -> subtract) is not run as add: it
+    compiles to a register program that subtracts."""
+    import numpy as np
+    import pw_vm
     folder, ir = _copy("p01_vector_add", tmp_path)
     ir.write_text(ir.read_text().replace("ElementwiseImpl('add')", "ElementwiseImpl('subtract')"))
-    with pytest.raises(CompileError):
-        compile_file(ir)
+    plan = compile_file(ir)
+    assert plan["op"] == "pointwise"
+    x0, x1 = (np.random.default_rng(s).standard_normal(1024).astype(np.float32) for s in (0, 1))
+    out = pw_vm.run(plan["params"]["program"], {"x0": x0, "x1": x1})
+    np.testing.assert_array_equal(out[plan["params"]["out"]], x0 - x1)
 
 
 def test_gelu_constant_values_are_checked(tmp_path):
+    """A GELU-shaped body with a wrong constant is not run as GELU: it compiles
+    to a register program of the formula as written."""
+    import numpy as np
+    import pw_vm
+    from oracle import expressions as O
+    from oracle import pointwise_ir
     folder, ir = _copy("phase9_gelu_erf_tail", tmp_path)
     meta = json.loads((folder / "meta.json").read_text())
     for arg in meta["kernels"][0]["args"]:
         if arg["name"] == "gelu_half":
             arg["data"] = [0.25]
     (folder / "meta.json").write_text(json.dumps(meta))
-    with pytest.raises(CompileError, match="GELU constant"):
-        compile_file(ir)
+    plan = compile_file(ir)
+    assert plan["op"] == "pointwise"
+    arrays = {a["name"]: O.input_array(a) for a in meta["kernels"][0]["args"] if not a.get("output")}
+    ref = pointwise_ir.evaluate(ir, arrays)
+    got = pw_vm.run(plan["params"]["program"], arrays)
+    for key, value in ref.items():
+        assert O.compare(got[key].reshape(value.shape), value, 1e-5, 2e-6)["pass"]
+        half = O.gelu(arrays["x"], "none", "f32") * np.float32(0.5)   # 0.25 x (1 + erf) = GELU / 2
+        assert O.compare(got[key].reshape(value.shape), half.reshape(value.shape), 1e-5, 2e-6)["pass"]
 
 
 def test_package_loader_reads_buffers():

@@ -33,7 +33,11 @@ PACKAGES = ["p00_scalar_add", "p01_vector_add", "p02_scale_shift", "p03_relu_mul
             "tensor_fused_guarded_epilogue", "tensor_global_bf16", "tensor_global_bf16_trans_ragged",
             "tensor_global_f16", "tensor_global_f16_ragged", "tensor_repack_f16", "tensor_shared_b128",
             "tensor_shared_b32", "tensor_shared_b64", "tensor_shared_bf16_trans", "tensor_shared_f16",
-            "tensor_shared_paired", "tensor_shared_paired_trans", "tensor_transposed_output"]
+            "tensor_shared_paired", "tensor_shared_paired_trans", "tensor_transposed_output",
+            # GELU regression packages run as register programs (several typed results per element)
+            "activation_gelu_f32", "activation_gelu_f16", "activation_gelu_bf16", "activation_gelu_special",
+            "activation_gelu_tanh_f32", "activation_gelu_tanh_f16", "activation_gelu_tanh_bf16",
+            "activation_gelu_tanh_special"]
 
 
 def torch_():
@@ -83,7 +87,7 @@ def test_package_alternate_seeds_against_oracle(name, offset, cuda_device):
     plan = compile_file(golden_ir(name))
     args = {a["name"]: a for a in meta["kernels"][0]["args"] if not a.get("output")}
     arrays = {n: O.input_array(a, offset) for n, a in args.items()}
-    ref = O.evaluate(plan, arrays)
+    ref = O.evaluate(plan, arrays, ir=golden_ir(name))
     out = run_package(golden(name), seed_offset=offset)
     for key, value in ref.items():
         assert_close(out[key], value, meta["rtol"], meta["atol"])
