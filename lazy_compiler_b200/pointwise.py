@@ -531,8 +531,8 @@ class PointwiseCompiler:
             self.env[s.name] = value
         elif k == "Write":
             buf = self.pkg.buffers.get(s.output)
-            if buf is None or s.output not in self.pkg.graph_outputs:
-                raise CompileError("pointwise programs write graph outputs only")
+            if buf is None or buf.role != "output":
+                raise CompileError("pointwise programs write the kernel's outputs only")
             if s.get("atomic") or s.get("swizzle", "NONE") not in (None, "NONE"):
                 raise CompileError("pointwise writes are plain stores")
             dt = vm_type(buf.dtype)

@@ -545,8 +545,8 @@ class FragmentInterpreter:
         if tuple(s.get("fragment_index") or (0, 0)) != (0, 0) and s.get("fragment_layout") not in (None, "m16n8k16"):
             raise CompileError("only the m16n8k16 fragment layout is supported")
         buf = self.pkg.buffers.get(s.dst_buffer)
-        if buf is None or s.dst_buffer in self.smem or s.dst_buffer not in self.pkg.graph_outputs:
-            raise CompileError("fragment stores must write a graph output")
+        if buf is None or s.dst_buffer in self.smem or buf.role != "output":
+            raise CompileError("fragment stores must write the kernel's output")
         if buf.dtype not in ("f32", "f16", "bf16"):
             raise CompileError("tensor outputs must be f32, f16 or bf16")
         if s.get("atomic") and buf.dtype != "f32":

@@ -103,3 +103,99 @@ def run_package(folder: str | Path, seed_offset: int = 0, device: str = "cuda",
         t = buffers[name]
         out[name] = (t.float() if t.dtype == torch.bfloat16 else t).cpu().numpy()
     return out
+
+
+# ---------------------------------------------------------------- /run requests
+
+_RUN_DTYPES = ("f32", "f16", "bf16", "f64", "i32")
+_LIMITS = {"warmup": 20, "iters": 200, "elements": 1 << 26, "max_return": 1 << 22}
+
+
+def _request_error(stage: str, message: str) -> dict:
+    return {"ok": False, "stage": stage, "stderr": message}
+
+
+def run_request(request: dict, device: str = "cuda") -> dict:
+    """One launch with the request and response of the reference runner's ``POST /run``.
+
+    The request carries, in place of ``ptx`` / ``cubin_id``, the ``plan`` that
+    ``compile.py`` printed for the kernel; ``entry``, ``grid``, ``block``,
+    ``smem_bytes``, ``zero_outputs``, ``warmup``, ``iters``, ``max_return`` and
+    the positional ``args`` (``seed`` / ``data`` / ``output``) mean what they
+    mean there (docs/API.md:26-72).  The launch geometry is checked against
+    the plan's meta.json geometry, as the runner launches exactly that.
+
+    Returns ``{"ok": True, "median_us", "iters", "outputs": {name: {"shape",
+    "dtype", "sum", "values", "truncated"}}}``, or ``{"ok": False, "stage",
+    "stderr"}`` with stage ``request`` (malformed or out-of-range request) or
+    ``run`` (the launch failed).  Outputs are zeroed before the first launch
+    and ``zero_outputs`` before every launch; ``median_us`` is the median of
+    ``iters`` launches timed with CUDA events.
+    """
+    import torch
+
+    from .runtime import LcError
+
+    plan = request.get("plan")
+    if not isinstance(plan, dict) or "op" not in plan:
+        return _request_error("request", "the request carries no compiled plan")
+    entry = request.get("entry")
+    if entry != plan.get("entry"):
+        return _request_error("run", f"entry {entry!r} is not the plan's kernel {plan.get('entry')!r}")
+    geometry = plan.get("reference_launch") or {}
+    for key in ("grid", "block"):
+        if key in request and key in geometry and list(request[key]) != list(geometry[key]):
+            return _request_error("request", f"{key} {request[key]} differs from the kernel's {geometry[key]}")
+    warmup, iters = int(request.get("warmup", 0)), int(request.get("iters", 1))
+    max_return = int(request.get("max_return", 4096))
+    if not (0 <= warmup <= _LIMITS["warmup"] and 1 <= iters <= _LIMITS["iters"]
+            and 0 <= max_return <= _LIMITS["max_return"]):
+        return _request_error("request", "warmup, iters or max_return out of range")
+    args = request.get("args")
+    if not isinstance(args, list) or [a.get("name") for a in args] != list(plan["arg_order"]):
+        return _request_error("request", f"args must be given in the kernel's order {plan['arg_order']}")
+    total = 0
+    for a in args:
+        if a.get("dtype") not in _RUN_DTYPES:
+            return _request_error("request", f"unsupported dtype {a.get('dtype')!r} for {a.get('name')}")
+        total += math.prod(a.get("shape") or [1])
+    if total > _LIMITS["elements"]:
+        return _request_error("request", "buffers exceed 2^26 elements")
+    dev = torch.device(device)
+    stream = torch.cuda.current_stream(dev)
+    buffers = {}
+    for a in args:
+        shape = tuple(a.get("shape") or [1])
+        if a.get("output"):
+            buffers[a["name"]] = torch.zeros(shape, dtype=_torch_dtype(a["dtype"]), device=dev)
+        else:
+            host = seeded_input(a)
+            buffers[a["name"]] = torch.as_tensor(np.ascontiguousarray(host)).to(dev, _torch_dtype(a["dtype"]))
+    pointers = {n: t.data_ptr() for n, t in buffers.items()}
+    zero = [n for n in request.get("zero_outputs", []) if n in buffers]
+    times = []
+    try:
+        for i in range(warmup + iters):
+            for n in zero:
+                buffers[n].zero_()
+            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            launch(plan, pointers, stream.cuda_stream)
+            stop.record(stream)
+            if i >= warmup:
+                times.append((start, stop))
+        torch.cuda.synchronize(dev)
+    except (LcError, ValueError, KeyError) as err:
+        return _request_error("run", str(err))
+    median = float(np.median([s.elapsed_time(e) * 1000.0 for s, e in times]))
+    outputs, budget = {}, max_return
+    for a in args:
+        if not a.get("output"):
+            continue
+        t = buffers[a["name"]]
+        values = (t.float() if t.dtype == torch.bfloat16 else t).cpu().numpy().ravel()
+        take = min(budget, values.size)
+        budget -= take
+        outputs[a["name"]] = {"shape": list(t.shape), "dtype": a["dtype"], "sum": float(values.astype(np.float64).sum()),
+                              "values": values[:take].tolist(), "truncated": take < values.size}
+    return {"ok": True, "median_us": round(median, 3), "iters": iters, "outputs": outputs}

@@ -176,3 +176,37 @@ def _transposed(folder):
 SYNTHETIC = {"bias_rows": _bias_rows, "half_io": _half_io, "bf16_mix": _bf16_mix, "int_select": _int_select,
              "compare_flags": _compare_flags, "erf_log": _erf_log, "vector_rows": _vector_rows,
              "transposed": _transposed}
+
+
+def chain_package(folder: Path, n: int = 4096) -> Path:
+    """Two kernels chained through an intermediate: t = 2 x, then out = t + y."""
+    folder.mkdir(parents=True, exist_ok=True)
+    i = var("i")
+    first = [load("xv", "x", [i], "f32"), let("two", lit(2.0, "f32"), "f32"),
+             assign("tv", "multiply", ["xv", "two"], "f32"), write("t", [i], ["tv"], "f32")]
+    second = [load("tv", "t", [i], "f32"), load("yv", "y", [i], "f32"),
+              assign("ov", "add", ["tv", "yv"], "f32"), write("out", [i], ["ov"], "f32")]
+    kernels = []
+    for entry, ins, out, body in (("k_first", ["x"], "t", first), ("k_second", ["t", "y"], "out", second)):
+        tile = (f"Tile(axes=(Axis(name='i', extent=Dim({n}), window=None),), body=({', '.join(body)},), "
+                "block_threads=None, aux_threads=0, raster_axes=None, raster_group=None, raster_orient='m')")
+        nodes = {name: {"op": "InputOp", "op_fields": {}, "inputs": [],
+                        "outputs": [{"name": name, "shape": [n], "dtype": "f32"}]} for name in ins}
+        nodes[out] = {"op": "KernelOp", "op_fields": {"body": [tile], "name": entry, "zero_delegated": [],
+                                                      "serial": []},
+                      "inputs": ins, "outputs": [{"name": out, "shape": [n], "dtype": "f32"}]}
+        (folder / f"{entry}.ir.json").write_text(json.dumps({"inputs": ins, "outputs": [out], "nodes": nodes}))
+        args = []
+        for name in ins:
+            if name == "t":
+                args.append({"name": "t", "dtype": "f32", "shape": [n], "intermediate": True})
+            else:
+                args.append({"name": name, "dtype": "f32", "shape": [n], "seed": 0 if name == "x" else 1})
+        args.append({"name": out, "dtype": "f32", "shape": [n], "output": True})
+        kernels.append({"node": out, "entry": entry, "arg_order": ins + [out], "grid": [1, 1, 1],
+                        "block": [256, 1, 1], "smem_bytes": 0, "zero_outputs": [], "args": args,
+                        "final": out == "out"})
+    meta = {"id": "chain", "rtol": 0, "atol": 0, "graph_inputs": ["x", "y"], "graph_outputs": ["out"],
+            "kernels": kernels}
+    (folder / "meta.json").write_text(json.dumps(meta))
+    return folder

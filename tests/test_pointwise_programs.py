@@ -81,7 +81,7 @@ REJECT = {
                          "affine|leaves"),
     "unsupported_power": ([W.load("v", "x", [I], "f32"), W.assign("p", "power", ["v", "v"], "f32"),
                            W.write("out", [I], ["p"], "f32")], "power"),
-    "write_to_input": ([W.load("v", "x", [I], "f32"), W.write("x", [I], ["v"], "f32")], "graph outputs|write"),
+    "write_to_input": ([W.load("v", "x", [I], "f32"), W.write("x", [I], ["v"], "f32")], "kernel.s outputs|write"),
 }
 
 
