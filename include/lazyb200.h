@@ -300,13 +300,25 @@ int lc_probe_mma(int variant, int groups, void *stream);
  * base + sum_d coef[d] * x[d] of buffer slot `buffer`, x the point's
  * coordinates over `extents` (row-major, last axis fastest); sizes[slot] is
  * the slot's element count and every form must stay inside it over the
- * whole tile (checked before launch). */
-#define LC_PW_MAX_CODE 384
+ * whole tile (checked before launch).
+ *
+ * Lane programs (the warp-level fragment algebra of ptx_tensor.py:164-618)
+ * use the operations after SEL: COORD reads coordinate `aux` of the point;
+ * LDX_* loads slot `aux` at the s32 index in register a, clamped into the
+ * buffer; STX_* stores register b at the index in register a when register
+ * c is non-zero and the index is inside the buffer (STX_ADD_F32 adds
+ * atomically); SHFL_XOR exchanges a register with the lane `aux` apart;
+ * PACK_F16X2 / PACK_BF16X2 round registers a (low half) and b (high half)
+ * into one 16-bit pair; MMA_F16 / MMA_BF16 run mma.sync m16n8k16 with D, A,
+ * B and C in registers dst..dst+3, a..a+3, b..b+1 and c..c+3.  A program
+ * that shuffles or multiplies needs a point count that is a multiple of 32:
+ * each warp then runs 32 consecutive points in lockstep. */
+#define LC_PW_MAX_CODE 1024
 #define LC_PW_MAX_CONST 128
 #define LC_PW_MAX_FORMS 32
 #define LC_PW_MAX_BUFFERS 16
 #define LC_PW_MAX_AXES 4
-#define LC_PW_MAX_REGS 48
+#define LC_PW_MAX_REGS 64
 
 enum lc_pw_op {
   LC_PW_MOV = 0,
@@ -375,6 +387,21 @@ enum lc_pw_op {
   LC_PW_PAND = 63,
   LC_PW_POR = 64,
   LC_PW_SEL = 65,
+  LC_PW_COORD = 66,
+  LC_PW_LDX_F32 = 67,
+  LC_PW_LDX_F16 = 68,
+  LC_PW_LDX_BF16 = 69,
+  LC_PW_LDX_S32 = 70,
+  LC_PW_STX_F32 = 71,
+  LC_PW_STX_F16 = 72,
+  LC_PW_STX_BF16 = 73,
+  LC_PW_STX_S32 = 74,
+  LC_PW_STX_ADD_F32 = 75,
+  LC_PW_SHFL_XOR = 76,
+  LC_PW_PACK_F16X2 = 77,
+  LC_PW_PACK_BF16X2 = 78,
+  LC_PW_MMA_F16 = 79,
+  LC_PW_MMA_BF16 = 80,
   LC_PW_NUM_OPS
 };
 

@@ -145,6 +145,67 @@ __global__ void __launch_bounds__(256) pointwise_kernel(const __grid_constant__ 
         case LC_PW_PAND: out = (A != 0u) & (B != 0u); break;
         case LC_PW_POR: out = (A != 0u) | (B != 0u); break;
         case LC_PW_SEL: out = A != 0u ? B : C; break;
+        case LC_PW_COORD: out = (uint32_t)x[aux]; break;
+        case LC_PW_LDX_F32: case LC_PW_LDX_F16: case LC_PW_LDX_BF16: case LC_PW_LDX_S32: {
+          const int64_t size = g.sizes[aux];
+          int64_t at = (int64_t)ia;
+          at = at < 0 ? 0 : (at >= size ? size - 1 : at);  // clamped: a load never leaves its buffer
+          const void *base = p.buffers[aux];
+          if (op == LC_PW_LDX_F16) out = w(__half2float(static_cast<const __half *>(base)[at]));
+          else if (op == LC_PW_LDX_BF16) out = w(__bfloat162float(static_cast<const __nv_bfloat16 *>(base)[at]));
+          else out = static_cast<const uint32_t *>(base)[at];
+          break;
+        }
+        case LC_PW_STX_F32: case LC_PW_STX_F16: case LC_PW_STX_BF16: case LC_PW_STX_S32:
+        case LC_PW_STX_ADD_F32: {
+          const int64_t at = (int64_t)ia;
+          if (C != 0u && at >= 0 && at < g.sizes[aux]) {
+            void *base = p.buffers[aux];
+            if (op == LC_PW_STX_F16) static_cast<__half *>(base)[at] = __float2half_rn(f(B));
+            else if (op == LC_PW_STX_BF16) static_cast<__nv_bfloat16 *>(base)[at] = __float2bfloat16_rn(f(B));
+            else if (op == LC_PW_STX_ADD_F32) atomicAdd(static_cast<float *>(base) + at, f(B));
+            else static_cast<uint32_t *>(base)[at] = B;
+          }
+          continue;
+        }
+        case LC_PW_SHFL_XOR:
+          __syncwarp();
+          out = __shfl_xor_sync(0xffffffffu, A, aux);
+          break;
+        case LC_PW_PACK_F16X2: {
+          __half2 h = __floats2half2_rn(f(A), f(B));
+          out = *reinterpret_cast<uint32_t *>(&h);
+          break;
+        }
+        case LC_PW_PACK_BF16X2: {
+          __nv_bfloat162 h = __floats2bfloat162_rn(f(A), f(B));
+          out = *reinterpret_cast<uint32_t *>(&h);
+          break;
+        }
+        case LC_PW_MMA_F16: case LC_PW_MMA_BF16: {
+          const int ra = (w0 >> 16) & 255, rb = w0 >> 24, rc = w1 & 255;
+          uint32_t d0, d1, d2, d3;
+          __syncwarp();
+          if (op == LC_PW_MMA_F16)
+            asm volatile(
+                "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7},"
+                " {%8, %9}, {%10, %11, %12, %13};"
+                : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+                : "r"(r[ra]), "r"(r[ra + 1]), "r"(r[ra + 2]), "r"(r[ra + 3]), "r"(r[rb]), "r"(r[rb + 1]),
+                  "r"(r[rc]), "r"(r[rc + 1]), "r"(r[rc + 2]), "r"(r[rc + 3]));
+          else
+            asm volatile(
+                "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7},"
+                " {%8, %9}, {%10, %11, %12, %13};"
+                : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+                : "r"(r[ra]), "r"(r[ra + 1]), "r"(r[ra + 2]), "r"(r[ra + 3]), "r"(r[rb]), "r"(r[rb + 1]),
+                  "r"(r[rc]), "r"(r[rc + 1]), "r"(r[rc + 2]), "r"(r[rc + 3]));
+          r[dst] = d0;
+          r[dst + 1] = d1;
+          r[dst + 2] = d2;
+          r[dst + 3] = d3;
+          continue;
+        }
         default: out = 0u; break;  // the host admits no other opcode
       }
       r[dst] = out;
@@ -199,6 +260,7 @@ extern "C" int lc_pointwise(const lc_pw_program *program, void *const *buffers, 
     if (!sane || fm.buffer < 0 || fm.buffer >= g.n_buffers || !form_in_range(g, fm))
       return fail(LC_ERR_INVALID, "lc_pointwise: form %d leaves its buffer", i);
   }
+  bool lockstep = false;
   for (int pc = 0; pc < g.n_code; ++pc) {
     const uint32_t w0 = g.code[pc][0], w1 = g.code[pc][1];
     const int op = w0 & 255;
@@ -209,10 +271,22 @@ extern "C" int lc_pointwise(const lc_pw_program *program, void *const *buffers, 
       return fail(LC_ERR_INVALID, "lc_pointwise: register out of range at %d", pc);
     if (op == LC_PW_CONST && aux >= g.n_consts)
       return fail(LC_ERR_INVALID, "lc_pointwise: constant out of range at %d", pc);
+    if (op == LC_PW_COORD && aux >= g.n_axes)
+      return fail(LC_ERR_INVALID, "lc_pointwise: coordinate out of range at %d", pc);
+    if (op >= LC_PW_LDX_F32 && op <= LC_PW_STX_ADD_F32 && aux >= g.n_buffers)
+      return fail(LC_ERR_INVALID, "lc_pointwise: buffer slot out of range at %d", pc);
+    if (op == LC_PW_SHFL_XOR && (aux < 1 || aux > 31))
+      return fail(LC_ERR_INVALID, "lc_pointwise: shuffle distance out of range at %d", pc);
+    if ((op == LC_PW_MMA_F16 || op == LC_PW_MMA_BF16) &&
+        ((int)dst + 3 >= g.n_regs || (int)a + 3 >= g.n_regs || (int)b + 1 >= g.n_regs || (int)c + 3 >= g.n_regs))
+      return fail(LC_ERR_INVALID, "lc_pointwise: MMA register tuple out of range at %d", pc);
+    if (op == LC_PW_SHFL_XOR || op == LC_PW_MMA_F16 || op == LC_PW_MMA_BF16) lockstep = true;
     if (op >= LC_PW_LD_F32 && op <= LC_PW_ST_S32 &&
         (aux >= g.n_forms || g.forms[aux].dtype != storage_of(op)))
       return fail(LC_ERR_INVALID, "lc_pointwise: form or storage type mismatch at %d", pc);
   }
+  if (lockstep && points % 32 != 0)
+    return fail(LC_ERR_INVALID, "lc_pointwise: a program that shuffles or multiplies needs whole warps of points");
   PointwiseArgs args;
   args.prog = g;
   for (int i = 0; i < LC_PW_MAX_BUFFERS; ++i) args.buffers[i] = i < g.n_buffers ? buffers[i] : nullptr;

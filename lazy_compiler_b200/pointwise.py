@@ -47,15 +47,18 @@ OPCODES = [
     "FEQ", "FNE", "FLT", "FLE", "FGT", "FGE",
     "IEQ", "INE", "ILT", "ILE", "IGT", "IGE",
     "PAND", "POR", "SEL",
+    # lane programs (fragment algebra, lazy_compiler_b200/fragment_vm.py)
+    "COORD", "LDX_F32", "LDX_F16", "LDX_BF16", "LDX_S32", "STX_F32", "STX_F16", "STX_BF16", "STX_S32",
+    "STX_ADD_F32", "SHFL_XOR", "PACK_F16X2", "PACK_BF16X2", "MMA_F16", "MMA_BF16",
 ]
 OP = {name: i for i, name in enumerate(OPCODES)}
 
-MAX_CODE = 384
+MAX_CODE = 1024
 MAX_CONST = 128
 MAX_FORMS = 32
 MAX_BUFFERS = 16
 MAX_AXES = 4
-MAX_REGS = 48
+MAX_REGS = 64
 
 _TYPES = {"float": "f32", "int": "s32", "i32": "s32", "__half": "f16", "half": "f16",
           "__nv_bfloat16": "bf16", "bool": "pred"}
@@ -149,10 +152,22 @@ class PointwiseCompiler:
         self.nvreg += 1
         return Val(self.nvreg - 1, dt)
 
+    _IMPURE = ("LD_", "ST_", "LDX_", "STX_", "SHFL_XOR", "MMA_")
+
     def emit(self, op: str, dt: str | None, *srcs: Val, aux: int = 0) -> Val | None:
+        # a pure operation on SSA values already computed is reused (fixed
+        # registers are mutable, so operations reading them are not)
+        key = None
+        if dt is not None and not op.startswith(self._IMPURE) and all(s.reg >= 0 for s in srcs):
+            key = (op, dt, tuple(s.reg for s in srcs), aux)
+            memo = self.__dict__.setdefault("_memo", {})
+            if key in memo:
+                return memo[key]
         dst = self.new(dt) if dt is not None else None
         regs = [s.reg for s in srcs] + [0] * (3 - len(srcs))
         self.code.append((OP[op], dst.reg if dst else 0, *regs, aux, len(srcs), dst is not None))
+        if key is not None:
+            self._memo[key] = dst
         return dst
 
     def const_word(self, word: int, dt: str) -> Val:
@@ -548,34 +563,44 @@ class PointwiseCompiler:
 
     # ------------------------------------------------------------ finishing
     def allocate(self) -> list:
-        """Map virtual registers to at most MAX_REGS physical ones (linear scan)."""
+        """Map virtual registers to physical ones (linear scan).
+
+        Register ids >= 0 are virtual; -1 - p names fixed physical register p
+        (the fragment registers of lane programs, below ``n_fixed``), which
+        virtual registers never share.
+        """
+        base = getattr(self, "n_fixed", 0)
         last: dict = {}
         for pc, (op, dst, a, b, c, aux, nsrc, has_dst) in enumerate(self.code):
             for r in (a, b, c)[:nsrc]:
-                last[r] = pc
+                if r >= 0:
+                    last[r] = pc
         free: list = []
         phys: dict = {}
-        top = 0
+        top = base
         out = []
         for pc, (op, dst, a, b, c, aux, nsrc, has_dst) in enumerate(self.code):
-            srcs = [phys[r] for r in (a, b, c)[:nsrc]]
+            srcs = [-1 - r if r < 0 else phys[r] for r in (a, b, c)[:nsrc]]
             for r in set((a, b, c)[:nsrc]):
-                if last.get(r) == pc:
+                if r >= 0 and last.get(r) == pc:
                     free.append(phys[r])
             d = 0
             if has_dst:
-                if free:
-                    d = free.pop()
+                if dst < 0:
+                    d = -1 - dst
                 else:
-                    d = top
-                    top += 1
-                phys[dst] = d
-                if dst not in last:
-                    free.append(d)
+                    if free:
+                        d = free.pop()
+                    else:
+                        d = top
+                        top += 1
+                    phys[dst] = d
+                    if dst not in last:
+                        free.append(d)
             srcs += [0] * (3 - len(srcs))
             out.append((op, d, *srcs, aux))
         if top > MAX_REGS:
-            raise CompileError(f"pointwise program needs {top} registers (at most {MAX_REGS})")
+            raise CompileError(f"program needs {top} registers (at most {MAX_REGS})")
         return out, top
 
     def coverage(self) -> str:

@@ -842,6 +842,37 @@ def _recognise_gemm(pkg: KernelPackage, tile: Node) -> Plan:
 
 # ----------------------------------------------------------------------------
 
+_FRAGMENT_KINDS = {"RegFragment", "LdmatrixLoad", "MmaSyncPtx", "RegStore", "FragmentApply",
+                   "FragmentRowReduce", "FragmentRepack"}
+
+
+def _recognise_fragments(pkg: KernelPackage, tile: Node, kinds: set) -> Plan:
+    """Tensor-fragment programs: a recognised product (tcgen05 GEMM, the
+    fragment attention tile, a quantised GEMM or repack chain) when the
+    program is one; otherwise, for one warp, the program itself as a lane
+    program with the reference's per-lane semantics."""
+    from . import fragment_vm, recognize_frag
+    from . import recognize_f32 as f32
+    single = recognize_frag.is_single_warp(pkg, tile)
+    reason = None
+    try:
+        if "FragmentRowReduce" in kinds:
+            return f32.recognise_fragment_attention(pkg, tile)
+        if "MmaSyncPtx" in kinds:
+            if single:
+                return recognize_frag.recognise_fragment_tile(pkg, tile)
+            return _recognise_gemm(pkg, tile)
+        raise CompileError("fragment algebra without a recognised product")
+    except CompileError as err:
+        reason = err
+    if not single:
+        raise reason
+    try:
+        return fragment_vm.compile_fragment_lanes(pkg, tile)
+    except CompileError as err:
+        raise CompileError(f"{reason}; as a lane program: {err}") from err
+
+
 def recognise(pkg: KernelPackage) -> Plan:
     """Map one loaded IR package to the launch plan of its B200 kernel."""
     if len(pkg.body) != 1 or pkg.body[0].kind != "Tile":
@@ -849,13 +880,8 @@ def recognise(pkg: KernelPackage) -> Plan:
     tile = pkg.body[0]
     kinds = {s.kind for s in _walk(tile.body)}
     from . import recognize_f32 as f32
-    if "FragmentRowReduce" in kinds:
-        return f32.recognise_fragment_attention(pkg, tile)
-    if "MmaSyncPtx" in kinds:
-        from . import recognize_frag
-        if recognize_frag.is_single_warp(pkg, tile):
-            return recognize_frag.recognise_fragment_tile(pkg, tile)
-        return _recognise_gemm(pkg, tile)
+    if kinds & _FRAGMENT_KINDS:
+        return _recognise_fragments(pkg, tile, kinds)
     if "CpAsyncCopy" in kinds:
         return f32.recognise_staged_gemm(pkg, tile)
     ev = _Eval(pkg)

@@ -311,6 +311,9 @@ def evaluate(plan: dict, arrays: dict, ir=None) -> dict:
     if op == "pointwise":
         if ir is None:
             raise ValueError("pointwise plans are evaluated from their IR: pass ir=")
+        if plan["params"].get("lanes"):
+            from oracle.fragment_ir import evaluate as evaluate_fragments
+            return evaluate_fragments(ir, arrays)
         from oracle.pointwise_ir import evaluate as evaluate_ir
         return evaluate_ir(ir, arrays)
     bind = plan["bind"]

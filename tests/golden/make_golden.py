@@ -40,6 +40,11 @@ PACKAGES = [
     "examples/phase9/gelu/activation_gelu_special", "examples/phase9/gelu/activation_gelu_tanh_special",
     # fragment attention tile (tests/test_fragment_rows.py)
     "examples/phase9/fragments/fragment_attention_tile_f16",
+    # fragment algebra: FragmentApply operand kinds, ordered row folds, MMA + row normalisation
+    *[f"examples/phase9/fragments/{name}" for name in (
+        "fragment_family_row_softmax", "fragment_masked_gmem_post", "fragment_mma_row_normalization",
+        "fragment_row_add_ordered", "fragment_row_maximum_ordered", "fragment_row_minimum_ordered",
+        "fragment_row_multiply_ordered")],
     # tensor-core lowering fixtures (tests/test_tensor_cores.py)
     *[f"examples/tensor/packages/{name}" for name in (
         "tensor_atomic_f32", "tensor_cp_async_shared", "tensor_family_live_index",

@@ -30,6 +30,44 @@ def _bf16(x):
     return np.where(np.isnan(x), np.float32(np.nan), out)
 
 
+def _half(words, bf16):
+    """The f32 values of the low and high 16-bit halves of packed words."""
+    lo, hi = words & np.uint32(0xFFFF), words >> 16
+    if bf16:
+        return (lo << 16).view(np.float32), (hi << 16).view(np.float32)
+    return (lo.astype(np.uint16).view(np.float16).astype(np.float32),
+            hi.astype(np.uint16).view(np.float16).astype(np.float32))
+
+
+def _mma(r, dst, a, b, c, bf16, n):
+    """mma.sync m16n8k16 per warp of 32 points: fragments gathered into
+    matrices, the product in float64 rounded once to f32 (the tensor core's
+    f32 accumulation agrees to the packages' tolerances)."""
+    lane = np.arange(n) % 32
+    g, t = lane // 4, lane % 4
+    for w0 in range(0, n, 32):
+        sl = slice(w0, w0 + 32)
+        A = np.zeros((16, 16))
+        B = np.zeros((16, 8))
+        C = np.zeros((16, 8))
+        for i in range(4):
+            lo, hi = _half(r[a + i][sl], bf16)
+            rows = g[sl] + (8 if i & 1 else 0)
+            cols = 2 * t[sl] + (8 if i & 2 else 0)
+            A[rows, cols], A[rows, cols + 1] = lo, hi
+        for i in range(2):
+            lo, hi = _half(r[b + i][sl], bf16)
+            k = 2 * t[sl] + (8 if i else 0)
+            B[k, g[sl]], B[k + 1, g[sl]] = lo, hi
+        for e in range(4):
+            C[g[sl] + (8 if e >= 2 else 0), 2 * t[sl] + (e & 1)] = _f(r[c + e][sl])
+        D = (A @ B + C).astype(np.float32)
+        for e in range(4):
+            r.setdefault(dst + e, np.zeros(n, np.uint32))
+            r[dst + e] = r[dst + e].copy()
+            r[dst + e][sl] = _w(D[g[sl] + (8 if e >= 2 else 0), 2 * t[sl] + (e & 1)])
+
+
 def run(prog: dict, arrays: dict) -> dict:
     ext = prog["extents"]
     grids = np.meshgrid(*[np.arange(e, dtype=np.int64) for e in ext], indexing="ij")
@@ -133,7 +171,66 @@ def run(prog: dict, arrays: dict) -> dict:
                 out = (((A != 0) & (B != 0)) if name == "PAND" else ((A != 0) | (B != 0))).astype(np.uint32)
             elif name == "SEL":
                 out = np.where(A != 0, B, C)
+            elif name == "COORD":
+                out = coords[aux].astype(np.int64).astype(np.uint32)
+            elif name.startswith("LDX_"):
+                data = bufs[aux]
+                at = np.clip(ia, 0, data.size - 1)
+                v = data[at]
+                out = v.astype(np.int32).view(np.uint32) if name == "LDX_S32" else _w(v.astype(np.float32))
+            elif name.startswith("STX_"):
+                bname = prog["buffers"][aux]
+                if bname not in outs:
+                    outs[bname] = np.full(prog["sizes"][aux], np.nan if name != "STX_S32" else 0,
+                                          np.float32 if name != "STX_S32" else np.int32)
+                live = (C != 0) & (ia >= 0) & (ia < prog["sizes"][aux])
+                val = B.view(np.int32) if name == "STX_S32" else _f(B)
+                if name == "STX_F16":
+                    val = val.astype(np.float16).astype(np.float32)
+                elif name == "STX_BF16":
+                    val = _bf16(val)
+                if name == "STX_ADD_F32":
+                    base = np.nan_to_num(outs[bname], nan=0.0)   # the runner zeroes atomic outputs
+                    for k in np.nonzero(live)[0]:
+                        base[ia[k]] += val[k]
+                    outs[bname] = base
+                else:
+                    outs[bname][ia[live]] = val[live]
+                continue
+            elif name == "SHFL_XOR":
+                out = A[np.arange(n) ^ aux]
+            elif name in ("PACK_F16X2", "PACK_BF16X2"):
+                if name == "PACK_F16X2":
+                    lo = fa.astype(np.float16).view(np.uint16).astype(np.uint32)
+                    hi = fb.astype(np.float16).view(np.uint16).astype(np.uint32)
+                else:
+                    lo = _bf16(fa).view(np.uint32) >> 16
+                    hi = _bf16(fb).view(np.uint32) >> 16
+                out = (hi << 16) | lo
+            elif name in ("MMA_F16", "MMA_BF16"):
+                _mma(r, dst, a, b, c, name == "MMA_BF16", n)
+                continue
             else:
                 raise ValueError(name)
             r[dst] = np.asarray(out, np.uint32)
     return outs
+
+
+def assert_faithful(ir, rtol=1e-5, atol=1e-6):
+    """The lane program compiled from ``ir`` computes what the fragment oracle
+    computes on the package's inputs (unwritten elements stay NaN in both)."""
+    import json
+
+    from lazy_compiler_b200.compiler import compile_file
+    from oracle import expressions as O
+    from oracle import fragment_ir
+
+    plan = compile_file(ir)
+    assert plan["op"] == "pointwise" and plan["params"].get("lanes"), plan["op"]
+    meta = json.loads((ir.parent / "meta.json").read_text())
+    arrays = {a["name"]: O.input_array(a, 0) for a in meta["kernels"][0]["args"] if not a.get("output")}
+    ref = fragment_ir.evaluate(ir, arrays)
+    got = run(plan["params"]["program"], arrays)
+    for key, value in ref.items():
+        np.testing.assert_allclose(got[key].reshape(value.shape), value, rtol=rtol, atol=atol, equal_nan=True)
+    return plan

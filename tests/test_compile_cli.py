@@ -276,17 +276,18 @@ def test_row_dot_with_changed_gelu_constant_is_rejected(tmp_path):
         compile_file(ir)
 
 
-def test_fragment_attention_without_exp_is_rejected(tmp_path):
+def test_fragment_attention_without_exp_is_not_attention(tmp_path):
+    """Without the exp the tile is no softmax: it runs as its own lane program."""
+    import pw_vm
     _, ir = _mutate("fragment_attention_tile_f16", tmp_path, "post=(ElementwiseImpl('exp'),)", "post=()")
-    with pytest.raises(CompileError, match="exp"):
-        compile_file(ir)
+    pw_vm.assert_faithful(ir)
 
 
-def test_fragment_attention_with_row_min_is_rejected(tmp_path):
+def test_fragment_attention_with_row_min_is_not_attention(tmp_path):
+    import pw_vm
     _, ir = _mutate("fragment_attention_tile_f16", tmp_path,
                     "FragmentRowReduce(top='pivot0', bot='pivot1', frags=('scores[0]', 'scores[1]'), "
                     "op=ElementwiseImpl('maximum')",
                     "FragmentRowReduce(top='pivot0', bot='pivot1', frags=('scores[0]', 'scores[1]'), "
                     "op=ElementwiseImpl('minimum')")
-    with pytest.raises(CompileError, match="row max"):
-        compile_file(ir)
+    pw_vm.assert_faithful(ir, rtol=2e-3, atol=2e-3)

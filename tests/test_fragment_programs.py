@@ -18,6 +18,7 @@ from conftest import golden, golden_ir, golden_meta
 from lazy_compiler_b200.compiler import compile_file
 from lazy_compiler_b200.ir import CompileError
 from oracle import expressions as O
+import pw_vm
 
 FIXTURES = sorted(p.name for p in golden("").iterdir() if p.name.startswith("tensor_"))
 
@@ -82,12 +83,27 @@ MUTATIONS = {
 }
 
 
+STAGED = {"read_without_swizzle", "missing_barrier", "missing_cp_async_wait"}
+
+
 @pytest.mark.parametrize("case", sorted(MUTATIONS))
-def test_wrong_programs_are_rejected(case, tmp_path):
+def test_wrong_programs_are_not_misrecognised(case, tmp_path):
+    """A changed program is never taken for the product it no longer computes.
+    Programs that stage through shared memory are then rejected; the others
+    run as lane programs that compute exactly what the changed IR says (the
+    fragment oracle on the same IR)."""
     name, old, new, meta_edit, match = MUTATIONS[case]
     ir = mutated(tmp_path, name, old, new, meta_edit)
+    if case in STAGED:
+        with pytest.raises(CompileError, match=match):
+            compile_file(ir)
+        return
+    from lazy_compiler_b200.recognize_frag import recognise_fragment_tile
+    from lazy_compiler_b200.ir import load_package
+    pkg = load_package(ir)
     with pytest.raises(CompileError, match=match):
-        compile_file(ir)
+        recognise_fragment_tile(pkg, pkg.body[0])
+    pw_vm.assert_faithful(ir)
 
 
 def test_second_store_of_paired_program_is_required(tmp_path):
@@ -98,5 +114,51 @@ def test_second_store_of_paired_program_is_required(tmp_path):
     dst = tmp_path / "tensor_shared_paired"
     shutil.copytree(golden("tensor_shared_paired"), dst)
     next(dst.glob("*.ir.json")).write_text(text[:start] + text[end:])
-    with pytest.raises(CompileError, match="exactly once"):
+    with pytest.raises(CompileError, match="exactly once|shared memory"):
         compile_file(next(dst.glob("*.ir.json")))
+
+
+FRAGMENT_ALGEBRA = sorted(p.name for p in golden("").iterdir()
+                          if p.name.startswith("fragment_") and p.name != "fragment_attention_tile_f16")
+
+
+@pytest.mark.parametrize("name", FRAGMENT_ALGEBRA)
+def test_fragment_algebra_lane_program_matches_golden(name):
+    """FragmentApply / FragmentRowReduce programs (examples/phase9/fragments) as lane programs."""
+    plan = compile_file(golden_ir(name))
+    assert plan["op"] == "pointwise" and plan["params"]["lanes"]
+    meta = golden_meta(name)
+    arrays = {a["name"]: O.input_array(a, 0) for a in meta["kernels"][0]["args"] if not a.get("output")}
+    got = pw_vm.run(plan["params"]["program"], arrays)
+    with np.load(golden(name) / "expected.npz") as z:
+        for key in z.files:
+            row = O.compare(got[key].reshape(z[key].shape), z[key], meta["rtol"], meta["atol"])
+            assert row["pass"], row
+
+
+@pytest.mark.parametrize("name", FRAGMENT_ALGEBRA + [f for f in FIXTURES if f not in (
+    "tensor_cp_async_shared",) and not f.startswith("tensor_shared")])
+def test_fragment_oracle_matches_golden(name):
+    from oracle import fragment_ir
+    meta = golden_meta(name)
+    arrays = {a["name"]: O.input_array(a, 0) for a in meta["kernels"][0]["args"] if not a.get("output")}
+    got = fragment_ir.evaluate(golden_ir(name), arrays)
+    with np.load(golden(name) / "expected.npz") as z:
+        for key in z.files:
+            assert O.compare(got[key].reshape(z[key].shape), z[key], meta["rtol"], meta["atol"])["pass"]
+
+
+@pytest.mark.parametrize("name", [f for f in FIXTURES if f != "tensor_cp_async_shared"
+                                  and not f.startswith("tensor_shared")])
+def test_tensor_fixtures_as_lane_programs(name):
+    """The lane compiler also reproduces the tensor-core fixtures (gathers, MMA, repack, store variants)."""
+    from lazy_compiler_b200.fragment_vm import compile_fragment_lanes
+    from lazy_compiler_b200.ir import load_package
+    pkg = load_package(golden_ir(name))
+    plan = compile_fragment_lanes(pkg, pkg.body[0]).to_json()
+    meta = golden_meta(name)
+    arrays = {a["name"]: O.input_array(a, 0) for a in meta["kernels"][0]["args"] if not a.get("output")}
+    got = pw_vm.run(plan["params"]["program"], arrays)
+    with np.load(golden(name) / "expected.npz") as z:
+        for key in z.files:
+            assert O.compare(got[key].reshape(z[key].shape), z[key], meta["rtol"], meta["atol"])["pass"]

@@ -37,7 +37,11 @@ PACKAGES = ["p00_scalar_add", "p01_vector_add", "p02_scale_shift", "p03_relu_mul
             # GELU regression packages run as register programs (several typed results per element)
             "activation_gelu_f32", "activation_gelu_f16", "activation_gelu_bf16", "activation_gelu_special",
             "activation_gelu_tanh_f32", "activation_gelu_tanh_f16", "activation_gelu_tanh_bf16",
-            "activation_gelu_tanh_special"]
+            "activation_gelu_tanh_special",
+            # fragment algebra as lane programs (FragmentApply, ordered FragmentRowReduce, MMA)
+            "fragment_family_row_softmax", "fragment_masked_gmem_post", "fragment_mma_row_normalization",
+            "fragment_row_add_ordered", "fragment_row_maximum_ordered", "fragment_row_minimum_ordered",
+            "fragment_row_multiply_ordered"]
 
 
 def torch_():
