@@ -402,6 +402,7 @@ enum lc_pw_op {
   LC_PW_PACK_BF16X2 = 78,
   LC_PW_MMA_F16 = 79,
   LC_PW_MMA_BF16 = 80,
+  LC_PW_FREM = 81,
   LC_PW_NUM_OPS
 };
 

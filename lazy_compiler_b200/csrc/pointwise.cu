@@ -206,6 +206,17 @@ __global__ void __launch_bounds__(256) pointwise_kernel(const __grid_constant__ 
           r[dst + 3] = d3;
           continue;
         }
+        case LC_PW_FREM: {  // floor remainder (fmodf is exact; one rounded add adjusts the sign)
+          const float xv = f(A), yv = f(B);
+          float rv = __int_as_float(0x7fc00000);
+          if (isfinite(xv) && !isnan(yv) && yv != 0.0f) {
+            rv = fmodf(xv, yv);
+            if (rv != 0.0f && ((xv < 0.0f) != (yv < 0.0f))) rv = __fadd_rn(rv, yv);
+            if (rv == 0.0f) rv = copysignf(0.0f, yv);
+          }
+          out = w(rv);
+          break;
+        }
         default: out = 0u; break;  // the host admits no other opcode
       }
       r[dst] = out;

@@ -50,6 +50,7 @@ OPCODES = [
     # lane programs (fragment algebra, lazy_compiler_b200/fragment_vm.py)
     "COORD", "LDX_F32", "LDX_F16", "LDX_BF16", "LDX_S32", "STX_F32", "STX_F16", "STX_BF16", "STX_S32",
     "STX_ADD_F32", "SHFL_XOR", "PACK_F16X2", "PACK_BF16X2", "MMA_F16", "MMA_BF16",
+    "FREM",
 ]
 OP = {name: i for i, name in enumerate(OPCODES)}
 
@@ -307,6 +308,11 @@ class PointwiseCompiler:
             return self.int_operation(name, args, binary)
         if name == "floor_divide":
             return self.emit("FFLOOR", "f32", self.binary("/", *args))
+        if name in ("mod", "remainder"):
+            # floor remainder: the exact |x| mod |y| with x's sign, then y added
+            # when the signs differ, a zero result taking y's sign; NaN for a
+            # non-finite x, a NaN or zero y (ptx_backend.py:840-892)
+            return self.emit("FREM", "f32", *args)
         if name in binary:
             return self.binary(binary[name], *args, dt="f32")
         x = args[0]

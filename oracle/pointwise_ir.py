@@ -188,6 +188,14 @@ class PointwiseOracle:
                 "sigmoid": lambda: 1.0 / (1.0 + np.exp(-x64)), "silu": lambda: x64 / (1.0 + np.exp(-x64)),
                 "fma": lambda: x64 * args[1].a.astype(np.float64) + args[2].a.astype(np.float64),
             }
+            if name in ("mod", "remainder"):
+                y = args[1].a
+                r = np.fmod(x, y)                                   # exact, sign of x
+                adjust = (r != 0) & ((x < 0) != (y < 0))
+                r = np.where(adjust, (r + y).astype(np.float32), r)
+                r = np.where(r == 0, np.copysign(np.float32(0), y), r)
+                r = np.where(~np.isfinite(x) | np.isnan(y) | (y == 0), np.float32(np.nan), r)
+                return V(r.astype(np.float32), "f32")
             if name in one:
                 return V(np.asarray(one[name]()).astype(np.float32), "f32")
             if name in ("gelu", "gelu_tanh"):

@@ -40,6 +40,8 @@ PACKAGES = [
     "examples/phase9/gelu/activation_gelu_special", "examples/phase9/gelu/activation_gelu_tanh_special",
     # fragment attention tile (tests/test_fragment_rows.py)
     "examples/phase9/fragments/fragment_attention_tile_f16",
+    # pointwise floor remainder of f32 bit patterns (phase8 remainder packages)
+    "examples/phase8/remainder/floating_f32_mod", "examples/phase8/remainder/floating_f32_remainder",
     # fragment algebra: FragmentApply operand kinds, ordered row folds, MMA + row normalisation
     *[f"examples/phase9/fragments/{name}" for name in (
         "fragment_family_row_softmax", "fragment_masked_gmem_post", "fragment_mma_row_normalization",

@@ -207,6 +207,13 @@ def run(prog: dict, arrays: dict) -> dict:
                     lo = _bf16(fa).view(np.uint32) >> 16
                     hi = _bf16(fb).view(np.uint32) >> 16
                 out = (hi << 16) | lo
+            elif name == "FREM":
+                r0 = np.fmod(fa, fb)
+                adjust = (r0 != 0) & ((fa < 0) != (fb < 0))
+                r0 = np.where(adjust, (r0 + fb).astype(np.float32), r0)
+                r0 = np.where(r0 == 0, np.copysign(np.float32(0), fb), r0)
+                r0 = np.where(~np.isfinite(fa) | np.isnan(fb) | (fb == 0), np.float32(np.nan), r0)
+                out = _w(r0.astype(np.float32))
             elif name in ("MMA_F16", "MMA_BF16"):
                 _mma(r, dst, a, b, c, name == "MMA_BF16", n)
                 continue

@@ -69,6 +69,13 @@ EXPECTED = {
     # GELU regression packages (examples/phase9/gelu): several typed results per element
     **{f"activation_gelu{t}_{k}": ("pointwise", {"out": "out", "points": 37 if k == "special" else 273})
        for t in ("", "_tanh") for k in ("f32", "f16", "bf16", "special")},
+    "floating_f32_mod": ("pointwise", {"out": "out", "points": 528}),
+    "floating_f32_remainder": ("pointwise", {"out": "out", "points": 528}),
+    # fragment algebra (examples/phase9/fragments) as lane programs
+    **{name: ("pointwise", {"points": 32, "lanes": True}) for name in (
+        "fragment_family_row_softmax", "fragment_masked_gmem_post", "fragment_mma_row_normalization",
+        "fragment_row_add_ordered", "fragment_row_maximum_ordered", "fragment_row_minimum_ordered",
+        "fragment_row_multiply_ordered")},
 }
 
 

@@ -41,7 +41,9 @@ PACKAGES = ["p00_scalar_add", "p01_vector_add", "p02_scale_shift", "p03_relu_mul
             # fragment algebra as lane programs (FragmentApply, ordered FragmentRowReduce, MMA)
             "fragment_family_row_softmax", "fragment_masked_gmem_post", "fragment_mma_row_normalization",
             "fragment_row_add_ordered", "fragment_row_maximum_ordered", "fragment_row_minimum_ordered",
-            "fragment_row_multiply_ordered"]
+            "fragment_row_multiply_ordered",
+            # f32 floor remainder of raw bit patterns (specials included), bit-exact
+            "floating_f32_mod", "floating_f32_remainder"]
 
 
 def torch_():

@@ -18,7 +18,8 @@ from lazy_compiler_b200.pointwise import OPCODES
 from oracle import expressions as O
 from oracle import pointwise_ir
 
-ACTIVATION = sorted(p.name for p in golden("").iterdir() if p.name.startswith("activation_"))
+ACTIVATION = sorted(p.name for p in golden("").iterdir()
+                    if p.name.startswith("activation_") or p.name.startswith("floating_f32_"))
 
 
 def inputs_of(meta, offset=0):
