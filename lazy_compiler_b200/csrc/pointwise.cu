@@ -47,6 +47,188 @@ __device__ __forceinline__ float round_bf16(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
+// Runs operations [begin, end) of a program for one point with coordinates
+// x.  `states` (read by STATE) and `partials` / `state_op` (folded by ACC)
+// belong to row programs; a pointwise program has neither.
+__device__ __forceinline__ void exec_range(const lc_pw_program &g, void *const *buffers, const int64_t *x,
+                                           uint32_t *r, int begin, int end, const float *states,
+                                           float *partials, const int32_t *state_op) {
+  for (int pc = begin; pc < end; ++pc) {
+    const uint32_t w0 = g.code[pc][0], w1 = g.code[pc][1];
+    const int op = w0 & 255, dst = (w0 >> 8) & 255;
+    const uint32_t A = r[(w0 >> 16) & 255], B = r[w0 >> 24], C = r[w1 & 255];
+    const int aux = (int)(w1 >> 8);
+    const int32_t ia = (int32_t)A, ib = (int32_t)B;
+    uint32_t out = 0;
+    if (op >= LC_PW_LD_F32 && op <= LC_PW_ST_S32) {
+      const lc_pw_form &fm = g.forms[aux];
+      int64_t at = fm.base;
+      for (int d = 0; d < g.n_axes; ++d) at += fm.coef[d] * x[d];
+      void *base = buffers[fm.buffer];
+      switch (op) {
+        case LC_PW_LD_F32: out = static_cast<const uint32_t *>(base)[at]; break;
+        case LC_PW_LD_F16: out = w(__half2float(static_cast<const __half *>(base)[at])); break;
+        case LC_PW_LD_BF16: out = w(__bfloat162float(static_cast<const __nv_bfloat16 *>(base)[at])); break;
+        case LC_PW_LD_S32: out = static_cast<const uint32_t *>(base)[at]; break;
+        case LC_PW_ST_F32: static_cast<uint32_t *>(base)[at] = A; continue;
+        case LC_PW_ST_F16: static_cast<__half *>(base)[at] = __float2half_rn(f(A)); continue;
+        case LC_PW_ST_BF16: static_cast<__nv_bfloat16 *>(base)[at] = __float2bfloat16_rn(f(A)); continue;
+        default: static_cast<uint32_t *>(base)[at] = A; continue;  // LC_PW_ST_S32
+      }
+      r[dst] = out;
+      continue;
+    }
+    switch (op) {
+      case LC_PW_MOV: out = A; break;
+      case LC_PW_CONST: out = g.consts[aux]; break;
+      case LC_PW_FADD: out = w(__fadd_rn(f(A), f(B))); break;
+      case LC_PW_FSUB: out = w(__fsub_rn(f(A), f(B))); break;
+      case LC_PW_FMUL: out = w(__fmul_rn(f(A), f(B))); break;
+      case LC_PW_FDIV: out = w(__fdiv_rn(f(A), f(B))); break;
+      case LC_PW_FFMA: out = w(__fmaf_rn(f(A), f(B), f(C))); break;
+      case LC_PW_FNEG: out = A ^ 0x80000000u; break;
+      case LC_PW_FABS: out = A & 0x7fffffffu; break;
+      case LC_PW_FMAX: out = w(fmaxf(f(A), f(B))); break;
+      case LC_PW_FMIN: out = w(fminf(f(A), f(B))); break;
+      case LC_PW_FSQRT: out = w(__fsqrt_rn(f(A))); break;
+      case LC_PW_FFLOOR: out = w(floorf(f(A))); break;
+      case LC_PW_FCEIL: out = w(ceilf(f(A))); break;
+      case LC_PW_FTRUNC: out = w(truncf(f(A))); break;
+      case LC_PW_FRINT: out = w(rintf(f(A))); break;
+      case LC_PW_FEX2: out = w(ex2_approx(f(A))); break;
+      case LC_PW_FLG2: out = w(lg2_approx(f(A))); break;
+      case LC_PW_FSIN: out = w(sin_approx(f(A))); break;
+      case LC_PW_FCOS: out = w(cos_approx(f(A))); break;
+      case LC_PW_FCOPYSIGN: out = (B & 0x7fffffffu) | (A & 0x80000000u); break;  // |b| with a's sign
+      case LC_PW_RND_F16: out = w(round_half(f(A))); break;
+      case LC_PW_RND_BF16: out = w(round_bf16(f(A))); break;
+      case LC_PW_F2I: out = (uint32_t)__float2int_rz(f(A)); break;
+      case LC_PW_I2F: out = w(__int2float_rn(ia)); break;
+      case LC_PW_I2H: out = w(__half2float(__int2half_rn(ia))); break;
+      case LC_PW_I2BF: out = w(__bfloat162float(__int2bfloat16_rn(ia))); break;
+      case LC_PW_IADD: out = A + B; break;
+      case LC_PW_ISUB: out = A - B; break;
+      case LC_PW_IMUL: out = A * B; break;
+      case LC_PW_IDIV:  // integer division by zero has no defined result; it yields 0 here
+        out = ib == 0 ? 0u : (ib == -1 ? 0u - A : (uint32_t)(ia / ib));
+        break;
+      case LC_PW_IREM: out = (ib == 0 || ib == -1) ? (ib == 0 ? A : 0u) : (uint32_t)(ia % ib); break;
+      case LC_PW_ISHL: out = B >= 32u ? 0u : A << B; break;  // shl.b32 clamps the count
+      case LC_PW_ISHR: out = (uint32_t)(ia >> (B >= 32u ? 31u : B)); break;
+      case LC_PW_IAND: out = A & B; break;
+      case LC_PW_IOR: out = A | B; break;
+      case LC_PW_IXOR: out = A ^ B; break;
+      case LC_PW_INOT: out = ~A; break;
+      case LC_PW_INEG: out = 0u - A; break;
+      case LC_PW_IABS: out = ia < 0 ? 0u - A : A; break;
+      case LC_PW_IMAX: out = (uint32_t)max(ia, ib); break;
+      case LC_PW_IMIN: out = (uint32_t)min(ia, ib); break;
+      case LC_PW_IPOPC: out = (uint32_t)__popc(A); break;
+      case LC_PW_FEQ: out = f(A) == f(B); break;
+      case LC_PW_FNE: out = !(f(A) == f(B)); break;  // unordered: true when either is NaN
+      case LC_PW_FLT: out = f(A) < f(B); break;
+      case LC_PW_FLE: out = f(A) <= f(B); break;
+      case LC_PW_FGT: out = f(A) > f(B); break;
+      case LC_PW_FGE: out = f(A) >= f(B); break;
+      case LC_PW_IEQ: out = ia == ib; break;
+      case LC_PW_INE: out = ia != ib; break;
+      case LC_PW_ILT: out = ia < ib; break;
+      case LC_PW_ILE: out = ia <= ib; break;
+      case LC_PW_IGT: out = ia > ib; break;
+      case LC_PW_IGE: out = ia >= ib; break;
+      case LC_PW_PAND: out = (A != 0u) & (B != 0u); break;
+      case LC_PW_POR: out = (A != 0u) | (B != 0u); break;
+      case LC_PW_SEL: out = A != 0u ? B : C; break;
+      case LC_PW_COORD: out = (uint32_t)x[aux]; break;
+      case LC_PW_LDX_F32: case LC_PW_LDX_F16: case LC_PW_LDX_BF16: case LC_PW_LDX_S32: {
+        const int64_t size = g.sizes[aux];
+        int64_t at = (int64_t)ia;
+        at = at < 0 ? 0 : (at >= size ? size - 1 : at);  // clamped: a load never leaves its buffer
+        const void *base = buffers[aux];
+        if (op == LC_PW_LDX_F16) out = w(__half2float(static_cast<const __half *>(base)[at]));
+        else if (op == LC_PW_LDX_BF16) out = w(__bfloat162float(static_cast<const __nv_bfloat16 *>(base)[at]));
+        else out = static_cast<const uint32_t *>(base)[at];
+        break;
+      }
+      case LC_PW_STX_F32: case LC_PW_STX_F16: case LC_PW_STX_BF16: case LC_PW_STX_S32:
+      case LC_PW_STX_ADD_F32: {
+        const int64_t at = (int64_t)ia;
+        if (C != 0u && at >= 0 && at < g.sizes[aux]) {
+          void *base = buffers[aux];
+          if (op == LC_PW_STX_F16) static_cast<__half *>(base)[at] = __float2half_rn(f(B));
+          else if (op == LC_PW_STX_BF16) static_cast<__nv_bfloat16 *>(base)[at] = __float2bfloat16_rn(f(B));
+          else if (op == LC_PW_STX_ADD_F32) atomicAdd(static_cast<float *>(base) + at, f(B));
+          else static_cast<uint32_t *>(base)[at] = B;
+        }
+        continue;
+      }
+      case LC_PW_SHFL_XOR:
+        __syncwarp();
+        out = __shfl_xor_sync(0xffffffffu, A, aux);
+        break;
+      case LC_PW_PACK_F16X2: {
+        __half2 h = __floats2half2_rn(f(A), f(B));
+        out = *reinterpret_cast<uint32_t *>(&h);
+        break;
+      }
+      case LC_PW_PACK_BF16X2: {
+        __nv_bfloat162 h = __floats2bfloat162_rn(f(A), f(B));
+        out = *reinterpret_cast<uint32_t *>(&h);
+        break;
+      }
+      case LC_PW_MMA_F16: case LC_PW_MMA_BF16: {
+        const int ra = (w0 >> 16) & 255, rb = w0 >> 24, rc = w1 & 255;
+        uint32_t d0, d1, d2, d3;
+        __syncwarp();
+        if (op == LC_PW_MMA_F16)
+          asm volatile(
+              "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7},"
+              " {%8, %9}, {%10, %11, %12, %13};"
+              : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+              : "r"(r[ra]), "r"(r[ra + 1]), "r"(r[ra + 2]), "r"(r[ra + 3]), "r"(r[rb]), "r"(r[rb + 1]),
+                "r"(r[rc]), "r"(r[rc + 1]), "r"(r[rc + 2]), "r"(r[rc + 3]));
+        else
+          asm volatile(
+              "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7},"
+              " {%8, %9}, {%10, %11, %12, %13};"
+              : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+              : "r"(r[ra]), "r"(r[ra + 1]), "r"(r[ra + 2]), "r"(r[ra + 3]), "r"(r[rb]), "r"(r[rb + 1]),
+                "r"(r[rc]), "r"(r[rc + 1]), "r"(r[rc + 2]), "r"(r[rc + 3]));
+        r[dst] = d0;
+        r[dst + 1] = d1;
+        r[dst + 2] = d2;
+        r[dst + 3] = d3;
+        continue;
+      }
+      case LC_PW_FREM: {  // floor remainder (fmodf is exact; one rounded add adjusts the sign)
+        const float xv = f(A), yv = f(B);
+        float rv = __int_as_float(0x7fc00000);
+        if (isfinite(xv) && !isnan(yv) && yv != 0.0f) {
+          rv = fmodf(xv, yv);
+          if (rv != 0.0f && ((xv < 0.0f) != (yv < 0.0f))) rv = __fadd_rn(rv, yv);
+          if (rv == 0.0f) rv = copysignf(0.0f, yv);
+        }
+        out = w(rv);
+        break;
+      }
+      case LC_PW_STATE: out = w(states[aux]); break;
+      case LC_PW_ACC: {  // fold register a into the thread's partial of state aux
+        const float v = f(A);
+        float &acc = partials[aux];
+        switch (state_op[aux]) {
+          case LC_RP_ADD: acc = __fadd_rn(acc, v); break;
+          case LC_RP_MUL: acc = __fmul_rn(acc, v); break;
+          case LC_RP_MAX: acc = fmaxf(acc, v); break;
+          default: acc = fminf(acc, v); break;
+        }
+        continue;
+      }
+      default: out = 0u; break;  // the host admits no other opcode
+    }
+    r[dst] = out;
+  }
+}
+
 __global__ void __launch_bounds__(256) pointwise_kernel(const __grid_constant__ PointwiseArgs p) {
   uint32_t r[LC_PW_MAX_REGS];
   for (int i = 0; i < LC_PW_MAX_REGS; ++i) r[i] = 0u;
@@ -59,167 +241,69 @@ __global__ void __launch_bounds__(256) pointwise_kernel(const __grid_constant__ 
       x[d] = rest % g.extents[d];
       rest /= g.extents[d];
     }
-    for (int pc = 0; pc < g.n_code; ++pc) {
-      const uint32_t w0 = g.code[pc][0], w1 = g.code[pc][1];
-      const int op = w0 & 255, dst = (w0 >> 8) & 255;
-      const uint32_t A = r[(w0 >> 16) & 255], B = r[w0 >> 24], C = r[w1 & 255];
-      const int aux = (int)(w1 >> 8);
-      const int32_t ia = (int32_t)A, ib = (int32_t)B;
-      uint32_t out = 0;
-      if (op >= LC_PW_LD_F32 && op <= LC_PW_ST_S32) {
-        const lc_pw_form &fm = g.forms[aux];
-        int64_t at = fm.base;
-        for (int d = 0; d < g.n_axes; ++d) at += fm.coef[d] * x[d];
-        void *base = p.buffers[fm.buffer];
-        switch (op) {
-          case LC_PW_LD_F32: out = static_cast<const uint32_t *>(base)[at]; break;
-          case LC_PW_LD_F16: out = w(__half2float(static_cast<const __half *>(base)[at])); break;
-          case LC_PW_LD_BF16: out = w(__bfloat162float(static_cast<const __nv_bfloat16 *>(base)[at])); break;
-          case LC_PW_LD_S32: out = static_cast<const uint32_t *>(base)[at]; break;
-          case LC_PW_ST_F32: static_cast<uint32_t *>(base)[at] = A; continue;
-          case LC_PW_ST_F16: static_cast<__half *>(base)[at] = __float2half_rn(f(A)); continue;
-          case LC_PW_ST_BF16: static_cast<__nv_bfloat16 *>(base)[at] = __float2bfloat16_rn(f(A)); continue;
-          default: static_cast<uint32_t *>(base)[at] = A; continue;  // LC_PW_ST_S32
-        }
-        r[dst] = out;
-        continue;
+    exec_range(g, p.buffers, x, r, 0, g.n_code, nullptr, nullptr, nullptr);
+  }
+}
+
+struct RowProgArgs {
+  lc_pw_program prog;
+  lc_rp_layout lay;
+  void *buffers[LC_PW_MAX_BUFFERS];
+};
+
+__device__ __forceinline__ float rp_identity(int op) {
+  return op == LC_RP_ADD ? 0.0f : op == LC_RP_MUL ? 1.0f : op == LC_RP_MAX ? -INFINITY : INFINITY;
+}
+__device__ __forceinline__ float rp_fold(int op, float a, float b) {
+  return op == LC_RP_ADD ? __fadd_rn(a, b) : op == LC_RP_MUL ? __fmul_rn(a, b)
+       : op == LC_RP_MAX ? fmaxf(a, b) : fminf(a, b);
+}
+
+// One CTA per row (grid-stride over rows); every pass strides the CTA's
+// threads over the row's columns, then combines its states: a butterfly in
+// each warp, then warp 0's lane 0 folds the warps in order, so the result
+// does not depend on timing.  All barriers are reached by every thread.
+__global__ void __launch_bounds__(256) rowprog_kernel(const __grid_constant__ RowProgArgs p) {
+  __shared__ float warp_part[8][LC_RP_MAX_STATES];
+  __shared__ float combined[LC_RP_MAX_STATES];
+  uint32_t r[LC_PW_MAX_REGS];
+  for (int i = 0; i < LC_PW_MAX_REGS; ++i) r[i] = 0u;
+  float states[LC_RP_MAX_STATES], partials[LC_RP_MAX_STATES];
+  for (int k = 0; k < LC_RP_MAX_STATES; ++k) states[k] = partials[k] = 0.0f;
+  const lc_pw_program &g = p.prog;
+  const lc_rp_layout &lay = p.lay;
+  const int64_t rows = g.extents[0], cols = g.extents[1];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    for (int pass = 0; pass < lay.n_passes; ++pass) {
+      for (int k = 0; k < lay.n_states; ++k)
+        if (lay.state_pass[k] == pass) partials[k] = rp_identity(lay.state_op[k]);
+      for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+        const int64_t x[LC_PW_MAX_AXES] = {row, c, 0, 0};
+        exec_range(g, p.buffers, x, r, lay.begin[pass], lay.end[pass], states, partials, lay.state_op);
       }
-      switch (op) {
-        case LC_PW_MOV: out = A; break;
-        case LC_PW_CONST: out = g.consts[aux]; break;
-        case LC_PW_FADD: out = w(__fadd_rn(f(A), f(B))); break;
-        case LC_PW_FSUB: out = w(__fsub_rn(f(A), f(B))); break;
-        case LC_PW_FMUL: out = w(__fmul_rn(f(A), f(B))); break;
-        case LC_PW_FDIV: out = w(__fdiv_rn(f(A), f(B))); break;
-        case LC_PW_FFMA: out = w(__fmaf_rn(f(A), f(B), f(C))); break;
-        case LC_PW_FNEG: out = A ^ 0x80000000u; break;
-        case LC_PW_FABS: out = A & 0x7fffffffu; break;
-        case LC_PW_FMAX: out = w(fmaxf(f(A), f(B))); break;
-        case LC_PW_FMIN: out = w(fminf(f(A), f(B))); break;
-        case LC_PW_FSQRT: out = w(__fsqrt_rn(f(A))); break;
-        case LC_PW_FFLOOR: out = w(floorf(f(A))); break;
-        case LC_PW_FCEIL: out = w(ceilf(f(A))); break;
-        case LC_PW_FTRUNC: out = w(truncf(f(A))); break;
-        case LC_PW_FRINT: out = w(rintf(f(A))); break;
-        case LC_PW_FEX2: out = w(ex2_approx(f(A))); break;
-        case LC_PW_FLG2: out = w(lg2_approx(f(A))); break;
-        case LC_PW_FSIN: out = w(sin_approx(f(A))); break;
-        case LC_PW_FCOS: out = w(cos_approx(f(A))); break;
-        case LC_PW_FCOPYSIGN: out = (B & 0x7fffffffu) | (A & 0x80000000u); break;  // |b| with a's sign
-        case LC_PW_RND_F16: out = w(round_half(f(A))); break;
-        case LC_PW_RND_BF16: out = w(round_bf16(f(A))); break;
-        case LC_PW_F2I: out = (uint32_t)__float2int_rz(f(A)); break;
-        case LC_PW_I2F: out = w(__int2float_rn(ia)); break;
-        case LC_PW_I2H: out = w(__half2float(__int2half_rn(ia))); break;
-        case LC_PW_I2BF: out = w(__bfloat162float(__int2bfloat16_rn(ia))); break;
-        case LC_PW_IADD: out = A + B; break;
-        case LC_PW_ISUB: out = A - B; break;
-        case LC_PW_IMUL: out = A * B; break;
-        case LC_PW_IDIV:  // integer division by zero has no defined result; it yields 0 here
-          out = ib == 0 ? 0u : (ib == -1 ? 0u - A : (uint32_t)(ia / ib));
-          break;
-        case LC_PW_IREM: out = (ib == 0 || ib == -1) ? (ib == 0 ? A : 0u) : (uint32_t)(ia % ib); break;
-        case LC_PW_ISHL: out = B >= 32u ? 0u : A << B; break;  // shl.b32 clamps the count
-        case LC_PW_ISHR: out = (uint32_t)(ia >> (B >= 32u ? 31u : B)); break;
-        case LC_PW_IAND: out = A & B; break;
-        case LC_PW_IOR: out = A | B; break;
-        case LC_PW_IXOR: out = A ^ B; break;
-        case LC_PW_INOT: out = ~A; break;
-        case LC_PW_INEG: out = 0u - A; break;
-        case LC_PW_IABS: out = ia < 0 ? 0u - A : A; break;
-        case LC_PW_IMAX: out = (uint32_t)max(ia, ib); break;
-        case LC_PW_IMIN: out = (uint32_t)min(ia, ib); break;
-        case LC_PW_IPOPC: out = (uint32_t)__popc(A); break;
-        case LC_PW_FEQ: out = f(A) == f(B); break;
-        case LC_PW_FNE: out = !(f(A) == f(B)); break;  // unordered: true when either is NaN
-        case LC_PW_FLT: out = f(A) < f(B); break;
-        case LC_PW_FLE: out = f(A) <= f(B); break;
-        case LC_PW_FGT: out = f(A) > f(B); break;
-        case LC_PW_FGE: out = f(A) >= f(B); break;
-        case LC_PW_IEQ: out = ia == ib; break;
-        case LC_PW_INE: out = ia != ib; break;
-        case LC_PW_ILT: out = ia < ib; break;
-        case LC_PW_ILE: out = ia <= ib; break;
-        case LC_PW_IGT: out = ia > ib; break;
-        case LC_PW_IGE: out = ia >= ib; break;
-        case LC_PW_PAND: out = (A != 0u) & (B != 0u); break;
-        case LC_PW_POR: out = (A != 0u) | (B != 0u); break;
-        case LC_PW_SEL: out = A != 0u ? B : C; break;
-        case LC_PW_COORD: out = (uint32_t)x[aux]; break;
-        case LC_PW_LDX_F32: case LC_PW_LDX_F16: case LC_PW_LDX_BF16: case LC_PW_LDX_S32: {
-          const int64_t size = g.sizes[aux];
-          int64_t at = (int64_t)ia;
-          at = at < 0 ? 0 : (at >= size ? size - 1 : at);  // clamped: a load never leaves its buffer
-          const void *base = p.buffers[aux];
-          if (op == LC_PW_LDX_F16) out = w(__half2float(static_cast<const __half *>(base)[at]));
-          else if (op == LC_PW_LDX_BF16) out = w(__bfloat162float(static_cast<const __nv_bfloat16 *>(base)[at]));
-          else out = static_cast<const uint32_t *>(base)[at];
-          break;
-        }
-        case LC_PW_STX_F32: case LC_PW_STX_F16: case LC_PW_STX_BF16: case LC_PW_STX_S32:
-        case LC_PW_STX_ADD_F32: {
-          const int64_t at = (int64_t)ia;
-          if (C != 0u && at >= 0 && at < g.sizes[aux]) {
-            void *base = p.buffers[aux];
-            if (op == LC_PW_STX_F16) static_cast<__half *>(base)[at] = __float2half_rn(f(B));
-            else if (op == LC_PW_STX_BF16) static_cast<__nv_bfloat16 *>(base)[at] = __float2bfloat16_rn(f(B));
-            else if (op == LC_PW_STX_ADD_F32) atomicAdd(static_cast<float *>(base) + at, f(B));
-            else static_cast<uint32_t *>(base)[at] = B;
-          }
-          continue;
-        }
-        case LC_PW_SHFL_XOR:
-          __syncwarp();
-          out = __shfl_xor_sync(0xffffffffu, A, aux);
-          break;
-        case LC_PW_PACK_F16X2: {
-          __half2 h = __floats2half2_rn(f(A), f(B));
-          out = *reinterpret_cast<uint32_t *>(&h);
-          break;
-        }
-        case LC_PW_PACK_BF16X2: {
-          __nv_bfloat162 h = __floats2bfloat162_rn(f(A), f(B));
-          out = *reinterpret_cast<uint32_t *>(&h);
-          break;
-        }
-        case LC_PW_MMA_F16: case LC_PW_MMA_BF16: {
-          const int ra = (w0 >> 16) & 255, rb = w0 >> 24, rc = w1 & 255;
-          uint32_t d0, d1, d2, d3;
-          __syncwarp();
-          if (op == LC_PW_MMA_F16)
-            asm volatile(
-                "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7},"
-                " {%8, %9}, {%10, %11, %12, %13};"
-                : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
-                : "r"(r[ra]), "r"(r[ra + 1]), "r"(r[ra + 2]), "r"(r[ra + 3]), "r"(r[rb]), "r"(r[rb + 1]),
-                  "r"(r[rc]), "r"(r[rc + 1]), "r"(r[rc + 2]), "r"(r[rc + 3]));
-          else
-            asm volatile(
-                "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7},"
-                " {%8, %9}, {%10, %11, %12, %13};"
-                : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
-                : "r"(r[ra]), "r"(r[ra + 1]), "r"(r[ra + 2]), "r"(r[ra + 3]), "r"(r[rb]), "r"(r[rb + 1]),
-                  "r"(r[rc]), "r"(r[rc + 1]), "r"(r[rc + 2]), "r"(r[rc + 3]));
-          r[dst] = d0;
-          r[dst + 1] = d1;
-          r[dst + 2] = d2;
-          r[dst + 3] = d3;
-          continue;
-        }
-        case LC_PW_FREM: {  // floor remainder (fmodf is exact; one rounded add adjusts the sign)
-          const float xv = f(A), yv = f(B);
-          float rv = __int_as_float(0x7fc00000);
-          if (isfinite(xv) && !isnan(yv) && yv != 0.0f) {
-            rv = fmodf(xv, yv);
-            if (rv != 0.0f && ((xv < 0.0f) != (yv < 0.0f))) rv = __fadd_rn(rv, yv);
-            if (rv == 0.0f) rv = copysignf(0.0f, yv);
-          }
-          out = w(rv);
-          break;
-        }
-        default: out = 0u; break;  // the host admits no other opcode
+      for (int k = 0; k < lay.n_states; ++k) {
+        if (lay.state_pass[k] != pass) continue;
+        float v = partials[k];
+        for (int o = 16; o > 0; o >>= 1) v = rp_fold(lay.state_op[k], v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) warp_part[warp][k] = v;
       }
-      r[dst] = out;
+      __syncthreads();
+      if (threadIdx.x == 0)
+        for (int k = 0; k < lay.n_states; ++k) {
+          if (lay.state_pass[k] != pass) continue;
+          float v = warp_part[0][k];
+          for (int w2 = 1; w2 < nwarps; ++w2) v = rp_fold(lay.state_op[k], v, warp_part[w2][k]);
+          combined[k] = v;
+        }
+      __syncthreads();
+      for (int k = 0; k < lay.n_states; ++k)
+        if (lay.state_pass[k] == pass) states[k] = combined[k];
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+      const int64_t x[LC_PW_MAX_AXES] = {row, 0, 0, 0};
+      exec_range(g, p.buffers, x, r, lay.final_begin, lay.final_end, states, partials, lay.state_op);
     }
   }
 }
@@ -246,30 +330,33 @@ int storage_of(int op) {
 }  // namespace
 }  // namespace lc
 
-extern "C" int lc_pointwise(const lc_pw_program *program, void *const *buffers, void *stream) {
-  using namespace lc;
-  if (!program || !buffers) return fail(LC_ERR_INVALID, "lc_pointwise: null program or buffers");
+namespace lc {
+namespace {
+// Checks a program before any launch; returns LC_OK or the failure, and the point count.
+int validate_program(const char *name, const lc_pw_program *program, void *const *buffers, bool row_program,
+                     int64_t *points_out) {
+  if (!program || !buffers) return fail(LC_ERR_INVALID, "%s: null program or buffers", name);
   const lc_pw_program &g = *program;
   if (g.n_code < 0 || g.n_code > LC_PW_MAX_CODE || g.n_consts < 0 || g.n_consts > LC_PW_MAX_CONST ||
       g.n_forms < 0 || g.n_forms > LC_PW_MAX_FORMS || g.n_buffers < 1 || g.n_buffers > LC_PW_MAX_BUFFERS ||
       g.n_axes < 1 || g.n_axes > LC_PW_MAX_AXES || g.n_regs < 1 || g.n_regs > LC_PW_MAX_REGS)
-    return fail(LC_ERR_INVALID, "lc_pointwise: program counts out of range");
+    return fail(LC_ERR_INVALID, "%s: program counts out of range", name);
   int64_t points = 1;
   for (int d = 0; d < g.n_axes; ++d) {
     if (g.extents[d] < 1 || g.extents[d] > ((int64_t)1 << 40))
-      return fail(LC_ERR_INVALID, "lc_pointwise: bad extent");
+      return fail(LC_ERR_INVALID, "%s: bad extent", name);
     points *= g.extents[d];
-    if (points > ((int64_t)1 << 40)) return fail(LC_ERR_INVALID, "lc_pointwise: tile too large");
+    if (points > ((int64_t)1 << 40)) return fail(LC_ERR_INVALID, "%s: tile too large", name);
   }
   for (int i = 0; i < g.n_buffers; ++i)
-    if (!buffers[i] || g.sizes[i] < 1) return fail(LC_ERR_INVALID, "lc_pointwise: buffer slot %d", i);
+    if (!buffers[i] || g.sizes[i] < 1) return fail(LC_ERR_INVALID, "%s: buffer slot %d", name, i);
   for (int i = 0; i < g.n_forms; ++i) {
     const lc_pw_form &fm = g.forms[i];
     bool sane = fm.base >= -((int64_t)1 << 50) && fm.base <= ((int64_t)1 << 50);
     for (int d = 0; d < g.n_axes; ++d)
       sane = sane && fm.coef[d] >= -((int64_t)1 << 40) && fm.coef[d] <= ((int64_t)1 << 40);
     if (!sane || fm.buffer < 0 || fm.buffer >= g.n_buffers || !form_in_range(g, fm))
-      return fail(LC_ERR_INVALID, "lc_pointwise: form %d leaves its buffer", i);
+      return fail(LC_ERR_INVALID, "%s: form %d leaves its buffer", name, i);
   }
   bool lockstep = false;
   for (int pc = 0; pc < g.n_code; ++pc) {
@@ -277,27 +364,43 @@ extern "C" int lc_pointwise(const lc_pw_program *program, void *const *buffers, 
     const int op = w0 & 255;
     const uint32_t dst = (w0 >> 8) & 255, a = (w0 >> 16) & 255, b = w0 >> 24, c = w1 & 255;
     const int aux = (int)(w1 >> 8);
-    if (op >= LC_PW_NUM_OPS) return fail(LC_ERR_INVALID, "lc_pointwise: bad opcode at %d", pc);
+    if (op >= LC_PW_NUM_OPS) return fail(LC_ERR_INVALID, "%s: bad opcode at %d", name, pc);
     if ((int)dst >= g.n_regs || (int)a >= g.n_regs || (int)b >= g.n_regs || (int)c >= g.n_regs)
-      return fail(LC_ERR_INVALID, "lc_pointwise: register out of range at %d", pc);
+      return fail(LC_ERR_INVALID, "%s: register out of range at %d", name, pc);
     if (op == LC_PW_CONST && aux >= g.n_consts)
-      return fail(LC_ERR_INVALID, "lc_pointwise: constant out of range at %d", pc);
+      return fail(LC_ERR_INVALID, "%s: constant out of range at %d", name, pc);
     if (op == LC_PW_COORD && aux >= g.n_axes)
-      return fail(LC_ERR_INVALID, "lc_pointwise: coordinate out of range at %d", pc);
+      return fail(LC_ERR_INVALID, "%s: coordinate out of range at %d", name, pc);
     if (op >= LC_PW_LDX_F32 && op <= LC_PW_STX_ADD_F32 && aux >= g.n_buffers)
-      return fail(LC_ERR_INVALID, "lc_pointwise: buffer slot out of range at %d", pc);
+      return fail(LC_ERR_INVALID, "%s: buffer slot out of range at %d", name, pc);
     if (op == LC_PW_SHFL_XOR && (aux < 1 || aux > 31))
-      return fail(LC_ERR_INVALID, "lc_pointwise: shuffle distance out of range at %d", pc);
+      return fail(LC_ERR_INVALID, "%s: shuffle distance out of range at %d", name, pc);
     if ((op == LC_PW_MMA_F16 || op == LC_PW_MMA_BF16) &&
         ((int)dst + 3 >= g.n_regs || (int)a + 3 >= g.n_regs || (int)b + 1 >= g.n_regs || (int)c + 3 >= g.n_regs))
-      return fail(LC_ERR_INVALID, "lc_pointwise: MMA register tuple out of range at %d", pc);
+      return fail(LC_ERR_INVALID, "%s: MMA register tuple out of range at %d", name, pc);
     if (op == LC_PW_SHFL_XOR || op == LC_PW_MMA_F16 || op == LC_PW_MMA_BF16) lockstep = true;
+    if ((op == LC_PW_STATE || op == LC_PW_ACC) &&
+        (!row_program || aux >= LC_RP_MAX_STATES || (op == LC_PW_ACC && (int)a >= g.n_regs)))
+      return fail(LC_ERR_INVALID, "%s: state operation outside a row program at %d", name, pc);
     if (op >= LC_PW_LD_F32 && op <= LC_PW_ST_S32 &&
         (aux >= g.n_forms || g.forms[aux].dtype != storage_of(op)))
-      return fail(LC_ERR_INVALID, "lc_pointwise: form or storage type mismatch at %d", pc);
+      return fail(LC_ERR_INVALID, "%s: form or storage type mismatch at %d", name, pc);
   }
+  if (row_program && (lockstep || g.n_axes != 2))
+    return fail(LC_ERR_INVALID, "%s: a row program runs over (row, column) without warp operations", name);
   if (lockstep && points % 32 != 0)
-    return fail(LC_ERR_INVALID, "lc_pointwise: a program that shuffles or multiplies needs whole warps of points");
+    return fail(LC_ERR_INVALID, "%s: a program that shuffles or multiplies needs whole warps of points", name);
+  *points_out = points;
+  return LC_OK;
+}
+}  // namespace
+}  // namespace lc
+
+extern "C" int lc_pointwise(const lc_pw_program *program, void *const *buffers, void *stream) {
+  using namespace lc;
+  int64_t points = 0;
+  if (int rc = validate_program("lc_pointwise", program, buffers, false, &points)) return rc;
+  const lc_pw_program &g = *program;
   PointwiseArgs args;
   args.prog = g;
   for (int i = 0; i < LC_PW_MAX_BUFFERS; ++i) args.buffers[i] = i < g.n_buffers ? buffers[i] : nullptr;
@@ -307,4 +410,39 @@ extern "C" int lc_pointwise(const lc_pw_program *program, void *const *buffers, 
   if (blocks > cap) blocks = cap;
   pointwise_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(args);
   return check_launch("lc_pointwise");
+}
+
+extern "C" int lc_rowprog(const lc_pw_program *program, const lc_rp_layout *layout, void *const *buffers,
+                          void *stream) {
+  using namespace lc;
+  int64_t points = 0;
+  if (int rc = validate_program("lc_rowprog", program, buffers, true, &points)) return rc;
+  if (!layout) return fail(LC_ERR_INVALID, "lc_rowprog: null layout");
+  const lc_rp_layout &lay = *layout;
+  const int n_code = program->n_code;
+  if (lay.n_passes < 0 || lay.n_passes > LC_RP_MAX_PASSES || lay.n_states < 0 || lay.n_states > LC_RP_MAX_STATES)
+    return fail(LC_ERR_INVALID, "lc_rowprog: layout counts out of range");
+  auto range_ok = [&](int b, int e) { return 0 <= b && b <= e && e <= n_code; };
+  for (int i = 0; i < lay.n_passes; ++i)
+    if (!range_ok(lay.begin[i], lay.end[i])) return fail(LC_ERR_INVALID, "lc_rowprog: pass %d range", i);
+  if (!range_ok(lay.final_begin, lay.final_end)) return fail(LC_ERR_INVALID, "lc_rowprog: final range");
+  for (int k = 0; k < lay.n_states; ++k)
+    if (lay.state_op[k] < LC_RP_ADD || lay.state_op[k] > LC_RP_MIN || lay.state_pass[k] < 0 ||
+        lay.state_pass[k] >= lay.n_passes)
+      return fail(LC_ERR_INVALID, "lc_rowprog: state %d", k);
+  for (int pc = 0; pc < n_code; ++pc) {
+    const int op = program->code[pc][0] & 255, aux = (int)(program->code[pc][1] >> 8);
+    if ((op == LC_PW_STATE || op == LC_PW_ACC) && aux >= lay.n_states)
+      return fail(LC_ERR_INVALID, "lc_rowprog: state index out of range at %d", pc);
+  }
+  RowProgArgs args;
+  args.prog = *program;
+  args.lay = lay;
+  for (int i = 0; i < LC_PW_MAX_BUFFERS; ++i) args.buffers[i] = i < program->n_buffers ? buffers[i] : nullptr;
+  const int64_t rows = program->extents[0];
+  int64_t blocks = rows;
+  const int64_t cap = (int64_t)sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  rowprog_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(args);
+  return check_launch("lc_rowprog");
 }

@@ -51,6 +51,8 @@ OPCODES = [
     "COORD", "LDX_F32", "LDX_F16", "LDX_BF16", "LDX_S32", "STX_F32", "STX_F16", "STX_BF16", "STX_S32",
     "STX_ADD_F32", "SHFL_XOR", "PACK_F16X2", "PACK_BF16X2", "MMA_F16", "MMA_BF16",
     "FREM",
+    # row programs (lazy_compiler_b200/rowprog.py)
+    "STATE", "ACC",
 ]
 OP = {name: i for i, name in enumerate(OPCODES)}
 

@@ -632,6 +632,8 @@ def _recognise_reduction(pkg: KernelPackage, tile: Node, ev: _Eval) -> Plan:
                 w = ev.writes[0]
                 if w["values"][0] != ("red", acc) or w["index"] != (_aff({row_name: 1}),):
                     raise CompileError("row dot product must write acc[row]")
+                if _numel(pkg.buffers[w["buffer"]].shape) != rows:
+                    raise CompileError("row dot output does not have one element per row")
                 for b_ in (xb, yb, w["buffer"]):
                     if pkg.buffers[b_].dtype != "f32":
                         raise CompileError("row dot products are f32")
@@ -650,9 +652,11 @@ def _recognise_reduction(pkg: KernelPackage, tile: Node, ev: _Eval) -> Plan:
         if two_d:
             if value != ("red", acc) or w["index"] != (_aff({row_name: 1}),):
                 raise CompileError("row reduction must write acc[row]")
+            if _numel(pkg.buffers[out].shape) != rows:
+                raise CompileError("row reduction output does not have one element per row")
             return _plan(pkg, "rowsum_f32", "lc_rowsum_f32", {"x": x, "out": out},
                          {"rows": rows, "cols": cols}, {"io": "f32"})
-        if w["index"] not in ((), (_aff({}),)):
+        if w["index"] not in ((), (_aff({}),)) or _numel(pkg.buffers[out].shape) != 1:
             raise CompileError("whole-array reduction writes a scalar")
         if value == ("red", acc):
             return _plan(pkg, "sum_f32", "lc_sum_f32", {"x": x, "out": out}, {"n": cols}, {"io": "f32"})
@@ -900,7 +904,14 @@ def recognise(pkg: KernelPackage) -> Plan:
             return f32.recognise_attention(pkg, tile, ev)
         if f32.looks_like_dot(ev):
             return f32.recognise_dot_gemm(pkg, tile, ev)
-        return _recognise_reduction(pkg, tile, ev)
+        try:
+            return _recognise_reduction(pkg, tile, ev)
+        except CompileError as err:
+            from .rowprog import compile_rowprog
+            try:
+                return compile_rowprog(pkg, tile, ev)
+            except CompileError as err2:
+                raise CompileError(f"{err}; as a row program: {err2}") from err2
     if ev.loops:
         raise CompileError("loops without a reduction are not a supported operation class")
     try:

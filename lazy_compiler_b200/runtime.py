@@ -52,6 +52,7 @@ SIGNATURES = {
     "lc_gemm_ex": [_INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_path": [_INT, _INT, _P, _P, _I64, _I64, _I64],
     "lc_pointwise": [_P, _P, _P],
+    "lc_rowprog": [_P, _P, _P, _P],
     "lc_gemm_mixed": [_INT, _INT, _INT, _INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_chain": [_INT, _INT, _INT, _INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P],
     "lc_attention_f32": [_INT, _INT, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
@@ -101,6 +102,28 @@ def pw_program(prog: dict) -> PwProgram:
         for d, c in enumerate(f["coef"]):
             g.forms[i].coef[d] = c
     return g
+
+
+RP_MAX_PASSES, RP_MAX_STATES = 4, 8
+
+
+class RpLayout(ctypes.Structure):
+    _fields_ = [("n_passes", ctypes.c_int32), ("n_states", ctypes.c_int32), ("final_begin", ctypes.c_int32),
+                ("final_end", ctypes.c_int32), ("begin", ctypes.c_int32 * RP_MAX_PASSES),
+                ("end", ctypes.c_int32 * RP_MAX_PASSES), ("state_op", ctypes.c_int32 * RP_MAX_STATES),
+                ("state_pass", ctypes.c_int32 * RP_MAX_STATES)]
+
+
+def rp_layout(layout: dict) -> RpLayout:
+    """The C struct of a row program's layout (a plan's ``params["layout"]``)."""
+    lay = RpLayout()
+    lay.n_passes, lay.n_states = len(layout["passes"]), len(layout["state_op"])
+    lay.final_begin, lay.final_end = layout["final"]
+    for i, (b, e) in enumerate(layout["passes"]):
+        lay.begin[i], lay.end[i] = b, e
+    for k, (op, ps) in enumerate(zip(layout["state_op"], layout["state_pass"])):
+        lay.state_op[k], lay.state_pass[k] = op, ps
+    return lay
 
 
 _lock = threading.Lock()
@@ -199,6 +222,11 @@ def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
         ptrs = (ctypes.c_void_p * PW_MAX_BUFFERS)(*[int(pointers[b[f"buf{i}"]]) for i in range(len(prog["buffers"]))])
         g = pw_program(prog)
         call("lc_pointwise", ctypes.c_void_p(ctypes.addressof(g)), ptrs, s)
+    elif op == "rowprog":
+        prog = p["program"]
+        ptrs = (ctypes.c_void_p * PW_MAX_BUFFERS)(*[int(pointers[b[f"buf{i}"]]) for i in range(len(prog["buffers"]))])
+        g, lay = pw_program(prog), rp_layout(p["layout"])
+        call("lc_rowprog", ctypes.c_void_p(ctypes.addressof(g)), ctypes.c_void_p(ctypes.addressof(lay)), ptrs, s)
     elif op == "gemm_mixed":
         d = plan["dtypes"]
         bias = ptr("bias") if "bias" in b else ctypes.c_void_p(0)

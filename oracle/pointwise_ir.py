@@ -291,7 +291,8 @@ class PointwiseOracle:
                                                            if t != "s32" else -1,
                                                            np.float32 if t != "s32" else np.int32))
                 for lane, name in enumerate(s.values):
-                    out[self.flat(s.output, s.index) + lane] = conv(self.env[name], t).a
+                    vals = conv(self.env[name], t).a
+                    out[np.broadcast_to(self.flat(s.output, s.index) + lane, vals.shape)] = vals
             else:
                 raise ValueError(f"oracle: statement {k}")
         return {k: v.reshape(tuple(self.pkg.buffers[k].shape) or (1,)) for k, v in self.out.items()}

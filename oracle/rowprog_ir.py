@@ -1,0 +1,98 @@
+"""CPU oracle of reduction / fused row Tiles — TEST INFRASTRUCTURE ONLY.
+
+Evaluates a Tile of [row,] cooperating threads directly from its IR with
+numpy, by what the schedule computes rather than how: the threads of a
+StridedLoop pass collectively visit every column of the row, so a pass's
+body is evaluated on all (row, column) points at once, each Accum folds its
+per-element values over the columns (float64, then rounded to f32), and
+after the pass the accumulator is that row's fold — the WarpShuffle /
+TreeHalve combines only distribute it.  A write guarded to the first thread
+is a per-row write.  Scalar statements follow oracle/pointwise_ir.py's rules.
+Accumulators with an explicit base (coupled online states) are not covered.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from oracle.pointwise_ir import PointwiseOracle, V, conv
+
+_FOLD = {"add": np.sum, "sum": np.sum, "multiply": np.prod, "mul": np.prod,
+         "maximum": np.max, "max": np.max, "minimum": np.min, "min": np.min}
+_IDENTITY = {"add": 0.0, "sum": 0.0, "multiply": 1.0, "mul": 1.0, "maximum": -np.inf, "max": -np.inf,
+             "minimum": np.inf, "min": np.inf}
+
+
+class RowOracle(PointwiseOracle):
+    def __init__(self, pkg, tile, arrays):
+        axes = [(a.name, int(a.extent.value)) for a in tile.axes]
+        self.pkg = pkg
+        self.co = axes[-1][0]
+        self.row = axes[0][0] if len(axes) == 2 else "__row"
+        self.rows = axes[0][1] if len(axes) == 2 else 1
+        self.arrays = {k: np.asarray(v).ravel() for k, v in arrays.items()}
+        self.env = {}
+        self.out = {}
+        self.set_domain(None, 1)
+
+    def set_domain(self, col, cols):
+        r = np.repeat(np.arange(self.rows, dtype=np.int64), cols)
+        self.coord = {self.row: r, self.co: np.zeros_like(r)}
+        if col is not None:
+            self.coord[col] = np.tile(np.arange(cols, dtype=np.int64), self.rows)
+        self.cols = cols
+
+    def widen(self, cols):
+        """Row values seen inside a pass: one copy per column."""
+        for k, v in list(self.env.items()):
+            if isinstance(v, V) and v.a.shape == (self.rows,):
+                self.env[k] = V(np.repeat(v.a, cols), v.t)
+
+    def narrow(self, cols):
+        for k, v in list(self.env.items()):
+            if isinstance(v, V) and v.a.shape == (self.rows * cols,):
+                self.env[k] = V(v.a.reshape(self.rows, cols)[:, 0], v.t)
+
+    def run_rows(self, body) -> dict:
+        for s in body:
+            k = s.kind
+            if k in ("StridedLoop", "Loop"):
+                cols = int(s.axis.extent.value)
+                folds = {}
+                self.widen(cols)
+                self.set_domain(s.axis.name, cols)
+                for inner in s.body:
+                    if inner.kind == "Accum":
+                        opname = inner.op.name if hasattr(inner.op, "name") else str(inner.op)
+                        value = conv(self.env[inner.value] if isinstance(inner.value, str)
+                                     else self.expr(inner.value), "f32").a
+                        folds[inner.name] = (opname, value)
+                    else:
+                        self.run_rows([inner])
+                self.narrow(cols)
+                self.set_domain(None, 1)
+                for name, (opname, value) in folds.items():
+                    with np.errstate(all="ignore"):
+                        r = _FOLD[opname](value.reshape(self.rows, cols).astype(np.float64), axis=1)
+                    self.env[name] = V(r.astype(np.float32), "f32")
+            elif k == "Init":
+                self.env[s.name] = V(np.full(self.rows, _IDENTITY.get(str(s.identity), float(s.identity)),
+                                             np.float32), "f32")
+            elif k in ("WarpShuffle", "TreeHalve", "Smem", "Sync"):
+                continue
+            elif k == "Cond":
+                self.run_rows(s.body)
+            elif k == "Write" and s.output not in self.pkg.buffers:
+                continue                    # shared-memory staging of partials
+            else:
+                self.run([s])
+        return {k: v.reshape(tuple(self.pkg.buffers[k].shape) or (1,)) for k, v in self.out.items()}
+
+
+def evaluate(ir_path, arrays: dict) -> dict:
+    """Outputs of the reduction package at ``ir_path`` on named input arrays."""
+    from lazy_compiler_b200.ir import load_package
+    pkg = load_package(ir_path)
+    (tile,) = pkg.body
+    return RowOracle(pkg, tile, arrays).run_rows(tile.body)

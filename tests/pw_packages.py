@@ -210,3 +210,123 @@ def chain_package(folder: Path, n: int = 4096) -> Path:
             "kernels": kernels}
     (folder / "meta.json").write_text(json.dumps(meta))
     return folder
+
+
+# ---------------------------------------------------------------- reduction / fused row programs
+
+def row_package(folder: Path, name: str, rows: int, cols: int, inputs: dict, output: tuple, pass1: list,
+                accs: list, final: list = (), final_writes: list = (), pass2: list = (), block: int = 128,
+                rtol=1e-5, atol=1e-6) -> Path:
+    """A Tile [a0 rows, a1_co block] with the reference's reduction schedule:
+    pass 1 strides the block over the row (body + Accum of each (acc, op, value)),
+    a warp butterfly and a shared-memory tree combine each accumulator, then an
+    optional second pass (loop variable a2) and per-row statements guarded to
+    thread 0."""
+    row, co = var("a0"), var("a1_co")
+    f32 = dt("f32")
+    loop1 = list(pass1) + [f"Accum(name='{a}', value='{v}', op=ElementwiseImpl('{o}'), dtype={f32}, axes=('a1',), base=None)"
+                          for a, o, v in accs]
+    states = tuple(a for a, _, _ in accs)
+    combine = ", ".join(f"Assign(name='{a}', op=ElementwiseImpl('{o}'), args=('{a}', '{a}__o'), dtype=None)"
+                        for a, o, _ in accs)
+    st = ", ".join(repr(a) for a in states) + ","
+    stb = ", ".join(repr(a + "__o") for a in states) + ","
+    warps = block // 32
+    body = [f"StridedLoop(axis=Axis(name='a1', extent=Dim({cols}), window=None), start={co}, step={lit(block)}, "
+            f"body=({', '.join(loop1)},), unroll=False, end=None, seed=True)",
+            f"WarpShuffle(state=({st}), state_b=({stb}), combine_states=({combine},), length=32, dtype={f32})"]
+    for a in states:
+        body.append(f"Smem(name='{a}_smem', extents=({warps},), dtype='float', align=0)")
+    body.append(f"Cond(cond=BinaryExpr(op='==', left=Var(name='lane'), right={lit(0)}), body=(" +
+                ", ".join(f"Write(output='{a}_smem', index=(Var(name='warp'),), values=('{a}',), value_dtype={f32}, "
+                          "atomic=False, swizzle='NONE')" for a in states) + ",), else_body=())")
+    body.append("Sync(barrier_id=0, count=None, warp=False)")
+    smem = ", ".join(repr(a + "_smem") for a in states) + ","
+    body.append(f"TreeHalve(bufs=({smem}), state=({st}), state_b=({stb}), combine_states=({combine},), "
+                f"length={warps}, tid_var='warp', dtype={f32}, barrier_id=0, barrier_count=None, inner=None)")
+    if pass2:
+        body.append(f"StridedLoop(axis=Axis(name='a2', extent=Dim({cols}), window=None), start={co}, "
+                    f"step={lit(block)}, body=({', '.join(pass2)},), unroll=False, end=None, seed=True)")
+    if final or final_writes:
+        body.append(f"Cond(cond=BinaryExpr(op='==', left={co}, right={lit(0)}), body=(" +
+                    ", ".join(list(final) + list(final_writes)) + ",), else_body=())")
+    folder.mkdir(parents=True, exist_ok=True)
+    tile = (f"Tile(axes=(Axis(name='a0', extent=Dim({rows}), window=None), Axis(name='a1_co', extent=Dim({block}), "
+            f"window=None)), body=({', '.join(body)},), block_threads={block}, aux_threads=0, raster_axes=None, "
+            "raster_group=None, raster_orient='m')")
+    out_name, out_shape, out_dtype = output
+    entry = f"k_{name}"
+    nodes = {n: {"op": "InputOp", "op_fields": {}, "inputs": [], "outputs": [{"name": n, "shape": list(s), "dtype": d}]}
+             for n, (s, d) in inputs.items()}
+    nodes[out_name] = {"op": "KernelOp", "op_fields": {"body": [tile], "name": entry, "zero_delegated": [],
+                                                       "serial": []},
+                       "inputs": list(inputs), "outputs": [{"name": out_name, "shape": list(out_shape),
+                                                            "dtype": out_dtype}]}
+    (folder / f"{entry}.ir.json").write_text(json.dumps({"inputs": list(inputs), "outputs": [out_name], "nodes": nodes}))
+    args = [{"name": n, "dtype": d, "shape": list(s), "seed": i} for i, (n, (s, d)) in enumerate(inputs.items())]
+    args.append({"name": out_name, "dtype": out_dtype, "shape": list(out_shape), "output": True})
+    meta = {"id": name, "rtol": rtol, "atol": atol, "graph_inputs": list(inputs), "graph_outputs": [out_name],
+            "kernels": [{"node": out_name, "entry": entry, "arg_order": list(inputs) + [out_name], "grid": [rows, 1, 1],
+                         "block": [block, 1, 1], "smem_bytes": 0, "zero_outputs": [], "args": args, "final": True}]}
+    (folder / "meta.json").write_text(json.dumps(meta))
+    return folder / f"{entry}.ir.json"
+
+
+def _x(cols):
+    return load("xv", "x", [var("a0"), var("a1")], "f32")
+
+
+def _row_max(folder):
+    return row_package(folder, "row_max", 37, 300, {"x": ((37, 300), "f32")}, ("out", (37,), "f32"),
+                       [_x(300)], [("m", "maximum", "xv")], final_writes=[write("out", [var("a0")], ["m"], "f32")])
+
+
+def _row_min_abs(folder):
+    return row_package(folder, "row_min_abs", 16, 1000, {"x": ((16, 1000), "f32")}, ("out", (16,), "f32"),
+                       [_x(1000), assign("ax", "abs", ["xv"], "f32")], [("m", "minimum", "ax")],
+                       final_writes=[write("out", [var("a0")], ["m"], "f32")])
+
+
+def _variance(folder):
+    cols = 777
+    return row_package(folder, "variance", 24, cols, {"x": ((24, cols), "f32")}, ("out", (24,), "f32"),
+                       [_x(cols), assign("sq", "multiply", ["xv", "xv"], "f32")],
+                       [("s1", "add", "xv"), ("s2", "add", "sq")],
+                       final=[let("inv", lit(1.0 / cols, "f32"), "f32"), assign("mean", "multiply", ["s1", "inv"], "f32"),
+                              assign("msq", "multiply", ["s2", "inv"], "f32"),
+                              assign("m2", "multiply", ["mean", "mean"], "f32"),
+                              assign("var", "subtract", ["msq", "m2"], "f32")],
+                       final_writes=[write("out", [var("a0")], ["var"], "f32")], rtol=1e-4, atol=1e-5)
+
+
+def _log_sum_exp(folder):
+    """Row max, then a second pass is a write; here the sum of exp(x - 0) and its log."""
+    cols = 512
+    return row_package(folder, "log_sum_exp", 20, cols, {"x": ((20, cols), "f32")}, ("out", (20,), "f32"),
+                       [_x(cols), assign("e", "exp", ["xv"], "f32")], [("s", "add", "e")],
+                       final=[assign("l", "log", ["s"], "f32")],
+                       final_writes=[write("out", [var("a0")], ["l"], "f32")], rtol=1e-5, atol=1e-5)
+
+
+def _center_rows(folder):
+    """Two passes: the row mean, then every element minus it, scaled by w[col]."""
+    cols = 640
+    a0, a2 = var("a0"), var("a2")
+    return row_package(folder, "center_rows", 33, cols, {"x": ((33, cols), "f32"), "w": ((cols,), "f32")},
+                       ("out", (33, cols), "f32"), [_x(cols)], [("s", "add", "xv")],
+                       pass2=[load("x2", "x", [a0, a2], "f32"), load("wv", "w", [a2], "f32"),
+                              let("inv", lit(1.0 / cols, "f32"), "f32"), assign("mean", "multiply", ["s", "inv"], "f32"),
+                              assign("d", "subtract", ["x2", "mean"], "f32"), assign("o", "multiply", ["d", "wv"], "f32"),
+                              write("out", [a0, a2], ["o"], "f32")], rtol=1e-5, atol=1e-5)
+
+
+def _half_row_sum(folder):
+    """f16 storage: the row sum of x (f16) written as f16."""
+    cols = 256
+    return row_package(folder, "half_row_sum", 40, cols, {"x": ((40, cols), "f16")}, ("out", (40,), "f16"),
+                       [load("xv", "x", [var("a0"), var("a1")], "f16")], [("s", "add", "xv")],
+                       final_writes=[write("out", [var("a0")], ["s"], "f16")], rtol=2e-3, atol=2e-3)
+
+
+ROW_SYNTHETIC = {"row_max": _row_max, "row_min_abs": _row_min_abs, "variance": _variance,
+                 "log_sum_exp": _log_sum_exp, "center_rows": _center_rows, "half_row_sum": _half_row_sum}

@@ -68,7 +68,7 @@ def _mma(r, dst, a, b, c, bf16, n):
             r[dst + e][sl] = _w(D[g[sl] + (8 if e >= 2 else 0), 2 * t[sl] + (e & 1)])
 
 
-def run(prog: dict, arrays: dict) -> dict:
+def run(prog: dict, arrays: dict, _states=None, _acc=None) -> dict:
     ext = prog["extents"]
     grids = np.meshgrid(*[np.arange(e, dtype=np.int64) for e in ext], indexing="ij")
     coords = [g.ravel() for g in grids]
@@ -207,6 +207,11 @@ def run(prog: dict, arrays: dict) -> dict:
                     lo = _bf16(fa).view(np.uint32) >> 16
                     hi = _bf16(fb).view(np.uint32) >> 16
                 out = (hi << 16) | lo
+            elif name == "STATE":
+                out = _w(_states[aux])
+            elif name == "ACC":
+                _acc[aux] = _f(A).copy()
+                continue
             elif name == "FREM":
                 r0 = np.fmod(fa, fb)
                 adjust = (r0 != 0) & ((fa < 0) != (fb < 0))
@@ -241,3 +246,37 @@ def assert_faithful(ir, rtol=1e-5, atol=1e-6):
     for key, value in ref.items():
         np.testing.assert_allclose(got[key].reshape(value.shape), value, rtol=rtol, atol=atol, equal_nan=True)
     return plan
+
+
+def run_rows(prog: dict, layout: dict, arrays: dict) -> dict:
+    """A row program on the CPU: each pass over every (row, column) point at
+    once, its ACC values folded per row (float64, then f32), the final
+    operations once per row."""
+    rows, cols = prog["extents"]
+    states = {}
+    outs = {}
+    fold = {0: np.sum, 1: np.prod, 2: np.max, 3: np.min}
+    for p, (b, e) in enumerate(layout["passes"]):
+        sub = dict(prog, code=prog["code"][b:e])
+        acc = {}
+        part = _run(sub, arrays, rows, cols, states, acc, outs)
+        for k, values in acc.items():
+            with np.errstate(all="ignore"):
+                states[k] = fold[layout["state_op"][k]](values.reshape(rows, cols).astype(np.float64), axis=1)
+    b, e = layout["final"]
+    sub = dict(prog, code=prog["code"][b:e])
+    _run(sub, arrays, rows, 1, states, {}, outs)
+    return outs
+
+
+def _run(prog, arrays, rows, cols, states, acc, outs):
+    """One range of a row program over rows x cols points (STATE broadcasts per row)."""
+    expanded = {k: np.repeat(np.asarray(v, np.float32), cols) for k, v in states.items()}
+    p2 = dict(prog, extents=[rows, cols])
+    res = run(p2, arrays, _states=expanded, _acc=acc)
+    for k, v in res.items():
+        if k in outs:
+            mask = ~np.isnan(v) if v.dtype.kind == "f" else np.ones(v.shape, bool)
+            outs[k][mask] = v[mask]
+        else:
+            outs[k] = v

@@ -1,0 +1,99 @@
+"""Row programs (reductions and fused row operations of any op mix), on CPU:
+the compiled program, interpreted in numpy (tests/pw_vm.py), against the
+row oracle (oracle/rowprog_ir.py) and the reference's golden vectors; the
+checks that keep a body from being compiled as something it is not."""
+import json
+
+import numpy as np
+import pytest
+
+import pw_packages as W
+import pw_vm
+from conftest import golden, golden_ir, golden_meta
+from lazy_compiler_b200.compiler import compile_file
+from lazy_compiler_b200.ir import CompileError, load_package, static_extent
+from lazy_compiler_b200.recognize import _Eval
+from lazy_compiler_b200.rowprog import compile_rowprog
+from oracle import expressions as O
+from oracle import rowprog_ir
+
+REDUCTIONS = ["r01_array_sum", "r02_big_sum", "r03_mean", "r04_row_sum", "f01_rmsnorm", "f03_l2norm",
+              "phase9_gelu_row_dot"]
+
+
+def inputs_of(meta, offset=0):
+    return {a["name"]: O.input_array(a, offset) for a in meta["kernels"][0]["args"] if not a.get("output")}
+
+
+def forced_plan(ir):
+    pkg = load_package(ir)
+    tile = pkg.body[0]
+    ev = _Eval(pkg)
+    ev.smem = set()
+    for a in tile.axes:
+        ev.axes[a.name] = static_extent(a.extent)
+    ev.run(tile.body)
+    return compile_rowprog(pkg, tile, ev).to_json()
+
+
+@pytest.mark.parametrize("name", REDUCTIONS)
+def test_row_oracle_matches_golden(name):
+    meta = golden_meta(name)
+    got = rowprog_ir.evaluate(golden_ir(name), inputs_of(meta))
+    with np.load(golden(name) / "expected.npz") as z:
+        for key in z.files:
+            assert O.compare(got[key].reshape(z[key].shape), z[key], meta["rtol"], meta["atol"])["pass"]
+
+
+@pytest.mark.parametrize("name", REDUCTIONS)
+def test_fixed_reductions_as_row_programs(name):
+    """The fixed classes, forced through the row compiler, reproduce their golden vectors."""
+    plan = forced_plan(golden_ir(name))
+    meta = golden_meta(name)
+    got = pw_vm.run_rows(plan["params"]["program"], plan["params"]["layout"], inputs_of(meta))
+    with np.load(golden(name) / "expected.npz") as z:
+        for key in z.files:
+            assert O.compare(got[key].reshape(z[key].shape), z[key], meta["rtol"], meta["atol"])["pass"]
+
+
+@pytest.mark.parametrize("name", sorted(W.ROW_SYNTHETIC))
+def test_synthetic_row_program_matches_oracle(name, tmp_path):
+    ir = W.ROW_SYNTHETIC[name](tmp_path / name)
+    plan = compile_file(ir)
+    assert plan["op"] == "rowprog"
+    meta = json.loads((tmp_path / name / "meta.json").read_text())
+    for offset in (0, 2):
+        arrays = inputs_of(meta, offset)
+        ref = rowprog_ir.evaluate(ir, arrays)
+        got = pw_vm.run_rows(plan["params"]["program"], plan["params"]["layout"], arrays)
+        for key, value in ref.items():
+            assert O.compare(got[key].reshape(value.shape), value, meta["rtol"], meta["atol"])["pass"]
+
+
+def test_combine_must_use_the_accumulator_operation(tmp_path):
+    """Accumulating by max but combining partial results by add is not a row max."""
+    ir = W.ROW_SYNTHETIC["row_max"](tmp_path / "m")
+    text = ir.read_text()
+    ir.write_text(text.replace("Assign(name='m', op=ElementwiseImpl('maximum')",
+                               "Assign(name='m', op=ElementwiseImpl('add')"))
+    with pytest.raises(CompileError, match="combines by add"):
+        compile_file(ir)
+
+
+def test_state_read_before_its_pass_combines_is_rejected(tmp_path):
+    """A per-element write in the accumulating pass cannot see the row's total."""
+    ir = W.row_package(tmp_path / "early", "early", 8, 64, {"x": ((8, 64), "f32")}, ("out", (8, 64), "f32"),
+                       [W.load("xv", "x", [W.var("a0"), W.var("a1")], "f32"),
+                        W.assign("y", "multiply", ["xv", "s"], "f32"),
+                        W.write("out", [W.var("a0"), W.var("a1")], ["y"], "f32")],
+                       [("s", "add", "xv")])
+    with pytest.raises(CompileError):
+        compile_file(ir)
+
+
+def test_row_outputs_must_be_covered(tmp_path):
+    ir = W.row_package(tmp_path / "hole", "hole", 8, 64, {"x": ((8, 64), "f32")}, ("out", (9,), "f32"),
+                       [W.load("xv", "x", [W.var("a0"), W.var("a1")], "f32")], [("s", "add", "xv")],
+                       final_writes=[W.write("out", [W.var("a0")], ["s"], "f32")])
+    with pytest.raises(CompileError, match="cover"):
+        compile_file(ir)
