@@ -404,7 +404,9 @@ enum lc_pw_op {
   LC_PW_MMA_BF16 = 80,
   LC_PW_FREM = 81,
   LC_PW_STATE = 82,
-  LC_PW_ACC = 83,
+  LC_PW_PARTIAL = 83,
+  LC_PW_PARTNER = 84,
+  LC_PW_SETP = 85,
   LC_PW_NUM_OPS
 };
 
@@ -435,25 +437,27 @@ int lc_pointwise(const lc_pw_program *program, void *const *buffers, void *strea
 /* ---------------------------------------------------------------- row programs
  * Reductions and fused row operations (the reference's categories 2 and 4:
  * StridedLoop passes over a row with Accum, WarpShuffle / TreeHalve combines,
- * a guarded per-row write or a second, writing pass; ptx_backend.py:1496-1744)
- * as register programs over the point space (row, column) = extents[0..1]:
- * one CTA per row runs each pass's operations [begin, end) for every column
- * it strides over; ACC folds a register into the thread's partial of a state
- * (LC_RP_* per state), after the pass the partials of its states combine
- * across the CTA in a fixed order and STATE reads them in later passes; the
- * final operations run once per row (column 0) on one thread. */
+ * a guarded per-row write or a further, writing pass; ptx_backend.py:1496-1744)
+ * as register programs over the point space (row, column) = extents[0..1].
+ * One CTA per row.  For each pass, every thread seeds its partials of the
+ * pass's states (state_init), runs operations [begin, end) for each column it
+ * strides over (PARTIAL reads and SETP writes its running partial, so an
+ * Accum with or without a base is an explicit update), then the partials
+ * combine: warp_begin..warp_end runs at each level of a lane butterfly
+ * (PARTNER reads the other lane's partial), tree_begin..tree_end folds the
+ * warps' results in order on one thread.  Later passes and the final
+ * operations (once per row, column 0, one thread) read combined states with
+ * STATE. */
 #define LC_RP_MAX_PASSES 4
 #define LC_RP_MAX_STATES 8
-#define LC_RP_ADD 0
-#define LC_RP_MUL 1
-#define LC_RP_MAX 2
-#define LC_RP_MIN 3
 
 typedef struct {
   int32_t n_passes, n_states, final_begin, final_end;
   int32_t begin[LC_RP_MAX_PASSES], end[LC_RP_MAX_PASSES];
-  int32_t state_op[LC_RP_MAX_STATES];   /* LC_RP_ADD / MUL / MAX / MIN */
-  int32_t state_pass[LC_RP_MAX_STATES]; /* the pass that accumulates the state */
+  int32_t warp_begin[LC_RP_MAX_PASSES], warp_end[LC_RP_MAX_PASSES];
+  int32_t tree_begin[LC_RP_MAX_PASSES], tree_end[LC_RP_MAX_PASSES];
+  uint32_t state_init[LC_RP_MAX_STATES]; /* f32 bits of each state's seed */
+  int32_t state_pass[LC_RP_MAX_STATES];  /* the pass that accumulates the state */
 } lc_rp_layout;
 
 /* Runs a row program (validated like lc_pointwise, plus its layout). */

@@ -48,11 +48,11 @@ __device__ __forceinline__ float round_bf16(float x) {
 }
 
 // Runs operations [begin, end) of a program for one point with coordinates
-// x.  `states` (read by STATE) and `partials` / `state_op` (folded by ACC)
-// belong to row programs; a pointwise program has neither.
+// x.  `states` (STATE), `partials` (PARTIAL, SETP) and `partners` (PARTNER)
+// belong to row programs; a pointwise program has none.
 __device__ __forceinline__ void exec_range(const lc_pw_program &g, void *const *buffers, const int64_t *x,
                                            uint32_t *r, int begin, int end, const float *states,
-                                           float *partials, const int32_t *state_op) {
+                                           float *partials, const float *partners) {
   for (int pc = begin; pc < end; ++pc) {
     const uint32_t w0 = g.code[pc][0], w1 = g.code[pc][1];
     const int op = w0 & 255, dst = (w0 >> 8) & 255;
@@ -212,17 +212,9 @@ __device__ __forceinline__ void exec_range(const lc_pw_program &g, void *const *
         break;
       }
       case LC_PW_STATE: out = w(states[aux]); break;
-      case LC_PW_ACC: {  // fold register a into the thread's partial of state aux
-        const float v = f(A);
-        float &acc = partials[aux];
-        switch (state_op[aux]) {
-          case LC_RP_ADD: acc = __fadd_rn(acc, v); break;
-          case LC_RP_MUL: acc = __fmul_rn(acc, v); break;
-          case LC_RP_MAX: acc = fmaxf(acc, v); break;
-          default: acc = fminf(acc, v); break;
-        }
-        continue;
-      }
+      case LC_PW_PARTIAL: out = w(partials[aux]); break;
+      case LC_PW_PARTNER: out = w(partners[aux]); break;
+      case LC_PW_SETP: partials[aux] = f(A); continue;
       default: out = 0u; break;  // the host admits no other opcode
     }
     r[dst] = out;
@@ -251,60 +243,63 @@ struct RowProgArgs {
   void *buffers[LC_PW_MAX_BUFFERS];
 };
 
-__device__ __forceinline__ float rp_identity(int op) {
-  return op == LC_RP_ADD ? 0.0f : op == LC_RP_MUL ? 1.0f : op == LC_RP_MAX ? -INFINITY : INFINITY;
-}
-__device__ __forceinline__ float rp_fold(int op, float a, float b) {
-  return op == LC_RP_ADD ? __fadd_rn(a, b) : op == LC_RP_MUL ? __fmul_rn(a, b)
-       : op == LC_RP_MAX ? fmaxf(a, b) : fminf(a, b);
-}
-
-// One CTA per row (grid-stride over rows); every pass strides the CTA's
-// threads over the row's columns, then combines its states: a butterfly in
-// each warp, then warp 0's lane 0 folds the warps in order, so the result
-// does not depend on timing.  All barriers are reached by every thread.
+// One CTA per row (grid-stride over rows).  Each pass: seed the partials,
+// stride the threads over the row's columns, combine the partials with the
+// program's own combine steps — a lane butterfly in each warp, then the
+// warps' results folded in warp order by one thread — and broadcast the
+// states.  Every barrier is reached by every thread of the CTA.
 __global__ void __launch_bounds__(256) rowprog_kernel(const __grid_constant__ RowProgArgs p) {
   __shared__ float warp_part[8][LC_RP_MAX_STATES];
   __shared__ float combined[LC_RP_MAX_STATES];
   uint32_t r[LC_PW_MAX_REGS];
   for (int i = 0; i < LC_PW_MAX_REGS; ++i) r[i] = 0u;
-  float states[LC_RP_MAX_STATES], partials[LC_RP_MAX_STATES];
-  for (int k = 0; k < LC_RP_MAX_STATES; ++k) states[k] = partials[k] = 0.0f;
+  float states[LC_RP_MAX_STATES], partials[LC_RP_MAX_STATES], partners[LC_RP_MAX_STATES];
+  for (int k = 0; k < LC_RP_MAX_STATES; ++k) states[k] = partials[k] = partners[k] = 0.0f;
   const lc_pw_program &g = p.prog;
   const lc_rp_layout &lay = p.lay;
   const int64_t rows = g.extents[0], cols = g.extents[1];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const int64_t xr[LC_PW_MAX_AXES] = {row, 0, 0, 0};
     for (int pass = 0; pass < lay.n_passes; ++pass) {
+      bool has_states = false;
       for (int k = 0; k < lay.n_states; ++k)
-        if (lay.state_pass[k] == pass) partials[k] = rp_identity(lay.state_op[k]);
+        if (lay.state_pass[k] == pass) {
+          partials[k] = __uint_as_float(lay.state_init[k]);
+          has_states = true;
+        }
       for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
         const int64_t x[LC_PW_MAX_AXES] = {row, c, 0, 0};
-        exec_range(g, p.buffers, x, r, lay.begin[pass], lay.end[pass], states, partials, lay.state_op);
+        exec_range(g, p.buffers, x, r, lay.begin[pass], lay.end[pass], states, partials, partners);
       }
-      for (int k = 0; k < lay.n_states; ++k) {
-        if (lay.state_pass[k] != pass) continue;
-        float v = partials[k];
-        for (int o = 16; o > 0; o >>= 1) v = rp_fold(lay.state_op[k], v, __shfl_xor_sync(0xffffffffu, v, o));
-        if (lane == 0) warp_part[warp][k] = v;
+      if (!has_states) continue;  // uniform: the layout is the same for every thread
+      for (int o = 16; o > 0; o >>= 1) {
+        for (int k = 0; k < lay.n_states; ++k)
+          if (lay.state_pass[k] == pass) partners[k] = __shfl_xor_sync(0xffffffffu, partials[k], o);
+        exec_range(g, p.buffers, xr, r, lay.warp_begin[pass], lay.warp_end[pass], states, partials, partners);
       }
+      if (lane == 0)
+        for (int k = 0; k < lay.n_states; ++k)
+          if (lay.state_pass[k] == pass) warp_part[warp][k] = partials[k];
       __syncthreads();
-      if (threadIdx.x == 0)
-        for (int k = 0; k < lay.n_states; ++k) {
-          if (lay.state_pass[k] != pass) continue;
-          float v = warp_part[0][k];
-          for (int w2 = 1; w2 < nwarps; ++w2) v = rp_fold(lay.state_op[k], v, warp_part[w2][k]);
-          combined[k] = v;
+      if (threadIdx.x == 0) {
+        for (int k = 0; k < lay.n_states; ++k)
+          if (lay.state_pass[k] == pass) partials[k] = warp_part[0][k];
+        for (int w2 = 1; w2 < nwarps; ++w2) {
+          for (int k = 0; k < lay.n_states; ++k)
+            if (lay.state_pass[k] == pass) partners[k] = warp_part[w2][k];
+          exec_range(g, p.buffers, xr, r, lay.tree_begin[pass], lay.tree_end[pass], states, partials, partners);
         }
+        for (int k = 0; k < lay.n_states; ++k)
+          if (lay.state_pass[k] == pass) combined[k] = partials[k];
+      }
       __syncthreads();
       for (int k = 0; k < lay.n_states; ++k)
         if (lay.state_pass[k] == pass) states[k] = combined[k];
       __syncthreads();
     }
-    if (threadIdx.x == 0) {
-      const int64_t x[LC_PW_MAX_AXES] = {row, 0, 0, 0};
-      exec_range(g, p.buffers, x, r, lay.final_begin, lay.final_end, states, partials, lay.state_op);
-    }
+    if (threadIdx.x == 0)
+      exec_range(g, p.buffers, xr, r, lay.final_begin, lay.final_end, states, partials, partners);
   }
 }
 
@@ -379,8 +374,8 @@ int validate_program(const char *name, const lc_pw_program *program, void *const
         ((int)dst + 3 >= g.n_regs || (int)a + 3 >= g.n_regs || (int)b + 1 >= g.n_regs || (int)c + 3 >= g.n_regs))
       return fail(LC_ERR_INVALID, "%s: MMA register tuple out of range at %d", name, pc);
     if (op == LC_PW_SHFL_XOR || op == LC_PW_MMA_F16 || op == LC_PW_MMA_BF16) lockstep = true;
-    if ((op == LC_PW_STATE || op == LC_PW_ACC) &&
-        (!row_program || aux >= LC_RP_MAX_STATES || (op == LC_PW_ACC && (int)a >= g.n_regs)))
+    if ((op == LC_PW_STATE || op == LC_PW_PARTIAL || op == LC_PW_PARTNER || op == LC_PW_SETP) &&
+        (!row_program || aux >= LC_RP_MAX_STATES))
       return fail(LC_ERR_INVALID, "%s: state operation outside a row program at %d", name, pc);
     if (op >= LC_PW_LD_F32 && op <= LC_PW_ST_S32 &&
         (aux >= g.n_forms || g.forms[aux].dtype != storage_of(op)))
@@ -424,15 +419,16 @@ extern "C" int lc_rowprog(const lc_pw_program *program, const lc_rp_layout *layo
     return fail(LC_ERR_INVALID, "lc_rowprog: layout counts out of range");
   auto range_ok = [&](int b, int e) { return 0 <= b && b <= e && e <= n_code; };
   for (int i = 0; i < lay.n_passes; ++i)
-    if (!range_ok(lay.begin[i], lay.end[i])) return fail(LC_ERR_INVALID, "lc_rowprog: pass %d range", i);
+    if (!range_ok(lay.begin[i], lay.end[i]) || !range_ok(lay.warp_begin[i], lay.warp_end[i]) ||
+        !range_ok(lay.tree_begin[i], lay.tree_end[i]))
+      return fail(LC_ERR_INVALID, "lc_rowprog: pass %d range", i);
   if (!range_ok(lay.final_begin, lay.final_end)) return fail(LC_ERR_INVALID, "lc_rowprog: final range");
   for (int k = 0; k < lay.n_states; ++k)
-    if (lay.state_op[k] < LC_RP_ADD || lay.state_op[k] > LC_RP_MIN || lay.state_pass[k] < 0 ||
-        lay.state_pass[k] >= lay.n_passes)
+    if (lay.state_pass[k] < 0 || lay.state_pass[k] >= lay.n_passes)
       return fail(LC_ERR_INVALID, "lc_rowprog: state %d", k);
   for (int pc = 0; pc < n_code; ++pc) {
     const int op = program->code[pc][0] & 255, aux = (int)(program->code[pc][1] >> 8);
-    if ((op == LC_PW_STATE || op == LC_PW_ACC) && aux >= lay.n_states)
+    if ((op == LC_PW_STATE || op == LC_PW_PARTIAL || op == LC_PW_PARTNER || op == LC_PW_SETP) && aux >= lay.n_states)
       return fail(LC_ERR_INVALID, "lc_rowprog: state index out of range at %d", pc);
   }
   RowProgArgs args;

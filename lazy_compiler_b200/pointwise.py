@@ -52,7 +52,7 @@ OPCODES = [
     "STX_ADD_F32", "SHFL_XOR", "PACK_F16X2", "PACK_BF16X2", "MMA_F16", "MMA_BF16",
     "FREM",
     # row programs (lazy_compiler_b200/rowprog.py)
-    "STATE", "ACC",
+    "STATE", "PARTIAL", "PARTNER", "SETP",
 ]
 OP = {name: i for i, name in enumerate(OPCODES)}
 
@@ -155,7 +155,7 @@ class PointwiseCompiler:
         self.nvreg += 1
         return Val(self.nvreg - 1, dt)
 
-    _IMPURE = ("LD_", "ST_", "LDX_", "STX_", "SHFL_XOR", "MMA_")
+    _IMPURE = ("LD_", "ST_", "LDX_", "STX_", "SHFL_XOR", "MMA_", "PARTIAL", "PARTNER", "SETP")
 
     def emit(self, op: str, dt: str | None, *srcs: Val, aux: int = 0) -> Val | None:
         # a pure operation on SSA values already computed is reused (fixed

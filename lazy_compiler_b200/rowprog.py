@@ -11,15 +11,16 @@ row dot products at full bandwidth; this module compiles every other such
 body to a row program for csrc/pointwise.cu's ``lc_rowprog``:
 
 * each pass's per-element expressions compile, with the scalar rules of
-  pointwise programs, to register operations over (row, column); each
-  accumulator's value feeds an ACC operation into its state;
-* after the pass the states combine across the CTA in a fixed order (their
-  Accum operation: add, multiply, maximum or minimum) and later passes and
-  the final per-row writes read them with STATE;
+  pointwise programs, to register operations over (row, column); every
+  Accum is an explicit update of the thread's running partial
+  (``partial = op(base or partial, value)``, PARTIAL / SETP), in statement
+  order, so coupled online states (the f02 softmax's max and rescaled sum)
+  are as expressible as plain sums;
+* after the pass the partials combine with the Tile's own combine programs:
+  the WarpShuffle's ``combine_states`` at every level of a lane butterfly,
+  the TreeHalve's across the warps in order; later passes and the final
+  per-row writes read the combined states with STATE;
 * every written element must be written exactly once.
-
-Accumulators that fold through an explicit ``base`` (coupled online states)
-are not taken here; the online softmax has its own kernel.
 """
 from __future__ import annotations
 
@@ -32,7 +33,8 @@ from .pointwise import MAX_CODE, MAX_CONST, PointwiseCompiler, Program, Val
 
 MAX_PASSES = 4
 MAX_STATES = 8
-FOLDS = {"add": 0, "multiply": 1, "maximum": 2, "minimum": 3}
+IDENTITY = {"add": 0.0, "sum": 0.0, "multiply": 1.0, "prod": 1.0, "maximum": -math.inf, "max": -math.inf,
+            "minimum": math.inf, "min": math.inf}
 
 
 def _aff_dict(form) -> dict:
@@ -56,10 +58,14 @@ class RowProgramCompiler(PointwiseCompiler):
         self.rows = axes[0][1] if len(axes) == 2 else 1
         self.code, self.consts, self.forms, self.form_index = [], {}, [], {}
         self.slots, self.env, self.nvreg, self.writes = {}, {}, 0, []
-        self.state_slot: dict = {}
-        self.state_op: list = []
+        self.state_slot: dict = {}   # accumulator -> slot, once its pass has combined
+        self.live: dict = {}         # accumulator -> slot, inside its pass
+        self.state_init: list = []
         self.state_pass: list = []
         self.pass_ranges: list = []
+        self.warp_ranges: list = []
+        self.tree_ranges: list = []
+        self.tile = tile
         self.pass_writes: list = []      # (buffer, form) of per-element writes
         self.final_writes: list = []     # (buffer, form) of per-row writes
         self.cols = None
@@ -80,7 +86,11 @@ class RowProgramCompiler(PointwiseCompiler):
                     raise CompileError(f"row programs load f32, f16 or bf16, not {b.dtype}")
                 f = self.sym_form(buf, index)
                 return self.convert(self.emit("LD_" + dt.upper(), dt, aux=f), "f32")
-            if tag in ("red", "acc"):
+            if tag == "acc":
+                if e[1] not in self.live:
+                    raise CompileError(f"{e[1]} is read outside the pass that accumulates it")
+                return self.emit("PARTIAL", "f32", aux=self.live[e[1]])
+            if tag == "red":
                 if e[1] not in self.state_slot:
                     raise CompileError(f"{e[1]} is read before its pass completes")
                 return self.emit("STATE", "f32", aux=self.state_slot[e[1]])
@@ -140,6 +150,43 @@ class RowProgramCompiler(PointwiseCompiler):
             (self.final_writes if final else self.pass_writes).append((w["buffer"], f))
 
     # ------------------------------------------------------------ structure
+    def begin_range(self) -> int:
+        self.__dict__["_memo"] = {}     # a range runs on its own: no value crosses ranges
+        return len(self.code)
+
+    def combines(self) -> list:
+        """(WarpShuffle, TreeHalve) after each pass, in pass order."""
+        found, p = [], -1
+        for s in self.tile.body:
+            if s.kind in ("StridedLoop", "Loop"):
+                p += 1
+                found.append([None, None])
+            elif s.kind == "WarpShuffle" and p >= 0:
+                found[p][0] = s
+            elif s.kind == "TreeHalve" and p >= 0:
+                found[p][1] = s
+        return found
+
+    def combine_program(self, node: Node, slots: dict) -> tuple:
+        """Compile a combine_states program: state names read the own partial,
+        partner names the other's; the states' final values are written back."""
+        begin = self.begin_range()
+        saved = self.env
+        self.env = {}
+        for a, b in zip(node.state, node.state_b):
+            if a not in slots:
+                raise CompileError(f"{a} is combined but not accumulated in this pass")
+            self.env[a] = self.emit("PARTIAL", "f32", aux=slots[a])
+            self.env[b] = self.emit("PARTNER", "f32", aux=slots[a])
+        for st in node.get("combine_states") or ():
+            if st.kind not in ("Assign", "Let"):
+                raise CompileError(f"unsupported combine statement {st.kind}")
+            PointwiseCompiler.statement(self, st)
+        for a in node.state:
+            self.emit("SETP", None, self.convert(self.env[a], "f32"), aux=slots[a])
+        self.env = saved
+        return begin, len(self.code)
+
     def compile_rows(self) -> tuple:
         ev = self.ev
         loops = ev.loops
@@ -157,37 +204,57 @@ class RowProgramCompiler(PointwiseCompiler):
             elif loop["extent"] != self.cols:
                 raise CompileError("row-program passes cover different column counts")
         reds = ev.reductions
-        combined = ev.trees | ev.shuffled
-        for name, red in reds.items():
-            if red["base"] is not None:
-                raise CompileError("accumulators with an explicit base (coupled states) are not row programs")
-            if red["op"] not in FOLDS:
-                raise CompileError(f"accumulator operation {red['op']} is not add, multiply, maximum or minimum")
-            if name not in combined:
-                raise CompileError(f"accumulator {name} is not combined across the block")
         if len(reds) > MAX_STATES:
             raise CompileError("row program has too many accumulators")
+        combines = self.combines()
+        if len(combines) != len(loops):
+            raise CompileError("row-program passes must be top-level loops")
+        inits = {s.name: float(s.identity) for s in self.tile.body if s.kind == "Init"}
         self.extents = (self.rows, self.cols)
         for p, loop in enumerate(loops):
             self.axes = [self.row, loop["axis"]]
-            begin = len(self.code)
             accs = [n for n in loop["accums"] if n in reds]
+            slots = {}
             for name in accs:
-                value = self.sym(reds[name]["value"])
-                slot = len(self.state_op)
-                self.emit("ACC", None, value, aux=slot)
-                self.state_op.append(FOLDS[reds[name]["op"]])
+                slots[name] = len(self.state_pass)
+                op = reds[name]["op"]
+                seed = inits.get(name, IDENTITY.get(op))
+                if seed is None:
+                    raise CompileError(f"no seed for accumulator {name} ({op})")
+                from .pointwise import f32_word
+                self.state_init.append(f32_word(seed))
                 self.state_pass.append(p)
+            self.live = slots
+            begin = self.begin_range()
+            for name in accs:
+                red = reds[name]
+                if red["base"] is not None:
+                    new = self.sym(red["value"])         # op(base, value) as the IR states it
+                else:
+                    partial = self.emit("PARTIAL", "f32", aux=slots[name])
+                    new = self.convert(self.operation(red["op"], [partial, self.sym(red["value"])], "f32"), "f32")
+                self.emit("SETP", None, new, aux=slots[name])
             for w in ev.writes:
                 if w["loop"] == loop["axis"]:
                     if w["cond"]:
                         raise CompileError("conditional writes inside a row pass are not supported")
                     self.store(w, final=False)
             self.pass_ranges.append((begin, len(self.code)))
-            for slot, name in zip(range(len(self.state_op) - len(accs), len(self.state_op)), accs):
-                self.state_slot[name] = slot
+            warp, tree = combines[p]
+            if accs:
+                if warp is None or tree is None or int(warp.get("length") or 0) != 32:
+                    raise CompileError("a pass's accumulators must be combined by a warp butterfly and a block tree")
+                if set(warp.state) != set(accs) or set(tree.state) != set(accs):
+                    raise CompileError("the combines do not cover exactly the pass's accumulators")
+                self.warp_ranges.append(self.combine_program(warp, slots))
+                self.tree_ranges.append(self.combine_program(tree, slots))
+            else:
+                self.warp_ranges.append((0, 0))
+                self.tree_ranges.append((0, 0))
+            self.live = {}
+            self.state_slot.update(slots)
         self.axes = [self.row, "__col"]
-        final_begin = len(self.code)
+        final_begin = self.begin_range()
         for w in ev.writes:
             if w["loop"] is None:
                 if w["cond"] and not self.lead_guard(w["cond"]):
@@ -227,8 +294,9 @@ class RowProgramCompiler(PointwiseCompiler):
                 raise CompileError(f"row-program writes do not cover {out} exactly once")
 
     def layout(self, final: tuple) -> dict:
-        return {"passes": [list(r) for r in self.pass_ranges], "final": list(final),
-                "state_op": list(self.state_op), "state_pass": list(self.state_pass)}
+        return {"passes": [list(r) for r in self.pass_ranges], "warp": [list(r) for r in self.warp_ranges],
+                "tree": [list(r) for r in self.tree_ranges], "final": list(final),
+                "state_init": list(self.state_init), "state_pass": list(self.state_pass)}
 
 
 def _add_const(form, k: int):
@@ -237,27 +305,9 @@ def _add_const(form, k: int):
     return frozenset((t, c) for t, c in d.items() if c != 0)
 
 
-def _check_combines(tile: Node, reds: dict) -> None:
-    """Each WarpShuffle / TreeHalve combine must fold a state with its partner
-    by the state's own Accum operation (state = op(state, partner))."""
-    from .recognize import _walk
-    for s in _walk(tile.body):
-        if s.kind not in ("WarpShuffle", "TreeHalve"):
-            continue
-        pairs = dict(zip(s.state, s.state_b))
-        for a in s.get("combine_states") or ():
-            op = a.op.name if isinstance(a.op, Node) else str(a.op)
-            name = a.name
-            if a.kind != "Assign" or name not in pairs or tuple(a.args) != (name, pairs[name]):
-                raise CompileError("a combine step is not state = op(state, partner)")
-            if name in reds and op != reds[name]["op"]:
-                raise CompileError(f"{name} combines by {op} but accumulates by {reds[name]['op']}")
-
-
 def compile_rowprog(pkg: KernelPackage, tile: Node, ev):
     """Plan of a reduction / fused row Tile as a row program."""
     from .recognize import _plan
-    _check_combines(tile, ev.reductions)
     comp = RowProgramCompiler(pkg, tile, ev)
     final = comp.compile_rows()
     code, nregs = comp.allocate()

@@ -110,19 +110,23 @@ RP_MAX_PASSES, RP_MAX_STATES = 4, 8
 class RpLayout(ctypes.Structure):
     _fields_ = [("n_passes", ctypes.c_int32), ("n_states", ctypes.c_int32), ("final_begin", ctypes.c_int32),
                 ("final_end", ctypes.c_int32), ("begin", ctypes.c_int32 * RP_MAX_PASSES),
-                ("end", ctypes.c_int32 * RP_MAX_PASSES), ("state_op", ctypes.c_int32 * RP_MAX_STATES),
+                ("end", ctypes.c_int32 * RP_MAX_PASSES), ("warp_begin", ctypes.c_int32 * RP_MAX_PASSES),
+                ("warp_end", ctypes.c_int32 * RP_MAX_PASSES), ("tree_begin", ctypes.c_int32 * RP_MAX_PASSES),
+                ("tree_end", ctypes.c_int32 * RP_MAX_PASSES), ("state_init", ctypes.c_uint32 * RP_MAX_STATES),
                 ("state_pass", ctypes.c_int32 * RP_MAX_STATES)]
 
 
 def rp_layout(layout: dict) -> RpLayout:
     """The C struct of a row program's layout (a plan's ``params["layout"]``)."""
     lay = RpLayout()
-    lay.n_passes, lay.n_states = len(layout["passes"]), len(layout["state_op"])
+    lay.n_passes, lay.n_states = len(layout["passes"]), len(layout["state_pass"])
     lay.final_begin, lay.final_end = layout["final"]
-    for i, (b, e) in enumerate(layout["passes"]):
+    for i, ((b, e), (wb, we), (tb, te)) in enumerate(zip(layout["passes"], layout["warp"], layout["tree"])):
         lay.begin[i], lay.end[i] = b, e
-    for k, (op, ps) in enumerate(zip(layout["state_op"], layout["state_pass"])):
-        lay.state_op[k], lay.state_pass[k] = op, ps
+        lay.warp_begin[i], lay.warp_end[i] = wb, we
+        lay.tree_begin[i], lay.tree_end[i] = tb, te
+    for k, (init, ps) in enumerate(zip(layout["state_init"], layout["state_pass"])):
+        lay.state_init[k], lay.state_pass[k] = init, ps
     return lay
 
 

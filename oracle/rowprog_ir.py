@@ -8,7 +8,12 @@ per-element values over the columns (float64, then rounded to f32), and
 after the pass the accumulator is that row's fold — the WarpShuffle /
 TreeHalve combines only distribute it.  A write guarded to the first thread
 is a per-row write.  Scalar statements follow oracle/pointwise_ir.py's rules.
-Accumulators with an explicit base (coupled online states) are not covered.
+
+A pass whose accumulators fold through an explicit base (coupled online
+states, the f02 softmax) has no closed-form fold: there every one of the
+block's threads updates its running states over its strided columns in
+order, and the threads' states merge one after another through the
+WarpShuffle's own combine statements.
 """
 from __future__ import annotations
 
@@ -28,7 +33,7 @@ class RowOracle(PointwiseOracle):
     def __init__(self, pkg, tile, arrays):
         axes = [(a.name, int(a.extent.value)) for a in tile.axes]
         self.pkg = pkg
-        self.co = axes[-1][0]
+        self.co, self.block = axes[-1]
         self.row = axes[0][0] if len(axes) == 2 else "__row"
         self.rows = axes[0][1] if len(axes) == 2 else 1
         self.arrays = {k: np.asarray(v).ravel() for k, v in arrays.items()}
@@ -54,9 +59,63 @@ class RowOracle(PointwiseOracle):
             if isinstance(v, V) and v.a.shape == (self.rows * cols,):
                 self.env[k] = V(v.a.reshape(self.rows, cols)[:, 0], v.t)
 
+    def coupled_pass(self, loop, combine, block):
+        """Per-thread sequential folds, then thread-by-thread merges (see the module docstring)."""
+        cols = int(loop.axis.extent.value)
+        accs = [st for st in loop.body if st.kind == "Accum"]
+        names = [a.name for a in accs]
+        inits = {st.name: float(st.identity) for st in self.tile_body if st.kind == "Init"}
+        ident = {a.name: inits.get(a.name, _IDENTITY[a.op.name if hasattr(a.op, "name") else str(a.op)])
+                 for a in accs}
+        n = self.rows * block
+        part = {nm: np.full(n, ident[nm], np.float32) for nm in names}
+        saved = dict(self.env)
+        r = np.repeat(np.arange(self.rows, dtype=np.int64), block)
+        t = np.tile(np.arange(block, dtype=np.int64), self.rows)
+        for it in range(-(-cols // block)):
+            c = it * block + t
+            valid = c < cols
+            self.coord = {self.row: r, self.co: t, loop.axis.name: np.minimum(c, cols - 1)}
+            self.env = {k: (V(np.repeat(v.a, block), v.t) if isinstance(v, V) and v.a.shape == (self.rows,) else v)
+                        for k, v in saved.items()}
+            for nm in names:
+                self.env[nm] = V(part[nm], "f32")
+            for st in loop.body:
+                if st.kind == "Accum":
+                    opname = st.op.name if hasattr(st.op, "name") else str(st.op)
+                    base = self.env[st.base] if st.get("base") else self.env[st.name]
+                    value = self.env[st.value] if isinstance(st.value, str) else self.expr(st.value)
+                    new = conv(self.op(opname, [conv(base, "f32"), conv(value, "f32")], "f32"), "f32").a
+                    part[st.name] = np.where(valid, new, part[st.name]).astype(np.float32)
+                    self.env[st.name] = V(part[st.name], "f32")
+                elif st.kind != "Write":
+                    self.run([st])
+        self.env = saved
+        self.set_domain(None, 1)
+        own = {nm: part[nm].reshape(self.rows, block)[:, 0].copy() for nm in names}
+        for th in range(1, block):
+            env = dict(self.env)
+            self.env = dict(env)
+            for a, b in zip(combine.state, combine.state_b):
+                self.env[a] = V(own[a], "f32")
+                self.env[b] = V(part[a].reshape(self.rows, block)[:, th], "f32")
+            for st in combine.get("combine_states") or ():
+                self.run([st])
+            for a in combine.state:
+                own[a] = conv(self.env[a], "f32").a.copy()
+            self.env = env
+        for nm in names:
+            self.env[nm] = V(own[nm], "f32")
+
     def run_rows(self, body) -> dict:
-        for s in body:
+        self.tile_body = body
+        items = list(body)
+        for i, s in enumerate(items):
             k = s.kind
+            if k in ("StridedLoop", "Loop") and any(st.kind == "Accum" and st.get("base") for st in s.body):
+                combine = next(x for x in items[i + 1:] if x.kind == "WarpShuffle")
+                self.coupled_pass(s, combine, self.block)
+                continue
             if k in ("StridedLoop", "Loop"):
                 cols = int(s.axis.extent.value)
                 folds = {}
@@ -80,7 +139,7 @@ class RowOracle(PointwiseOracle):
                 self.env[s.name] = V(np.full(self.rows, _IDENTITY.get(str(s.identity), float(s.identity)),
                                              np.float32), "f32")
             elif k in ("WarpShuffle", "TreeHalve", "Smem", "Sync"):
-                continue
+                continue    # the pass above already produced the combined states
             elif k == "Cond":
                 self.run_rows(s.body)
             elif k == "Write" and s.output not in self.pkg.buffers:

@@ -330,3 +330,43 @@ def _half_row_sum(folder):
 
 ROW_SYNTHETIC = {"row_max": _row_max, "row_min_abs": _row_min_abs, "variance": _variance,
                  "log_sum_exp": _log_sum_exp, "center_rows": _center_rows, "half_row_sum": _half_row_sum}
+
+
+# ---------------------------------------------------------------- online-softmax variants (coupled states)
+
+def _from_f02(folder: Path, name: str, edits: list) -> Path:
+    """A copy of the f02 online-softmax package with textual edits of its IR."""
+    import shutil
+    src = Path(__file__).resolve().parent / "golden" / "packages" / "f02_row_softmax"
+    shutil.copytree(src, folder)
+    ir = next(folder.glob("*.ir.json"))
+    text = ir.read_text()
+    for old, new in edits:
+        assert old in text, old
+        text = text.replace(old, new)
+    ir.write_text(text)
+    meta = json.loads((folder / "meta.json").read_text())
+    meta["id"] = name
+    meta["rtol"], meta["atol"] = 1e-5, 1e-6
+    (folder / "meta.json").write_text(json.dumps(meta))
+    return ir
+
+
+def _log_softmax(folder):
+    """log softmax: x - max - log(sum exp(x - max)) from the same coupled states."""
+    return _from_f02(folder, "log_softmax", [
+        ("Assign(name='v4', op=ElementwiseImpl('exp'), args=('v3',)",
+         "Assign(name='v4', op=ElementwiseImpl('log'), args=('acc1',)"),
+        ("Assign(name='v5', op=ElementwiseImpl('multiply'), args=('v2', 'v4')",
+         "Assign(name='v5', op=ElementwiseImpl('subtract'), args=('v3', 'v4')")])
+
+
+def _softmax_times_x(folder):
+    """softmax(x) * x (an attention-like reweighting of the row by itself)."""
+    return _from_f02(folder, "softmax_times_x", [
+        ("Assign(name='v5', op=ElementwiseImpl('multiply'), args=('v2', 'v4')",
+         "Assign(name='v6', op=ElementwiseImpl('multiply'), args=('v2', 'v4'), dtype=None), "
+         "Assign(name='v5', op=ElementwiseImpl('multiply'), args=('v6', 'in2')")])
+
+
+ROW_COUPLED = {"log_softmax": _log_softmax, "softmax_times_x": _softmax_times_x}

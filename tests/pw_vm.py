@@ -68,11 +68,21 @@ def _mma(r, dst, a, b, c, bf16, n):
             r[dst + e][sl] = _w(D[g[sl] + (8 if e >= 2 else 0), 2 * t[sl] + (e & 1)])
 
 
-def run(prog: dict, arrays: dict, _states=None, _acc=None) -> dict:
-    ext = prog["extents"]
-    grids = np.meshgrid(*[np.arange(e, dtype=np.int64) for e in ext], indexing="ij")
-    coords = [g.ravel() for g in grids]
+def run(prog: dict, arrays: dict, coords=None, states=None, partials=None, partners=None, mask=None,
+        outs=None) -> dict:
+    """Run a program (or one range of it: ``prog["code"]``) over every point.
+
+    ``coords`` overrides the points (one coordinate array per axis);
+    ``states`` / ``partials`` / ``partners`` map state slots to per-point
+    arrays for row programs (SETP writes ``partials`` in place); ``mask``
+    limits stores and SETP to some points; ``outs`` collects outputs across
+    calls."""
+    if coords is None:
+        ext = prog["extents"]
+        grids = np.meshgrid(*[np.arange(e, dtype=np.int64) for e in ext], indexing="ij")
+        coords = [g.ravel() for g in grids]
     n = coords[0].size
+    live = np.ones(n, bool) if mask is None else mask
     bufs = []
     for name, size in zip(prog["buffers"], prog["sizes"]):
         if name in arrays:
@@ -80,7 +90,7 @@ def run(prog: dict, arrays: dict, _states=None, _acc=None) -> dict:
             bufs.append(a.astype(np.float32) if a.dtype == np.float16 else a.copy())
         else:
             bufs.append(None)
-    outs = {}
+    outs = {} if outs is None else outs
     r = {}
     consts = np.asarray(prog["consts"], np.uint64).astype(np.uint32)
     with np.errstate(all="ignore"):
@@ -104,7 +114,7 @@ def run(prog: dict, arrays: dict, _states=None, _acc=None) -> dict:
                         val = val.astype(np.float16).astype(np.float32)
                     elif name == "ST_BF16":
                         val = _bf16(val)
-                    outs[bname][at] = val
+                    outs[bname][at[live]] = val[live]
                 continue
             fa, fb, fc = (_f(x) if x is not None else None for x in (A, B, C))
             ia, ib = (x.view(np.int32).astype(np.int64) if x is not None else None for x in (A, B))
@@ -208,9 +218,13 @@ def run(prog: dict, arrays: dict, _states=None, _acc=None) -> dict:
                     hi = _bf16(fb).view(np.uint32) >> 16
                 out = (hi << 16) | lo
             elif name == "STATE":
-                out = _w(_states[aux])
-            elif name == "ACC":
-                _acc[aux] = _f(A).copy()
+                out = _w(np.broadcast_to(np.asarray(states[aux], np.float32), (n,)))
+            elif name == "PARTIAL":
+                out = _w(np.asarray(partials[aux], np.float32))
+            elif name == "PARTNER":
+                out = _w(np.asarray(partners[aux], np.float32))
+            elif name == "SETP":
+                partials[aux] = np.where(live, _f(A), partials[aux]).astype(np.float32)
                 continue
             elif name == "FREM":
                 r0 = np.fmod(fa, fb)
@@ -248,35 +262,36 @@ def assert_faithful(ir, rtol=1e-5, atol=1e-6):
     return plan
 
 
-def run_rows(prog: dict, layout: dict, arrays: dict) -> dict:
-    """A row program on the CPU: each pass over every (row, column) point at
-    once, its ACC values folded per row (float64, then f32), the final
-    operations once per row."""
+def run_rows(prog: dict, layout: dict, arrays: dict, block: int = 128) -> dict:
+    """A row program on the CPU, as its schedule runs it: every thread of a
+    ``block``-wide CTA folds its strided columns into its partials in column
+    order, the partials combine thread by thread through the tree's combine
+    operations, the final operations run once per row."""
     rows, cols = prog["extents"]
-    states = {}
-    outs = {}
-    fold = {0: np.sum, 1: np.prod, 2: np.max, 3: np.min}
+    states, outs = {}, {}
+    r_idx = np.repeat(np.arange(rows, dtype=np.int64), block)
+    t_idx = np.tile(np.arange(block, dtype=np.int64), rows)
+    per_row = [np.arange(rows, dtype=np.int64), np.zeros(rows, np.int64)]
+
+    def sub(b, e):
+        return dict(prog, code=prog["code"][b:e])
+
     for p, (b, e) in enumerate(layout["passes"]):
-        sub = dict(prog, code=prog["code"][b:e])
-        acc = {}
-        part = _run(sub, arrays, rows, cols, states, acc, outs)
-        for k, values in acc.items():
-            with np.errstate(all="ignore"):
-                states[k] = fold[layout["state_op"][k]](values.reshape(rows, cols).astype(np.float64), axis=1)
-    b, e = layout["final"]
-    sub = dict(prog, code=prog["code"][b:e])
-    _run(sub, arrays, rows, 1, states, {}, outs)
+        slots = [k for k, ps in enumerate(layout["state_pass"]) if ps == p]
+        partials = {k: np.full(rows * block, np.uint32(layout["state_init"][k]), np.uint32).view(np.float32)
+                    for k in slots}
+        wide = {k: np.repeat(np.asarray(v, np.float32), block) for k, v in states.items()}
+        for it in range(-(-cols // block)):
+            c = it * block + t_idx
+            run(sub(b, e), arrays, coords=[r_idx, np.minimum(c, cols - 1)], states=wide, partials=partials,
+                mask=c < cols, outs=outs)
+        if slots:
+            tb, te = layout["tree"][p]
+            own = {k: partials[k].reshape(rows, block)[:, 0].copy() for k in slots}
+            for t in range(1, block):
+                partner = {k: partials[k].reshape(rows, block)[:, t] for k in slots}
+                run(sub(tb, te), arrays, coords=per_row, states=states, partials=own, partners=partner, outs=outs)
+            states.update(own)
+    fb, fe = layout["final"]
+    run(sub(fb, fe), arrays, coords=per_row, states=states, partials={}, outs=outs)
     return outs
-
-
-def _run(prog, arrays, rows, cols, states, acc, outs):
-    """One range of a row program over rows x cols points (STATE broadcasts per row)."""
-    expanded = {k: np.repeat(np.asarray(v, np.float32), cols) for k, v in states.items()}
-    p2 = dict(prog, extents=[rows, cols])
-    res = run(p2, arrays, _states=expanded, _acc=acc)
-    for k, v in res.items():
-        if k in outs:
-            mask = ~np.isnan(v) if v.dtype.kind == "f" else np.ones(v.shape, bool)
-            outs[k][mask] = v[mask]
-        else:
-            outs[k] = v

@@ -61,7 +61,20 @@ def test_row_program_validation(tmp_path, cuda_device):
     lay.end[0] = 10_000                     # a pass range past the program
     assert status(runtime.pw_program(prog), lay) == -1
     lay = runtime.rp_layout(layout)
-    lay.state_op[0] = 9                     # unknown fold
+    lay.state_pass[0] = 3                   # a state of a pass that does not exist
     assert status(runtime.pw_program(prog), lay) == -1
     # a pointwise launch may not use state operations
     assert lib.lc_pointwise(ctypes.c_void_p(ctypes.addressof(runtime.pw_program(prog))), ptrs, None) == -1
+
+
+@pytest.mark.parametrize("name", sorted(W.ROW_COUPLED))
+def test_online_softmax_variants_on_gpu(name, tmp_path, cuda_device):
+    ir = W.ROW_COUPLED[name](tmp_path / name)
+    meta = json.loads((tmp_path / name / "meta.json").read_text())
+    for offset in (0, 5):
+        arrays = {a["name"]: O.input_array(a, offset) for a in meta["kernels"][0]["args"] if not a.get("output")}
+        ref = rowprog_ir.evaluate(ir, arrays)
+        out = run_package(tmp_path / name, inputs=arrays)
+        for key, value in ref.items():
+            row = O.compare(out[key], value, 1e-5, 1e-6)
+            assert row["pass"], (key, row)

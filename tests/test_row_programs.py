@@ -17,8 +17,8 @@ from lazy_compiler_b200.rowprog import compile_rowprog
 from oracle import expressions as O
 from oracle import rowprog_ir
 
-REDUCTIONS = ["r01_array_sum", "r02_big_sum", "r03_mean", "r04_row_sum", "f01_rmsnorm", "f03_l2norm",
-              "phase9_gelu_row_dot"]
+REDUCTIONS = ["r01_array_sum", "r02_big_sum", "r03_mean", "r04_row_sum", "f01_rmsnorm", "f02_row_softmax",
+              "f03_l2norm", "phase9_gelu_row_dot"]
 
 
 def inputs_of(meta, offset=0):
@@ -70,25 +70,22 @@ def test_synthetic_row_program_matches_oracle(name, tmp_path):
             assert O.compare(got[key].reshape(value.shape), value, meta["rtol"], meta["atol"])["pass"]
 
 
-def test_combine_must_use_the_accumulator_operation(tmp_path):
-    """Accumulating by max but combining partial results by add is not a row max."""
+def test_combine_program_is_the_one_the_tile_states(tmp_path):
+    """Accumulating by max but combining by add is run as written (the
+    thread-by-thread merge of the oracle agrees), not taken for a row max."""
     ir = W.ROW_SYNTHETIC["row_max"](tmp_path / "m")
     text = ir.read_text()
     ir.write_text(text.replace("Assign(name='m', op=ElementwiseImpl('maximum')",
                                "Assign(name='m', op=ElementwiseImpl('add')"))
-    with pytest.raises(CompileError, match="combines by add"):
-        compile_file(ir)
-
-
-def test_state_read_before_its_pass_combines_is_rejected(tmp_path):
-    """A per-element write in the accumulating pass cannot see the row's total."""
-    ir = W.row_package(tmp_path / "early", "early", 8, 64, {"x": ((8, 64), "f32")}, ("out", (8, 64), "f32"),
-                       [W.load("xv", "x", [W.var("a0"), W.var("a1")], "f32"),
-                        W.assign("y", "multiply", ["xv", "s"], "f32"),
-                        W.write("out", [W.var("a0"), W.var("a1")], ["y"], "f32")],
-                       [("s", "add", "xv")])
-    with pytest.raises(CompileError):
-        compile_file(ir)
+    plan = compile_file(ir)
+    assert plan["op"] == "rowprog"
+    meta = json.loads((tmp_path / "m" / "meta.json").read_text())
+    arrays = inputs_of(meta)
+    got = pw_vm.run_rows(plan["params"]["program"], plan["params"]["layout"], arrays)
+    x = arrays["x"].astype(np.float64)
+    # 128 threads each take the max of their columns; the merge adds the maxima
+    per_thread = np.stack([x[:, t::128].max(axis=1) for t in range(128)], axis=1)
+    np.testing.assert_allclose(got["out"], per_thread.sum(axis=1), rtol=1e-5, atol=1e-5)
 
 
 def test_row_outputs_must_be_covered(tmp_path):
@@ -97,3 +94,27 @@ def test_row_outputs_must_be_covered(tmp_path):
                        final_writes=[W.write("out", [W.var("a0")], ["s"], "f32")])
     with pytest.raises(CompileError, match="cover"):
         compile_file(ir)
+
+
+@pytest.mark.parametrize("name", sorted(W.ROW_COUPLED))
+def test_online_softmax_variants_run_as_row_programs(name, tmp_path):
+    """Coupled online states (Accum through a base, merged by the Tile's own
+    combine statements) are not the fixed softmax when the output changes:
+    they run as row programs that match the row oracle."""
+    ir = W.ROW_COUPLED[name](tmp_path / name)
+    plan = compile_file(ir)
+    assert plan["op"] == "rowprog"
+    meta = json.loads((tmp_path / name / "meta.json").read_text())
+    arrays = inputs_of(meta, 1)
+    ref = rowprog_ir.evaluate(ir, arrays)
+    got = pw_vm.run_rows(plan["params"]["program"], plan["params"]["layout"], arrays)
+    for key, value in ref.items():
+        assert O.compare(got[key].reshape(value.shape), value, 1e-5, 1e-6)["pass"]
+
+
+def test_f02_as_row_program_matches_golden():
+    plan = forced_plan(golden_ir("f02_row_softmax"))
+    meta = golden_meta("f02_row_softmax")
+    got = pw_vm.run_rows(plan["params"]["program"], plan["params"]["layout"], inputs_of(meta))
+    with np.load(golden("f02_row_softmax") / "expected.npz") as z:
+        assert O.compare(got["softmax"].reshape(z["softmax"].shape), z["softmax"], meta["rtol"], meta["atol"])["pass"]
