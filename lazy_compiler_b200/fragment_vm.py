@@ -338,8 +338,8 @@ class LaneCompiler(PointwiseCompiler):
                 if kind == "gmem":
                     buffer, index = arg
                     buf = self.pkg.buffers.get(buffer)
-                    if buf is None or buf.role == "output" and buffer not in self.pkg.arg_order:
-                        raise CompileError("fragment GMEM operand needs a known buffer")
+                    if buf is None or buffer not in self.pkg.arg_order:
+                        raise CompileError("fragment GMEM operand needs a kernel argument")
                     at = self.flat_index(buffer, tuple(index))
                     v = self.emit(_LOADX[vm_type(buf.dtype)], vm_type(buf.dtype), at, aux=self.slot(buffer))
                     return self.convert(v, "f32")

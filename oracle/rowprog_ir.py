@@ -17,7 +17,6 @@ WarpShuffle's own combine statements.
 """
 from __future__ import annotations
 
-import math
 
 import numpy as np
 

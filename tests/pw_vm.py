@@ -6,8 +6,6 @@ program compiler's typing and lowering against the IR oracle without a GPU.
 The approximate PTX instructions (ex2/lg2/sin/cos.approx) are replaced by
 accurate numpy functions; everything else is bit-exact IEEE arithmetic.
 """
-import math
-
 import numpy as np
 
 from lazy_compiler_b200.pointwise import OPCODES
