@@ -312,12 +312,19 @@ int lc_probe_mma(int variant, int groups, void *stream);
  * into one 16-bit pair; MMA_F16 / MMA_BF16 run mma.sync m16n8k16 with D, A,
  * B and C in registers dst..dst+3, a..a+3, b..b+1 and c..c+3.  A program
  * that shuffles or multiplies needs a point count that is a multiple of 32:
- * each warp then runs 32 consecutive points in lockstep. */
+ * each warp then runs 32 consecutive points in lockstep.
+ *
+ * Serial programs (per-point runtime loops, the reference's Loop with Accum
+ * inside one thread's work, ptx_backend.py:1496-1554) use LOOPB / LOOPE:
+ * aux = slot | pc << 4; loop `slot` counts coordinate n_axes + slot from 0
+ * to extents[n_axes + slot]; LOOPB jumps past its LOOPE (pc) when the extent
+ * is 0, LOOPE jumps back to its LOOPB (pc) while the count is below it.
+ * Forms may depend on loop coordinates. */
 #define LC_PW_MAX_CODE 1024
 #define LC_PW_MAX_CONST 128
 #define LC_PW_MAX_FORMS 32
 #define LC_PW_MAX_BUFFERS 16
-#define LC_PW_MAX_AXES 4
+#define LC_PW_MAX_AXES 8
 #define LC_PW_MAX_REGS 64
 
 enum lc_pw_op {
@@ -407,6 +414,8 @@ enum lc_pw_op {
   LC_PW_PARTIAL = 83,
   LC_PW_PARTNER = 84,
   LC_PW_SETP = 85,
+  LC_PW_LOOPB = 86,
+  LC_PW_LOOPE = 87,
   LC_PW_NUM_OPS
 };
 
@@ -420,8 +429,8 @@ typedef struct {
 #define LC_S32 3 /* storage code of int32 buffers in pointwise programs */
 
 typedef struct {
-  int32_t n_code, n_consts, n_forms, n_buffers, n_axes, n_regs;
-  int64_t extents[LC_PW_MAX_AXES];
+  int32_t n_code, n_consts, n_forms, n_buffers, n_axes, n_regs, n_loops, reserved;
+  int64_t extents[LC_PW_MAX_AXES]; /* n_axes tile extents, then n_loops loop extents */
   int64_t sizes[LC_PW_MAX_BUFFERS];
   uint32_t code[LC_PW_MAX_CODE][2];
   uint32_t consts[LC_PW_MAX_CONST];

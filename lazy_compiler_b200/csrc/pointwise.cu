@@ -50,7 +50,7 @@ __device__ __forceinline__ float round_bf16(float x) {
 // Runs operations [begin, end) of a program for one point with coordinates
 // x.  `states` (STATE), `partials` (PARTIAL, SETP) and `partners` (PARTNER)
 // belong to row programs; a pointwise program has none.
-__device__ __forceinline__ void exec_range(const lc_pw_program &g, void *const *buffers, const int64_t *x,
+__device__ __forceinline__ void exec_range(const lc_pw_program &g, void *const *buffers, int64_t *x,
                                            uint32_t *r, int begin, int end, const float *states,
                                            float *partials, const float *partners) {
   for (int pc = begin; pc < end; ++pc) {
@@ -63,7 +63,7 @@ __device__ __forceinline__ void exec_range(const lc_pw_program &g, void *const *
     if (op >= LC_PW_LD_F32 && op <= LC_PW_ST_S32) {
       const lc_pw_form &fm = g.forms[aux];
       int64_t at = fm.base;
-      for (int d = 0; d < g.n_axes; ++d) at += fm.coef[d] * x[d];
+      for (int d = 0; d < g.n_axes + g.n_loops; ++d) at += fm.coef[d] * x[d];
       void *base = buffers[fm.buffer];
       switch (op) {
         case LC_PW_LD_F32: out = static_cast<const uint32_t *>(base)[at]; break;
@@ -211,6 +211,17 @@ __device__ __forceinline__ void exec_range(const lc_pw_program &g, void *const *
         out = w(rv);
         break;
       }
+      case LC_PW_LOOPB: {  // enter loop (aux & 15): count from 0, skip the body of an empty loop
+        const int d = g.n_axes + (aux & 15);
+        x[d] = 0;
+        if (g.extents[d] <= 0) pc = aux >> 4;
+        continue;
+      }
+      case LC_PW_LOOPE: {  // next iteration of loop (aux & 15), back to its LOOPB
+        const int d = g.n_axes + (aux & 15);
+        if (++x[d] < g.extents[d]) pc = aux >> 4;
+        continue;
+      }
       case LC_PW_STATE: out = w(states[aux]); break;
       case LC_PW_PARTIAL: out = w(partials[aux]); break;
       case LC_PW_PARTNER: out = w(partners[aux]); break;
@@ -227,7 +238,7 @@ __global__ void __launch_bounds__(256) pointwise_kernel(const __grid_constant__ 
   const lc_pw_program &g = p.prog;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gid < p.points; gid += stride) {
-    int64_t x[LC_PW_MAX_AXES] = {0, 0, 0, 0};
+    int64_t x[LC_PW_MAX_AXES] = {0, 0, 0, 0, 0, 0, 0, 0};
     int64_t rest = gid;
     for (int d = g.n_axes - 1; d >= 0; --d) {
       x[d] = rest % g.extents[d];
@@ -260,7 +271,7 @@ __global__ void __launch_bounds__(256) rowprog_kernel(const __grid_constant__ Ro
   const int64_t rows = g.extents[0], cols = g.extents[1];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-    const int64_t xr[LC_PW_MAX_AXES] = {row, 0, 0, 0};
+    int64_t xr[LC_PW_MAX_AXES] = {row, 0, 0, 0, 0, 0, 0, 0};
     for (int pass = 0; pass < lay.n_passes; ++pass) {
       bool has_states = false;
       for (int k = 0; k < lay.n_states; ++k)
@@ -269,7 +280,7 @@ __global__ void __launch_bounds__(256) rowprog_kernel(const __grid_constant__ Ro
           has_states = true;
         }
       for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
-        const int64_t x[LC_PW_MAX_AXES] = {row, c, 0, 0};
+        int64_t x[LC_PW_MAX_AXES] = {row, c, 0, 0, 0, 0, 0, 0};
         exec_range(g, p.buffers, x, r, lay.begin[pass], lay.end[pass], states, partials, partners);
       }
       if (!has_states) continue;  // uniform: the layout is the same for every thread
@@ -305,7 +316,7 @@ __global__ void __launch_bounds__(256) rowprog_kernel(const __grid_constant__ Ro
 
 bool form_in_range(const lc_pw_program &g, const lc_pw_form &fm) {
   int64_t lo = fm.base, hi = fm.base;
-  for (int d = 0; d < g.n_axes; ++d) {
+  for (int d = 0; d < g.n_axes + g.n_loops; ++d) {
     const int64_t span = fm.coef[d] * (g.extents[d] - 1);
     if (span < 0) lo += span;
     else hi += span;
@@ -334,7 +345,8 @@ int validate_program(const char *name, const lc_pw_program *program, void *const
   const lc_pw_program &g = *program;
   if (g.n_code < 0 || g.n_code > LC_PW_MAX_CODE || g.n_consts < 0 || g.n_consts > LC_PW_MAX_CONST ||
       g.n_forms < 0 || g.n_forms > LC_PW_MAX_FORMS || g.n_buffers < 1 || g.n_buffers > LC_PW_MAX_BUFFERS ||
-      g.n_axes < 1 || g.n_axes > LC_PW_MAX_AXES || g.n_regs < 1 || g.n_regs > LC_PW_MAX_REGS)
+      g.n_axes < 1 || g.n_axes > LC_PW_MAX_AXES || g.n_regs < 1 || g.n_regs > LC_PW_MAX_REGS ||
+      g.n_loops < 0 || g.n_axes + g.n_loops > LC_PW_MAX_AXES || (row_program && g.n_loops != 0))
     return fail(LC_ERR_INVALID, "%s: program counts out of range", name);
   int64_t points = 1;
   for (int d = 0; d < g.n_axes; ++d) {
@@ -343,12 +355,14 @@ int validate_program(const char *name, const lc_pw_program *program, void *const
     points *= g.extents[d];
     if (points > ((int64_t)1 << 40)) return fail(LC_ERR_INVALID, "%s: tile too large", name);
   }
+  for (int d = g.n_axes; d < g.n_axes + g.n_loops; ++d)
+    if (g.extents[d] < 0 || g.extents[d] > 0x7fffffff) return fail(LC_ERR_INVALID, "%s: bad loop extent", name);
   for (int i = 0; i < g.n_buffers; ++i)
     if (!buffers[i] || g.sizes[i] < 1) return fail(LC_ERR_INVALID, "%s: buffer slot %d", name, i);
   for (int i = 0; i < g.n_forms; ++i) {
     const lc_pw_form &fm = g.forms[i];
     bool sane = fm.base >= -((int64_t)1 << 50) && fm.base <= ((int64_t)1 << 50);
-    for (int d = 0; d < g.n_axes; ++d)
+    for (int d = 0; d < g.n_axes + g.n_loops; ++d)
       sane = sane && fm.coef[d] >= -((int64_t)1 << 40) && fm.coef[d] <= ((int64_t)1 << 40);
     if (!sane || fm.buffer < 0 || fm.buffer >= g.n_buffers || !form_in_range(g, fm))
       return fail(LC_ERR_INVALID, "%s: form %d leaves its buffer", name, i);
@@ -374,6 +388,17 @@ int validate_program(const char *name, const lc_pw_program *program, void *const
         ((int)dst + 3 >= g.n_regs || (int)a + 3 >= g.n_regs || (int)b + 1 >= g.n_regs || (int)c + 3 >= g.n_regs))
       return fail(LC_ERR_INVALID, "%s: MMA register tuple out of range at %d", name, pc);
     if (op == LC_PW_SHFL_XOR || op == LC_PW_MMA_F16 || op == LC_PW_MMA_BF16) lockstep = true;
+    if (op == LC_PW_LOOPB || op == LC_PW_LOOPE) {
+      // a well-formed pair: LOOPB at pc names its LOOPE, which names it back, on the same loop
+      const int slot = aux & 15, other = aux >> 4;
+      const bool begin = op == LC_PW_LOOPB;
+      if (slot >= g.n_loops || other < 0 || other >= g.n_code || (begin ? other <= pc : other >= pc))
+        return fail(LC_ERR_INVALID, "%s: malformed loop at %d", name, pc);
+      const uint32_t m0 = g.code[other][0], m1 = g.code[other][1];
+      if ((int)(m0 & 255) != (begin ? LC_PW_LOOPE : LC_PW_LOOPB) || (int)((m1 >> 8) & 15) != slot ||
+          (int)(m1 >> 12) != pc)
+        return fail(LC_ERR_INVALID, "%s: unmatched loop at %d", name, pc);
+    }
     if ((op == LC_PW_STATE || op == LC_PW_PARTIAL || op == LC_PW_PARTNER || op == LC_PW_SETP) &&
         (!row_program || aux >= LC_RP_MAX_STATES))
       return fail(LC_ERR_INVALID, "%s: state operation outside a row program at %d", name, pc);

@@ -53,6 +53,8 @@ OPCODES = [
     "FREM",
     # row programs (lazy_compiler_b200/rowprog.py)
     "STATE", "PARTIAL", "PARTNER", "SETP",
+    # serial programs (lazy_compiler_b200/serial.py)
+    "LOOPB", "LOOPE",
 ]
 OP = {name: i for i, name in enumerate(OPCODES)}
 
@@ -60,7 +62,7 @@ MAX_CODE = 1024
 MAX_CONST = 128
 MAX_FORMS = 32
 MAX_BUFFERS = 16
-MAX_AXES = 4
+MAX_AXES = 8
 MAX_REGS = 64
 
 _TYPES = {"float": "f32", "int": "s32", "i32": "s32", "__half": "f16", "half": "f16",
@@ -121,13 +123,14 @@ class Program:
     extents: tuple = ()
     n_regs: int = 0
     sizes: list = field(default_factory=list)      # elements of each buffer slot
+    loops: list = field(default_factory=list)      # extents of the runtime loops (serial programs)
 
     def to_json(self) -> dict:
         return {"code": [list(c) for c in self.code], "consts": list(self.consts),
                 "forms": [{"buffer": f.buffer, "dtype": f.dtype, "base": f.base, "coef": list(f.coef)}
                           for f in self.forms],
                 "buffers": list(self.buffers), "extents": list(self.extents), "n_regs": self.n_regs,
-                "sizes": list(self.sizes)}
+                "sizes": list(self.sizes), "loops": list(self.loops)}
 
 
 class PointwiseCompiler:
@@ -155,7 +158,7 @@ class PointwiseCompiler:
         self.nvreg += 1
         return Val(self.nvreg - 1, dt)
 
-    _IMPURE = ("LD_", "ST_", "LDX_", "STX_", "SHFL_XOR", "MMA_", "PARTIAL", "PARTNER", "SETP")
+    _IMPURE = ("LD_", "ST_", "LDX_", "STX_", "SHFL_XOR", "MMA_", "PARTIAL", "PARTNER", "SETP", "LOOP")
 
     def emit(self, op: str, dt: str | None, *srcs: Val, aux: int = 0) -> Val | None:
         # a pure operation on SSA values already computed is reused (fixed
@@ -570,12 +573,14 @@ class PointwiseCompiler:
             raise CompileError(f"{k} is not part of a pointwise program")
 
     # ------------------------------------------------------------ finishing
-    def allocate(self) -> list:
+    def allocate(self, extend: dict | None = None) -> list:
         """Map virtual registers to physical ones (linear scan).
 
         Register ids >= 0 are virtual; -1 - p names fixed physical register p
-        (the fragment registers of lane programs, below ``n_fixed``), which
-        virtual registers never share.
+        (the fragment registers of lane programs and the accumulators of
+        serial programs, below ``n_fixed``), which virtual registers never
+        share.  ``extend`` keeps registers allocated up to a later pc (values
+        a loop's back edge reads again).
         """
         base = getattr(self, "n_fixed", 0)
         last: dict = {}
@@ -583,6 +588,8 @@ class PointwiseCompiler:
             for r in (a, b, c)[:nsrc]:
                 if r >= 0:
                     last[r] = pc
+        for r, pc in (extend or {}).items():
+            last[r] = max(last.get(r, pc), pc)
         free: list = []
         phys: dict = {}
         top = base

@@ -900,26 +900,36 @@ def recognise(pkg: KernelPackage) -> Plan:
             return _pointwise_program(pkg, tile, err)
         raise
     if ev.loops and ev.reductions:
-        if f32.looks_like_attention(ev):
-            return f32.recognise_attention(pkg, tile, ev)
-        if f32.looks_like_dot(ev):
-            return f32.recognise_dot_gemm(pkg, tile, ev)
+        # the fixed classes first, then the general row and serial programs
         try:
+            if f32.looks_like_attention(ev):
+                return f32.recognise_attention(pkg, tile, ev)
+            if f32.looks_like_dot(ev):
+                return f32.recognise_dot_gemm(pkg, tile, ev)
             return _recognise_reduction(pkg, tile, ev)
         except CompileError as err:
             from .rowprog import compile_rowprog
             try:
                 return compile_rowprog(pkg, tile, ev)
             except CompileError as err2:
-                raise CompileError(f"{err}; as a row program: {err2}") from err2
+                return _serial_program(pkg, tile, f"{err}; as a row program: {err2}")
     if ev.loops:
-        raise CompileError("loops without a reduction are not a supported operation class")
+        return _serial_program(pkg, tile, "loops without a reduction")
     try:
         return _recognise_pointwise(pkg, tile, ev)
     except CompileError as err:
         if straight:
             return _pointwise_program(pkg, tile, err)
         raise
+
+
+def _serial_program(pkg: KernelPackage, tile: Node, reason: str) -> Plan:
+    """A body with per-point runtime loops that no recogniser took: a serial program."""
+    from .serial import compile_serial
+    try:
+        return compile_serial(pkg, tile)
+    except CompileError as err:
+        raise CompileError(f"{reason}; as a serial program: {err}") from err
 
 
 def _pointwise_program(pkg: KernelPackage, tile: Node, reason: CompileError) -> Plan:

@@ -67,7 +67,7 @@ SIGNATURES = {
 # pointwise programs (include/lazyb200.h lc_pw_program)
 LC_S32 = 3
 STORAGE_CODES = {"f32": LC_F32, "f16": LC_F16, "bf16": LC_BF16, "s32": LC_S32}
-PW_MAX_CODE, PW_MAX_CONST, PW_MAX_FORMS, PW_MAX_BUFFERS, PW_MAX_AXES = 1024, 128, 32, 16, 4
+PW_MAX_CODE, PW_MAX_CONST, PW_MAX_FORMS, PW_MAX_BUFFERS, PW_MAX_AXES = 1024, 128, 32, 16, 8
 
 
 class PwForm(ctypes.Structure):
@@ -78,6 +78,7 @@ class PwForm(ctypes.Structure):
 class PwProgram(ctypes.Structure):
     _fields_ = [("n_code", ctypes.c_int32), ("n_consts", ctypes.c_int32), ("n_forms", ctypes.c_int32),
                 ("n_buffers", ctypes.c_int32), ("n_axes", ctypes.c_int32), ("n_regs", ctypes.c_int32),
+                ("n_loops", ctypes.c_int32), ("reserved", ctypes.c_int32),
                 ("extents", ctypes.c_int64 * PW_MAX_AXES), ("sizes", ctypes.c_int64 * PW_MAX_BUFFERS),
                 ("code", (ctypes.c_uint32 * 2) * PW_MAX_CODE), ("consts", ctypes.c_uint32 * PW_MAX_CONST),
                 ("forms", PwForm * PW_MAX_FORMS)]
@@ -88,7 +89,9 @@ def pw_program(prog: dict) -> PwProgram:
     g = PwProgram()
     g.n_code, g.n_consts, g.n_forms = len(prog["code"]), len(prog["consts"]), len(prog["forms"])
     g.n_buffers, g.n_axes, g.n_regs = len(prog["buffers"]), len(prog["extents"]), max(1, prog["n_regs"])
-    for d, e in enumerate(prog["extents"]):
+    loops = prog.get("loops", [])
+    g.n_loops = len(loops)
+    for d, e in enumerate(list(prog["extents"]) + list(loops)):
         g.extents[d] = e
     for i, size in enumerate(prog["sizes"]):
         g.sizes[i] = size

@@ -1,0 +1,210 @@
+"""Serial programs: per-point bodies with runtime loops.
+
+The reference's schedules give some matmul and attention-like IR (the
+scalar a02 attention, small contractions) the serial form: every tile point
+is one output element, and its thread runs Loop nests with Accum statements
+in registers (ptx_backend.py:1496-1554: an s32 induction variable, the
+accumulators seeded with their identity on loop entry, ``base`` giving the
+coupled online-softmax updates) before a Write.  This module compiles such a
+body, when no recogniser takes it, to a register program for
+csrc/pointwise.cu:
+
+* the tile axes are the point space; each loop is a runtime loop
+  (LOOPB / LOOPE) whose counter is an extra coordinate that loads and
+  stores may be affine in;
+* an accumulator lives in a fixed register, set to its identity where the
+  IR seeds it (a seeded loop's entry, or an Init) and updated in statement
+  order as ``op(base or accumulator, value)``;
+* values computed before a loop and read inside it stay live for the whole
+  loop (the register allocator extends them across the back edge);
+* every output element must be written exactly once over the tile points
+  and the loop iterations that enclose the write.
+
+Loops with a per-thread start, a captured end or a non-unit step, and
+conditional statements, are not taken here.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from .ir import CompileError, KernelPackage, Node, static_extent
+from .pointwise import MAX_AXES, MAX_CODE, MAX_CONST, OP, PointwiseCompiler, Program, Val, vm_type
+
+IDENTITY = {"add": 0.0, "sum": 0.0, "multiply": 1.0, "prod": 1.0, "maximum": -math.inf, "max": -math.inf,
+            "minimum": math.inf, "min": math.inf}
+
+
+class SerialCompiler(PointwiseCompiler):
+    """Lowers a per-point body with runtime loops (see the module docstring)."""
+
+    def __init__(self, pkg: KernelPackage, tile: Node):
+        super().__init__(pkg, tile)
+        self.tile_axes = len(self.axes)
+        self.loop_extents: list = []
+        self.loop_ranges: list = []     # (LOOPB pc, LOOPE pc)
+        self.loop_stack: list = []      # slots of the enclosing loops
+        self.accs: dict = {}            # accumulator -> fixed register id
+        self.n_fixed = 0
+        self.store_loops: list = []     # (buffer, form, enclosing loop slots)
+
+    # ------------------------------------------------------------ statements
+    def statement(self, s: Node) -> None:
+        k = s.kind
+        if k in ("Loop", "StridedLoop"):
+            self.loop(s)
+        elif k == "Accum":
+            self.accum(s)
+        elif k == "Init":
+            reg = self.acc_register(s.name)
+            self.put(reg, self.literal(float(s.identity), vm_type(s.get("dtype") or "f32")))
+        elif k == "Write":
+            before = len(self.writes)
+            super().statement(s)
+            for buffer, form in self.writes[before:]:
+                self.store_loops.append((buffer, form, tuple(self.loop_stack)))
+        elif k in ("Load", "Let", "Assign", "Select"):
+            super().statement(s)
+        else:
+            raise CompileError(f"{k} is not part of a serial program")
+
+    def acc_register(self, name: str) -> int:
+        if name not in self.accs:
+            self.accs[name] = -1 - self.n_fixed
+            self.n_fixed += 1
+        reg = self.accs[name]
+        self.env[name] = Val(reg, "f32")
+        return reg
+
+    def put(self, reg: int, v: Val) -> None:
+        self.code.append((OP["MOV"], reg, self.convert(v, "f32").reg, 0, 0, 0, 1, True))
+
+    def accum(self, s: Node) -> None:
+        op = s.op.name if isinstance(s.op, Node) else str(s.op)
+        reg = self.acc_register(s.name)
+        base = self.lookup(s.base) if s.get("base") else Val(reg, "f32")
+        value = self.lookup(s.value) if isinstance(s.value, str) else self.expr(s.value)
+        dt = vm_type(s.get("dtype") or "f32")
+        if dt != "f32":
+            raise CompileError("serial accumulators are f32")
+        new = self.operation(op, [self.convert(base, "f32"), self.convert(value, "f32")], "f32")
+        self.put(reg, new)
+        self.env[s.name] = Val(reg, "f32")
+
+    def loop(self, s: Node) -> None:
+        if s.kind == "StridedLoop":
+            start, step = s.get("start"), s.get("step")
+            if s.get("end") is not None or not _is_int(start, 0) or not _is_int(step, 1):
+                raise CompileError("serial loops count from 0 in steps of 1 over their extent")
+        extent = static_extent(s.axis.extent)
+        slot = len(self.loop_extents)
+        if self.tile_axes + slot + 1 > MAX_AXES:
+            raise CompileError("too many loops for a serial program")
+        self.loop_extents.append(extent)
+        self.axes.append(s.axis.name)
+        self.extents = tuple(self.extents) + (extent,)
+        if s.get("seed", True):
+            for inner in s.body:
+                if isinstance(inner, Node) and inner.kind == "Accum":
+                    op = inner.op.name if isinstance(inner.op, Node) else str(inner.op)
+                    if op not in IDENTITY:
+                        raise CompileError(f"no identity for accumulator operation {op}")
+                    self.put(self.acc_register(inner.name), self.literal(IDENTITY[op], "f32"))
+        self.__dict__["_memo"] = {}
+        begin = len(self.code)
+        self.code.append([OP["LOOPB"], 0, 0, 0, 0, 0, 0, False])
+        self.loop_stack.append(slot)
+        saved = dict(self.env)
+        for inner in s.body:
+            self.statement(inner)
+        # names bound inside the loop go out of scope; accumulators stay visible
+        self.env = {**saved, **{n: Val(r, "f32") for n, r in self.accs.items()}}
+        self.loop_stack.pop()
+        self.__dict__["_memo"] = {}
+        end = len(self.code)
+        self.code.append([OP["LOOPE"], 0, 0, 0, 0, 0, 0, False])
+        self.code[begin] = (OP["LOOPB"], 0, 0, 0, 0, slot | end << 4, 0, False)
+        self.code[end] = (OP["LOOPE"], 0, 0, 0, 0, slot | begin << 4, 0, False)
+        self.loop_ranges.append((begin, end))
+
+    # ------------------------------------------------------------ registers
+    def allocate(self) -> list:
+        """Linear scan, with values read inside a loop but defined before it kept
+        allocated to the loop's end (the back edge reads them again)."""
+        defined: dict = {}
+        for pc, (op, dst, a, b, c, aux, nsrc, has_dst) in enumerate(self.code):
+            if has_dst and dst >= 0:
+                defined.setdefault(dst, pc)
+        extend: dict = {}
+        for begin, end in self.loop_ranges:
+            for pc in range(begin, end + 1):
+                op, dst, a, b, c, aux, nsrc, has_dst = self.code[pc]
+                for r in (a, b, c)[:nsrc]:
+                    if r >= 0 and defined.get(r, 0) < begin:
+                        extend[r] = max(extend.get(r, 0), end)
+        return super().allocate(extend)
+
+    # ------------------------------------------------------------ finishing
+    def serial_coverage(self) -> str:
+        outs = {b for b, _, _ in self.store_loops}
+        if len(outs) != 1:
+            raise CompileError("serial programs write one output")
+        out = outs.pop()
+        size = math.prod(self.pkg.buffers[out].shape or (1,))
+        points = math.prod(self.extents[:self.tile_axes])
+        total = sum(points * math.prod(self.loop_extents[sl] for sl in loops) for _, _, loops in self.store_loops)
+        if total != size or total > (1 << 26):
+            raise CompileError(f"serial writes cover {total} elements of {out} ({size})")
+        seen = np.zeros(size, np.int64)
+        for _, f, loops in self.store_loops:
+            form = self.forms[f]
+            dims = list(range(self.tile_axes)) + [self.tile_axes + sl for sl in loops]
+            grids = np.meshgrid(*[np.arange(self.extents[d], dtype=np.int64) for d in dims], indexing="ij")
+            flat = form.base + sum(form.coef[d] * g for d, g in zip(dims, grids))
+            np.add.at(seen, np.asarray(flat).ravel(), 1)
+        if np.any(seen != 1):
+            raise CompileError("serial writes do not cover the output exactly once")
+        return out
+
+    def compile_serial(self, body: tuple) -> Program:
+        for s in body:
+            self.statement(s)
+        if not self.store_loops:
+            raise CompileError("serial program writes nothing")
+        out = self.serial_coverage()
+        n_coords = self.tile_axes + len(self.loop_extents)
+        for f in self.forms:
+            f.coef = tuple(f.coef) + (0,) * (n_coords - len(f.coef))
+        code, nregs = self.allocate()
+        if len(code) > MAX_CODE or len(self.consts) > MAX_CONST:
+            raise CompileError("serial program too long")
+        consts = [0] * len(self.consts)
+        for word, i in self.consts.items():
+            consts[i] = word
+        names = list(self.slots)
+        prog = Program(code, consts, self.forms, names, tuple(self.extents[:self.tile_axes]), nregs,
+                       [math.prod(self.pkg.buffers[b].shape or (1,)) for b in names], list(self.loop_extents))
+        self.out = out
+        return prog
+
+
+def _is_int(e, value: int) -> bool:
+    if e is None:
+        return True
+    if isinstance(e, int):
+        return e == value
+    return isinstance(e, Node) and e.kind == "Literal" and e.value == value
+
+
+def compile_serial(pkg: KernelPackage, tile: Node):
+    """Plan of a per-point body with runtime loops as a serial program."""
+    from .recognize import _plan
+    comp = SerialCompiler(pkg, tile)
+    prog = comp.compile_serial(tuple(tile.body))
+    bind = {f"buf{i}": name for i, name in enumerate(prog.buffers)}
+    return _plan(pkg, "pointwise", "lc_pointwise", bind,
+                 {"program": prog.to_json(), "out": comp.out, "points": math.prod(prog.extents), "serial": True},
+                 {name: pkg.buffers[name].dtype for name in prog.buffers})
+
+

@@ -370,3 +370,60 @@ def _softmax_times_x(folder):
 
 
 ROW_COUPLED = {"log_softmax": _log_softmax, "softmax_times_x": _softmax_times_x}
+
+
+# ---------------------------------------------------------------- serial programs (per-point runtime loops)
+
+def serial_package(folder: Path, name: str, inputs: dict, output: tuple, axes: list, body: list, rtol=1e-5,
+                   atol=1e-6) -> Path:
+    return package(folder, name, inputs, output, axes, body, rtol=rtol, atol=atol)
+
+
+def loop(name, extent, body, seed=True):
+    return (f"Loop(axis=Axis(name='{name}', extent=Dim({extent}), window=None), body=({', '.join(body)},), "
+            f"unroll=False, seed={seed})")
+
+
+def accum(name, value, op, base=None):
+    b = repr(base) if base else "None"
+    return f"Accum(name='{name}', value='{value}', op=ElementwiseImpl('{op}'), dtype={dt('f32')}, axes=(), base={b})"
+
+
+def _serial_matmul_relu(folder):
+    i, j, k = var("i"), var("j"), var("k")
+    return serial_package(folder, "serial_matmul_relu", {"a": ((24, 40), "f32"), "b": ((40, 17), "f32"),
+                                                         "bias": ((17,), "f32")},
+                          ("out", (24, 17), "f32"), [("i", 24), ("j", 17)],
+                          [loop("k", 40, [load("av", "a", [i, k], "f32"), load("bv", "b", [k, j], "f32"),
+                                          assign("p", "multiply", ["av", "bv"], "f32"), accum("acc", "p", "add")]),
+                           load("cv", "bias", [j], "f32"), assign("s", "add", ["acc", "cv"], "f32"),
+                           assign("r", "relu", ["s"], "f32"), write("out", [i, j], ["r"], "f32")])
+
+
+def _serial_row_max_argmax_value(folder):
+    """Per point: the max over k of |x[i, k] * w[k]| (a serial max reduction)."""
+    i, k = var("i"), var("k")
+    return serial_package(folder, "serial_max_abs", {"x": ((50, 70), "f32"), "w": ((70,), "f32")},
+                          ("out", (50,), "f32"), [("i", 50)],
+                          [loop("k", 70, [load("xv", "x", [i, k], "f32"), load("wv", "w", [k], "f32"),
+                                          assign("p", "multiply", ["xv", "wv"], "f32"),
+                                          assign("q", "abs", ["p"], "f32"), accum("m", "q", "maximum")]),
+                           write("out", [i], ["m"], "f32")])
+
+
+def _serial_nested(folder):
+    """Nested loops: out[i] = sum_k exp(sum_d q[i, d] * kt[d, k] / 4)."""
+    i, k, d = var("i"), var("k"), var("d")
+    return serial_package(folder, "serial_nested", {"q": ((12, 8), "f32"), "kt": ((8, 20), "f32")},
+                          ("out", (12,), "f32"), [("i", 12)],
+                          [let("quarter", lit(0.25, "f32"), "f32"),
+                           loop("k", 20, [loop("d", 8, [load("qv", "q", [i, d], "f32"), load("kv", "kt", [d, k], "f32"),
+                                                        assign("p", "multiply", ["qv", "kv"], "f32"),
+                                                        accum("dot", "p", "add")]),
+                                          assign("s", "multiply", ["dot", "quarter"], "f32"),
+                                          assign("e", "exp", ["s"], "f32"), accum("tot", "e", "add")]),
+                           write("out", [i], ["tot"], "f32")], rtol=1e-5, atol=1e-6)
+
+
+SERIAL_SYNTHETIC = {"serial_matmul_relu": _serial_matmul_relu, "serial_max_abs": _serial_row_max_argmax_value,
+                    "serial_nested": _serial_nested}

@@ -92,7 +92,25 @@ def run(prog: dict, arrays: dict, coords=None, states=None, partials=None, partn
     r = {}
     consts = np.asarray(prog["consts"], np.uint64).astype(np.uint32)
     with np.errstate(all="ignore"):
-        for op, dst, a, b, c, aux in prog["code"]:
+        code = prog["code"]
+        loops = list(prog.get("loops", []))
+        coords = list(coords) + [np.zeros(n, np.int64) for _ in loops]   # loop counters follow the axes
+        n_axes = len(coords) - len(loops)
+        pc = -1
+        while pc + 1 < len(code):
+            pc += 1
+            op, dst, a, b, c, aux = code[pc]
+            if OPCODES[op] == "LOOPB":
+                coords[n_axes + (aux & 15)] = np.zeros(n, np.int64)
+                if loops[aux & 15] <= 0:
+                    pc = aux >> 4
+                continue
+            if OPCODES[op] == "LOOPE":
+                d = n_axes + (aux & 15)
+                coords[d] = coords[d] + 1
+                if coords[d][0] < loops[aux & 15]:
+                    pc = aux >> 4
+                continue
             name = OPCODES[op]
             A, B, C = r.get(a), r.get(b), r.get(c)
             if name.startswith(("LD_", "ST_")):
