@@ -316,10 +316,11 @@ int lc_probe_mma(int variant, int groups, void *stream);
  *
  * Serial programs (per-point runtime loops, the reference's Loop with Accum
  * inside one thread's work, ptx_backend.py:1496-1554) use LOOPB / LOOPE:
- * aux = slot | pc << 4; loop `slot` counts coordinate n_axes + slot from 0
- * to extents[n_axes + slot]; LOOPB jumps past its LOOPE (pc) when the extent
- * is 0, LOOPE jumps back to its LOOPB (pc) while the count is below it.
- * Forms may depend on loop coordinates. */
+ * aux = depth | pc << 4; the loop at nesting `depth` counts coordinate
+ * n_axes + depth from 0 to the s32 in register a, never past
+ * extents[n_axes + depth] (the largest extent of any loop at that depth,
+ * over which the forms are validated); LOOPB jumps past its LOOPE (pc) when
+ * the count is empty, LOOPE jumps back to its LOOPB (pc) while below it. */
 #define LC_PW_MAX_CODE 1024
 #define LC_PW_MAX_CONST 128
 #define LC_PW_MAX_FORMS 32
@@ -447,7 +448,8 @@ int lc_pointwise(const lc_pw_program *program, void *const *buffers, void *strea
  * Reductions and fused row operations (the reference's categories 2 and 4:
  * StridedLoop passes over a row with Accum, WarpShuffle / TreeHalve combines,
  * a guarded per-row write or a further, writing pass; ptx_backend.py:1496-1744)
- * as register programs over the point space (row, column) = extents[0..1].
+ * as register programs over the point space (row coordinates..., column):
+ * extents[0 .. n_axes-2] are the row axes, extents[n_axes-1] the column.
  * One CTA per row.  For each pass, every thread seeds its partials of the
  * pass's states (state_init), runs operations [begin, end) for each column it
  * strides over (PARTIAL reads and SETP writes its running partial, so an

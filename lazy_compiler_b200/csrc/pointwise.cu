@@ -211,15 +211,17 @@ __device__ __forceinline__ void exec_range(const lc_pw_program &g, void *const *
         out = w(rv);
         break;
       }
-      case LC_PW_LOOPB: {  // enter loop (aux & 15): count from 0, skip the body of an empty loop
+      case LC_PW_LOOPB: {  // enter a loop at depth aux & 15: count from 0, skip an empty body
         const int d = g.n_axes + (aux & 15);
+        const int64_t limit = min((int64_t)ia, g.extents[d]);  // never past the validated extent
         x[d] = 0;
-        if (g.extents[d] <= 0) pc = aux >> 4;
+        if (limit <= 0) pc = aux >> 4;
         continue;
       }
-      case LC_PW_LOOPE: {  // next iteration of loop (aux & 15), back to its LOOPB
+      case LC_PW_LOOPE: {  // next iteration, back to the matching LOOPB
         const int d = g.n_axes + (aux & 15);
-        if (++x[d] < g.extents[d]) pc = aux >> 4;
+        const int64_t limit = min((int64_t)ia, g.extents[d]);
+        if (++x[d] < limit) pc = aux >> 4;
         continue;
       }
       case LC_PW_STATE: out = w(states[aux]); break;
@@ -268,10 +270,17 @@ __global__ void __launch_bounds__(256) rowprog_kernel(const __grid_constant__ Ro
   for (int k = 0; k < LC_RP_MAX_STATES; ++k) states[k] = partials[k] = partners[k] = 0.0f;
   const lc_pw_program &g = p.prog;
   const lc_rp_layout &lay = p.lay;
-  const int64_t rows = g.extents[0], cols = g.extents[1];
+  const int R = g.n_axes - 1;   // row coordinates, then the column
+  int64_t rows = 1;
+  for (int d = 0; d < R; ++d) rows *= g.extents[d];
+  const int64_t cols = g.extents[R];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-    int64_t xr[LC_PW_MAX_AXES] = {row, 0, 0, 0, 0, 0, 0, 0};
+    int64_t xr[LC_PW_MAX_AXES] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int64_t rest = row, d = R - 1; d >= 0; --d) {
+      xr[d] = rest % g.extents[d];
+      rest /= g.extents[d];
+    }
     for (int pass = 0; pass < lay.n_passes; ++pass) {
       bool has_states = false;
       for (int k = 0; k < lay.n_states; ++k)
@@ -280,7 +289,9 @@ __global__ void __launch_bounds__(256) rowprog_kernel(const __grid_constant__ Ro
           has_states = true;
         }
       for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
-        int64_t x[LC_PW_MAX_AXES] = {row, c, 0, 0, 0, 0, 0, 0};
+        int64_t x[LC_PW_MAX_AXES];
+        for (int d = 0; d < LC_PW_MAX_AXES; ++d) x[d] = xr[d];
+        x[R] = c;
         exec_range(g, p.buffers, x, r, lay.begin[pass], lay.end[pass], states, partials, partners);
       }
       if (!has_states) continue;  // uniform: the layout is the same for every thread
@@ -406,7 +417,7 @@ int validate_program(const char *name, const lc_pw_program *program, void *const
         (aux >= g.n_forms || g.forms[aux].dtype != storage_of(op)))
       return fail(LC_ERR_INVALID, "%s: form or storage type mismatch at %d", name, pc);
   }
-  if (row_program && (lockstep || g.n_axes != 2))
+  if (row_program && (lockstep || g.n_axes < 2))
     return fail(LC_ERR_INVALID, "%s: a row program runs over (row, column) without warp operations", name);
   if (lockstep && points % 32 != 0)
     return fail(LC_ERR_INVALID, "%s: a program that shuffles or multiplies needs whole warps of points", name);
@@ -460,7 +471,8 @@ extern "C" int lc_rowprog(const lc_pw_program *program, const lc_rp_layout *layo
   args.prog = *program;
   args.lay = lay;
   for (int i = 0; i < LC_PW_MAX_BUFFERS; ++i) args.buffers[i] = i < program->n_buffers ? buffers[i] : nullptr;
-  const int64_t rows = program->extents[0];
+  int64_t rows = 1;
+  for (int d = 0; d + 1 < program->n_axes; ++d) rows *= program->extents[d];
   int64_t blocks = rows;
   const int64_t cap = (int64_t)sm_count() * 8;
   if (blocks > cap) blocks = cap;

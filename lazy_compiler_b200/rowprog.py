@@ -46,16 +46,16 @@ class RowProgramCompiler(PointwiseCompiler):
 
     def __init__(self, pkg: KernelPackage, tile: Node, ev):
         axes = [(a.name, static_extent(a.extent)) for a in tile.axes]
-        if not 1 <= len(axes) <= 2:
-            raise CompileError("row programs take a [row,] cooperative Tile")
+        if not 1 <= len(axes) <= 7:
+            raise CompileError("row programs take row axes and one cooperative axis")
         self.pkg = pkg
         self.ev = ev
         self.co, self.block = axes[-1]
         block = tile.get("block_threads") or self.block
         if block != self.block:
             raise CompileError("the cooperative axis must span the block")
-        self.row = axes[0][0] if len(axes) == 2 else "__row"
-        self.rows = axes[0][1] if len(axes) == 2 else 1
+        self.row_axes = axes[:-1] or [("__row", 1)]
+        self.rows = math.prod(e for _, e in self.row_axes)
         self.code, self.consts, self.forms, self.form_index = [], {}, [], {}
         self.slots, self.env, self.nvreg, self.writes = {}, {}, 0, []
         self.state_slot: dict = {}   # accumulator -> slot, once its pass has combined
@@ -210,9 +210,9 @@ class RowProgramCompiler(PointwiseCompiler):
         if len(combines) != len(loops):
             raise CompileError("row-program passes must be top-level loops")
         inits = {s.name: float(s.identity) for s in self.tile.body if s.kind == "Init"}
-        self.extents = (self.rows, self.cols)
+        self.extents = tuple(e for _, e in self.row_axes) + (self.cols,)
         for p, loop in enumerate(loops):
-            self.axes = [self.row, loop["axis"]]
+            self.axes = [n for n, _ in self.row_axes] + [loop["axis"]]
             accs = [n for n in loop["accums"] if n in reds]
             slots = {}
             for name in accs:
@@ -253,7 +253,7 @@ class RowProgramCompiler(PointwiseCompiler):
                 self.tree_ranges.append((0, 0))
             self.live = {}
             self.state_slot.update(slots)
-        self.axes = [self.row, "__col"]
+        self.axes = [n for n, _ in self.row_axes] + ["__col"]
         final_begin = self.begin_range()
         for w in ev.writes:
             if w["loop"] is None:
@@ -273,7 +273,9 @@ class RowProgramCompiler(PointwiseCompiler):
 
     def check_coverage(self) -> None:
         outs = {b for b, _ in self.pass_writes + self.final_writes}
-        rows = np.arange(self.rows, dtype=np.int64)
+        R = len(self.row_axes)
+        row_grid = np.meshgrid(*[np.arange(e, dtype=np.int64) for _, e in self.row_axes], indexing="ij")
+        row_coords = [g.ravel() for g in row_grid]
         for out in outs:
             size = math.prod(self.pkg.buffers[out].shape or (1,))
             if size > (1 << 26):
@@ -283,13 +285,14 @@ class RowProgramCompiler(PointwiseCompiler):
                 if b != out:
                     continue
                 form = self.forms[f]
-                r, c = np.meshgrid(rows, np.arange(self.cols, dtype=np.int64), indexing="ij")
-                np.add.at(seen, (form.base + form.coef[0] * r + form.coef[1] * c).ravel(), 1)
+                flat = form.base + sum(form.coef[d] * row_coords[d] for d in range(R))
+                cols = np.arange(self.cols, dtype=np.int64)
+                np.add.at(seen, (flat[:, None] + form.coef[R] * cols[None, :]).ravel(), 1)
             for b, f in self.final_writes:
                 if b != out:
                     continue
                 form = self.forms[f]
-                np.add.at(seen, form.base + form.coef[0] * rows, 1)
+                np.add.at(seen, form.base + sum(form.coef[d] * row_coords[d] for d in range(R)), 1)
             if np.any(seen != 1):
                 raise CompileError(f"row-program writes do not cover {out} exactly once")
 
@@ -317,7 +320,7 @@ def compile_rowprog(pkg: KernelPackage, tile: Node, ev):
     for word, i in comp.consts.items():
         consts[i] = word
     names = list(comp.slots)
-    prog = Program(code, consts, comp.forms, names, (comp.rows, comp.cols), nregs,
+    prog = Program(code, consts, comp.forms, names, tuple(e for _, e in comp.row_axes) + (comp.cols,), nregs,
                    [math.prod(pkg.buffers[b].shape or (1,)) for b in names])
     bind = {f"buf{i}": name for i, name in enumerate(names)}
     outs = sorted({b for b, _ in comp.pass_writes + comp.final_writes})

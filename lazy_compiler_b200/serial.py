@@ -44,10 +44,18 @@ class SerialCompiler(PointwiseCompiler):
         self.tile_axes = len(self.axes)
         self.loop_extents: list = []
         self.loop_ranges: list = []     # (LOOPB pc, LOOPE pc)
-        self.loop_stack: list = []      # slots of the enclosing loops
+        self.loop_stack: list = []      # (depth, extent) of the enclosing loops
         self.accs: dict = {}            # accumulator -> fixed register id
         self.n_fixed = 0
         self.store_loops: list = []     # (buffer, form, enclosing loop slots)
+        self.active: dict = {}          # loop variable -> its coordinate in the innermost enclosing loop
+
+    def affine(self, e) -> dict:
+        if isinstance(e, Node) and e.kind == "Var" and e.name in self.active:
+            return {self.active[e.name]: 1}
+        if isinstance(e, Node) and e.kind == "Var" and e.name not in self.axes[:self.tile_axes]:
+            raise CompileError(f"index variable {e.name!r} is not a tile axis or an enclosing loop")
+        return super().affine(e)
 
     # ------------------------------------------------------------ statements
     def statement(self, s: Node) -> None:
@@ -98,12 +106,20 @@ class SerialCompiler(PointwiseCompiler):
             if s.get("end") is not None or not _is_int(start, 0) or not _is_int(step, 1):
                 raise CompileError("serial loops count from 0 in steps of 1 over their extent")
         extent = static_extent(s.axis.extent)
-        slot = len(self.loop_extents)
-        if self.tile_axes + slot + 1 > MAX_AXES:
-            raise CompileError("too many loops for a serial program")
-        self.loop_extents.append(extent)
-        self.axes.append(s.axis.name)
-        self.extents = tuple(self.extents) + (extent,)
+        depth = len(self.loop_stack)       # loops at one depth are never active together
+        if self.tile_axes + depth + 1 > MAX_AXES:
+            raise CompileError("loops nested too deep for a serial program")
+        internal = f"#{depth}"
+        if depth == len(self.loop_extents):
+            self.loop_extents.append(extent)
+            self.axes.append(internal)
+            self.extents = tuple(self.extents) + (extent,)
+        else:
+            self.loop_extents[depth] = max(self.loop_extents[depth], extent)
+            self.extents = tuple(self.extents[:self.tile_axes + depth]) + (extent,) + \
+                tuple(self.extents[self.tile_axes + depth + 1:])
+        outer_binding = self.active.get(s.axis.name)
+        self.active[s.axis.name] = internal
         if s.get("seed", True):
             for inner in s.body:
                 if isinstance(inner, Node) and inner.kind == "Accum":
@@ -112,20 +128,25 @@ class SerialCompiler(PointwiseCompiler):
                         raise CompileError(f"no identity for accumulator operation {op}")
                     self.put(self.acc_register(inner.name), self.literal(IDENTITY[op], "f32"))
         self.__dict__["_memo"] = {}
+        count = self.literal(extent, "s32")
         begin = len(self.code)
-        self.code.append([OP["LOOPB"], 0, 0, 0, 0, 0, 0, False])
-        self.loop_stack.append(slot)
+        self.code.append(None)
+        self.loop_stack.append((depth, extent))
         saved = dict(self.env)
         for inner in s.body:
             self.statement(inner)
         # names bound inside the loop go out of scope; accumulators stay visible
         self.env = {**saved, **{n: Val(r, "f32") for n, r in self.accs.items()}}
         self.loop_stack.pop()
+        if outer_binding is None:
+            self.active.pop(s.axis.name, None)
+        else:
+            self.active[s.axis.name] = outer_binding
         self.__dict__["_memo"] = {}
         end = len(self.code)
-        self.code.append([OP["LOOPE"], 0, 0, 0, 0, 0, 0, False])
-        self.code[begin] = (OP["LOOPB"], 0, 0, 0, 0, slot | end << 4, 0, False)
-        self.code[end] = (OP["LOOPE"], 0, 0, 0, 0, slot | begin << 4, 0, False)
+        self.code.append(None)
+        self.code[begin] = (OP["LOOPB"], 0, count.reg, 0, 0, depth | end << 4, 1, False)
+        self.code[end] = (OP["LOOPE"], 0, count.reg, 0, 0, depth | begin << 4, 1, False)
         self.loop_ranges.append((begin, end))
 
     # ------------------------------------------------------------ registers
@@ -153,14 +174,15 @@ class SerialCompiler(PointwiseCompiler):
         out = outs.pop()
         size = math.prod(self.pkg.buffers[out].shape or (1,))
         points = math.prod(self.extents[:self.tile_axes])
-        total = sum(points * math.prod(self.loop_extents[sl] for sl in loops) for _, _, loops in self.store_loops)
+        total = sum(points * math.prod(ext for _, ext in loops) for _, _, loops in self.store_loops)
         if total != size or total > (1 << 26):
             raise CompileError(f"serial writes cover {total} elements of {out} ({size})")
         seen = np.zeros(size, np.int64)
         for _, f, loops in self.store_loops:
             form = self.forms[f]
-            dims = list(range(self.tile_axes)) + [self.tile_axes + sl for sl in loops]
-            grids = np.meshgrid(*[np.arange(self.extents[d], dtype=np.int64) for d in dims], indexing="ij")
+            dims = list(range(self.tile_axes)) + [self.tile_axes + depth for depth, _ in loops]
+            sizes = list(self.extents[:self.tile_axes]) + [ext for _, ext in loops]
+            grids = np.meshgrid(*[np.arange(e, dtype=np.int64) for e in sizes], indexing="ij")
             flat = form.base + sum(form.coef[d] * g for d, g in zip(dims, grids))
             np.add.at(seen, np.asarray(flat).ravel(), 1)
         if np.any(seen != 1):

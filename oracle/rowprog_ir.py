@@ -33,16 +33,18 @@ class RowOracle(PointwiseOracle):
         axes = [(a.name, int(a.extent.value)) for a in tile.axes]
         self.pkg = pkg
         self.co, self.block = axes[-1]
-        self.row = axes[0][0] if len(axes) == 2 else "__row"
-        self.rows = axes[0][1] if len(axes) == 2 else 1
+        self.row_axes = axes[:-1] or [("__row", 1)]
+        self.rows = int(np.prod([e for _, e in self.row_axes]))
+        grids = np.meshgrid(*[np.arange(e, dtype=np.int64) for _, e in self.row_axes], indexing="ij")
+        self.row_coords = {n: g.ravel() for (n, _), g in zip(self.row_axes, grids)}
         self.arrays = {k: np.asarray(v).ravel() for k, v in arrays.items()}
         self.env = {}
         self.out = {}
         self.set_domain(None, 1)
 
     def set_domain(self, col, cols):
-        r = np.repeat(np.arange(self.rows, dtype=np.int64), cols)
-        self.coord = {self.row: r, self.co: np.zeros_like(r)}
+        self.coord = {n: np.repeat(v, cols) for n, v in self.row_coords.items()}
+        self.coord[self.co] = np.zeros(self.rows * cols, np.int64)
         if col is not None:
             self.coord[col] = np.tile(np.arange(cols, dtype=np.int64), self.rows)
         self.cols = cols
@@ -69,12 +71,12 @@ class RowOracle(PointwiseOracle):
         n = self.rows * block
         part = {nm: np.full(n, ident[nm], np.float32) for nm in names}
         saved = dict(self.env)
-        r = np.repeat(np.arange(self.rows, dtype=np.int64), block)
         t = np.tile(np.arange(block, dtype=np.int64), self.rows)
         for it in range(-(-cols // block)):
             c = it * block + t
             valid = c < cols
-            self.coord = {self.row: r, self.co: t, loop.axis.name: np.minimum(c, cols - 1)}
+            self.coord = {n: np.repeat(v, block) for n, v in self.row_coords.items()}
+            self.coord.update({self.co: t, loop.axis.name: np.minimum(c, cols - 1)})
             self.env = {k: (V(np.repeat(v.a, block), v.t) if isinstance(v, V) and v.a.shape == (self.rows,) else v)
                         for k, v in saved.items()}
             for nm in names:

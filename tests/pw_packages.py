@@ -427,3 +427,39 @@ def _serial_nested(folder):
 
 SERIAL_SYNTHETIC = {"serial_matmul_relu": _serial_matmul_relu, "serial_max_abs": _serial_row_max_argmax_value,
                     "serial_nested": _serial_nested}
+
+
+# ---------------------------------------------------------------- op-mix variants of the reference's packages
+# (package, textual edits of its IR, plan op, oracle module name): bodies a fixed class no longer
+# matches, which must run as the general program they are.
+
+VARIANTS = {
+    "bias_gemm_tanh_gate": ("phase9_bias_gelu_gemm", [("ElementwiseImpl('erf')", "ElementwiseImpl('tanh')")],
+                            "rowprog", "rowprog_ir"),
+    "bias_gemm_relu": ("phase9_bias_gelu_gemm",
+                       [("Assign(name='v6', op=ElementwiseImpl('multiply'), args=('v4', 'v5')",
+                         "Assign(name='v6', op=ElementwiseImpl('relu'), args=('v1',)")], "rowprog", "rowprog_ir"),
+    "attention_sqrt_scale": ("a01_attention", [("ElementwiseImpl('reciprocal')", "ElementwiseImpl('sqrt')")],
+                             "pointwise", "serial_ir"),
+    "attention_128_negated_scale": ("a02_attention_128",
+                                    [("Assign(name='v1', op=ElementwiseImpl('reciprocal'), args=('in0',)",
+                                      "Assign(name='v1', op=ElementwiseImpl('negative'), args=('in0',)")],
+                                    "pointwise", "serial_ir"),
+    "row_sum_of_abs": ("r04_row_sum",
+                       [("Accum(name='acc0', value='in0'", "Assign(name='ax', op=ElementwiseImpl("
+                         "'abs'), args=('in0',), dtype=None), Accum(name='acc0', value='ax'")],
+                       "rowprog", "rowprog_ir"),
+}
+
+
+def variant(folder: Path, name: str) -> Path:
+    import shutil
+    src, edits, _, _ = VARIANTS[name]
+    shutil.copytree(Path(__file__).resolve().parent / "golden" / "packages" / src, folder)
+    ir = next(folder.glob("*.ir.json"))
+    text = ir.read_text()
+    for old, new in edits:
+        assert old in text, old
+        text = text.replace(old, new)
+    ir.write_text(text)
+    return ir

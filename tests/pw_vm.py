@@ -100,16 +100,17 @@ def run(prog: dict, arrays: dict, coords=None, states=None, partials=None, partn
         while pc + 1 < len(code):
             pc += 1
             op, dst, a, b, c, aux = code[pc]
-            if OPCODES[op] == "LOOPB":
-                coords[n_axes + (aux & 15)] = np.zeros(n, np.int64)
-                if loops[aux & 15] <= 0:
-                    pc = aux >> 4
-                continue
-            if OPCODES[op] == "LOOPE":
+            if OPCODES[op] in ("LOOPB", "LOOPE"):
                 d = n_axes + (aux & 15)
-                coords[d] = coords[d] + 1
-                if coords[d][0] < loops[aux & 15]:
-                    pc = aux >> 4
+                limit = min(int(r[a].view(np.int32)[0]), loops[aux & 15])
+                if OPCODES[op] == "LOOPB":
+                    coords[d] = np.zeros(n, np.int64)
+                    if limit <= 0:
+                        pc = aux >> 4
+                else:
+                    coords[d] = coords[d] + 1
+                    if coords[d][0] < limit:
+                        pc = aux >> 4
                 continue
             name = OPCODES[op]
             A, B, C = r.get(a), r.get(b), r.get(c)
@@ -283,11 +284,14 @@ def run_rows(prog: dict, layout: dict, arrays: dict, block: int = 128) -> dict:
     ``block``-wide CTA folds its strided columns into its partials in column
     order, the partials combine thread by thread through the tree's combine
     operations, the final operations run once per row."""
-    rows, cols = prog["extents"]
+    *row_ext, cols = prog["extents"]
+    rows = int(np.prod(row_ext))
     states, outs = {}, {}
-    r_idx = np.repeat(np.arange(rows, dtype=np.int64), block)
+    grids = np.meshgrid(*[np.arange(e, dtype=np.int64) for e in row_ext], indexing="ij")
+    row_coords = [g.ravel() for g in grids]
+    r_coords = [np.repeat(rc, block) for rc in row_coords]
     t_idx = np.tile(np.arange(block, dtype=np.int64), rows)
-    per_row = [np.arange(rows, dtype=np.int64), np.zeros(rows, np.int64)]
+    per_row = row_coords + [np.zeros(rows, np.int64)]
 
     def sub(b, e):
         return dict(prog, code=prog["code"][b:e])
@@ -299,7 +303,7 @@ def run_rows(prog: dict, layout: dict, arrays: dict, block: int = 128) -> dict:
         wide = {k: np.repeat(np.asarray(v, np.float32), block) for k, v in states.items()}
         for it in range(-(-cols // block)):
             c = it * block + t_idx
-            run(sub(b, e), arrays, coords=[r_idx, np.minimum(c, cols - 1)], states=wide, partials=partials,
+            run(sub(b, e), arrays, coords=r_coords + [np.minimum(c, cols - 1)], states=wide, partials=partials,
                 mask=c < cols, outs=outs)
         if slots:
             tb, te = layout["tree"][p]
