@@ -137,9 +137,12 @@ class PointwiseCompiler:
     """Lowers one pointwise Tile body to register operations (see the module docstring)."""
 
     def __init__(self, pkg: KernelPackage, tile: Node):
+        self.setup(pkg, [a.name for a in tile.axes], tuple(static_extent(a.extent) for a in tile.axes))
+
+    def setup(self, pkg: KernelPackage, axes: list, extents: tuple) -> None:
         self.pkg = pkg
-        self.axes = [a.name for a in tile.axes]
-        self.extents = tuple(static_extent(a.extent) for a in tile.axes)
+        self.axes = axes
+        self.extents = extents
         if not 1 <= len(self.axes) <= MAX_AXES:
             raise CompileError("pointwise Tiles take one to four axes")
         if any(e <= 0 for e in self.extents):

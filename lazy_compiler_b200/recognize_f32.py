@@ -39,6 +39,7 @@ from typing import Any
 import numpy as np
 
 from .ir import CompileError, KernelPackage, Node, static_extent
+from .post import compile_epilogue
 from .recognize import (_GELU_ERF_ANY, _GELU_ERF_B_ANY, _GELU_TANH_ANY, Plan, _aff, _aff_add,
                         _aff_const, _Eval, _flat, _is_load, _match, _numel, _plan, _scalar_buffer,
                         _scalar_of, _check_consts, op, V)
@@ -617,7 +618,11 @@ def recognise_staged_gemm(pkg: KernelPackage, tile: Node) -> Plan:
         for lane, value in enumerate(w["values"]):
             col = _aff_add(col0, _aff({1: lane}))
             epi, inner = strip_epilogue(pkg, value)
-            acc, bias = _split_bias(inner, _is_acc, col)
+            try:
+                acc, bias = _split_bias(inner, _is_acc, col)
+            except CompileError:
+                acc, epi = general_epilogue(pkg, value, row, col)
+                bias = None
             terms = ev.terms.get(acc[1])
             if not terms:
                 raise CompileError("staged GEMM writes an accumulator with no products")
@@ -643,6 +648,11 @@ def recognise_staged_gemm(pkg: KernelPackage, tile: Node) -> Plan:
                 ks.append(kf)
             k_sets.append(ks)
     a, b, bias, layout, epi = sig
+    post = None
+    if isinstance(epi, tuple):
+        post, epi = epi[1], "none"
+        if atomic:
+            raise CompileError("split-K partial sums cannot carry an epilogue")
     if atomic and (bias is not None or epi != "none"):
         raise CompileError("split-K partial sums cannot carry a bias or activation")
     k = pkg.buffers[a].shape[1]
@@ -669,7 +679,52 @@ def recognise_staged_gemm(pkg: KernelPackage, tile: Node) -> Plan:
             raise CompileError("the products do not cover the contraction exactly once")
     check_cover(pkg, [(n, e) for n, e in ev.tile_axes if n not in dict(split)], ev.writes, out,
                 repeat=1)
-    return _gemm_plan(pkg, a, b, bias, out, layout, epi, k)
+    plan = _gemm_plan(pkg, a, b, bias, out, layout, epi, k)
+    if post is not None:
+        plan.params["post"] = compile_epilogue(pkg, post, out, plan.params["m"], plan.params["n"])
+    return plan
+
+
+def general_epilogue(pkg: KernelPackage, value, row: frozenset, col: frozenset) -> tuple:
+    """(accumulator, ("expr", e)) for a written value that is any expression of
+    one accumulator, literals, scalar arguments and loads at the output's row
+    and column: e has the accumulator as ("acc",) and each load index
+    component as a constant or ("row" | "col", offset)."""
+    accs = set()
+
+    def component(c):
+        v = _aff_const(c)
+        if v is not None:
+            return v
+        for name, form in (("row", row), ("col", col)):
+            d = _aff_const(_aff_add(c, form, -1))
+            if d is not None:
+                return (name, d)
+        raise CompileError("an epilogue load is not addressed by the output position")
+
+    def norm(e):
+        if not isinstance(e, tuple) or not e:
+            raise CompileError(f"unsupported epilogue value {e!r}")
+        kind = e[0]
+        if kind == "acc":
+            accs.add(e)
+            return ("acc",)
+        if kind in ("lit", "s"):
+            return e
+        if kind == "ld":
+            if e[1] not in pkg.buffers:
+                raise CompileError("an epilogue reads shared memory")
+            return ("ld", e[1], tuple(component(c) for c in e[2]))
+        if kind == "op":
+            return ("op", e[1], *(norm(x) for x in e[2:]))
+        if kind == "cast":
+            return ("cast", e[1], norm(e[2]))
+        raise CompileError(f"unsupported epilogue value {kind}")
+
+    expr = norm(_drop_copies(canon_scalars(pkg, value)))
+    if len(accs) != 1:
+        raise CompileError("a GEMM epilogue must read exactly one accumulator")
+    return accs.pop(), ("expr", expr)
 
 
 # ----------------------------------------------------------------------------

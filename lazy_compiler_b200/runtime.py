@@ -258,3 +258,11 @@ def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
              p["d"], ctypes.c_float(p["scale"]), s)
     else:
         raise ValueError(f"plan op {op!r} has no C-ABI entry point")
+    if "post" in p:
+        # an epilogue program over the result, in place, on the same stream
+        post = p["post"]
+        prog = post["program"]
+        ptrs = (ctypes.c_void_p * PW_MAX_BUFFERS)(*[int(pointers[post["bind"][f"buf{i}"]])
+                                                     for i in range(len(prog["buffers"]))])
+        g = pw_program(prog)
+        call("lc_pointwise", ctypes.c_void_p(ctypes.addressof(g)), ptrs, s)

@@ -305,9 +305,16 @@ def evaluate(plan: dict, arrays: dict, ir=None) -> dict:
     """Reference outputs of one launch plan from named input arrays.
 
     Pointwise-program plans are checked against their IR (``ir``: the
-    package's kernel.ir.json), which oracle/pointwise_ir.py evaluates.
+    package's kernel.ir.json), which oracle/pointwise_ir.py evaluates; plans
+    with an epilogue program against oracle/staged_ir.py.
     """
     op = plan["op"]
+    if "post" in plan["params"]:
+        # a staged matmul storing an expression of its accumulators: the block oracle
+        if ir is None:
+            raise ValueError("plans with an epilogue program are evaluated from their IR: pass ir=")
+        from oracle.staged_ir import evaluate as evaluate_staged
+        return evaluate_staged(ir, arrays)
     if op == "pointwise":
         if ir is None:
             raise ValueError("pointwise plans are evaluated from their IR: pass ir=")

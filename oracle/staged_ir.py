@@ -1,0 +1,223 @@
+"""CPU oracle of block-cooperative Tile bodies — TEST INFRASTRUCTURE ONLY.
+
+Evaluates a Tile the way its blocks run it, over every thread of every block
+at once with numpy, in lockstep: statement by statement, loop iteration by
+loop iteration.  It covers the reference's staged scalar matmul
+(ptx_backend.py:1496-1554 Loop / StridedLoop / Accum, the cp.async copies
+into shared memory and their commit / wait, bar.sync, :1597-1631 plain and
+atomic Writes) and any body built from the same statements:
+
+* the trailing Tile axes whose extents multiply to ``block_threads`` are a
+  block's threads, the leading axes number the blocks; every Smem array is
+  one copy per block, filled with NaN so a read of an element no copy wrote
+  shows in the result;
+* a CpAsyncCopy lands at once (lockstep is one valid order of a race-free
+  program, and the copy's own wait comes before any read of it);
+* a loop with a per-thread start runs, for each thread, the iterations
+  ``start, start + step, ... < extent``; statements of an iteration a thread
+  does not run change nothing for it (accumulators, copies and writes are
+  masked; loads are clamped for masked threads);
+* Init / Accum as in the serial oracle: op(base or accumulator, value) in
+  statement order, an accumulator seeded with its identity on entry to a
+  seeding loop; integer index division and remainder as on non-negative
+  values, TernaryExpr indices per thread.
+
+Scalar rules and accurate float64 transcendentals come from
+oracle/pointwise_ir.py.  It shares only the IR reader with the product.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from oracle.pointwise_ir import PointwiseOracle, V, _t, conv
+from oracle.serial_ir import _IDENTITY
+
+
+class StagedOracle(PointwiseOracle):
+    def __init__(self, pkg, tile, arrays: dict):
+        super().__init__(pkg, tile, arrays)
+        threads = int(tile.get("block_threads") or (pkg.kernel_meta.get("block") or [0])[0])
+        prod, split = 1, len(self.axes)
+        while split > 0 and prod < threads:
+            split -= 1
+            prod *= self.ext[split]
+        if prod != threads:
+            raise ValueError("oracle: the trailing Tile axes do not form the thread block")
+        n = len(next(iter(self.coord.values())))
+        self.n = n
+        block = np.zeros(n, np.int64)
+        for name, extent in zip(self.axes[:split], self.ext[:split]):
+            block = block * extent + self.coord[name]
+        self.block = block
+        self.n_blocks = int(math.prod(self.ext[:split]))
+        self.mask = np.ones(n, bool)
+        self.smem: dict = {}
+        zero = set(pkg.kernel_meta.get("zero_outputs", []))
+        for name, buf in pkg.buffers.items():
+            if buf.role == "output" and name in zero:
+                t = _t(buf.dtype)
+                self.out[name] = np.zeros(math.prod(buf.shape or (1,)), np.float32 if t != "s32" else np.int32)
+
+    # -------------------------------------------------------- indices
+    def index(self, e):
+        if isinstance(e, int):
+            return np.int64(e)
+        if e.kind == "BinaryExpr" and e.op in ("/", "//", "%"):
+            a, b = self.index(e.left), self.index(e.right)
+            b = np.where(b == 0, 1, b)
+            return a // b if e.op != "%" else a % b
+        if e.kind == "BinaryExpr" and e.op in ("<", "<=", ">", ">=", "==", "!="):
+            a, b = self.index(e.left), self.index(e.right)
+            return {"<": a < b, "<=": a <= b, ">": a > b, ">=": a >= b, "==": a == b, "!=": a != b}[e.op]
+        if e.kind == "TernaryExpr":
+            return np.where(self.index(e.cond), self.index(e.if_true), self.index(e.if_false))
+        return super().index(e)
+
+    def _flat_smem(self, name, index):
+        shape = self.smem_shape[name]
+        idx = [np.asarray(self.index(i), np.int64) for i in index]
+        flat = sum(i * math.prod(shape[d + 1:]) for d, i in enumerate(idx))
+        return np.broadcast_to(flat, (self.n,))
+
+    def _clamped(self, flat, size):
+        flat = np.broadcast_to(np.asarray(flat, np.int64), (self.n,))
+        bad = self.mask & ((flat < 0) | (flat >= size))
+        if bad.any():
+            raise IndexError("oracle: an active thread addresses outside its buffer")
+        return np.where(self.mask, flat, 0)
+
+    # -------------------------------------------------------- statements
+    def run_block(self, body) -> None:
+        for s in body:
+            k = s.kind
+            if k == "Smem":
+                if not hasattr(self, "smem_shape"):
+                    self.smem_shape = {}
+                shape = tuple(int(x) for x in s.extents)
+                self.smem_shape[s.name] = shape
+                self.smem[s.name] = np.full((self.n_blocks, math.prod(shape)), np.nan, np.float32)
+            elif k == "CpAsyncCopy":
+                self.copy(s)
+            elif k in ("CpAsyncCommit", "CpAsyncWait", "Sync"):
+                pass
+            elif k == "Load" and s.input in self.smem:
+                size = self.smem[s.input].shape[1]
+                flat = self._flat_smem(s.input, s.index)
+                for lane, name in enumerate(s.names):
+                    self.env[name] = V(self.smem[s.input][self.block, self._clamped(flat + lane, size)], "f32")
+            elif k == "Load":
+                buf = self.pkg.buffers[s.input]
+                size = math.prod(buf.shape or (1,))
+                flat = self.flat(s.input, s.index)
+                t = _t(buf.dtype)
+                for lane, name in enumerate(s.names):
+                    vals = self.arrays[s.input][self._clamped(flat + lane, size)]
+                    self.env[name] = V(np.asarray(vals, np.float32 if t != "s32" else np.int32), t)
+            elif k in ("Loop", "StridedLoop"):
+                self.loop(s)
+            elif k == "Init":
+                self.env[s.name] = V(np.full(self.n, float(s.identity), np.float32), "f32")
+            elif k == "Accum":
+                opname = s.op.name if hasattr(s.op, "name") else str(s.op)
+                old = self.env[s.name]
+                base = self.env[s.base] if s.get("base") else old
+                value = self.env[s.value] if isinstance(s.value, str) else self.expr(s.value)
+                new = conv(self.op(opname, [conv(base, "f32"), conv(value, "f32")], "f32"), "f32")
+                self.env[s.name] = V(np.where(self.mask, new.a, conv(old, "f32").a), "f32")
+            elif k == "Cond":
+                saved = self.mask
+                self.mask = saved & np.broadcast_to(conv(self.expr(s.cond), "pred").a, (self.n,))
+                self.run_block(s.body)
+                self.mask = saved
+                if s.get("else_body"):
+                    self.mask = saved & ~np.broadcast_to(conv(self.expr(s.cond), "pred").a, (self.n,))
+                    self.run_block(s.else_body)
+                    self.mask = saved
+            elif k == "Write":
+                self.write(s)
+            else:
+                self.run([s])
+
+    def copy(self, s) -> None:
+        if s.get("swizzle", "NONE") not in (None, "NONE"):
+            raise ValueError("oracle: swizzled copies")
+        src = self.pkg.buffers[s.src]
+        elems = int(s.nbytes) // np.dtype(np.float32 if _t(src.dtype) == "f32" else np.float16).itemsize
+        sidx = list(s.smem_index)
+        lane = s.get("lane_index")
+        shape = self.smem_shape[s.smem]
+        pos = [np.asarray(self.index(i), np.int64) for i in sidx]
+        if lane is not None:
+            pos = [p + np.asarray(self.index(i), np.int64) for p, i in zip(pos, lane)]
+        dst = np.broadcast_to(sum(p * math.prod(shape[d + 1:]) for d, p in enumerate(pos)), (self.n,))
+        gsrc = self.flat(s.src, s.src_index)
+        size = math.prod(src.shape or (1,))
+        live = self.mask
+        for e in range(elems):
+            g = self._clamped(gsrc + e, size)
+            d = self._clamped(dst + e, self.smem[s.smem].shape[1])
+            vals = np.asarray(self.arrays[s.src][g], np.float32)
+            self.smem[s.smem][self.block[live], d[live]] = vals[live]
+
+    def write(self, s) -> None:
+        buf = self.pkg.buffers[s.output]
+        t = _t(buf.dtype)
+        size = math.prod(buf.shape or (1,))
+        out = self.out.setdefault(s.output, np.full(size, np.nan if t != "s32" else -1,
+                                                    np.float32 if t != "s32" else np.int32))
+        flat = self.flat(s.output, s.index)
+        live = self.mask
+        for lane, name in enumerate(s.values):
+            idx = self._clamped(flat + lane, size)
+            vals = np.broadcast_to(conv(self.env[name], t).a, (self.n,))
+            if s.get("atomic"):
+                acc = out.astype(np.float64)
+                np.add.at(acc, idx[live], vals[live].astype(np.float64))
+                out[:] = acc.astype(out.dtype)
+            else:
+                out[idx[live]] = vals[live]
+
+    def loop(self, s) -> None:
+        extent = int(s.axis.extent.value)
+        start = s.get("start")
+        step = s.get("step")
+        start_v = np.broadcast_to(np.asarray(self.index(start) if start is not None else 0, np.int64), (self.n,))
+        step_v = int(np.asarray(self.index(step))) if step is not None else 1
+        if step_v <= 0 or s.get("end") is not None:
+            raise ValueError("oracle: loops count up to their extent in positive steps")
+        if s.get("seed", True):
+            for inner in s.body:
+                if inner.kind == "Accum":
+                    opname = inner.op.name if hasattr(inner.op, "name") else str(inner.op)
+                    old = self.env.get(inner.name)
+                    seed = np.full(self.n, _IDENTITY[opname], np.float32)
+                    self.env[inner.name] = V(seed if old is None else np.where(self.mask, seed,
+                                                                               conv(old, "f32").a), "f32")
+        saved = self.mask
+        i = 0
+        while True:
+            var = start_v + i * step_v
+            live = saved & (var < extent)
+            if not live.any():
+                break
+            self.mask = live
+            self.coord[s.axis.name] = var
+            self.run_block(s.body)
+            i += 1
+        self.mask = saved
+        self.coord.pop(s.axis.name, None)
+
+    def result(self) -> dict:
+        return {k: v.reshape(tuple(self.pkg.buffers[k].shape) or (1,)) for k, v in self.out.items()}
+
+
+def evaluate(ir_path, arrays: dict) -> dict:
+    """Outputs of the block-cooperative package at ``ir_path`` on named input arrays."""
+    from lazy_compiler_b200.ir import load_package
+    pkg = load_package(ir_path)
+    (tile,) = pkg.body
+    oracle = StagedOracle(pkg, tile, arrays)
+    oracle.run_block(tile.body)
+    return oracle.result()

@@ -463,3 +463,91 @@ def variant(folder: Path, name: str) -> Path:
         text = text.replace(old, new)
     ir.write_text(text)
     return ir
+
+
+# ---------------------------------------------------------------- staged matmul epilogues
+# m01 (the staged cp.async matmul) with an expression of each accumulator
+# written instead of the accumulator; ``epilogue(acc_name, tag)`` returns the
+# statements and the name to write.  ``extra`` adds inputs {name: (shape, seed)}.
+
+def staged_epilogue(folder: Path, epilogue, extra: dict | None = None) -> Path:
+    import re
+    import shutil
+    shutil.copytree(Path(__file__).resolve().parent / "golden" / "packages" / "m01_matmul_512", folder)
+    ir = next(folder.glob("*.ir.json"))
+    graph = json.loads(ir.read_text())
+    node = graph["nodes"]["matmul"]
+    body = node["op_fields"]["body"][0]
+    pieces, pos, count = [], 0, 0
+    for m in re.finditer(r"Write\(output='matmul', index=\((.*?)\), values=\(([^)]*)\)", body):
+        row, col = _split_top(m.group(1))
+        names = [n.strip().strip("'") for n in m.group(2).split(",") if n.strip()]
+        stmts, new = [], []
+        for lane, name in enumerate(names):
+            s, out = epilogue(name, f"e{count}", row, bin_("+", col, lit(lane)))
+            count += 1
+            stmts += s
+            new.append(out)
+        pieces.append(body[pos:m.start()])
+        pieces.append(", ".join(stmts) + ", ")
+        values = ", ".join(f"'{n}'" for n in new) + ("," if len(new) == 1 else "")
+        pieces.append(body[m.start():m.start(2)] + values)
+        pos = m.end(2)
+    pieces.append(body[pos:])
+    node["op_fields"]["body"][0] = "".join(pieces)
+    meta = json.loads((folder / "meta.json").read_text())
+    kernel = meta["kernels"][0]
+    for name, (shape, seed) in (extra or {}).items():
+        graph["inputs"].append(name)
+        graph["nodes"][name] = {"op": "InputOp", "op_fields": {}, "inputs": [],
+                                "outputs": [{"name": name, "shape": list(shape), "dtype": "f32"}]}
+        node["inputs"].append(name)
+        meta["graph_inputs"].append(name)
+        kernel["arg_order"].insert(len(kernel["arg_order"]) - 1, name)
+        kernel["args"].insert(len(kernel["args"]) - 1, {"name": name, "dtype": "f32", "shape": list(shape),
+                                                         "seed": seed})
+    ir.write_text(json.dumps(graph))
+    (folder / "meta.json").write_text(json.dumps(meta))
+    return ir
+
+
+def _split_top(text: str) -> list:
+    """Top-level comma-separated parts of an IR tuple's text."""
+    parts, depth, start = [], 0, 0
+    for i, ch in enumerate(text):
+        if ch == "(":
+            depth += 1
+        elif ch == ")":
+            depth -= 1
+        elif ch == "," and depth == 0:
+            parts.append(text[start:i].strip())
+            start = i + 1
+    parts.append(text[start:].strip())
+    return [p for p in parts if p]
+
+
+def _staged_tanh(folder):
+    return staged_epilogue(folder, lambda acc, t, row, col: ([assign(t, "tanh", [acc])], t))
+
+
+def _staged_scaled_silu(folder):
+    # v = 0.25 * acc; v * sigmoid(v)
+    def epi(acc, t, row, col):
+        return ([let(f"{t}c", lit(0.25, "f32"), "f32"), assign(f"{t}v", "multiply", [acc, f"{t}c"]),
+                 assign(f"{t}g", "sigmoid", [f"{t}v"]), assign(t, "multiply", [f"{t}v", f"{t}g"])], t)
+    return staged_epilogue(folder, epi)
+
+
+def _staged_bias_residual(folder):
+    # relu(acc + bias[col]) + 0.5 * res[row, col]: the loads sit at the write position
+    def epi(acc, t, row, col):
+        return ([f"Load(names=('{t}b',), input='bias', index=({col},), dtype=None)",
+                 f"Load(names=('{t}r',), input='res', index=({row}, {col}), dtype=None)",
+                 assign(f"{t}s", "add", [acc, f"{t}b"]), assign(f"{t}a", "relu", [f"{t}s"]),
+                 let(f"{t}h", lit(0.5, "f32"), "f32"), assign(f"{t}q", "multiply", [f"{t}r", f"{t}h"]),
+                 assign(t, "add", [f"{t}a", f"{t}q"])], t)
+    return staged_epilogue(folder, epi, {"bias": ((512,), 2), "res": ((512, 512), 3)})
+
+
+STAGED_EPILOGUES = {"staged_tanh": _staged_tanh, "staged_scaled_silu": _staged_scaled_silu,
+                    "staged_bias_residual": _staged_bias_residual}
