@@ -122,15 +122,14 @@ __device__ __forceinline__ void raise_error(const SdpaParams &p, volatile int *a
   atomicCAS(p.err, 0, code);
 }
 
-// One lane waits, the warp agrees on the outcome.
+// Every lane waits (one lane waiting and broadcasting costs a divergent
+// branch and a shuffle on the softmax's critical path); the warp agrees on
+// the outcome, so a wait that gave up in any lane fails for all.
 __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
                                           const SdpaParams &p, int code) {
-  int ok = 0;
-  if ((threadIdx.x & 31) == 0) {
-    ok = mbar_wait(bar, parity, abort);
-    if (!ok) raise_error(p, abort, code);
-  }
-  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+  const int ok = __all_sync(0xffffffffu, mbar_wait(bar, parity, abort) ? 1 : 0);
+  if (!ok && (threadIdx.x & 31) == 0) raise_error(p, abort, code);
+  return ok != 0;
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -287,9 +286,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t ph = (g >> 1) & 1;
           const bool next = j + 1 < n;
           for (int t = 0; t < QT; ++t) {
-            if (!mbar_wait(&p_full[t], g & 1, abort) ||
+            // The operands (V(j), K(j+1), a free O) are ready long before the
+            // softmax's P, so they are waited for first: a wait costs a
+            // shared-memory round trip even when its phase has completed, and
+            // only the P wait should sit between the softmax and the MMAs.
+            if ((t == 0 && !mbar_wait(&v_full[st], ph, abort)) ||
+                (t == 0 && next && !mbar_wait(&k_full[(g + 1) & 1], ((g + 1) >> 1) & 1, abort)) ||
                 (j == 0 && local > 0 && !mbar_wait(&o_empty[t], (local - 1) & 1, abort)) ||
-                (t == 0 && !mbar_wait(&v_full[st], ph, abort))) {
+                !mbar_wait(&p_full[t], g & 1, abort)) {
               ok = false;
               break;
             }
@@ -297,11 +301,6 @@ __global__ void __launch_bounds__(THREADS, 1)
             issue_pv(t, g, j == 0);
             if (t == QT - 1) mma_commit(&v_empty[st]);
             if (next) {
-              if (t == 0 && !mbar_wait(&k_full[(g + 1) & 1], ((g + 1) >> 1) & 1, abort)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
               issue_s(t, g + 1);
               if (t == QT - 1) {
                 mma_commit(&k_empty[(g + 1) & 1]);
@@ -394,11 +393,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   #pragma unroll
           for (int i = 0; i < 16; ++i) {
             // p = 2^(s * scale * log2 e - m): one paired FMA, then MUFU ex2 or
-            // (one pair in four) the paired polynomial
+            // (one pair in sixteen) the paired polynomial
             const uint64_t x2 = ffma2(pack2(__uint_as_float(sr[c][2 * i]), __uint_as_float(sr[c][2 * i + 1])),
                                       scale2, neg_m2);
             uint64_t p2;
-            if ((i & 3) == 3) {
+            if (i == 15) {
               p2 = ex2_poly2(x2);
             } else {
               const float2 x = unpack2(x2);
