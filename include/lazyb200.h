@@ -303,7 +303,8 @@ int lc_probe_mma(int variant, int groups, void *stream);
  * whole tile (checked before launch).
  *
  * Lane programs (the warp-level fragment algebra of ptx_tensor.py:164-618)
- * use the operations after SEL: COORD reads coordinate `aux` of the point;
+ * use the operations after SEL: COORD reads coordinate `aux` of the point
+ * (any program: the tile axes, then the loop counters of serial programs);
  * LDX_* loads slot `aux` at the s32 index in register a, clamped into the
  * buffer; STX_* stores register b at the index in register a when register
  * c is non-zero and the index is inside the buffer (STX_ADD_F32 adds

@@ -389,7 +389,7 @@ int validate_program(const char *name, const lc_pw_program *program, void *const
       return fail(LC_ERR_INVALID, "%s: register out of range at %d", name, pc);
     if (op == LC_PW_CONST && aux >= g.n_consts)
       return fail(LC_ERR_INVALID, "%s: constant out of range at %d", name, pc);
-    if (op == LC_PW_COORD && aux >= g.n_axes)
+    if (op == LC_PW_COORD && aux >= g.n_axes + g.n_loops)
       return fail(LC_ERR_INVALID, "%s: coordinate out of range at %d", name, pc);
     if (op >= LC_PW_LDX_F32 && op <= LC_PW_STX_ADD_F32 && aux >= g.n_buffers)
       return fail(LC_ERR_INVALID, "%s: buffer slot out of range at %d", name, pc);

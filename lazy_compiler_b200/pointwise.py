@@ -450,8 +450,9 @@ class PointwiseCompiler:
             raise CompileError(f"unsupported expression {e!r}")
         k = e.kind
         if k == "Var":
-            if e.name in self.axes:
-                raise CompileError("tile coordinates as values are not supported in pointwise programs")
+            if e.name not in self.env and e.name in self.axes:
+                # a tile coordinate as a value: s32, as the reference binds its axes
+                return self.emit("COORD", "s32", aux=self.axes.index(e.name))
             return self.lookup(e.name)
         if k == "Literal":
             return self.literal(e.value, e.get("dtype") or ("f32" if isinstance(e.value, float) else "s32"))

@@ -896,9 +896,11 @@ def recognise(pkg: KernelPackage) -> Plan:
     try:
         ev.run(tile.body)
     except CompileError as err:
+        # the symbolic evaluation behind the fixed classes and row programs
+        # does not take this body: the general per-point paths may
         if straight:
             return _pointwise_program(pkg, tile, err)
-        raise
+        return _serial_program(pkg, tile, str(err))
     if ev.loops and ev.reductions:
         # the fixed classes first, then the general row and serial programs
         try:

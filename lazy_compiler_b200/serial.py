@@ -57,6 +57,15 @@ class SerialCompiler(PointwiseCompiler):
             raise CompileError(f"index variable {e.name!r} is not a tile axis or an enclosing loop")
         return super().affine(e)
 
+    def expr(self, e) -> Val:
+        if isinstance(e, Node) and e.kind == "Var" and e.name in self.active and e.name not in self.env:
+            # an enclosing loop's counter as a value (s32)
+            return self.emit("COORD", "s32", aux=self.axes.index(self.active[e.name]))
+        if isinstance(e, Node) and e.kind == "Var" and e.name not in self.env and \
+                e.name not in self.axes[:self.tile_axes]:
+            raise CompileError(f"{e.name!r} is not a tile axis, an enclosing loop or a value")
+        return super().expr(e)
+
     # ------------------------------------------------------------ statements
     def statement(self, s: Node) -> None:
         k = s.kind

@@ -235,6 +235,9 @@ class PointwiseOracle:
             return self.env[e]
         k = e.kind
         if k == "Var":
+            if e.name not in self.env and e.name in self.coord:
+                # a tile coordinate or loop counter as a value: s32
+                return V(np.asarray(self.coord[e.name]).astype(np.int32), "s32")
             return self.env[e.name]
         if k == "Literal":
             dt = e.get("dtype")

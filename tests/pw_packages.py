@@ -425,7 +425,37 @@ def _serial_nested(folder):
                            write("out", [i], ["tot"], "f32")], rtol=1e-5, atol=1e-6)
 
 
-SERIAL_SYNTHETIC = {"serial_matmul_relu": _serial_matmul_relu, "serial_max_abs": _serial_row_max_argmax_value,
+def _serial_lower_matmul(folder):
+    # out[i, j] = sum over k <= i of a[i, k] * b[k, j]: the loop counter and a tile
+    # coordinate as values (a causal-style mask)
+    i, j, k = var("i"), var("j"), var("k")
+    body = [loop("k", 24, [load("av", "a", [i, k], "f32"), load("bv", "b", [k, j], "f32"),
+                           assign("pv", "multiply", ["av", "bv"]),
+                           let("keep", "TernaryExpr(cond=BinaryExpr(op='<=', left=Var(name='k'), "
+                               "right=Var(name='i')), if_true=Var(name='pv'), if_false=" + lit(0.0, "f32") + ")"),
+                           accum("acc", "keep", "add")]),
+            write("out", [i, j], ["acc"], "f32")]
+    return serial_package(folder, "serial_lower_matmul", {"a": ((20, 24), "f32"), "b": ((24, 12), "f32")},
+                          ("out", (20, 12), "f32"), [("i", 20), ("j", 12)], body)
+
+
+def _pointwise_lower_mask(folder):
+    # out[i, j] = x[i, j] where j <= i, else -x[i, j] * (i - j): coordinates as values
+    i, j = var("i"), var("j")
+    return package(folder, "pointwise_lower_mask", {"x": ((32, 48), "f32")}, ("out", (32, 48), "f32"),
+                   [("i", 32), ("j", 48)],
+                   [load("xv", "x", [i, j], "f32"),
+                    let("d", "CastExpr(expr=BinaryExpr(op='-', left=Var(name='i'), right=Var(name='j')), "
+                        "dtype='float')", "f32"),
+                    assign("nx", "multiply", ["xv", "d"]), assign("mx", "negative", ["nx"]),
+                    let("v", "TernaryExpr(cond=BinaryExpr(op='<=', left=Var(name='j'), right=Var(name='i')), "
+                        "if_true=Var(name='xv'), if_false=Var(name='mx'))", "f32"),
+                    write("out", [i, j], ["v"], "f32")])
+
+
+SYNTHETIC["pointwise_lower_mask"] = _pointwise_lower_mask
+
+SERIAL_SYNTHETIC = {"serial_lower_matmul": _serial_lower_matmul, "serial_matmul_relu": _serial_matmul_relu, "serial_max_abs": _serial_row_max_argmax_value,
                     "serial_nested": _serial_nested}
 
 
