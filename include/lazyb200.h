@@ -418,6 +418,15 @@ enum lc_pw_op {
   LC_PW_SETP = 85,
   LC_PW_LOOPB = 86,
   LC_PW_LOOPE = 87,
+  LC_PW_BRA = 88,
+  LC_PW_BRZ = 89,
+  LC_PW_SLB = 90,
+  LC_PW_SLE = 91,
+  LC_PW_LDS = 92,
+  LC_PW_STS = 93,
+  LC_PW_BAR = 94,
+  LC_PW_WSYNC = 95,
+  LC_PW_TID = 96,
   LC_PW_NUM_OPS
 };
 
@@ -475,6 +484,48 @@ typedef struct {
 /* Runs a row program (validated like lc_pointwise, plus its layout). */
 int lc_rowprog(const lc_pw_program *program, const lc_rp_layout *layout, void *const *buffers,
                void *stream);
+
+/* ---------------------------------------------------------------- block programs
+ * Any Tile body run the way the reference's kernel runs it (ptx_backend.py
+ * :1375-1756 statements, loops, shuffles, shared trees, barriers;
+ * :1457-1492 cp.async copies, synchronous here): one CTA of `threads`
+ * threads per block of the Tile.  The tile axes are the program's axes:
+ * the first n_block_axes number the blocks, the rest (extents multiplying
+ * to `threads`) a block's threads; COORD reads either, and the loop
+ * counters follow them.  A block program may use, besides the lane-program
+ * operations:
+ *   BRA       jump forward to operation aux;
+ *   BRZ       jump forward to operation aux when register a is zero;
+ *   SLB / SLE a loop over coordinate slot aux & 15 (the partner operation's
+ *             index in aux >> 4) up to the limit in register b (never past
+ *             the slot's extent): SLB sets the counter to register a and
+ *             skips the body unless 0 <= counter < limit; SLE adds register
+ *             a (at least 1) and repeats while below the limit;
+ *   LDS / STS load from / store register b into shared array aux at the
+ *             s32 index in register a (loads clamped, stores skipped
+ *             outside the array);
+ *   BAR / WSYNC  __syncthreads() / __syncwarp();
+ *   TID       the thread's index in its CTA.
+ * Branches only go forward and every loop is bounded by its slot's extent,
+ * so a program ends.  Barriers, warp syncs and shuffles must be reached by
+ * every thread: the host admits them only outside every branch region and
+ * inside loops whose start, step and limit registers are written once, by
+ * CONST. */
+#define LC_BP_MAX_SMEM 8
+
+typedef struct {
+  int32_t threads;      /* threads per block: the product of the thread-axis extents */
+  int32_t n_block_axes; /* leading tile axes that number the blocks */
+  int32_t n_smem;       /* shared arrays */
+  int32_t reserved;
+  int32_t smem_offset[LC_BP_MAX_SMEM]; /* in 32-bit words from the start of dynamic shared memory */
+  int32_t smem_size[LC_BP_MAX_SMEM];   /* in 32-bit words */
+} lc_bp_layout;
+
+/* Runs a block program (validated like lc_pointwise, plus the branch, loop,
+ * shared-array and barrier rules above). */
+int lc_blockprog(const lc_pw_program *program, const lc_bp_layout *layout, void *const *buffers,
+                 void *stream);
 
 #ifdef __cplusplus
 }

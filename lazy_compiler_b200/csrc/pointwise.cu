@@ -49,10 +49,11 @@ __device__ __forceinline__ float round_bf16(float x) {
 
 // Runs operations [begin, end) of a program for one point with coordinates
 // x.  `states` (STATE), `partials` (PARTIAL, SETP) and `partners` (PARTNER)
-// belong to row programs; a pointwise program has none.
+// belong to row programs; `smem` and `bl` (LDS, STS) to block programs.
 __device__ __forceinline__ void exec_range(const lc_pw_program &g, void *const *buffers, int64_t *x,
                                            uint32_t *r, int begin, int end, const float *states,
-                                           float *partials, const float *partners) {
+                                           float *partials, const float *partners,
+                                           uint32_t *smem = nullptr, const lc_bp_layout *bl = nullptr) {
   for (int pc = begin; pc < end; ++pc) {
     const uint32_t w0 = g.code[pc][0], w1 = g.code[pc][1];
     const int op = w0 & 255, dst = (w0 >> 8) & 255;
@@ -224,6 +225,39 @@ __device__ __forceinline__ void exec_range(const lc_pw_program &g, void *const *
         if (++x[d] < limit) pc = aux >> 4;
         continue;
       }
+      case LC_PW_BRA: pc = aux - 1; continue;  // forward only (checked on the host)
+      case LC_PW_BRZ:
+        if (A == 0u) pc = aux - 1;
+        continue;
+      case LC_PW_SLB: {  // strided loop: counter = start (a), run while below the limit (b)
+        const int d = g.n_axes + (aux & 15);
+        const int64_t limit = min((int64_t)ib, g.extents[d]);  // never past the validated extent
+        x[d] = (int64_t)ia;
+        if (x[d] < 0 || x[d] >= limit) pc = aux >> 4;
+        continue;
+      }
+      case LC_PW_SLE: {  // counter += step (a, at least 1); repeat while below the limit (b)
+        const int d = g.n_axes + (aux & 15);
+        const int64_t limit = min((int64_t)ib, g.extents[d]);
+        x[d] += ia < 1 ? 1 : ia;
+        if (x[d] < limit) pc = aux >> 4;
+        continue;
+      }
+      case LC_PW_LDS: {
+        const int64_t size = bl->smem_size[aux];
+        int64_t at = (int64_t)ia;
+        at = at < 0 ? 0 : (at >= size ? size - 1 : at);
+        out = smem[bl->smem_offset[aux] + at];
+        break;
+      }
+      case LC_PW_STS: {
+        const int64_t at = (int64_t)ia;
+        if (at >= 0 && at < bl->smem_size[aux]) smem[bl->smem_offset[aux] + at] = B;
+        continue;
+      }
+      case LC_PW_BAR: __syncthreads(); continue;
+      case LC_PW_WSYNC: __syncwarp(); continue;
+      case LC_PW_TID: out = threadIdx.x; break;
       case LC_PW_STATE: out = w(states[aux]); break;
       case LC_PW_PARTIAL: out = w(partials[aux]); break;
       case LC_PW_PARTNER: out = w(partners[aux]); break;
@@ -325,6 +359,39 @@ __global__ void __launch_bounds__(256) rowprog_kernel(const __grid_constant__ Ro
   }
 }
 
+struct BlockProgArgs {
+  lc_pw_program prog;
+  lc_bp_layout lay;
+  void *buffers[LC_PW_MAX_BUFFERS];
+  int64_t blocks;
+};
+
+// One CTA per block of the Tile (grid-stride over blocks): every thread
+// decodes its block and thread coordinates and runs the whole program;
+// the program's own barriers order its shared memory.
+__global__ void __launch_bounds__(1024) blockprog_kernel(const __grid_constant__ BlockProgArgs p) {
+  extern __shared__ uint32_t bp_smem[];
+  uint32_t r[LC_PW_MAX_REGS];
+  for (int i = 0; i < LC_PW_MAX_REGS; ++i) r[i] = 0u;
+  const lc_pw_program &g = p.prog;
+  const int nb = p.lay.n_block_axes;
+  for (int64_t blk = blockIdx.x; blk < p.blocks; blk += gridDim.x) {
+    int64_t x[LC_PW_MAX_AXES] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int64_t rest = threadIdx.x;
+    for (int d = g.n_axes - 1; d >= nb; --d) {
+      x[d] = rest % g.extents[d];
+      rest /= g.extents[d];
+    }
+    rest = blk;
+    for (int d = nb - 1; d >= 0; --d) {
+      x[d] = rest % g.extents[d];
+      rest /= g.extents[d];
+    }
+    exec_range(g, p.buffers, x, r, 0, g.n_code, nullptr, nullptr, nullptr, bp_smem, &p.lay);
+    __syncthreads();  // the next block reuses the shared arrays
+  }
+}
+
 bool form_in_range(const lc_pw_program &g, const lc_pw_form &fm) {
   int64_t lo = fm.base, hi = fm.base;
   for (int d = 0; d < g.n_axes + g.n_loops; ++d) {
@@ -350,8 +417,54 @@ int storage_of(int op) {
 namespace lc {
 namespace {
 // Checks a program before any launch; returns LC_OK or the failure, and the point count.
-int validate_program(const char *name, const lc_pw_program *program, void *const *buffers, bool row_program,
-                     int64_t *points_out) {
+constexpr int kPointwise = 0, kRowProgram = 1, kBlockProgram = 2;
+
+bool block_only(int op) { return op >= LC_PW_BRA && op <= LC_PW_TID; }
+
+// A block program's barriers, warp syncs and shuffles must be reached by
+// every thread: none may sit inside a branch region, and every loop around
+// one must start and step by registers written exactly once, by CONST.
+int check_uniform_sync(const char *name, const lc_pw_program &g) {
+  int writes[LC_PW_MAX_REGS] = {0};
+  bool by_const[LC_PW_MAX_REGS] = {false};
+  for (int pc = 0; pc < g.n_code; ++pc) {
+    const int op = g.code[pc][0] & 255, dst = (g.code[pc][0] >> 8) & 255;
+    const bool writes_dst = !(op == LC_PW_BRA || op == LC_PW_BRZ || op == LC_PW_SLB || op == LC_PW_SLE ||
+                              op == LC_PW_STS || op == LC_PW_BAR || op == LC_PW_WSYNC || op == LC_PW_LOOPB ||
+                              op == LC_PW_LOOPE || op == LC_PW_SETP || (op >= LC_PW_ST_F32 && op <= LC_PW_ST_S32) ||
+                              (op >= LC_PW_STX_F32 && op <= LC_PW_STX_ADD_F32));
+    if (!writes_dst) continue;
+    const int n = (op == LC_PW_MMA_F16 || op == LC_PW_MMA_BF16) ? 4 : 1;
+    for (int k = 0; k < n; ++k) {
+      ++writes[dst + k];
+      by_const[dst + k] = op == LC_PW_CONST;
+    }
+  }
+  for (int pc = 0; pc < g.n_code; ++pc) {
+    const int op = g.code[pc][0] & 255;
+    if (!(op == LC_PW_BAR || op == LC_PW_WSYNC || op == LC_PW_SHFL_XOR)) continue;
+    for (int q = 0; q < pc; ++q) {
+      const int oq = g.code[q][0] & 255, aq = (int)(g.code[q][1] >> 8);
+      if ((oq == LC_PW_BRA || oq == LC_PW_BRZ) && aq > pc)
+        return fail(LC_ERR_INVALID, "%s: barrier or shuffle at %d inside the branch at %d", name, pc, q);
+      if (oq == LC_PW_SLB && (aq >> 4) > pc) {  // a loop around pc
+        const int start = (g.code[q][0] >> 16) & 255, limit = g.code[q][0] >> 24;
+        const int end = aq >> 4, step = (g.code[end][0] >> 16) & 255, limit2 = g.code[end][0] >> 24;
+        const auto once = [&](int reg) { return writes[reg] == 1 && by_const[reg]; };
+        if (!once(start) || !once(step) || !once(limit) || !once(limit2))
+          return fail(LC_ERR_INVALID, "%s: barrier or shuffle at %d inside a loop with a per-thread range", name,
+                      pc);
+      }
+      if (oq == LC_PW_LOOPB && (aq >> 4) > pc)
+        return fail(LC_ERR_INVALID, "%s: barrier or shuffle at %d inside a counted loop", name, pc);
+    }
+  }
+  return LC_OK;
+}
+
+int validate_program(const char *name, const lc_pw_program *program, void *const *buffers, int mode,
+                     int64_t *points_out, const lc_bp_layout *bl = nullptr) {
+  const bool row_program = mode == kRowProgram;
   if (!program || !buffers) return fail(LC_ERR_INVALID, "%s: null program or buffers", name);
   const lc_pw_program &g = *program;
   if (g.n_code < 0 || g.n_code > LC_PW_MAX_CODE || g.n_consts < 0 || g.n_consts > LC_PW_MAX_CONST ||
@@ -399,6 +512,22 @@ int validate_program(const char *name, const lc_pw_program *program, void *const
         ((int)dst + 3 >= g.n_regs || (int)a + 3 >= g.n_regs || (int)b + 1 >= g.n_regs || (int)c + 3 >= g.n_regs))
       return fail(LC_ERR_INVALID, "%s: MMA register tuple out of range at %d", name, pc);
     if (op == LC_PW_SHFL_XOR || op == LC_PW_MMA_F16 || op == LC_PW_MMA_BF16) lockstep = true;
+    if (block_only(op) && mode != kBlockProgram)
+      return fail(LC_ERR_INVALID, "%s: block-program operation outside a block program at %d", name, pc);
+    if ((op == LC_PW_BRA || op == LC_PW_BRZ) && (aux <= pc || aux > g.n_code))
+      return fail(LC_ERR_INVALID, "%s: branch at %d is not forward", name, pc);
+    if ((op == LC_PW_LDS || op == LC_PW_STS) && (!bl || aux >= bl->n_smem))
+      return fail(LC_ERR_INVALID, "%s: shared array out of range at %d", name, pc);
+    if (op == LC_PW_SLB || op == LC_PW_SLE) {
+      const int slot = aux & 15, other = aux >> 4;
+      const bool begin = op == LC_PW_SLB;
+      if (slot >= g.n_loops || other < 0 || other >= g.n_code || (begin ? other <= pc : other >= pc))
+        return fail(LC_ERR_INVALID, "%s: malformed loop at %d", name, pc);
+      const uint32_t m0 = g.code[other][0], m1 = g.code[other][1];
+      if ((int)(m0 & 255) != (begin ? LC_PW_SLE : LC_PW_SLB) || (int)((m1 >> 8) & 15) != slot ||
+          (int)(m1 >> 12) != pc)
+        return fail(LC_ERR_INVALID, "%s: unmatched loop at %d", name, pc);
+    }
     if (op == LC_PW_LOOPB || op == LC_PW_LOOPE) {
       // a well-formed pair: LOOPB at pc names its LOOPE, which names it back, on the same loop
       const int slot = aux & 15, other = aux >> 4;
@@ -419,6 +548,11 @@ int validate_program(const char *name, const lc_pw_program *program, void *const
   }
   if (row_program && (lockstep || g.n_axes < 2))
     return fail(LC_ERR_INVALID, "%s: a row program runs over (row, column) without warp operations", name);
+  if (mode == kBlockProgram) {
+    if (int rc = check_uniform_sync(name, g)) return rc;
+    *points_out = points;
+    return LC_OK;
+  }
   if (lockstep && points % 32 != 0)
     return fail(LC_ERR_INVALID, "%s: a program that shuffles or multiplies needs whole warps of points", name);
   *points_out = points;
@@ -430,7 +564,7 @@ int validate_program(const char *name, const lc_pw_program *program, void *const
 extern "C" int lc_pointwise(const lc_pw_program *program, void *const *buffers, void *stream) {
   using namespace lc;
   int64_t points = 0;
-  if (int rc = validate_program("lc_pointwise", program, buffers, false, &points)) return rc;
+  if (int rc = validate_program("lc_pointwise", program, buffers, kPointwise, &points)) return rc;
   const lc_pw_program &g = *program;
   PointwiseArgs args;
   args.prog = g;
@@ -447,7 +581,7 @@ extern "C" int lc_rowprog(const lc_pw_program *program, const lc_rp_layout *layo
                           void *stream) {
   using namespace lc;
   int64_t points = 0;
-  if (int rc = validate_program("lc_rowprog", program, buffers, true, &points)) return rc;
+  if (int rc = validate_program("lc_rowprog", program, buffers, kRowProgram, &points)) return rc;
   if (!layout) return fail(LC_ERR_INVALID, "lc_rowprog: null layout");
   const lc_rp_layout &lay = *layout;
   const int n_code = program->n_code;
@@ -478,4 +612,50 @@ extern "C" int lc_rowprog(const lc_pw_program *program, const lc_rp_layout *layo
   if (blocks > cap) blocks = cap;
   rowprog_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(args);
   return check_launch("lc_rowprog");
+}
+
+extern "C" int lc_blockprog(const lc_pw_program *program, const lc_bp_layout *layout, void *const *buffers,
+                            void *stream) {
+  using namespace lc;
+  if (!layout) return fail(LC_ERR_INVALID, "lc_blockprog: null layout");
+  const lc_bp_layout &lay = *layout;
+  if (lay.n_smem < 0 || lay.n_smem > LC_BP_MAX_SMEM) return fail(LC_ERR_INVALID, "lc_blockprog: shared arrays");
+  int64_t words = 0;
+  for (int i = 0; i < lay.n_smem; ++i) {
+    if (lay.smem_size[i] < 1 || lay.smem_offset[i] < 0 ||
+        (int64_t)lay.smem_offset[i] + lay.smem_size[i] > (int64_t)(200 * 1024 / 4))
+      return fail(LC_ERR_INVALID, "lc_blockprog: shared array %d", i);
+    const int64_t top = (int64_t)lay.smem_offset[i] + lay.smem_size[i];
+    if (top > words) words = top;
+  }
+  int64_t points = 0;
+  if (int rc = validate_program("lc_blockprog", program, buffers, kBlockProgram, &points, &lay)) return rc;
+  const lc_pw_program &g = *program;
+  if (lay.threads < 1 || lay.threads > 1024 || lay.n_block_axes < 0 || lay.n_block_axes >= g.n_axes)
+    return fail(LC_ERR_INVALID, "lc_blockprog: thread block");
+  int64_t threads = 1, blocks = 1;
+  for (int d = 0; d < g.n_axes; ++d) (d < lay.n_block_axes ? blocks : threads) *= g.extents[d];
+  if (threads != lay.threads) return fail(LC_ERR_INVALID, "lc_blockprog: thread axes do not make %d threads",
+                                          lay.threads);
+  BlockProgArgs args;
+  args.prog = g;
+  args.lay = lay;
+  for (int i = 0; i < LC_PW_MAX_BUFFERS; ++i) args.buffers[i] = i < g.n_buffers ? buffers[i] : nullptr;
+  args.blocks = blocks;
+  const size_t smem_bytes = (size_t)words * 4;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (int rc = check_cuda(cudaFuncSetAttribute(blockprog_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 200 * 1024),
+                            "lc_blockprog smem attribute"))
+      return rc;
+    configured[dev] = true;
+  }
+  int64_t grid = blocks;
+  const int64_t cap = (int64_t)sm_count() * 8;
+  if (grid > cap) grid = cap;
+  blockprog_kernel<<<(unsigned)grid, (unsigned)lay.threads, smem_bytes, as_stream(stream)>>>(args);
+  return check_launch("lc_blockprog");
 }

@@ -55,6 +55,8 @@ OPCODES = [
     "STATE", "PARTIAL", "PARTNER", "SETP",
     # serial programs (lazy_compiler_b200/serial.py)
     "LOOPB", "LOOPE",
+    # block programs (lazy_compiler_b200/blockprog.py)
+    "BRA", "BRZ", "SLB", "SLE", "LDS", "STS", "BAR", "WSYNC", "TID",
 ]
 OP = {name: i for i, name in enumerate(OPCODES)}
 

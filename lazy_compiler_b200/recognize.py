@@ -887,7 +887,10 @@ def recognise(pkg: KernelPackage) -> Plan:
     if kinds & _FRAGMENT_KINDS:
         return _recognise_fragments(pkg, tile, kinds)
     if "CpAsyncCopy" in kinds:
-        return f32.recognise_staged_gemm(pkg, tile)
+        try:
+            return f32.recognise_staged_gemm(pkg, tile)
+        except CompileError as err:
+            return _block_program(pkg, tile, f"not a staged GEMM: {err}")
     ev = _Eval(pkg)
     ev.smem = set()
     for axis in tile.axes:
@@ -926,12 +929,22 @@ def recognise(pkg: KernelPackage) -> Plan:
 
 
 def _serial_program(pkg: KernelPackage, tile: Node, reason: str) -> Plan:
-    """A body with per-point runtime loops that no recogniser took: a serial program."""
+    """A body with per-point runtime loops that no recogniser took: a serial
+    program, or failing that a block program."""
     from .serial import compile_serial
     try:
         return compile_serial(pkg, tile)
     except CompileError as err:
-        raise CompileError(f"{reason}; as a serial program: {err}") from err
+        return _block_program(pkg, tile, f"{reason}; as a serial program: {err}")
+
+
+def _block_program(pkg: KernelPackage, tile: Node, reason: str) -> Plan:
+    """The last general path: the body run statement for statement, one CTA per block."""
+    from .blockprog import compile_blockprog
+    try:
+        return compile_blockprog(pkg, tile)
+    except CompileError as err:
+        raise CompileError(f"{reason}; as a block program: {err}") from err
 
 
 def _pointwise_program(pkg: KernelPackage, tile: Node, reason: CompileError) -> Plan:

@@ -33,8 +33,10 @@ from .pointwise import MAX_CODE, MAX_CONST, PointwiseCompiler, Program, Val
 
 MAX_PASSES = 4
 MAX_STATES = 8
-IDENTITY = {"add": 0.0, "sum": 0.0, "multiply": 1.0, "prod": 1.0, "maximum": -math.inf, "max": -math.inf,
-            "minimum": math.inf, "min": math.inf}
+# Fold identities as Emmy seeds them: max / min start at the finite -1e30 / 1e30
+# (an empty lane's state then combines without inf - inf).
+IDENTITY = {"add": 0.0, "sum": 0.0, "multiply": 1.0, "prod": 1.0, "maximum": -1e30, "max": -1e30,
+            "minimum": 1e30, "min": 1e30, "fmax": -1e30, "fmin": 1e30}
 
 
 def _aff_dict(form) -> dict:

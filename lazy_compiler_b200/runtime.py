@@ -53,6 +53,7 @@ SIGNATURES = {
     "lc_gemm_path": [_INT, _INT, _P, _P, _I64, _I64, _I64],
     "lc_pointwise": [_P, _P, _P],
     "lc_rowprog": [_P, _P, _P, _P],
+    "lc_blockprog": [_P, _P, _P, _P],
     "lc_gemm_mixed": [_INT, _INT, _INT, _INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_chain": [_INT, _INT, _INT, _INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P],
     "lc_attention_f32": [_INT, _INT, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
@@ -130,6 +131,24 @@ def rp_layout(layout: dict) -> RpLayout:
         lay.tree_begin[i], lay.tree_end[i] = tb, te
     for k, (init, ps) in enumerate(zip(layout["state_init"], layout["state_pass"])):
         lay.state_init[k], lay.state_pass[k] = init, ps
+    return lay
+
+
+BP_MAX_SMEM = 8
+
+
+class BpLayout(ctypes.Structure):
+    _fields_ = [("threads", ctypes.c_int32), ("n_block_axes", ctypes.c_int32), ("n_smem", ctypes.c_int32),
+                ("reserved", ctypes.c_int32), ("smem_offset", ctypes.c_int32 * BP_MAX_SMEM),
+                ("smem_size", ctypes.c_int32 * BP_MAX_SMEM)]
+
+
+def bp_layout(layout: dict) -> BpLayout:
+    """The C struct of a block program's layout (a plan's ``params["layout"]``)."""
+    lay = BpLayout()
+    lay.threads, lay.n_block_axes, lay.n_smem = layout["threads"], layout["n_block_axes"], len(layout["smem"])
+    for i, (off, size) in enumerate(layout["smem"]):
+        lay.smem_offset[i], lay.smem_size[i] = off, size
     return lay
 
 
@@ -234,6 +253,11 @@ def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
         ptrs = (ctypes.c_void_p * PW_MAX_BUFFERS)(*[int(pointers[b[f"buf{i}"]]) for i in range(len(prog["buffers"]))])
         g, lay = pw_program(prog), rp_layout(p["layout"])
         call("lc_rowprog", ctypes.c_void_p(ctypes.addressof(g)), ctypes.c_void_p(ctypes.addressof(lay)), ptrs, s)
+    elif op == "blockprog":
+        prog = p["program"]
+        ptrs = (ctypes.c_void_p * PW_MAX_BUFFERS)(*[int(pointers[b[f"buf{i}"]]) for i in range(len(prog["buffers"]))])
+        g, lay = pw_program(prog), bp_layout(p["layout"])
+        call("lc_blockprog", ctypes.c_void_p(ctypes.addressof(g)), ctypes.c_void_p(ctypes.addressof(lay)), ptrs, s)
     elif op == "gemm_mixed":
         d = plan["dtypes"]
         bias = ptr("bias") if "bias" in b else ctypes.c_void_p(0)

@@ -32,8 +32,10 @@ import numpy as np
 from .ir import CompileError, KernelPackage, Node, static_extent
 from .pointwise import MAX_AXES, MAX_CODE, MAX_CONST, OP, PointwiseCompiler, Program, Val, vm_type
 
-IDENTITY = {"add": 0.0, "sum": 0.0, "multiply": 1.0, "prod": 1.0, "maximum": -math.inf, "max": -math.inf,
-            "minimum": math.inf, "min": math.inf}
+# Fold identities as Emmy seeds them: max / min start at the finite -1e30 / 1e30
+# (an empty lane's state then combines without inf - inf).
+IDENTITY = {"add": 0.0, "sum": 0.0, "multiply": 1.0, "prod": 1.0, "maximum": -1e30, "max": -1e30,
+            "minimum": 1e30, "min": 1e30, "fmax": -1e30, "fmin": 1e30}
 
 
 class SerialCompiler(PointwiseCompiler):

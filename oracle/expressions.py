@@ -309,6 +309,12 @@ def evaluate(plan: dict, arrays: dict, ir=None) -> dict:
     with an epilogue program against oracle/staged_ir.py.
     """
     op = plan["op"]
+    if plan["params"].get("block"):
+        # a block program: the block oracle runs the IR the same way
+        if ir is None:
+            raise ValueError("block-program plans are evaluated from their IR: pass ir=")
+        from oracle.staged_ir import evaluate as evaluate_staged
+        return evaluate_staged(ir, arrays)
     if "post" in plan["params"]:
         # a staged matmul storing an expression of its accumulators: the block oracle
         if ir is None:

@@ -24,8 +24,10 @@ from oracle.pointwise_ir import PointwiseOracle, V, conv
 
 _FOLD = {"add": np.sum, "sum": np.sum, "multiply": np.prod, "mul": np.prod,
          "maximum": np.max, "max": np.max, "minimum": np.min, "min": np.min}
-_IDENTITY = {"add": 0.0, "sum": 0.0, "multiply": 1.0, "mul": 1.0, "maximum": -np.inf, "max": -np.inf,
-             "minimum": np.inf, "min": np.inf}
+# Fold identities as Emmy seeds them: max / min start at the finite -1e30 / 1e30
+# (an empty lane's state then combines without inf - inf).
+_IDENTITY = {"add": 0.0, "sum": 0.0, "multiply": 1.0, "mul": 1.0, "maximum": -1e30, "max": -1e30,
+             "minimum": 1e30, "min": 1e30, "fmax": -1e30, "fmin": 1e30}
 
 
 class RowOracle(PointwiseOracle):

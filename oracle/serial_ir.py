@@ -14,8 +14,10 @@ import numpy as np
 
 from oracle.pointwise_ir import PointwiseOracle, V, conv
 
-_IDENTITY = {"add": 0.0, "sum": 0.0, "multiply": 1.0, "prod": 1.0, "maximum": -np.inf, "max": -np.inf,
-             "minimum": np.inf, "min": np.inf}
+# Fold identities as Emmy seeds them: max / min start at the finite -1e30 / 1e30
+# (an empty lane's state then combines without inf - inf).
+_IDENTITY = {"add": 0.0, "sum": 0.0, "multiply": 1.0, "prod": 1.0, "maximum": -1e30, "max": -1e30,
+             "minimum": 1e30, "min": 1e30, "fmax": -1e30, "fmin": 1e30}
 
 
 class SerialOracle(PointwiseOracle):

@@ -54,6 +54,14 @@ class StagedOracle(PointwiseOracle):
         self.n_blocks = int(math.prod(self.ext[:split]))
         self.mask = np.ones(n, bool)
         self.smem: dict = {}
+        self.smem_shape: dict = {}
+        tid = np.zeros(n, np.int64)
+        for name, extent in zip(self.axes[split:], self.ext[split:]):
+            tid = tid * extent + self.coord[name]
+        self.threads = threads
+        self.coord["lane"], self.coord["warp"] = tid % 32, tid // 32
+        self.env["lane"] = V((tid % 32).astype(np.int32), "s32")
+        self.env["warp"] = V((tid // 32).astype(np.int32), "s32")
         zero = set(pkg.kernel_meta.get("zero_outputs", []))
         for name, buf in pkg.buffers.items():
             if buf.role == "output" and name in zero:
@@ -93,8 +101,6 @@ class StagedOracle(PointwiseOracle):
         for s in body:
             k = s.kind
             if k == "Smem":
-                if not hasattr(self, "smem_shape"):
-                    self.smem_shape = {}
                 shape = tuple(int(x) for x in s.extents)
                 self.smem_shape[s.name] = shape
                 self.smem[s.name] = np.full((self.n_blocks, math.prod(shape)), np.nan, np.float32)
@@ -135,8 +141,21 @@ class StagedOracle(PointwiseOracle):
                     self.mask = saved & ~np.broadcast_to(conv(self.expr(s.cond), "pred").a, (self.n,))
                     self.run_block(s.else_body)
                     self.mask = saved
+            elif k == "Write" and s.output in self.smem:
+                size = self.smem[s.output].shape[1]
+                flat = self._flat_smem(s.output, s.index)
+                live = self.mask
+                for lane, name in enumerate(s.values):
+                    idx = np.broadcast_to(flat + lane, (self.n,))
+                    ok = live & (idx >= 0) & (idx < size)
+                    vals = np.broadcast_to(conv(self.env[name], "f32").a, (self.n,))
+                    self.smem[s.output][self.block[ok], idx[ok]] = vals[ok]
             elif k == "Write":
                 self.write(s)
+            elif k == "WarpShuffle":
+                self.shuffle(s)
+            elif k == "TreeHalve":
+                self.tree(s)
             else:
                 self.run([s])
 
@@ -208,6 +227,63 @@ class StagedOracle(PointwiseOracle):
             i += 1
         self.mask = saved
         self.coord.pop(s.axis.name, None)
+
+    def merge(self, s) -> None:
+        for a in s.combine_states:
+            opname = a.op.name if hasattr(a.op, "name") else str(a.op)
+            self.env[a.name] = conv(self.op(opname, [conv(self.env[x], "f32") for x in a.args], "f32"), "f32")
+
+    def shuffle(self, s) -> None:
+        """The reference's butterfly: at each level every lane takes the states of
+        the lane ``delta`` away and runs the combine statements."""
+        if self.threads % 32 and int(s.length) > 1:
+            raise ValueError("oracle: shuffles need whole warps")
+        saved = dict(self.env)
+        points = np.arange(self.n)
+        delta = int(s.length) // 2
+        while delta:
+            for a, b in zip(s.state, s.state_b):
+                self.env[b] = V(conv(self.env[a], "f32").a[points ^ delta], "f32")
+            self.merge(s)
+            delta //= 2
+        kept = {name: self.env[name] for name in s.state}
+        self.env = {**saved, **kept}
+
+    def tree(self, s) -> None:
+        """The reference's shared tree: at each level the threads below ``delta``
+        (lane 0 of each warp when the tree runs over warps) fold the slot
+        ``delta`` away into their own; then every thread reads slot ``inner``."""
+        tid = np.asarray(self.coord[s.tid_var] if s.tid_var in self.coord else self.env[s.tid_var].a, np.int64)
+        inner = s.get("inner")
+        if inner:
+            base = np.asarray(self.coord.get(inner[0], None) if inner[0] in self.coord
+                              else self.env[inner[0]].a, np.int64)
+            scale = int(inner[1])
+        else:
+            base, scale = np.zeros(self.n, np.int64), 1
+        slot = tid * scale + base
+        saved = dict(self.env)
+        delta = int(s.length) // 2
+        while delta:
+            worker = self.mask & (tid < delta)
+            if s.tid_var == "warp" and not inner:
+                worker = worker & (self.coord["lane"] == 0)
+            other = slot + delta * scale
+            for buf, a, b in zip(s.bufs, s.state, s.state_b):
+                arr = self.smem[buf]
+                size = arr.shape[1]
+                self.env[a] = V(arr[self.block, np.clip(slot, 0, size - 1)], "f32")
+                self.env[b] = V(arr[self.block, np.clip(other, 0, size - 1)], "f32")
+            self.merge(s)
+            for buf, name in zip(s.bufs, s.state):
+                arr = self.smem[buf]
+                vals = np.broadcast_to(conv(self.env[name], "f32").a, (self.n,))
+                arr[self.block[worker], slot[worker]] = vals[worker]
+            delta //= 2
+        self.env = saved
+        for buf, name in zip(s.bufs, s.state):
+            arr = self.smem[buf]
+            self.env[name] = V(arr[self.block, np.clip(base, 0, arr.shape[1] - 1)], "f32")
 
     def result(self) -> dict:
         return {k: v.reshape(tuple(self.pkg.buffers[k].shape) or (1,)) for k, v in self.out.items()}

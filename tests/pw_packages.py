@@ -475,6 +475,18 @@ VARIANTS = {
                                     [("Assign(name='v1', op=ElementwiseImpl('reciprocal'), args=('in0',)",
                                       "Assign(name='v1', op=ElementwiseImpl('negative'), args=('in0',)")],
                                     "pointwise", "serial_ir"),
+    "gelu_attention_tanh_score": ("phase9_gelu_attention",
+                                  [("Assign(name='v1', op=ElementwiseImpl('multiply'), args=('acc0', 'in3')",
+                                    "Assign(name='v1', op=ElementwiseImpl('tanh'), args=('acc0',)")],
+                                  "blockprog", "staged_ir"),
+    "split_k_relu_a": ("m02_matmul_rect",
+                       [("Assign(name='acc0__v__c0_0', op=ElementwiseImpl('multiply'), args=('in1__c0_0', 'in0__c0_0')",
+                         "Assign(name='r0', op=ElementwiseImpl('relu'), args=('in0__c0_0',), dtype=None), "
+                         "Assign(name='acc0__v__c0_0', op=ElementwiseImpl('multiply'), args=('in1__c0_0', 'r0')"),
+                        ("Assign(name='acc0__v__c1_0', op=ElementwiseImpl('multiply'), args=('in1__c0_0', 'in0__c1_0')",
+                         "Assign(name='r1', op=ElementwiseImpl('relu'), args=('in0__c1_0',), dtype=None), "
+                         "Assign(name='acc0__v__c1_0', op=ElementwiseImpl('multiply'), args=('in1__c0_0', 'r1')")],
+                       "blockprog", "staged_ir"),
     "row_sum_of_abs": ("r04_row_sum",
                        [("Accum(name='acc0', value='in0'", "Assign(name='ax', op=ElementwiseImpl("
                          "'abs'), args=('in0',), dtype=None), Accum(name='acc0', value='ax'")],

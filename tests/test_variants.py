@@ -29,6 +29,8 @@ def cpu(plan, arrays):
     p = plan["params"]
     if plan["op"] == "rowprog":
         return pw_vm.run_rows(p["program"], p["layout"], arrays)
+    if plan["op"] == "blockprog":
+        return pw_vm.run_block(p["program"], p["layout"], arrays)
     return pw_vm.run(p["program"], arrays)
 
 
