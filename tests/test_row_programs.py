@@ -88,12 +88,21 @@ def test_combine_program_is_the_one_the_tile_states(tmp_path):
     np.testing.assert_allclose(got["out"], per_thread.sum(axis=1), rtol=1e-5, atol=1e-5)
 
 
-def test_row_outputs_must_be_covered(tmp_path):
+def test_row_outputs_not_covered_run_as_written(tmp_path):
+    """An output the rows do not cover is no row program; the block program
+    writes what the IR writes and leaves the rest as the runner filled it."""
     ir = W.row_package(tmp_path / "hole", "hole", 8, 64, {"x": ((8, 64), "f32")}, ("out", (9,), "f32"),
                        [W.load("xv", "x", [W.var("a0"), W.var("a1")], "f32")], [("s", "add", "xv")],
                        final_writes=[W.write("out", [W.var("a0")], ["s"], "f32")])
-    with pytest.raises(CompileError, match="cover"):
-        compile_file(ir)
+    plan = compile_file(ir)
+    assert plan["op"] == "blockprog"
+    from oracle import staged_ir
+    meta = json.loads((tmp_path / "hole" / "meta.json").read_text())
+    arrays = inputs_of(meta, 0)
+    ref = staged_ir.evaluate(ir, arrays)["out"]
+    got = pw_vm.run_block(plan["params"]["program"], plan["params"]["layout"], arrays)["out"]
+    assert np.isnan(ref[8]) and np.isnan(got[8])
+    np.testing.assert_allclose(got[:8], ref[:8], rtol=1e-5)
 
 
 @pytest.mark.parametrize("name", sorted(W.ROW_COUPLED))
