@@ -267,9 +267,7 @@ class BlockCompiler(SerialCompiler):
 
     def block_loop(self, s: Node) -> None:
         extent = static_extent(s.axis.extent)
-        if s.get("end") is not None:
-            raise CompileError("loops with a captured end are not supported")
-        start, step = s.get("start"), s.get("step")
+        start, step, end_expr = s.get("start"), s.get("step"), s.get("end")
         depth = len(self.loop_stack)
         if self.tile_axes + depth + 1 > MAX_AXES:
             raise CompileError("loops nested too deep for a block program")
@@ -281,7 +279,7 @@ class BlockCompiler(SerialCompiler):
             self.loop_extents[depth] = max(self.loop_extents[depth], extent)
         literal = lambda e: e is None or isinstance(e, int) or (isinstance(e, Node) and e.kind == "Literal")  # noqa: E731
         value = lambda e, default: default if e is None else (e if isinstance(e, int) else int(e.value))  # noqa: E731
-        uniform = literal(start) and literal(step)
+        uniform = literal(start) and literal(step) and literal(end_expr)
         if s.get("seed", True):
             for inner in s.body:
                 if isinstance(inner, Node) and inner.kind == "Accum":
@@ -295,11 +293,14 @@ class BlockCompiler(SerialCompiler):
                 raise CompileError("loop step must be positive")
             first = self.fixed_const(value(start, 0))
             stride = self.fixed_const(step_v)
-            limit = self.fixed_const(extent)
+            limit = self.fixed_const(value(end_expr, extent))
         else:
             first = self.int_expr(start) if start is not None else self.literal(0)
             stride = self.int_expr(step) if step is not None else self.literal(1)
-            limit = self.literal(extent)
+            # a captured end is evaluated once on entry (ptx_backend.py:1531-1543)
+            limit = self.int_expr(end_expr) if end_expr is not None else self.literal(extent)
+        if end_expr is not None:
+            self.env[s.axis.name + "_end"] = limit
         outer_binding = self.active.get(s.axis.name)
         self.active[s.axis.name] = internal
         self.clear_memo()

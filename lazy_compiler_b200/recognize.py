@@ -953,4 +953,4 @@ def _pointwise_program(pkg: KernelPackage, tile: Node, reason: CompileError) -> 
     try:
         return compile_pointwise(pkg, tile)
     except CompileError as err:
-        raise CompileError(f"{err} (and not a fixed pointwise class: {reason})") from err
+        return _block_program(pkg, tile, f"{err} (and not a fixed pointwise class: {reason})")

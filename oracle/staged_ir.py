@@ -204,8 +204,14 @@ class StagedOracle(PointwiseOracle):
         step = s.get("step")
         start_v = np.broadcast_to(np.asarray(self.index(start) if start is not None else 0, np.int64), (self.n,))
         step_v = int(np.asarray(self.index(step))) if step is not None else 1
-        if step_v <= 0 or s.get("end") is not None:
-            raise ValueError("oracle: loops count up to their extent in positive steps")
+        if step_v <= 0:
+            raise ValueError("oracle: loops count up in positive steps")
+        end = s.get("end")
+        # a captured end is evaluated once on entry and replaces the extent as the bound
+        bound = np.broadcast_to(np.asarray(self.index(end), np.int64), (self.n,)) if end is not None \
+            else np.full(self.n, extent, np.int64)
+        if end is not None:
+            self.env[s.axis.name + "_end"] = V(bound.astype(np.int32), "s32")
         if s.get("seed", True):
             for inner in s.body:
                 if inner.kind == "Accum":
@@ -218,7 +224,7 @@ class StagedOracle(PointwiseOracle):
         i = 0
         while True:
             var = start_v + i * step_v
-            live = saved & (var < extent)
+            live = saved & (var < bound)
             if not live.any():
                 break
             self.mask = live

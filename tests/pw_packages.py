@@ -593,3 +593,46 @@ def _staged_bias_residual(folder):
 
 STAGED_EPILOGUES = {"staged_tanh": _staged_tanh, "staged_scaled_silu": _staged_scaled_silu,
                     "staged_bias_residual": _staged_bias_residual}
+
+
+# ---------------------------------------------------------------- block programs
+def block_package(folder: Path, name: str, inputs: dict, output: tuple, axes: list, body: list, threads: int,
+                  rtol=1e-5, atol=1e-6) -> Path:
+    """``package`` with the Tile's trailing axes a block of ``threads`` threads."""
+    ir = package(folder, name, inputs, output, axes, body, rtol, atol)
+    ir.write_text(ir.read_text().replace("block_threads=None", f"block_threads={threads}"))
+    meta = json.loads((folder / "meta.json").read_text())
+    meta["kernels"][0]["block"] = [threads, 1, 1]
+    (folder / "meta.json").write_text(json.dumps(meta))
+    return ir
+
+
+def _captured_end_rows(folder):
+    # out[r, t] = sum of x[r, c] over c = t, t + 16, ... below r * 10 + 20 (a per-row captured end)
+    r, t = var("r"), var("t")
+    end = bin_("+", bin_("*", r, lit(10)), lit(20))
+    body = [f"Init(name='acc', identity=0.0, dtype={dt('f32')})",
+            f"StridedLoop(axis=Axis(name='c', extent=Dim(64), window=None), start={t}, step={lit(16)}, "
+            f"body=({load('xv', 'x', [r, var('c')], 'f32')}, {accum('acc', 'xv', 'add')}), unroll=False, "
+            f"end={end}, seed=False)",
+            write("out", [r, t], ["acc"], "f32")]
+    return block_package(folder, "captured_end_rows", {"x": ((4, 64), "f32")}, ("out", (4, 16), "f32"),
+                         [("r", 4), ("t", 16)], body, 16)
+
+
+def _shared_transpose(folder):
+    # each block stages a 16 x 16 tile in shared memory, syncs, and writes it transposed
+    b, t = var("b"), var("t")
+    row, col = bin_("/", t, lit(16)), bin_("%", t, lit(16))
+    body = ["Smem(name='tile', extents=(16, 16), dtype='float', align=0)",
+            load("xv", "x", [b, row, col], "f32"),
+            f"Write(output='tile', index=({row}, {col}), values=('xv',), value_dtype={dt('f32')}, atomic=False, "
+            "swizzle='NONE')",
+            "Sync(barrier_id=0, count=None, warp=False)",
+            f"Load(names=('tv',), input='tile', index=({col}, {row}), dtype=None)",
+            write("out", [b, row, col], ["tv"], "f32")]
+    return block_package(folder, "shared_transpose", {"x": ((3, 16, 16), "f32")}, ("out", (3, 16, 16), "f32"),
+                         [("b", 3), ("t", 256)], body, 256)
+
+
+BLOCK_SYNTHETIC = {"captured_end_rows": _captured_end_rows, "shared_transpose": _shared_transpose}

@@ -127,3 +127,36 @@ def test_block_program_on_gpu(name, cuda_device):
         for key, value in ref.items():
             row = O.compare(got[key].reshape(value.shape), value, meta["rtol"], meta["atol"])
             assert row["pass"], (name, offset, key, row)
+
+
+@pytest.mark.parametrize("name", sorted(__import__("pw_packages").BLOCK_SYNTHETIC))
+def test_synthetic_block_program_matches_oracle(name, tmp_path):
+    import json
+    import pw_packages as W
+    from lazy_compiler_b200.compiler import compile_file
+    ir = W.BLOCK_SYNTHETIC[name](tmp_path / name)
+    plan = compile_file(ir)
+    assert plan["op"] == "blockprog"
+    meta = json.loads((tmp_path / name / "meta.json").read_text())
+    for offset in (0, 2):
+        arrays = inputs_of(meta, offset)
+        ref = staged_ir.evaluate(ir, arrays)
+        got = pw_vm.run_block(plan["params"]["program"], plan["params"]["layout"], arrays)
+        for key, value in ref.items():
+            assert not np.isnan(value).any()
+            np.testing.assert_allclose(got[key].reshape(value.shape), value, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", sorted(__import__("pw_packages").BLOCK_SYNTHETIC))
+def test_synthetic_block_program_on_gpu(name, tmp_path, cuda_device):
+    import json
+    import pw_packages as W
+    from lazy_compiler_b200.runner import run_package
+    ir = W.BLOCK_SYNTHETIC[name](tmp_path / name)
+    meta = json.loads((tmp_path / name / "meta.json").read_text())
+    arrays = inputs_of(meta, 1)
+    ref = staged_ir.evaluate(ir, arrays)
+    got = run_package(ir.parent, inputs=arrays)
+    for key, value in ref.items():
+        np.testing.assert_allclose(np.asarray(got[key]).reshape(value.shape), value, rtol=1e-6, atol=1e-6)
