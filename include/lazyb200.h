@@ -322,12 +322,12 @@ int lc_probe_mma(int variant, int groups, void *stream);
  * extents[n_axes + depth] (the largest extent of any loop at that depth,
  * over which the forms are validated); LOOPB jumps past its LOOPE (pc) when
  * the count is empty, LOOPE jumps back to its LOOPB (pc) while below it. */
-#define LC_PW_MAX_CODE 1024
+#define LC_PW_MAX_CODE 2048
 #define LC_PW_MAX_CONST 128
 #define LC_PW_MAX_FORMS 32
 #define LC_PW_MAX_BUFFERS 16
 #define LC_PW_MAX_AXES 8
-#define LC_PW_MAX_REGS 64
+#define LC_PW_MAX_REGS 128
 
 enum lc_pw_op {
   LC_PW_MOV = 0,

@@ -60,12 +60,12 @@ OPCODES = [
 ]
 OP = {name: i for i, name in enumerate(OPCODES)}
 
-MAX_CODE = 1024
+MAX_CODE = 2048
 MAX_CONST = 128
 MAX_FORMS = 32
 MAX_BUFFERS = 16
 MAX_AXES = 8
-MAX_REGS = 64
+MAX_REGS = 128
 
 _TYPES = {"float": "f32", "int": "s32", "i32": "s32", "__half": "f16", "half": "f16",
           "__nv_bfloat16": "bf16", "bool": "pred"}

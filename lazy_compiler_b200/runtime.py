@@ -68,7 +68,7 @@ SIGNATURES = {
 # pointwise programs (include/lazyb200.h lc_pw_program)
 LC_S32 = 3
 STORAGE_CODES = {"f32": LC_F32, "f16": LC_F16, "bf16": LC_BF16, "s32": LC_S32}
-PW_MAX_CODE, PW_MAX_CONST, PW_MAX_FORMS, PW_MAX_BUFFERS, PW_MAX_AXES = 1024, 128, 32, 16, 8
+PW_MAX_CODE, PW_MAX_CONST, PW_MAX_FORMS, PW_MAX_BUFFERS, PW_MAX_AXES = 2048, 128, 32, 16, 8
 
 
 class PwForm(ctypes.Structure):
