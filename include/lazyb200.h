@@ -466,7 +466,10 @@ int lc_pointwise(const lc_pw_program *program, void *const *buffers, void *strea
  * Accum with or without a base is an explicit update), then the partials
  * combine: warp_begin..warp_end runs at each level of a lane butterfly
  * (PARTNER reads the other lane's partial), tree_begin..tree_end folds the
- * warps' results in order on one thread.  Later passes and the final
+ * warps' results pairwise, halving (warp i with warp i + d for d = W/2 ...
+ * 1, as the reference's shared tree does), on one thread.  The CTA has the
+ * Tile's own `threads`, so every thread folds the columns the reference's
+ * thread folds, in the same order.  Later passes and the final
  * operations (once per row, column 0, one thread) read combined states with
  * STATE. */
 #define LC_RP_MAX_PASSES 4
@@ -479,6 +482,7 @@ typedef struct {
   int32_t tree_begin[LC_RP_MAX_PASSES], tree_end[LC_RP_MAX_PASSES];
   uint32_t state_init[LC_RP_MAX_STATES]; /* f32 bits of each state's seed */
   int32_t state_pass[LC_RP_MAX_STATES];  /* the pass that accumulates the state */
+  int32_t threads;                       /* the Tile's block: 32 x a power of two, at most 1024 */
 } lc_rp_layout;
 
 /* Runs a row program (validated like lc_pointwise, plus its layout). */

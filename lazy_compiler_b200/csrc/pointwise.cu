@@ -295,8 +295,8 @@ struct RowProgArgs {
 // program's own combine steps — a lane butterfly in each warp, then the
 // warps' results folded in warp order by one thread — and broadcast the
 // states.  Every barrier is reached by every thread of the CTA.
-__global__ void __launch_bounds__(256) rowprog_kernel(const __grid_constant__ RowProgArgs p) {
-  __shared__ float warp_part[8][LC_RP_MAX_STATES];
+__global__ void __launch_bounds__(1024) rowprog_kernel(const __grid_constant__ RowProgArgs p) {
+  __shared__ float warp_part[32][LC_RP_MAX_STATES];
   __shared__ float combined[LC_RP_MAX_STATES];
   uint32_t r[LC_PW_MAX_REGS];
   for (int i = 0; i < LC_PW_MAX_REGS; ++i) r[i] = 0u;
@@ -339,15 +339,20 @@ __global__ void __launch_bounds__(256) rowprog_kernel(const __grid_constant__ Ro
           if (lay.state_pass[k] == pass) warp_part[warp][k] = partials[k];
       __syncthreads();
       if (threadIdx.x == 0) {
+        // the reference's tree: at each level warp i takes warp i + d, d halving
+        for (int d = nwarps >> 1; d > 0; d >>= 1)
+          for (int i = 0; i < d; ++i) {
+            for (int k = 0; k < lay.n_states; ++k)
+              if (lay.state_pass[k] == pass) {
+                partials[k] = warp_part[i][k];
+                partners[k] = warp_part[i + d][k];
+              }
+            exec_range(g, p.buffers, xr, r, lay.tree_begin[pass], lay.tree_end[pass], states, partials, partners);
+            for (int k = 0; k < lay.n_states; ++k)
+              if (lay.state_pass[k] == pass) warp_part[i][k] = partials[k];
+          }
         for (int k = 0; k < lay.n_states; ++k)
-          if (lay.state_pass[k] == pass) partials[k] = warp_part[0][k];
-        for (int w2 = 1; w2 < nwarps; ++w2) {
-          for (int k = 0; k < lay.n_states; ++k)
-            if (lay.state_pass[k] == pass) partners[k] = warp_part[w2][k];
-          exec_range(g, p.buffers, xr, r, lay.tree_begin[pass], lay.tree_end[pass], states, partials, partners);
-        }
-        for (int k = 0; k < lay.n_states; ++k)
-          if (lay.state_pass[k] == pass) combined[k] = partials[k];
+          if (lay.state_pass[k] == pass) combined[k] = warp_part[0][k];
       }
       __syncthreads();
       for (int k = 0; k < lay.n_states; ++k)
@@ -596,6 +601,8 @@ extern "C" int lc_rowprog(const lc_pw_program *program, const lc_rp_layout *layo
   for (int k = 0; k < lay.n_states; ++k)
     if (lay.state_pass[k] < 0 || lay.state_pass[k] >= lay.n_passes)
       return fail(LC_ERR_INVALID, "lc_rowprog: state %d", k);
+  if (lay.threads < 32 || lay.threads > 1024 || lay.threads % 32 || ((lay.threads / 32) & (lay.threads / 32 - 1)))
+    return fail(LC_ERR_INVALID, "lc_rowprog: %d threads is not 32 times a power of two up to 1024", lay.threads);
   for (int pc = 0; pc < n_code; ++pc) {
     const int op = program->code[pc][0] & 255, aux = (int)(program->code[pc][1] >> 8);
     if ((op == LC_PW_STATE || op == LC_PW_PARTIAL || op == LC_PW_PARTNER || op == LC_PW_SETP) && aux >= lay.n_states)
@@ -610,7 +617,7 @@ extern "C" int lc_rowprog(const lc_pw_program *program, const lc_rp_layout *layo
   int64_t blocks = rows;
   const int64_t cap = (int64_t)sm_count() * 8;
   if (blocks > cap) blocks = cap;
-  rowprog_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(args);
+  rowprog_kernel<<<(unsigned)blocks, (unsigned)lay.threads, 0, as_stream(stream)>>>(args);
   return check_launch("lc_rowprog");
 }
 

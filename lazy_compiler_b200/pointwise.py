@@ -508,10 +508,13 @@ class PointwiseCompiler:
             raise CompileError(f"unknown buffer {buffer}")
         shape = tuple(buf.shape) or (1,)
         total: dict = {}
-        if len(index) == 1 or (len(index) > 1 and len(index) != len(shape)):
-            terms = [(self.affine(i), 1) for i in index]
-        else:
-            terms = [(self.affine(i), math.prod(shape[d + 1:])) for d, i in enumerate(index)]
+        strides = [1] * len(index) if len(index) == 1 or (len(index) > 1 and len(index) != len(shape)) else \
+            [math.prod(shape[d + 1:]) for d in range(len(index))]
+        try:
+            terms = [(self.affine(i), st) for i, st in zip(index, strides)]
+        except CompileError:
+            # a row-major split of one axis (x[a // c, a % c]) flattens back to the axis
+            terms = [(self.flat_affine(index, strides), 1)]
         for aff, stride in terms:
             for k, v in aff.items():
                 total[k] = total.get(k, 0) + v * stride
@@ -533,6 +536,29 @@ class PointwiseCompiler:
             self.form_index[key] = len(self.forms)
             self.forms.append(Form(self.slots[buffer], vm_type(buf.dtype), base, coef))
         return self.form_index[key]
+
+    def flat_affine(self, index: tuple, strides: list) -> dict:
+        """The flattened offset of an index with div / mod terms, when the terms
+        recombine (c * (x // c) + x % c == x) into an affine form of the axes."""
+        from .recognize import _aff, _aff_add, _aff_scale, _Eval
+        ev = _Eval(self.pkg)
+        total = _aff({})
+        for i, stride in zip(index, strides):
+            if not isinstance(i, Node):
+                raise CompileError(f"pointwise index {i!r} is not affine in the tile axes")
+            total = _aff_add(total, _aff_scale(ev.index(i), stride))
+        active = getattr(self, "active", {})
+        out: dict = {}
+        for term, coef in total:
+            if term == 1:
+                out[1] = out.get(1, 0) + coef
+            elif isinstance(term, str) and term in active:
+                out[active[term]] = out.get(active[term], 0) + coef
+            elif isinstance(term, str) and term in self.axes:
+                out[term] = out.get(term, 0) + coef
+            else:
+                raise CompileError("pointwise index is not affine in the tile axes")
+        return out
 
     def statement(self, s: Node) -> None:
         k = s.kind

@@ -578,6 +578,68 @@ def _rowdot_terms(pkg: KernelPackage, value: Any, x_index: tuple):
     return None
 
 
+_COMMUTATIVE = ("add", "multiply", "maximum", "minimum")
+
+
+def canon_expr(e):
+    """An expression with copies dropped and commutative arguments ordered."""
+    if isinstance(e, tuple) and e and e[0] == "op":
+        if e[1] == "copy" and len(e) == 3:
+            return canon_expr(e[2])
+        args = [canon_expr(a) for a in e[2:]]
+        if e[1] in _COMMUTATIVE and len(args) == 2:
+            args = sorted(args, key=repr)
+        return ("op", e[1], *args)
+    return e
+
+
+def combine_result(node: Node) -> dict | None:
+    """Each state after one step of a WarpShuffle / TreeHalve combine, as an
+    expression of ("self", state) and ("other", state)."""
+    env: dict = {}
+    for a, b in zip(node.state, node.state_b):
+        env[a], env[b] = ("self", a), ("other", a)
+    for st in node.get("combine_states") or ():
+        if st.kind == "Assign":
+            opn = st.op.name if isinstance(st.op, Node) else str(st.op)
+            env[st.name] = ("op", opn, *(env.get(x, ("?", x)) if isinstance(x, str) else ("?",) for x in st.args))
+        elif st.kind == "Let" and _is_lit(st.value):
+            env[st.name] = ("lit", float(st.value.value))
+        else:
+            return None
+    return {a: canon_expr(env[a]) for a in node.state}
+
+
+def fold_combine(name: str, opn: str) -> tuple:
+    return ("op", opn, ("self", name), ("other", name))
+
+
+def online_combine(mx: str, states: list) -> dict:
+    """The online-softmax merge: the larger max, and every state rescaled to it."""
+    gn = ("op", "maximum", ("self", mx), ("other", mx))
+    out = {mx: gn}
+    for s in states:
+        out[s] = ("op", "add", ("op", "multiply", ("op", "exp", ("op", "subtract", ("self", mx), gn)), ("self", s)),
+                  ("op", "multiply", ("op", "exp", ("op", "subtract", ("other", mx), gn)), ("other", s)))
+    return out
+
+
+def combines_are(tile: Node, expected: dict) -> bool:
+    """Every WarpShuffle / TreeHalve of the Tile combines the given states as expected."""
+    seen = set()
+    for node in _walk(tile.body):
+        if not isinstance(node, Node) or node.kind not in ("WarpShuffle", "TreeHalve"):
+            continue
+        result = combine_result(node)
+        if result is None:
+            return False
+        for name in node.state:
+            seen.add(name)
+            if name not in expected or result[name] != canon_expr(expected[name]):
+                return False
+    return seen >= set(expected)
+
+
 def _recognise_reduction(pkg: KernelPackage, tile: Node, ev: _Eval) -> Plan:
     axes = [(a.name, static_extent(a.extent)) for a in tile.axes]
     block = tile.get("block_threads") or axes[-1][1]
@@ -616,6 +678,8 @@ def _recognise_reduction(pkg: KernelPackage, tile: Node, ev: _Eval) -> Plan:
         (acc, red), = reds.items()
         if red["op"] != "add" or red["base"] is not None:
             raise CompileError("unsupported accumulator")
+        if not combines_are(tile, {acc: fold_combine(acc, "add")}):
+            raise CompileError("the partial sums are not combined by addition")
         if len(ev.writes) != 1 or not cond_ok(ev.writes[0]):
             raise CompileError("reduction result must be written once by thread 0")
         w = ev.writes[0]
@@ -697,9 +761,14 @@ def _recognise_reduction(pkg: KernelPackage, tile: Node, ev: _Eval) -> Plan:
         if not _match(pattern, value, {}):
             raise CompileError("softmax output expression not recognised")
         # the running sum must rescale by exp(old - new) and add exp(x - new)
-        srep = repr(reds[sm]["value"])
-        if "'exp'" not in srep or "'maximum'" not in srep:
+        xl = reds[mx]["value"]
+        gn = ("op", "maximum", ("acc", mx), xl)
+        online = ("op", "add", ("op", "multiply", ("acc", sm), ("op", "exp", ("op", "subtract", ("acc", mx), gn))),
+                  ("op", "multiply", ("op", "exp", ("op", "subtract", xl, gn)), ("lit", 1.0)))
+        if canon_expr(reds[sm]["value"]) != canon_expr(online):
             raise CompileError("softmax sum is not an online rescaled exponential sum")
+        if not combines_are(tile, online_combine(mx, [sm])):
+            raise CompileError("softmax partial states are not merged online")
         return _plan(pkg, "softmax_f32", "lc_softmax_f32", {"x": x, "out": out},
                      {"rows": rows, "cols": cols}, {"io": "f32"})
 
@@ -707,6 +776,8 @@ def _recognise_reduction(pkg: KernelPackage, tile: Node, ev: _Eval) -> Plan:
     b = _match(op("multiply", V("x", _is_load(index=x_index)), V("x")), red["value"], {})
     if red["op"] != "add" or not b:
         raise CompileError("row norm must accumulate a sum of squares")
+    if red["base"] is not None or not combines_are(tile, {acc: fold_combine(acc, "add")}):
+        raise CompileError("the partial sums of squares are not combined by addition")
     x = b["x"][1]
     # L2: x * recip(sqrt(acc))
     if _match(op("multiply", V("x", _is_load(x, x2)), op("reciprocal", op("sqrt", ("red", acc)))), value, {}):

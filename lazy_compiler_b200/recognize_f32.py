@@ -40,7 +40,8 @@ import numpy as np
 
 from .ir import CompileError, KernelPackage, Node, static_extent
 from .post import compile_epilogue
-from .recognize import (_GELU_ERF_ANY, _GELU_ERF_B_ANY, _GELU_TANH_ANY, Plan, _aff, _aff_add,
+from .recognize import (_GELU_ERF_ANY, _GELU_ERF_B_ANY, _GELU_TANH_ANY, Plan, _aff, _aff_add, combines_are,
+                        fold_combine, online_combine,
                         _aff_const, _Eval, _flat, _is_load, _match, _numel, _plan, _scalar_buffer,
                         _scalar_of, _check_consts, op, V)
 
@@ -183,7 +184,7 @@ def _loop_info(ev: _Eval, axis: str) -> dict:
 
 
 def _contraction_form(tile: Node, ev: _Eval, loop: dict, extent: int, states: list[str],
-                      writes: list) -> dict | None:
+                      writes: list, combine: dict) -> dict | None:
     """How a contraction loop covers [0, extent): serially, or strided over the block.
 
     Returns {} for the serial form, {co_axis: 0} (the pinned cooperative axis)
@@ -202,6 +203,8 @@ def _contraction_form(tile: Node, ev: _Eval, loop: dict, extent: int, states: li
             raise CompileError("block contraction must combine a full warp butterfly and a block tree")
         if any(s not in ev.trees or s not in ev.shuffled for s in states):
             raise CompileError("every block-contracted state must be block-reduced")
+        if not combines_are(tile, combine):
+            raise CompileError("the block's partial states are not combined as the contraction needs")
         for w in writes:
             c = w["cond"]
             if not (len(c) == 1 and c[0].kind == "BinaryExpr" and c[0].op == "==" and c[0].left.kind == "Var"
@@ -310,7 +313,11 @@ def recognise_attention(pkg: KernelPackage, tile: Node, ev: _Eval) -> Plan:
     jl = _loop_info(ev, j)
     if jl["start"] != _aff({}) or jl["step"] != 1 or jl["extent"] != d:
         raise CompileError("the score's dot product must walk the head dimension")
-    fixed = _contraction_form(tile, ev, _loop_info(ev, key), s_kv, states, ev.writes)
+    merge: dict = {}
+    for k in range(0, len(states), 3):
+        S_, L_, M_ = states[k:k + 3]
+        merge.update(online_combine(M_, [L_, S_]))
+    fixed = _contraction_form(tile, ev, _loop_info(ev, key), s_kv, states, ev.writes, merge)
     check_cover(pkg, _tile_axes(tile), ev.writes, out, fixed)
     return _plan(pkg, "attention_f32", "lc_attention_f32",
                  {"scale": c, "q": q, "kt": kt, "v": v, "o": out},
@@ -397,7 +404,8 @@ def recognise_dot_gemm(pkg: KernelPackage, tile: Node, ev: _Eval) -> Plan:
         states.append(acc[1])
     a, b, bias, layout, epi, kaxis = sig
     k = pkg.buffers[a].shape[1] if len(pkg.buffers[a].shape) == 2 else -1
-    fixed = _contraction_form(tile, ev, _loop_info(ev, kaxis), k, states, ev.writes)
+    fixed = _contraction_form(tile, ev, _loop_info(ev, kaxis), k, states, ev.writes,
+                              {name: fold_combine(name, "add") for name in states})
     if len(ev.loops) != 1:
         raise CompileError("GEMM dot form has loops besides the contraction")
     check_cover(pkg, _tile_axes(tile), ev.writes, out, fixed)

@@ -244,7 +244,9 @@ class RowProgramCompiler(PointwiseCompiler):
             self.pass_ranges.append((begin, len(self.code)))
             warp, tree = combines[p]
             if accs:
-                if warp is None or tree is None or int(warp.get("length") or 0) != 32:
+                if warp is None or tree is None or int(warp.get("length") or 0) != 32 or \
+                        int(tree.get("length") or 0) * 32 != self.block or tree.get("tid_var") != "warp" or \
+                        tree.get("inner"):
                     raise CompileError("a pass's accumulators must be combined by a warp butterfly and a block tree")
                 if set(warp.state) != set(accs) or set(tree.state) != set(accs):
                     raise CompileError("the combines do not cover exactly the pass's accumulators")
@@ -301,7 +303,7 @@ class RowProgramCompiler(PointwiseCompiler):
     def layout(self, final: tuple) -> dict:
         return {"passes": [list(r) for r in self.pass_ranges], "warp": [list(r) for r in self.warp_ranges],
                 "tree": [list(r) for r in self.tree_ranges], "final": list(final),
-                "state_init": list(self.state_init), "state_pass": list(self.state_pass)}
+                "state_init": list(self.state_init), "state_pass": list(self.state_pass), "threads": self.block}
 
 
 def _add_const(form, k: int):

@@ -117,7 +117,7 @@ class RpLayout(ctypes.Structure):
                 ("end", ctypes.c_int32 * RP_MAX_PASSES), ("warp_begin", ctypes.c_int32 * RP_MAX_PASSES),
                 ("warp_end", ctypes.c_int32 * RP_MAX_PASSES), ("tree_begin", ctypes.c_int32 * RP_MAX_PASSES),
                 ("tree_end", ctypes.c_int32 * RP_MAX_PASSES), ("state_init", ctypes.c_uint32 * RP_MAX_STATES),
-                ("state_pass", ctypes.c_int32 * RP_MAX_STATES)]
+                ("state_pass", ctypes.c_int32 * RP_MAX_STATES), ("threads", ctypes.c_int32)]
 
 
 def rp_layout(layout: dict) -> RpLayout:
@@ -131,6 +131,7 @@ def rp_layout(layout: dict) -> RpLayout:
         lay.tree_begin[i], lay.tree_end[i] = tb, te
     for k, (init, ps) in enumerate(zip(layout["state_init"], layout["state_pass"])):
         lay.state_init[k], lay.state_pass[k] = init, ps
+    lay.threads = layout.get("threads", 256)
     return lay
 
 

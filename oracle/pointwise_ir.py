@@ -214,6 +214,9 @@ class PointwiseOracle:
             return self.coord[e.name]
         if k == "BinaryExpr":
             a, b = self.index(e.left), self.index(e.right)
+            if e.op in ("/", "//", "%"):   # C integer division and remainder, truncating toward zero
+                q = np.trunc(np.asarray(a, np.float64) / np.asarray(b, np.float64)).astype(np.int64)
+                return q if e.op != "%" else a - b * q
             return {"+": a + b, "-": a - b, "*": a * b}[e.op]
         raise ValueError(f"oracle: index {e!r}")
 

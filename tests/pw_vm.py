@@ -285,11 +285,14 @@ def assert_faithful(ir, rtol=1e-5, atol=1e-6):
     return plan
 
 
-def run_rows(prog: dict, layout: dict, arrays: dict, block: int = 128) -> dict:
-    """A row program on the CPU, as its schedule runs it: every thread of a
-    ``block``-wide CTA folds its strided columns into its partials in column
-    order, the partials combine thread by thread through the tree's combine
-    operations, the final operations run once per row."""
+def run_rows(prog: dict, layout: dict, arrays: dict, block: int | None = None) -> dict:
+    """A row program on the CPU, as its schedule runs it: every thread of the
+    Tile's ``threads``-wide CTA folds its strided columns into its partials in
+    column order; the partials combine through the warp operations at each
+    level of a lane butterfly (xor 16 ... 1), then lane 0 of each warp through
+    the tree operations pairwise, halving (warp i with warp i + d); the final
+    operations run once per row."""
+    block = block or layout.get("threads", 128)
     *row_ext, cols = prog["extents"]
     rows = int(np.prod(row_ext))
     states, outs = {}, {}
@@ -298,6 +301,7 @@ def run_rows(prog: dict, layout: dict, arrays: dict, block: int = 128) -> dict:
     r_coords = [np.repeat(rc, block) for rc in row_coords]
     t_idx = np.tile(np.arange(block, dtype=np.int64), rows)
     per_row = row_coords + [np.zeros(rows, np.int64)]
+    lanes = np.arange(rows * block, dtype=np.int64)
 
     def sub(b, e):
         return dict(prog, code=prog["code"][b:e])
@@ -312,12 +316,24 @@ def run_rows(prog: dict, layout: dict, arrays: dict, block: int = 128) -> dict:
             run(sub(b, e), arrays, coords=r_coords + [np.minimum(c, cols - 1)], states=wide, partials=partials,
                 mask=c < cols, outs=outs)
         if slots:
+            wb, we = layout["warp"][p]
+            for o in (16, 8, 4, 2, 1):
+                partner = {k: partials[k][lanes ^ o] for k in slots}
+                run(sub(wb, we), arrays, coords=r_coords + [np.zeros(rows * block, np.int64)], states=wide,
+                    partials=partials, partners=partner, outs=outs)
             tb, te = layout["tree"][p]
-            own = {k: partials[k].reshape(rows, block)[:, 0].copy() for k in slots}
-            for t in range(1, block):
-                partner = {k: partials[k].reshape(rows, block)[:, t] for k in slots}
-                run(sub(tb, te), arrays, coords=per_row, states=states, partials=own, partners=partner, outs=outs)
-            states.update(own)
+            nwarps = block // 32
+            part = {k: partials[k].reshape(rows, block)[:, ::32].copy() for k in slots}
+            d = nwarps // 2
+            while d:
+                for i in range(d):
+                    own = {k: part[k][:, i].copy() for k in slots}
+                    other = {k: part[k][:, i + d] for k in slots}
+                    run(sub(tb, te), arrays, coords=per_row, states=states, partials=own, partners=other, outs=outs)
+                    for k in slots:
+                        part[k][:, i] = own[k]
+                d //= 2
+            states.update({k: part[k][:, 0].copy() for k in slots})
     fb, fe = layout["final"]
     run(sub(fb, fe), arrays, coords=per_row, states=states, partials={}, outs=outs)
     return outs
