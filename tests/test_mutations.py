@@ -28,11 +28,16 @@ FOLDS = ["add", "maximum", "minimum"]
 PACKAGES = ["r04_row_sum", "f01_rmsnorm", "f02_row_softmax", "f03_l2norm", "phase9_gelu_row_dot",
             "phase9_gelu_attention", "a02_attention_128", "m02_matmul_rect", "p03_relu_mul", "p02_scale_shift",
             "r01_array_sum", "r03_mean", "phase9_gelu_erf_tail", "phase9_gelu_tanh_matrix", "phase9_bias_gelu_gemm",
-            "activation_gelu_f32", "p01_vector_add"]
+            "activation_gelu_f32", "p01_vector_add", "fragment_family_row_softmax", "fragment_attention_tile_f16",
+            "fragment_row_add_ordered", "fragment_mma_row_normalization", "tensor_fused_guarded_epilogue",
+            "fragment_masked_gmem_post"]
 SEEDS = int(__import__("os").environ.get("LC_MUTATION_SEEDS", "3"))
 CASES = [(name, seed) for name in PACKAGES for seed in range(SEEDS)]
 
 ASSIGN = re.compile(r"Assign\(name='([^']+)', op=ElementwiseImpl\('(\w+)'\), args=\(([^)]*)\)")
+FRAG_APPLY = re.compile(r"FragmentApply\(out='[^']+', op=ElementwiseImpl\('(\w+)'\), args=.*?kinds=\(([^)]*)\)")
+FRAG_REDUCE = re.compile(r"FragmentRowReduce\(top='[^']+', bot='[^']+', frags=\([^)]*\), op=ElementwiseImpl\('(\w+)'\)")
+FRAG_BINARY = ["add", "subtract", "multiply", "divide", "maximum", "minimum"]
 ACCUM = re.compile(r"(Accum\(name='[^']+', value='[^']+', op=ElementwiseImpl\(')(\w+)('\))")
 
 
@@ -48,6 +53,15 @@ def mutate(text: str, seed: int) -> tuple:
     for m in ACCUM.finditer(text):
         if m.group(2) in FOLDS:
             sites.append((m.start(2), m.end(2), FOLDS))
+    for m in FRAG_APPLY.finditer(text):
+        arity = len([k for k in m.group(2).split(",") if k.strip()])
+        if m.group(1) in FRAG_BINARY and arity == 2:
+            sites.append((m.start(1), m.end(1), FRAG_BINARY))
+        elif m.group(1) in UNARY and arity == 1:
+            sites.append((m.start(1), m.end(1), UNARY))
+    for m in FRAG_REDUCE.finditer(text):
+        if m.group(1) in FOLDS:
+            sites.append((m.start(1), m.end(1), FOLDS))
     if not sites:
         pytest.skip("no mutable operation")
     picked = sorted(rng.sample(sites, min(len(sites), 2)), reverse=True)
@@ -64,6 +78,9 @@ def ir_oracle(ir, arrays):
     pkg = load_package(ir)
     tile = pkg.body[0]
     kinds = {s.kind for s in tile.body}
+    if any(k.startswith(("Fragment", "RegFragment", "RegStore", "MmaSync", "Ldmatrix")) for k in kinds):
+        from oracle import fragment_ir
+        return fragment_ir.evaluate(ir, arrays)
     if tile.get("block_threads"):
         from oracle import staged_ir
         return staged_ir.evaluate(ir, arrays)
