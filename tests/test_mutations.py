@@ -38,6 +38,7 @@ ASSIGN = re.compile(r"Assign\(name='([^']+)', op=ElementwiseImpl\('(\w+)'\), arg
 FRAG_APPLY = re.compile(r"FragmentApply\(out='[^']+', op=ElementwiseImpl\('(\w+)'\), args=.*?kinds=\(([^)]*)\)")
 FRAG_REDUCE = re.compile(r"FragmentRowReduce\(top='[^']+', bot='[^']+', frags=\([^)]*\), op=ElementwiseImpl\('(\w+)'\)")
 FRAG_BINARY = ["add", "subtract", "multiply", "divide", "maximum", "minimum"]
+FLOAT_LITERAL = re.compile(r"Literal\(value=(-?[0-9]+\.[0-9]*(?:e[-+]?[0-9]+)?), dtype=(?!'int')")
 ACCUM = re.compile(r"(Accum\(name='[^']+', value='[^']+', op=ElementwiseImpl\(')(\w+)('\))")
 
 
@@ -62,6 +63,9 @@ def mutate(text: str, seed: int) -> tuple:
     for m in FRAG_REDUCE.finditer(text):
         if m.group(1) in FOLDS:
             sites.append((m.start(1), m.end(1), FOLDS))
+    for m in FLOAT_LITERAL.finditer(text):
+        value = float(m.group(1))
+        sites.append((m.start(1), m.end(1), [repr(value * 1.5 + 0.25), repr(-value), repr(value * 0.5)]))
     if not sites:
         pytest.skip("no mutable operation")
     picked = sorted(rng.sample(sites, min(len(sites), 2)), reverse=True)
