@@ -10,7 +10,6 @@ packages are timed at their own (small) shapes, kernel launches only (the
 launcher's zeroing of split-K outputs is excluded for both).
 """
 import argparse
-import ctypes
 import json
 import sys
 from pathlib import Path

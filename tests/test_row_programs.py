@@ -11,7 +11,7 @@ import pw_packages as W
 import pw_vm
 from conftest import golden, golden_ir, golden_meta
 from lazy_compiler_b200.compiler import compile_file
-from lazy_compiler_b200.ir import CompileError, load_package, static_extent
+from lazy_compiler_b200.ir import load_package, static_extent
 from lazy_compiler_b200.recognize import _Eval
 from lazy_compiler_b200.rowprog import compile_rowprog
 from oracle import expressions as O
