@@ -531,6 +531,14 @@ typedef struct {
 int lc_blockprog(const lc_pw_program *program, const lc_bp_layout *layout, void *const *buffers,
                  void *stream);
 
+/* The same block program run natively: `image` is an sm_100a module
+ * (cubin) whose kernel lc_jit_block(struct {void *buffers[16]; long long
+ * blocks;}) is the program translated to CUDA C, statement for statement
+ * (lazy_compiler_b200/jit.py).  The program and layout are validated as for
+ * lc_blockprog before the launch; the module is loaded once per device. */
+int lc_jit_blockprog(const void *image, size_t image_size, const lc_pw_program *program,
+                     const lc_bp_layout *layout, void *const *buffers, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,6 +8,11 @@
 // The program itself lives in the kernel's parameter space (a
 // __grid_constant__ struct): every lane of a warp reads the same operation
 // at the same time, a broadcast from the constant bank.
+#include <cuda.h>
+
+#include <mutex>
+#include <vector>
+
 #include "common.cuh"
 
 namespace lc {
@@ -621,35 +626,102 @@ extern "C" int lc_rowprog(const lc_pw_program *program, const lc_rp_layout *layo
   return check_launch("lc_rowprog");
 }
 
-extern "C" int lc_blockprog(const lc_pw_program *program, const lc_bp_layout *layout, void *const *buffers,
-                            void *stream) {
-  using namespace lc;
-  if (!layout) return fail(LC_ERR_INVALID, "lc_blockprog: null layout");
+namespace lc {
+namespace {
+// Validates a block program and fills the launch: the kernel arguments, the
+// dynamic shared memory and the grid.
+int prepare_blockprog(const char *name, const lc_pw_program *program, const lc_bp_layout *layout,
+                      void *const *buffers, BlockProgArgs *args, size_t *smem_bytes, int64_t *grid) {
+  if (!layout) return fail(LC_ERR_INVALID, "%s: null layout", name);
   const lc_bp_layout &lay = *layout;
-  if (lay.n_smem < 0 || lay.n_smem > LC_BP_MAX_SMEM) return fail(LC_ERR_INVALID, "lc_blockprog: shared arrays");
+  if (lay.n_smem < 0 || lay.n_smem > LC_BP_MAX_SMEM) return fail(LC_ERR_INVALID, "%s: shared arrays", name);
   int64_t words = 0;
   for (int i = 0; i < lay.n_smem; ++i) {
     if (lay.smem_size[i] < 1 || lay.smem_offset[i] < 0 ||
         (int64_t)lay.smem_offset[i] + lay.smem_size[i] > (int64_t)(200 * 1024 / 4))
-      return fail(LC_ERR_INVALID, "lc_blockprog: shared array %d", i);
+      return fail(LC_ERR_INVALID, "%s: shared array %d", name, i);
     const int64_t top = (int64_t)lay.smem_offset[i] + lay.smem_size[i];
     if (top > words) words = top;
   }
   int64_t points = 0;
-  if (int rc = validate_program("lc_blockprog", program, buffers, kBlockProgram, &points, &lay)) return rc;
+  if (int rc = validate_program(name, program, buffers, kBlockProgram, &points, &lay)) return rc;
   const lc_pw_program &g = *program;
   if (lay.threads < 1 || lay.threads > 1024 || lay.n_block_axes < 0 || lay.n_block_axes >= g.n_axes)
-    return fail(LC_ERR_INVALID, "lc_blockprog: thread block");
+    return fail(LC_ERR_INVALID, "%s: thread block", name);
   int64_t threads = 1, blocks = 1;
   for (int d = 0; d < g.n_axes; ++d) (d < lay.n_block_axes ? blocks : threads) *= g.extents[d];
-  if (threads != lay.threads) return fail(LC_ERR_INVALID, "lc_blockprog: thread axes do not make %d threads",
-                                          lay.threads);
+  if (threads != lay.threads)
+    return fail(LC_ERR_INVALID, "%s: thread axes do not make %d threads", name, lay.threads);
+  args->prog = g;
+  args->lay = lay;
+  for (int i = 0; i < LC_PW_MAX_BUFFERS; ++i) args->buffers[i] = i < g.n_buffers ? buffers[i] : nullptr;
+  args->blocks = blocks;
+  *smem_bytes = (size_t)words * 4;
+  const int64_t cap = (int64_t)sm_count() * 8;
+  *grid = blocks > cap ? cap : blocks;
+  return LC_OK;
+}
+
+// Modules of natively compiled block programs, loaded once per device and image.
+struct JitModule {
+  uint64_t key;
+  int device;
+  CUfunction function;
+};
+std::mutex jit_mutex;
+std::vector<JitModule> jit_modules;
+
+template <typename T>
+T driver_entry(const char *symbol) {
+  void *ptr = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(symbol, &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return reinterpret_cast<T>(ptr);
+}
+
+int jit_function(const void *image, size_t size, CUfunction *out) {
+  uint64_t key = 1469598103934665603ull;  // FNV-1a over the image
+  for (size_t i = 0; i < size; ++i) key = (key ^ static_cast<const uint8_t *>(image)[i]) * 1099511628211ull;
+  key ^= size;
+  int dev = 0;
+  if (int rc = check_cuda(cudaGetDevice(&dev), "lc_jit_blockprog: device")) return rc;
+  std::lock_guard<std::mutex> guard(jit_mutex);
+  for (const JitModule &m : jit_modules)
+    if (m.key == key && m.device == dev) {
+      *out = m.function;
+      return LC_OK;
+    }
+  using LoadFn = CUresult (*)(CUmodule *, const void *);
+  using GetFn = CUresult (*)(CUfunction *, CUmodule, const char *);
+  using AttrFn = CUresult (*)(CUfunction, CUfunction_attribute, int);
+  auto load = driver_entry<LoadFn>("cuModuleLoadData");
+  auto get = driver_entry<GetFn>("cuModuleGetFunction");
+  auto attr = driver_entry<AttrFn>("cuFuncSetAttribute");
+  if (!load || !get || !attr) return fail(LC_ERR_CUDA, "lc_jit_blockprog: driver entry points unavailable");
+  cudaFree(nullptr);  // the primary context is current for this thread
+  CUmodule module = nullptr;
+  CUfunction function = nullptr;
+  if (load(&module, image) != CUDA_SUCCESS) return fail(LC_ERR_CUDA, "lc_jit_blockprog: module load failed");
+  if (get(&function, module, "lc_jit_block") != CUDA_SUCCESS)
+    return fail(LC_ERR_CUDA, "lc_jit_blockprog: kernel lc_jit_block not in the module");
+  if (attr(function, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, 200 * 1024) != CUDA_SUCCESS)
+    return fail(LC_ERR_CUDA, "lc_jit_blockprog: shared memory attribute");
+  jit_modules.push_back({key, dev, function});
+  *out = function;
+  return LC_OK;
+}
+}  // namespace
+}  // namespace lc
+
+extern "C" int lc_blockprog(const lc_pw_program *program, const lc_bp_layout *layout, void *const *buffers,
+                            void *stream) {
+  using namespace lc;
   BlockProgArgs args;
-  args.prog = g;
-  args.lay = lay;
-  for (int i = 0; i < LC_PW_MAX_BUFFERS; ++i) args.buffers[i] = i < g.n_buffers ? buffers[i] : nullptr;
-  args.blocks = blocks;
-  const size_t smem_bytes = (size_t)words * 4;
+  size_t smem_bytes = 0;
+  int64_t grid = 0;
+  if (int rc = prepare_blockprog("lc_blockprog", program, layout, buffers, &args, &smem_bytes, &grid)) return rc;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -660,9 +732,34 @@ extern "C" int lc_blockprog(const lc_pw_program *program, const lc_bp_layout *la
       return rc;
     configured[dev] = true;
   }
-  int64_t grid = blocks;
-  const int64_t cap = (int64_t)sm_count() * 8;
-  if (grid > cap) grid = cap;
-  blockprog_kernel<<<(unsigned)grid, (unsigned)lay.threads, smem_bytes, as_stream(stream)>>>(args);
+  blockprog_kernel<<<(unsigned)grid, (unsigned)args.lay.threads, smem_bytes, as_stream(stream)>>>(args);
   return check_launch("lc_blockprog");
+}
+
+extern "C" int lc_jit_blockprog(const void *image, size_t image_size, const lc_pw_program *program,
+                                const lc_bp_layout *layout, void *const *buffers, void *stream) {
+  using namespace lc;
+  if (!image || image_size < 16) return fail(LC_ERR_INVALID, "lc_jit_blockprog: no module image");
+  BlockProgArgs args;
+  size_t smem_bytes = 0;
+  int64_t grid = 0;
+  if (int rc = prepare_blockprog("lc_jit_blockprog", program, layout, buffers, &args, &smem_bytes, &grid))
+    return rc;
+  CUfunction function = nullptr;
+  if (int rc = jit_function(image, image_size, &function)) return rc;
+  using LaunchFn = CUresult (*)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
+                                CUstream, void **, void **);
+  static LaunchFn launch = driver_entry<LaunchFn>("cuLaunchKernel");
+  if (!launch) return fail(LC_ERR_CUDA, "lc_jit_blockprog: cuLaunchKernel unavailable");
+  struct {
+    void *buffers[LC_PW_MAX_BUFFERS];
+    long long blocks;
+  } kargs;
+  for (int i = 0; i < LC_PW_MAX_BUFFERS; ++i) kargs.buffers[i] = args.buffers[i];
+  kargs.blocks = (long long)args.blocks;
+  void *params[] = {&kargs};
+  if (launch(function, (unsigned)grid, 1, 1, (unsigned)args.lay.threads, 1, 1, (unsigned)smem_bytes,
+             reinterpret_cast<CUstream>(stream), params, nullptr) != CUDA_SUCCESS)
+    return fail(LC_ERR_CUDA, "lc_jit_blockprog: launch failed");
+  return LC_OK;
 }

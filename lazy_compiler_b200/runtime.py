@@ -54,6 +54,7 @@ SIGNATURES = {
     "lc_pointwise": [_P, _P, _P],
     "lc_rowprog": [_P, _P, _P, _P],
     "lc_blockprog": [_P, _P, _P, _P],
+    "lc_jit_blockprog": [_P, ctypes.c_size_t, _P, _P, _P, _P],
     "lc_gemm_mixed": [_INT, _INT, _INT, _INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_chain": [_INT, _INT, _INT, _INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P],
     "lc_attention_f32": [_INT, _INT, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
@@ -202,6 +203,23 @@ def call(name: str, *args) -> None:
         raise LcError(name, status, last_error())
 
 
+_PREPARED: dict = {}
+
+
+def _prepared(params: dict, build):
+    """The C structs (and native module image) of a plan's program, built once
+    per program: repeated launches of one plan skip rebuilding them."""
+    key = id(params["program"])
+    entry = _PREPARED.get(key)
+    if entry is None or entry[0] is not params["program"]:
+        entry = (params["program"], build())
+        with _lock:
+            if len(_PREPARED) >= 256:
+                _PREPARED.pop(next(iter(_PREPARED)))
+            _PREPARED[key] = entry
+    return entry[1]
+
+
 def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
     """Launch the kernel a ``compile.py`` plan names.
 
@@ -247,18 +265,28 @@ def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
     elif op == "pointwise":
         prog = p["program"]
         ptrs = (ctypes.c_void_p * PW_MAX_BUFFERS)(*[int(pointers[b[f"buf{i}"]]) for i in range(len(prog["buffers"]))])
-        g = pw_program(prog)
+        g, _, _ = _prepared(p, lambda: (pw_program(prog), None, None))
         call("lc_pointwise", ctypes.c_void_p(ctypes.addressof(g)), ptrs, s)
     elif op == "rowprog":
         prog = p["program"]
         ptrs = (ctypes.c_void_p * PW_MAX_BUFFERS)(*[int(pointers[b[f"buf{i}"]]) for i in range(len(prog["buffers"]))])
-        g, lay = pw_program(prog), rp_layout(p["layout"])
+        g, lay, _ = _prepared(p, lambda: (pw_program(prog), rp_layout(p["layout"]), None))
         call("lc_rowprog", ctypes.c_void_p(ctypes.addressof(g)), ctypes.c_void_p(ctypes.addressof(lay)), ptrs, s)
     elif op == "blockprog":
         prog = p["program"]
         ptrs = (ctypes.c_void_p * PW_MAX_BUFFERS)(*[int(pointers[b[f"buf{i}"]]) for i in range(len(prog["buffers"]))])
-        g, lay = pw_program(prog), bp_layout(p["layout"])
-        call("lc_blockprog", ctypes.c_void_p(ctypes.addressof(g)), ctypes.c_void_p(ctypes.addressof(lay)), ptrs, s)
+
+        def build():
+            from . import jit
+            cubin = jit.block_cubin(prog, p["layout"])
+            image = ctypes.create_string_buffer(cubin, len(cubin)) if cubin is not None else None
+            return pw_program(prog), bp_layout(p["layout"]), image
+        g, lay, image = _prepared(p, build)
+        if image is not None:
+            call("lc_jit_blockprog", ctypes.cast(image, ctypes.c_void_p), len(image.raw),
+                 ctypes.c_void_p(ctypes.addressof(g)), ctypes.c_void_p(ctypes.addressof(lay)), ptrs, s)
+        else:
+            call("lc_blockprog", ctypes.c_void_p(ctypes.addressof(g)), ctypes.c_void_p(ctypes.addressof(lay)), ptrs, s)
     elif op == "gemm_mixed":
         d = plan["dtypes"]
         bias = ptr("bias") if "bias" in b else ctypes.c_void_p(0)
