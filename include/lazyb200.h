@@ -539,6 +539,13 @@ int lc_blockprog(const lc_pw_program *program, const lc_bp_layout *layout, void 
 int lc_jit_blockprog(const void *image, size_t image_size, const lc_pw_program *program,
                      const lc_bp_layout *layout, void *const *buffers, void *stream);
 
+/* A pointwise or serial program run natively: `image` is an sm_100a module
+ * whose kernel lc_jit_point(struct {void *buffers[16]; long long points;})
+ * runs the program for each point, grid-stride; validated as for
+ * lc_pointwise before the launch. */
+int lc_jit_pointwise(const void *image, size_t image_size, const lc_pw_program *program, void *const *buffers,
+                     void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -681,12 +681,13 @@ T driver_entry(const char *symbol) {
   return reinterpret_cast<T>(ptr);
 }
 
-int jit_function(const void *image, size_t size, CUfunction *out) {
+int jit_function(const void *image, size_t size, const char *kernel, CUfunction *out) {
   uint64_t key = 1469598103934665603ull;  // FNV-1a over the image
   for (size_t i = 0; i < size; ++i) key = (key ^ static_cast<const uint8_t *>(image)[i]) * 1099511628211ull;
   key ^= size;
+  for (const char *c = kernel; *c; ++c) key = (key ^ (uint8_t)*c) * 1099511628211ull;
   int dev = 0;
-  if (int rc = check_cuda(cudaGetDevice(&dev), "lc_jit_blockprog: device")) return rc;
+  if (int rc = check_cuda(cudaGetDevice(&dev), "native program: device")) return rc;
   std::lock_guard<std::mutex> guard(jit_mutex);
   for (const JitModule &m : jit_modules)
     if (m.key == key && m.device == dev) {
@@ -704,8 +705,8 @@ int jit_function(const void *image, size_t size, CUfunction *out) {
   CUmodule module = nullptr;
   CUfunction function = nullptr;
   if (load(&module, image) != CUDA_SUCCESS) return fail(LC_ERR_CUDA, "lc_jit_blockprog: module load failed");
-  if (get(&function, module, "lc_jit_block") != CUDA_SUCCESS)
-    return fail(LC_ERR_CUDA, "lc_jit_blockprog: kernel lc_jit_block not in the module");
+  if (get(&function, module, kernel) != CUDA_SUCCESS)
+    return fail(LC_ERR_CUDA, "native program: kernel %s not in the module", kernel);
   if (attr(function, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, 200 * 1024) != CUDA_SUCCESS)
     return fail(LC_ERR_CUDA, "lc_jit_blockprog: shared memory attribute");
   jit_modules.push_back({key, dev, function});
@@ -746,7 +747,7 @@ extern "C" int lc_jit_blockprog(const void *image, size_t image_size, const lc_p
   if (int rc = prepare_blockprog("lc_jit_blockprog", program, layout, buffers, &args, &smem_bytes, &grid))
     return rc;
   CUfunction function = nullptr;
-  if (int rc = jit_function(image, image_size, &function)) return rc;
+  if (int rc = jit_function(image, image_size, "lc_jit_block", &function)) return rc;
   using LaunchFn = CUresult (*)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
                                 CUstream, void **, void **);
   static LaunchFn launch = driver_entry<LaunchFn>("cuLaunchKernel");
@@ -761,5 +762,33 @@ extern "C" int lc_jit_blockprog(const void *image, size_t image_size, const lc_p
   if (launch(function, (unsigned)grid, 1, 1, (unsigned)args.lay.threads, 1, 1, (unsigned)smem_bytes,
              reinterpret_cast<CUstream>(stream), params, nullptr) != CUDA_SUCCESS)
     return fail(LC_ERR_CUDA, "lc_jit_blockprog: launch failed");
+  return LC_OK;
+}
+
+extern "C" int lc_jit_pointwise(const void *image, size_t image_size, const lc_pw_program *program,
+                                void *const *buffers, void *stream) {
+  using namespace lc;
+  if (!image || image_size < 16) return fail(LC_ERR_INVALID, "lc_jit_pointwise: no module image");
+  int64_t points = 0;
+  if (int rc = validate_program("lc_jit_pointwise", program, buffers, kPointwise, &points)) return rc;
+  CUfunction function = nullptr;
+  if (int rc = jit_function(image, image_size, "lc_jit_point", &function)) return rc;
+  using LaunchFn = CUresult (*)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
+                                CUstream, void **, void **);
+  static LaunchFn launch = driver_entry<LaunchFn>("cuLaunchKernel");
+  if (!launch) return fail(LC_ERR_CUDA, "lc_jit_pointwise: cuLaunchKernel unavailable");
+  struct {
+    void *buffers[LC_PW_MAX_BUFFERS];
+    long long points;
+  } kargs;
+  for (int i = 0; i < LC_PW_MAX_BUFFERS; ++i) kargs.buffers[i] = i < program->n_buffers ? buffers[i] : nullptr;
+  kargs.points = (long long)points;
+  int64_t blocks = (points + 255) / 256;
+  const int64_t cap = (int64_t)sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  void *params[] = {&kargs};
+  if (launch(function, (unsigned)blocks, 1, 1, 256, 1, 1, 0, reinterpret_cast<CUstream>(stream), params,
+             nullptr) != CUDA_SUCCESS)
+    return fail(LC_ERR_CUDA, "lc_jit_pointwise: launch failed");
   return LC_OK;
 }

@@ -26,6 +26,7 @@ import threading
 from .pointwise import OPCODES
 
 KERNEL = "lc_jit_block"
+POINT_KERNEL = "lc_jit_point"
 
 _PREAMBLE = r"""
 typedef unsigned int u32;
@@ -105,6 +106,23 @@ def block_source(prog: dict, layout: dict) -> str:
     lines.append("    rest = blk;")
     for d in range(nb - 1, -1, -1):
         lines.append(f"    x{d} = rest % {extents[d]}; rest /= {extents[d]};")
+    lines += _statements(prog, smem)
+    lines.append(f"  L{len(code)}: ;")
+    lines.append("    __syncthreads();")
+    lines.append("  }")
+    lines.append("}")
+    return _PREAMBLE + "\n".join(lines) + "\n"
+
+
+def _statements(prog: dict, smem: list) -> list:
+    """One labelled C statement per operation (raises Untranslatable)."""
+    code = prog["code"]
+    n_axes = len(prog["extents"])
+    loops = [int(e) for e in prog.get("loops", [])]
+    sizes = [int(x) for x in prog["sizes"]]
+    consts = [int(c) & 0xFFFFFFFF for c in prog["consts"]]
+    forms = prog.get("forms", [])
+    lines = []
     for pc, (op, dst, a, b, c, aux) in enumerate(code):
         name = OPCODES[op]
         A, B, C = f"r{a}", f"r{b}", f"r{c}"
@@ -170,11 +188,51 @@ def block_source(prog: dict, layout: dict) -> str:
                 stmt = f"x{d} = (i64)(int){A}; if (x{d} < 0 || x{d} >= {limit}) goto L{other + 1};"
             else:
                 stmt = f"x{d} += ((int){A} < 1 ? 1 : (int){A}); if (x{d} < {limit}) goto L{other + 1};"
+        elif name.startswith(("LD_", "ST_")):
+            fm = forms[aux]
+            at = " + ".join([f"{int(fm['base'])}LL"] + [f"{int(k)}LL * x{d}" for d, k in enumerate(fm["coef"]) if int(k)])
+            ptr = f"p.buffers[{fm['buffer']}]"
+            stmt = {"LD_F32": f"r{dst} = ((const u32 *){ptr})[{at}];",
+                    "LD_S32": f"r{dst} = ((const u32 *){ptr})[{at}];",
+                    "LD_F16": f"r{dst} = w(from_h(((const unsigned short *){ptr})[{at}]));",
+                    "LD_BF16": f"r{dst} = w(from_bf(((const unsigned short *){ptr})[{at}]));",
+                    "ST_F32": f"((u32 *){ptr})[{at}] = {A};", "ST_S32": f"((u32 *){ptr})[{at}] = {A};",
+                    "ST_F16": f"((unsigned short *){ptr})[{at}] = to_h(f({A}));",
+                    "ST_BF16": f"((unsigned short *){ptr})[{at}] = to_bf(f({A}));"}[name]
+        elif name in ("LOOPB", "LOOPE"):
+            d = n_axes + (aux & 15)
+            other = aux >> 4
+            limit = f"min((i64)(int){A}, {loops[aux & 15]}LL)"
+            if name == "LOOPB":
+                stmt = f"x{d} = 0; if ({limit} <= 0) goto L{other + 1};"
+            else:
+                stmt = f"if (++x{d} < {limit}) goto L{other + 1};"
         if stmt is None:
             raise Untranslatable(name)
         lines.append(f"  L{pc}: {stmt}")
-    lines.append(f"  L{len(code)}: ;")
-    lines.append("    __syncthreads();")
+    return lines
+
+
+def point_source(prog: dict) -> str:
+    """CUDA C of a pointwise or serial program: one point per thread, grid-stride
+    (raises Untranslatable; lane programs, whose warps exchange registers,
+    stay with the interpreter)."""
+    if any(OPCODES[c[0]] in ("SHFL_XOR", "MMA_F16", "MMA_BF16", "PACK_F16X2", "PACK_BF16X2") for c in prog["code"]):
+        raise Untranslatable("lane operations")
+    extents = [int(e) for e in prog["extents"]]
+    loops = [int(e) for e in prog.get("loops", [])]
+    n_axes = len(extents)
+    n_regs = max(1, prog["n_regs"])
+    lines = [f"extern \"C\" __global__ void __launch_bounds__(256) {POINT_KERNEL}(const __grid_constant__ JitArgs p) {{"]
+    lines.append("  u32 " + ", ".join(f"r{i} = 0u" for i in range(n_regs)) + ";")
+    lines.append("  i64 " + ", ".join(f"x{d} = 0" for d in range(n_axes + len(loops))) + ";")
+    lines.append("  for (i64 gid = (i64)blockIdx.x * blockDim.x + threadIdx.x; gid < p.blocks;"
+                 " gid += (i64)gridDim.x * blockDim.x) {")
+    lines.append("    i64 rest = gid;")
+    for d in range(n_axes - 1, -1, -1):
+        lines.append(f"    x{d} = rest % {extents[d]}; rest /= {extents[d]};")
+    lines += _statements(prog, [])
+    lines.append(f"  L{len(prog['code'])}: ;")
     lines.append("  }")
     lines.append("}")
     return _PREAMBLE + "\n".join(lines) + "\n"
@@ -217,6 +275,16 @@ def compile_cubin(source: str) -> bytes:
     with _lock:
         _cache[key] = cubin
     return cubin
+
+
+def point_cubin(prog: dict) -> bytes | None:
+    """The compiled native kernel of a pointwise or serial program, or None."""
+    if not enabled():
+        return None
+    try:
+        return compile_cubin(point_source(prog))
+    except (Untranslatable, ImportError):
+        return None
 
 
 def block_cubin(prog: dict, layout: dict) -> bytes | None:

@@ -55,6 +55,7 @@ SIGNATURES = {
     "lc_rowprog": [_P, _P, _P, _P],
     "lc_blockprog": [_P, _P, _P, _P],
     "lc_jit_blockprog": [_P, ctypes.c_size_t, _P, _P, _P, _P],
+    "lc_jit_pointwise": [_P, ctypes.c_size_t, _P, _P, _P],
     "lc_gemm_mixed": [_INT, _INT, _INT, _INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_chain": [_INT, _INT, _INT, _INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P],
     "lc_attention_f32": [_INT, _INT, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
@@ -265,8 +266,18 @@ def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
     elif op == "pointwise":
         prog = p["program"]
         ptrs = (ctypes.c_void_p * PW_MAX_BUFFERS)(*[int(pointers[b[f"buf{i}"]]) for i in range(len(prog["buffers"]))])
-        g, _, _ = _prepared(p, lambda: (pw_program(prog), None, None))
-        call("lc_pointwise", ctypes.c_void_p(ctypes.addressof(g)), ptrs, s)
+
+        def build_point():
+            from . import jit
+            cubin = jit.point_cubin(prog)
+            image = ctypes.create_string_buffer(cubin, len(cubin)) if cubin is not None else None
+            return pw_program(prog), None, image
+        g, _, image = _prepared(p, build_point)
+        if image is not None:
+            call("lc_jit_pointwise", ctypes.cast(image, ctypes.c_void_p), len(image.raw),
+                 ctypes.c_void_p(ctypes.addressof(g)), ptrs, s)
+        else:
+            call("lc_pointwise", ctypes.c_void_p(ctypes.addressof(g)), ptrs, s)
     elif op == "rowprog":
         prog = p["program"]
         ptrs = (ctypes.c_void_p * PW_MAX_BUFFERS)(*[int(pointers[b[f"buf{i}"]]) for i in range(len(prog["buffers"]))])
