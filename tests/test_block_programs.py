@@ -160,3 +160,35 @@ def test_synthetic_block_program_on_gpu(name, tmp_path, cuda_device):
     got = run_package(ir.parent, inputs=arrays)
     for key, value in ref.items():
         np.testing.assert_allclose(np.asarray(got[key]).reshape(value.shape), value, rtol=1e-6, atol=1e-6)
+
+
+def _nvrtc_available():
+    try:
+        from cuda.bindings import nvrtc  # noqa: F401
+        return True
+    except ImportError:
+        return False
+
+
+@pytest.mark.skipif(not _nvrtc_available(), reason="NVRTC is not installed")
+@pytest.mark.parametrize("name", BLOCK_PACKAGES)
+def test_native_translation_compiles(name):
+    """Every golden package's block program, and its serial / pointwise plan,
+    translates to CUDA C that NVRTC compiles for sm_100a (no GPU needed)."""
+    from lazy_compiler_b200 import jit
+    pkg = load_package(golden_ir(name))
+    p = compile_blockprog(pkg, pkg.body[0]).to_json()["params"]
+    cubin = jit.compile_cubin(jit.block_source(p["program"], p["layout"]))
+    assert len(cubin) > 1000
+
+
+@pytest.mark.skipif(not _nvrtc_available(), reason="NVRTC is not installed")
+def test_native_translation_of_serial_and_pointwise_programs(tmp_path):
+    import pw_packages as W
+    from lazy_compiler_b200 import jit
+    from lazy_compiler_b200.compiler import compile_file
+    for name, build in list(W.SERIAL_SYNTHETIC.items()) + list(W.SYNTHETIC.items()):
+        plan = compile_file(build(tmp_path / name))
+        if plan["params"].get("lanes"):
+            continue
+        assert jit.point_cubin(plan["params"]["program"]) is not None, name
