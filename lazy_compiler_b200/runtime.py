@@ -221,6 +221,21 @@ def _prepared(params: dict, build):
     return entry[1]
 
 
+def _launch_point(params: dict, prog: dict, ptrs, s) -> None:
+    """A pointwise or serial program: natively compiled when it can be, else interpreted."""
+    def build():
+        from . import jit
+        cubin = jit.point_cubin(prog)
+        image = ctypes.create_string_buffer(cubin, len(cubin)) if cubin is not None else None
+        return pw_program(prog), None, image
+    g, _, image = _prepared(params, build)
+    if image is not None:
+        call("lc_jit_pointwise", ctypes.cast(image, ctypes.c_void_p), len(image.raw),
+             ctypes.c_void_p(ctypes.addressof(g)), ptrs, s)
+    else:
+        call("lc_pointwise", ctypes.c_void_p(ctypes.addressof(g)), ptrs, s)
+
+
 def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
     """Launch the kernel a ``compile.py`` plan names.
 
@@ -266,18 +281,7 @@ def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
     elif op == "pointwise":
         prog = p["program"]
         ptrs = (ctypes.c_void_p * PW_MAX_BUFFERS)(*[int(pointers[b[f"buf{i}"]]) for i in range(len(prog["buffers"]))])
-
-        def build_point():
-            from . import jit
-            cubin = jit.point_cubin(prog)
-            image = ctypes.create_string_buffer(cubin, len(cubin)) if cubin is not None else None
-            return pw_program(prog), None, image
-        g, _, image = _prepared(p, build_point)
-        if image is not None:
-            call("lc_jit_pointwise", ctypes.cast(image, ctypes.c_void_p), len(image.raw),
-                 ctypes.c_void_p(ctypes.addressof(g)), ptrs, s)
-        else:
-            call("lc_pointwise", ctypes.c_void_p(ctypes.addressof(g)), ptrs, s)
+        _launch_point(p, prog, ptrs, s)
     elif op == "rowprog":
         prog = p["program"]
         ptrs = (ctypes.c_void_p * PW_MAX_BUFFERS)(*[int(pointers[b[f"buf{i}"]]) for i in range(len(prog["buffers"]))])
@@ -328,5 +332,4 @@ def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
         prog = post["program"]
         ptrs = (ctypes.c_void_p * PW_MAX_BUFFERS)(*[int(pointers[post["bind"][f"buf{i}"]])
                                                      for i in range(len(prog["buffers"]))])
-        g = pw_program(prog)
-        call("lc_pointwise", ctypes.c_void_p(ctypes.addressof(g)), ptrs, s)
+        _launch_point(post, prog, ptrs, s)
