@@ -283,8 +283,8 @@ def point_cubin(prog: dict) -> bytes | None:
         return None
     try:
         return compile_cubin(point_source(prog))
-    except (Untranslatable, ImportError):
-        return None
+    except (Untranslatable, ImportError, RuntimeError):
+        return None      # the interpreter runs it
 
 
 def block_cubin(prog: dict, layout: dict) -> bytes | None:
@@ -293,5 +293,5 @@ def block_cubin(prog: dict, layout: dict) -> bytes | None:
         return None
     try:
         return compile_cubin(block_source(prog, layout))
-    except (Untranslatable, ImportError):
-        return None
+    except (Untranslatable, ImportError, RuntimeError):
+        return None      # the interpreter runs it
