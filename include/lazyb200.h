@@ -546,6 +546,13 @@ int lc_jit_blockprog(const void *image, size_t image_size, const lc_pw_program *
 int lc_jit_pointwise(const void *image, size_t image_size, const lc_pw_program *program, void *const *buffers,
                      void *stream);
 
+/* A row program run natively: `image` is an sm_100a module whose kernel
+ * lc_jit_rows(struct {void *buffers[16]; long long rows;}) runs the passes,
+ * butterflies, halving trees and final operations as lc_rowprog does, one
+ * CTA of layout->threads per row; validated as for lc_rowprog. */
+int lc_jit_rowprog(const void *image, size_t image_size, const lc_pw_program *program,
+                   const lc_rp_layout *layout, void *const *buffers, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -587,42 +587,55 @@ extern "C" int lc_pointwise(const lc_pw_program *program, void *const *buffers, 
   return check_launch("lc_pointwise");
 }
 
-extern "C" int lc_rowprog(const lc_pw_program *program, const lc_rp_layout *layout, void *const *buffers,
-                          void *stream) {
-  using namespace lc;
+namespace lc {
+namespace {
+// Validates a row program and its layout; returns the row count.
+int prepare_rowprog(const char *name, const lc_pw_program *program, const lc_rp_layout *layout,
+                    void *const *buffers, int64_t *rows_out) {
   int64_t points = 0;
-  if (int rc = validate_program("lc_rowprog", program, buffers, kRowProgram, &points)) return rc;
-  if (!layout) return fail(LC_ERR_INVALID, "lc_rowprog: null layout");
+  if (int rc = validate_program(name, program, buffers, kRowProgram, &points)) return rc;
+  if (!layout) return fail(LC_ERR_INVALID, "%s: null layout", name);
   const lc_rp_layout &lay = *layout;
   const int n_code = program->n_code;
   if (lay.n_passes < 0 || lay.n_passes > LC_RP_MAX_PASSES || lay.n_states < 0 || lay.n_states > LC_RP_MAX_STATES)
-    return fail(LC_ERR_INVALID, "lc_rowprog: layout counts out of range");
+    return fail(LC_ERR_INVALID, "%s: layout counts out of range", name);
   auto range_ok = [&](int b, int e) { return 0 <= b && b <= e && e <= n_code; };
   for (int i = 0; i < lay.n_passes; ++i)
     if (!range_ok(lay.begin[i], lay.end[i]) || !range_ok(lay.warp_begin[i], lay.warp_end[i]) ||
         !range_ok(lay.tree_begin[i], lay.tree_end[i]))
-      return fail(LC_ERR_INVALID, "lc_rowprog: pass %d range", i);
-  if (!range_ok(lay.final_begin, lay.final_end)) return fail(LC_ERR_INVALID, "lc_rowprog: final range");
+      return fail(LC_ERR_INVALID, "%s: pass %d range", name, i);
+  if (!range_ok(lay.final_begin, lay.final_end)) return fail(LC_ERR_INVALID, "%s: final range", name);
   for (int k = 0; k < lay.n_states; ++k)
     if (lay.state_pass[k] < 0 || lay.state_pass[k] >= lay.n_passes)
-      return fail(LC_ERR_INVALID, "lc_rowprog: state %d", k);
+      return fail(LC_ERR_INVALID, "%s: state %d", name, k);
   if (lay.threads < 32 || lay.threads > 1024 || lay.threads % 32 || ((lay.threads / 32) & (lay.threads / 32 - 1)))
-    return fail(LC_ERR_INVALID, "lc_rowprog: %d threads is not 32 times a power of two up to 1024", lay.threads);
+    return fail(LC_ERR_INVALID, "%s: %d threads is not 32 times a power of two up to 1024", name, lay.threads);
   for (int pc = 0; pc < n_code; ++pc) {
     const int op = program->code[pc][0] & 255, aux = (int)(program->code[pc][1] >> 8);
     if ((op == LC_PW_STATE || op == LC_PW_PARTIAL || op == LC_PW_PARTNER || op == LC_PW_SETP) && aux >= lay.n_states)
-      return fail(LC_ERR_INVALID, "lc_rowprog: state index out of range at %d", pc);
+      return fail(LC_ERR_INVALID, "%s: state index out of range at %d", name, pc);
   }
-  RowProgArgs args;
-  args.prog = *program;
-  args.lay = lay;
-  for (int i = 0; i < LC_PW_MAX_BUFFERS; ++i) args.buffers[i] = i < program->n_buffers ? buffers[i] : nullptr;
   int64_t rows = 1;
   for (int d = 0; d + 1 < program->n_axes; ++d) rows *= program->extents[d];
+  *rows_out = rows;
+  return LC_OK;
+}
+}  // namespace
+}  // namespace lc
+
+extern "C" int lc_rowprog(const lc_pw_program *program, const lc_rp_layout *layout, void *const *buffers,
+                          void *stream) {
+  using namespace lc;
+  int64_t rows = 0;
+  if (int rc = prepare_rowprog("lc_rowprog", program, layout, buffers, &rows)) return rc;
+  RowProgArgs args;
+  args.prog = *program;
+  args.lay = *layout;
+  for (int i = 0; i < LC_PW_MAX_BUFFERS; ++i) args.buffers[i] = i < program->n_buffers ? buffers[i] : nullptr;
   int64_t blocks = rows;
   const int64_t cap = (int64_t)sm_count() * 8;
   if (blocks > cap) blocks = cap;
-  rowprog_kernel<<<(unsigned)blocks, (unsigned)lay.threads, 0, as_stream(stream)>>>(args);
+  rowprog_kernel<<<(unsigned)blocks, (unsigned)layout->threads, 0, as_stream(stream)>>>(args);
   return check_launch("lc_rowprog");
 }
 
@@ -790,5 +803,33 @@ extern "C" int lc_jit_pointwise(const void *image, size_t image_size, const lc_p
   if (launch(function, (unsigned)blocks, 1, 1, 256, 1, 1, 0, reinterpret_cast<CUstream>(stream), params,
              nullptr) != CUDA_SUCCESS)
     return fail(LC_ERR_CUDA, "lc_jit_pointwise: launch failed");
+  return LC_OK;
+}
+
+extern "C" int lc_jit_rowprog(const void *image, size_t image_size, const lc_pw_program *program,
+                              const lc_rp_layout *layout, void *const *buffers, void *stream) {
+  using namespace lc;
+  if (!image || image_size < 16) return fail(LC_ERR_INVALID, "lc_jit_rowprog: no module image");
+  int64_t rows = 0;
+  if (int rc = prepare_rowprog("lc_jit_rowprog", program, layout, buffers, &rows)) return rc;
+  CUfunction function = nullptr;
+  if (int rc = jit_function(image, image_size, "lc_jit_rows", &function)) return rc;
+  using LaunchFn = CUresult (*)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
+                                CUstream, void **, void **);
+  static LaunchFn launch = driver_entry<LaunchFn>("cuLaunchKernel");
+  if (!launch) return fail(LC_ERR_CUDA, "lc_jit_rowprog: cuLaunchKernel unavailable");
+  struct {
+    void *buffers[LC_PW_MAX_BUFFERS];
+    long long rows;
+  } kargs;
+  for (int i = 0; i < LC_PW_MAX_BUFFERS; ++i) kargs.buffers[i] = i < program->n_buffers ? buffers[i] : nullptr;
+  kargs.rows = (long long)rows;
+  int64_t blocks = rows;
+  const int64_t cap = (int64_t)sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  void *params[] = {&kargs};
+  if (launch(function, (unsigned)blocks, 1, 1, (unsigned)layout->threads, 1, 1, 0,
+             reinterpret_cast<CUstream>(stream), params, nullptr) != CUDA_SUCCESS)
+    return fail(LC_ERR_CUDA, "lc_jit_rowprog: launch failed");
   return LC_OK;
 }

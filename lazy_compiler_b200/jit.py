@@ -27,6 +27,7 @@ from .pointwise import OPCODES
 
 KERNEL = "lc_jit_block"
 POINT_KERNEL = "lc_jit_point"
+ROWS_KERNEL = "lc_jit_rows"
 
 _PREAMBLE = r"""
 typedef unsigned int u32;
@@ -114,8 +115,8 @@ def block_source(prog: dict, layout: dict) -> str:
     return _PREAMBLE + "\n".join(lines) + "\n"
 
 
-def _statements(prog: dict, smem: list) -> list:
-    """One labelled C statement per operation (raises Untranslatable)."""
+def _statements(prog: dict, smem: list, begin: int = 0, end: int | None = None) -> list:
+    """One labelled C statement per operation of [begin, end) (raises Untranslatable)."""
     code = prog["code"]
     n_axes = len(prog["extents"])
     loops = [int(e) for e in prog.get("loops", [])]
@@ -123,7 +124,8 @@ def _statements(prog: dict, smem: list) -> list:
     consts = [int(c) & 0xFFFFFFFF for c in prog["consts"]]
     forms = prog.get("forms", [])
     lines = []
-    for pc, (op, dst, a, b, c, aux) in enumerate(code):
+    for pc in range(begin, len(code) if end is None else end):
+        op, dst, a, b, c, aux = code[pc]
         name = OPCODES[op]
         A, B, C = f"r{a}", f"r{b}", f"r{c}"
 
@@ -199,6 +201,14 @@ def _statements(prog: dict, smem: list) -> list:
                     "ST_F32": f"((u32 *){ptr})[{at}] = {A};", "ST_S32": f"((u32 *){ptr})[{at}] = {A};",
                     "ST_F16": f"((unsigned short *){ptr})[{at}] = to_h(f({A}));",
                     "ST_BF16": f"((unsigned short *){ptr})[{at}] = to_bf(f({A}));"}[name]
+        elif name == "STATE":
+            stmt = f"r{dst} = w(st{aux});"
+        elif name == "PARTIAL":
+            stmt = f"r{dst} = w(pa{aux});"
+        elif name == "PARTNER":
+            stmt = f"r{dst} = w(pn{aux});"
+        elif name == "SETP":
+            stmt = f"pa{aux} = f({A});"
         elif name in ("LOOPB", "LOOPE"):
             d = n_axes + (aux & 15)
             other = aux >> 4
@@ -211,6 +221,69 @@ def _statements(prog: dict, smem: list) -> list:
             raise Untranslatable(name)
         lines.append(f"  L{pc}: {stmt}")
     return lines
+
+
+def rows_source(prog: dict, layout: dict) -> str:
+    """CUDA C of a row program: one CTA of the Tile's threads per row, the
+    passes, the lane butterfly, the halving tree and the final operations
+    as the interpreter's rowprog kernel runs them (raises Untranslatable)."""
+    extents = [int(e) for e in prog["extents"]]
+    R = len(extents) - 1
+    cols = extents[R]
+    n_regs = max(1, prog["n_regs"])
+    n_states = len(layout["state_pass"])
+    ns = max(1, n_states)
+    threads = int(layout["threads"])
+    L = [f"extern \"C\" __global__ void __launch_bounds__({threads}) {ROWS_KERNEL}(const __grid_constant__ JitArgs p) {{",
+         f"  __shared__ float warp_part[32][{ns}];",
+         f"  __shared__ float combined[{ns}];",
+         "  u32 " + ", ".join(f"r{i} = 0u" for i in range(n_regs)) + ";",
+         "  i64 " + ", ".join(f"x{d} = 0" for d in range(R + 1)) + ";",
+         "  float " + ", ".join(f"st{k} = 0.0f, pa{k} = 0.0f, pn{k} = 0.0f" for k in range(ns)) + ";",
+         "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;",
+         "  for (i64 row = blockIdx.x; row < p.blocks; row += gridDim.x) {",
+         "    i64 rest = row;"]
+    for d in range(R - 1, -1, -1):
+        L.append(f"    x{d} = rest % {extents[d]}; rest /= {extents[d]};")
+    for pss, (b, e) in enumerate(layout["passes"]):
+        slots = [k for k, ps in enumerate(layout["state_pass"]) if ps == pss]
+        for k in slots:
+            L.append(f"    pa{k} = __uint_as_float({int(layout['state_init'][k]) & 0xFFFFFFFF}u);")
+        L.append(f"    for (i64 c = threadIdx.x; c < {cols}; c += blockDim.x) {{")
+        L.append(f"      x{R} = c;")
+        L += ["    " + t for t in _statements(prog, [], b, e)]
+        L.append(f"    }}")
+        L.append(f"    x{R} = 0;")
+        if not slots:
+            continue
+        wb, we = layout["warp"][pss]
+        tb, te = layout["tree"][pss]
+        L.append("    for (int o = 16; o > 0; o >>= 1) {")
+        for k in slots:
+            L.append(f"      pn{k} = __shfl_xor_sync(0xffffffffu, pa{k}, o);")
+        L += ["    " + t for t in _statements(prog, [], wb, we)]
+        L.append("    }")
+        L.append("    if (lane == 0) { " + " ".join(f"warp_part[warp][{k}] = pa{k};" for k in slots) + " }")
+        L.append("    __syncthreads();")
+        L.append("    if (threadIdx.x == 0) {")
+        L.append("      for (int d = nwarps >> 1; d > 0; d >>= 1)")
+        L.append("        for (int i = 0; i < d; ++i) {")
+        L.append("          " + " ".join(f"pa{k} = warp_part[i][{k}]; pn{k} = warp_part[i + d][{k}];" for k in slots))
+        L += ["      " + t for t in _statements(prog, [], tb, te)]
+        L.append("          " + " ".join(f"warp_part[i][{k}] = pa{k};" for k in slots))
+        L.append("        }")
+        L.append("      " + " ".join(f"combined[{k}] = warp_part[0][{k}];" for k in slots))
+        L.append("    }")
+        L.append("    __syncthreads();")
+        L.append("    " + " ".join(f"st{k} = combined[{k}];" for k in slots))
+        L.append("    __syncthreads();")
+    fb, fe = layout["final"]
+    L.append("    if (threadIdx.x == 0) {")
+    L += ["    " + t for t in _statements(prog, [], fb, fe)]
+    L.append("    }")
+    L.append("  }")
+    L.append("}")
+    return _PREAMBLE + "\n".join(L) + "\n"
 
 
 def point_source(prog: dict) -> str:
@@ -283,6 +356,16 @@ def point_cubin(prog: dict) -> bytes | None:
         return None
     try:
         return compile_cubin(point_source(prog))
+    except (Untranslatable, ImportError, RuntimeError):
+        return None      # the interpreter runs it
+
+
+def rows_cubin(prog: dict, layout: dict) -> bytes | None:
+    """The compiled native kernel of a row program, or None (interpreter)."""
+    if not enabled():
+        return None
+    try:
+        return compile_cubin(rows_source(prog, layout))
     except (Untranslatable, ImportError, RuntimeError):
         return None      # the interpreter runs it
 

@@ -56,6 +56,7 @@ SIGNATURES = {
     "lc_blockprog": [_P, _P, _P, _P],
     "lc_jit_blockprog": [_P, ctypes.c_size_t, _P, _P, _P, _P],
     "lc_jit_pointwise": [_P, ctypes.c_size_t, _P, _P, _P],
+    "lc_jit_rowprog": [_P, ctypes.c_size_t, _P, _P, _P, _P],
     "lc_gemm_mixed": [_INT, _INT, _INT, _INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_chain": [_INT, _INT, _INT, _INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P],
     "lc_attention_f32": [_INT, _INT, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
@@ -285,8 +286,18 @@ def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
     elif op == "rowprog":
         prog = p["program"]
         ptrs = (ctypes.c_void_p * PW_MAX_BUFFERS)(*[int(pointers[b[f"buf{i}"]]) for i in range(len(prog["buffers"]))])
-        g, lay, _ = _prepared(p, lambda: (pw_program(prog), rp_layout(p["layout"]), None))
-        call("lc_rowprog", ctypes.c_void_p(ctypes.addressof(g)), ctypes.c_void_p(ctypes.addressof(lay)), ptrs, s)
+
+        def build_rows():
+            from . import jit
+            cubin = jit.rows_cubin(prog, p["layout"])
+            image = ctypes.create_string_buffer(cubin, len(cubin)) if cubin is not None else None
+            return pw_program(prog), rp_layout(p["layout"]), image
+        g, lay, image = _prepared(p, build_rows)
+        if image is not None:
+            call("lc_jit_rowprog", ctypes.cast(image, ctypes.c_void_p), len(image.raw),
+                 ctypes.c_void_p(ctypes.addressof(g)), ctypes.c_void_p(ctypes.addressof(lay)), ptrs, s)
+        else:
+            call("lc_rowprog", ctypes.c_void_p(ctypes.addressof(g)), ctypes.c_void_p(ctypes.addressof(lay)), ptrs, s)
     elif op == "blockprog":
         prog = p["program"]
         ptrs = (ctypes.c_void_p * PW_MAX_BUFFERS)(*[int(pointers[b[f"buf{i}"]]) for i in range(len(prog["buffers"]))])

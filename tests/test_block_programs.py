@@ -192,3 +192,22 @@ def test_native_translation_of_serial_and_pointwise_programs(tmp_path):
         if plan["params"].get("lanes"):
             continue
         assert jit.point_cubin(plan["params"]["program"]) is not None, name
+
+
+@pytest.mark.skipif(not _nvrtc_available(), reason="NVRTC is not installed")
+@pytest.mark.parametrize("name", ["r04_row_sum", "f01_rmsnorm", "f02_row_softmax", "f03_l2norm",
+                                  "phase9_gelu_row_dot"])
+def test_native_translation_of_row_programs(name):
+    from lazy_compiler_b200 import jit
+    from lazy_compiler_b200.ir import static_extent
+    from lazy_compiler_b200.recognize import _Eval
+    from lazy_compiler_b200.rowprog import compile_rowprog
+    pkg = load_package(golden_ir(name))
+    tile = pkg.body[0]
+    ev = _Eval(pkg)
+    ev.smem = set()
+    for axis in tile.axes:
+        ev.axes[axis.name] = static_extent(axis.extent)
+    ev.run(tile.body)
+    p = compile_rowprog(pkg, tile, ev).to_json()["params"]
+    assert jit.rows_cubin(p["program"], p["layout"]) is not None
