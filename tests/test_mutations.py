@@ -164,3 +164,65 @@ def test_mutated_package_on_gpu(name, seed, tmp_path, cuda_device):
             ok = np.isclose(out, want, rtol=2e-3, atol=2e-4 * max(scale, 1.0), equal_nan=True) | \
                 (np.isinf(out) & np.isinf(want) & (np.sign(out) == np.sign(want)))
             assert ok.all(), (name, changes, key, np.argwhere(~ok)[:3], out[~ok][:3], want[~ok][:3])
+
+
+# ---------------------------------------------------------------- shapes
+# The row packages at other (odd) shapes: the row and column axes of the
+# Tile and its loops rescaled, the buffers' shapes and the column count
+# constant with them, as a schedule for another size would have them.
+ROW_AXES = {"r04_row_sum": ({"a0": "rows", "a1": "cols"}, {"x": ("rows", "cols"), "sum_1": ("rows",)}),
+            "f01_rmsnorm": ({"a0": "rows", "a1": "cols", "a2": "cols"},
+                            {"x": ("rows", "cols"), "w": ("cols",), "mul_1": ("rows", "cols")}),
+            "f02_row_softmax": ({"a0": "rows", "a1": "cols", "a3": "cols"},
+                                {"x": ("rows", "cols"), "softmax": ("rows", "cols")}),
+            "f03_l2norm": ({"a0": "rows", "a1": "cols", "a2": "cols"}, {"x": ("rows", "cols"), "div": ("rows", "cols")})}
+SHAPES = [(37, 300), (5, 1000), (64, 129)]
+
+
+@pytest.mark.parametrize("name", sorted(ROW_AXES))
+@pytest.mark.parametrize("rows,cols", SHAPES)
+def test_row_package_at_other_shapes(name, rows, cols, tmp_path):
+    from oracle.rescale import rescale_body
+    size = {"rows": rows, "cols": cols}
+    axes, shapes = ROW_AXES[name]
+    folder = tmp_path / name
+    shutil.copytree(golden(name), folder)
+    ir = next(folder.glob("*.ir.json"))
+    graph = json.loads(ir.read_text())
+    for node in graph["nodes"].values():
+        if node["op"] == "KernelOp":
+            node["op_fields"]["body"] = [rescale_body(b, {a: size[v] for a, v in axes.items()})
+                                         for b in node["op_fields"]["body"]]
+        for out in node.get("outputs", []):
+            if out["name"] in shapes:
+                out["shape"] = [size[v] for v in shapes[out["name"]]]
+    ir.write_text(json.dumps(graph))
+    meta = json.loads((folder / "meta.json").read_text())
+    for arg in meta["kernels"][0]["args"]:
+        if arg["name"] in shapes:
+            arg["shape"] = [size[v] for v in shapes[arg["name"]]]
+        if arg["name"] == "mean_count":
+            arg["data"] = [float(cols)]
+    meta["kernels"][0]["grid"] = [rows, 1, 1]
+    (folder / "meta.json").write_text(json.dumps(meta))
+    plan = compile_file(ir)
+    arrays = {a["name"]: O.input_array(a, 1) for a in meta["kernels"][0]["args"] if not a.get("output")}
+    ref = ir_oracle(ir, arrays)
+    got = run_plan_cpu(plan, arrays, ir)
+    for key, value in ref.items():
+        assert not np.isnan(value).any()
+        np.testing.assert_allclose(np.asarray(got[key], np.float64).reshape(value.shape), value,
+                                   rtol=2e-4, atol=2e-5, err_msg=f"{name} {rows}x{cols} {plan['op']}")
+    return folder, ir, arrays, ref
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", sorted(ROW_AXES))
+@pytest.mark.parametrize("rows,cols", SHAPES)
+def test_row_package_at_other_shapes_on_gpu(name, rows, cols, tmp_path, cuda_device):
+    from lazy_compiler_b200.runner import run_package
+    folder, ir, arrays, ref = test_row_package_at_other_shapes(name, rows, cols, tmp_path)
+    got = run_package(folder, inputs=arrays)
+    for key, value in ref.items():
+        np.testing.assert_allclose(np.asarray(got[key], np.float64).reshape(value.shape), value,
+                                   rtol=1e-3, atol=1e-4, err_msg=f"{name} {rows}x{cols}")
