@@ -179,9 +179,8 @@ ROW_AXES = {"r04_row_sum": ({"a0": "rows", "a1": "cols"}, {"x": ("rows", "cols")
 SHAPES = [(37, 300), (5, 1000), (64, 129)]
 
 
-@pytest.mark.parametrize("name", sorted(ROW_AXES))
-@pytest.mark.parametrize("rows,cols", SHAPES)
-def test_row_package_at_other_shapes(name, rows, cols, tmp_path):
+def reshaped_case(name, rows, cols, tmp_path):
+    """The package at rows x cols, checked on the CPU; returns it for the device."""
     from oracle.rescale import rescale_body
     size = {"rows": rows, "cols": cols}
     axes, shapes = ROW_AXES[name]
@@ -216,12 +215,18 @@ def test_row_package_at_other_shapes(name, rows, cols, tmp_path):
     return folder, ir, arrays, ref
 
 
+@pytest.mark.parametrize("name", sorted(ROW_AXES))
+@pytest.mark.parametrize("rows,cols", SHAPES)
+def test_row_package_at_other_shapes(name, rows, cols, tmp_path):
+    reshaped_case(name, rows, cols, tmp_path)
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("name", sorted(ROW_AXES))
 @pytest.mark.parametrize("rows,cols", SHAPES)
 def test_row_package_at_other_shapes_on_gpu(name, rows, cols, tmp_path, cuda_device):
     from lazy_compiler_b200.runner import run_package
-    folder, ir, arrays, ref = test_row_package_at_other_shapes(name, rows, cols, tmp_path)
+    folder, ir, arrays, ref = reshaped_case(name, rows, cols, tmp_path)
     got = run_package(folder, inputs=arrays)
     for key, value in ref.items():
         np.testing.assert_allclose(np.asarray(got[key], np.float64).reshape(value.shape), value,
