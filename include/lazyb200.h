@@ -132,14 +132,27 @@ int lc_sum_finalize(const double *total, const float *count, float *out, void *s
  * the GPU's memory at start-up), and launch paths that must not pay
  * cudaMalloc's implicit device-wide synchronisation.  No counterpart in the
  * reference; it is the same kernel as lc_sum_f32 with its per-CTA partials in
- * a fixed device array of LC_SUM_NOALLOC_SCRATCH_BYTES inside the library
- * (held on every GPU that loads the library until the process exits).
- *  - n may be at most LC_SUM_NOALLOC_MAX_N; larger n returns LC_ERR_UNSUPPORTED.
+ * a fixed device array of LC_SUM_NOALLOC_SCRATCH_BYTES inside the library,
+ * resident on every device where the library's kernels have been loaded,
+ * until the process exits.
+ *  - The array bounds the number of CTAs, not n: the grid is clamped to
+ *    LC_SUM_NOALLOC_MAX_BLOCKS partials and the kernel strides over any n.
+ *    n is capped at LC_SUM_NOALLOC_MAX_N (2^32 elements, 16 GiB of f32) as a
+ *    documented contract of this entry point; larger n returns
+ *    LC_ERR_UNSUPPORTED (use lc_sum_f32).
  *  - The first call on a device looks up the array's device address
- *    (cudaGetSymbolAddress) with that device current; make that first call
- *    before any stream capture.
- *  - All calls share the array: calls that overlap on the GPU (other streams,
- *    other threads) race and must be serialised by the caller. */
+ *    (cudaGetSymbolAddress, with that device current).  Under CUDA's lazy
+ *    module loading that lookup is also what loads the library's module on
+ *    the device, which is not allowed during stream capture, so make the
+ *    first call on each device before any stream capture.
+ *  - The address is cached per device index for the life of the process:
+ *    the library must not outlive a device reset (cudaDeviceReset or any
+ *    other teardown of the primary context).  lc_sum_f32's per-stream
+ *    workspace has the same rule.
+ *  - All calls share the array, and it keeps the last call's contents (the
+ *    CTA counter is cleared on the stream before every launch): calls that
+ *    overlap on the GPU (other streams, other threads) race and must be
+ *    serialised by the caller. */
 #define LC_SUM_NOALLOC_MAX_BLOCKS 1024
 #define LC_SUM_NOALLOC_MAX_N (((int64_t)1) << 32)
 #define LC_SUM_NOALLOC_SCRATCH_BYTES (LC_SUM_NOALLOC_MAX_BLOCKS * 8 + 256)
@@ -274,13 +287,6 @@ int lc_sdpa_f16(const void *q, const void *k, const void *v, void *o, int64_t bh
 int lc_sdpa_path(const void *q, const void *k, const void *v, const void *o, int64_t s_q,
                  int64_t s_kv, int64_t d);
 
-/* Diagnostic: one CTA per SM issues `groups` groups of 8 back-to-back
- * tcgen05.mma (M128 N128 K16) of form `variant` (0 A and B from shared
- * memory, B K-major; 1 A from tensor memory, B MN-major; 2 shared memory with
- * B MN-major; 3 and 4 alternate form 0 with form 1 or 2 every 2 groups; 5-9
- * vary the accumulator reuse, see probe_mma.cu) on zeroed operands.  Timing it measures the tensor pipe's rate for each form
- * and the cost of switching forms.  No reference counterpart. */
-int lc_probe_mma(int variant, int groups, void *stream);
 
 
 /* ---------------------------------------------------------------- pointwise programs

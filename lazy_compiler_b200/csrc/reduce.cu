@@ -135,9 +135,10 @@ int launch_sum(const char *name, const float *x, int64_t n, int mode, const floa
 // reserves the GPU's memory at start-up), and launch paths that must not pay
 // cudaMalloc's implicit device-wide synchronisation.  lc_sum_f32_noalloc runs
 // the same kernel with its scratch in this fixed-size device array instead.
-// Every GPU that loads the library holds the array (LC_SUM_NOALLOC_SCRATCH_BYTES)
-// until the process exits; all calls share it, so calls that overlap on the
-// GPU (different streams, or other threads) race on it.
+// Every device on which the library's module has been loaded holds the array
+// (LC_SUM_NOALLOC_SCRATCH_BYTES) until the process exits; all calls share it,
+// so calls that overlap on the GPU (different streams, or other threads) race
+// on it.  The array bounds the number of CTAs (one f64 partial each), not n.
 namespace {
 static __device__ __align__(256) unsigned char
     g_sum_noalloc_scratch[LC_SUM_NOALLOC_MAX_BLOCKS * sizeof(double) + 256];
@@ -147,7 +148,10 @@ unsigned char *g_noalloc_address[64] = {nullptr};
 
 // Device address of g_sum_noalloc_scratch on the current device.  Host code
 // only sees a host-side stand-in under that name, so the address is looked up
-// once per device (with that device current) and cached.
+// once per device (with that device current) and cached for the life of the
+// process; a device reset would invalidate it, and the library must not
+// outlive one.  The lookup also loads the module on the device under lazy
+// loading, so the first call per device must precede any stream capture.
 int noalloc_scratch(unsigned char **out) {
   int dev = 0;
   if (int rc = lc::check_cuda(cudaGetDevice(&dev), "lc_sum_f32_noalloc: cudaGetDevice")) return rc;
@@ -185,10 +189,8 @@ extern "C" int lc_sum_f32_noalloc(const float *x, float *out, int64_t n, void *s
   int64_t blocks = (n + per_block - 1) / per_block;
   const int64_t cap = (int64_t)sm_count() * kBlocksPerSm;
   if (blocks > cap) blocks = cap;
-  if (blocks > LC_SUM_NOALLOC_MAX_BLOCKS)
-    return fail(LC_ERR_UNSUPPORTED,
-                "lc_sum_f32_noalloc: this device needs %lld partials, the scratch holds %d",
-                (long long)blocks, LC_SUM_NOALLOC_MAX_BLOCKS);
+  // grid-stride and int64-indexed: a grid clamped to the array's partials covers any n
+  if (blocks > LC_SUM_NOALLOC_MAX_BLOCKS) blocks = LC_SUM_NOALLOC_MAX_BLOCKS;
   if (blocks < 1) blocks = 1;
   // the CTA ticket counter must start at zero; the array keeps the last call's contents
   if (int rc = check_cuda(cudaMemsetAsync(counter, 0, sizeof(unsigned int), s),

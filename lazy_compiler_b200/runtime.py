@@ -63,7 +63,6 @@ SIGNATURES = {
     "lc_attention_tile_f16q": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
     "lc_device_status": [_P],
     "lc_selftest_bounded_wait": [_I64, _P],
-    "lc_probe_mma": [_INT, _INT, _P],
     "lc_sdpa_f16": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, ctypes.c_float, _P],
     "lc_sdpa_path": [_P, _P, _P, _P, _I64, _I64, _I64],
 }

@@ -1,24 +1,81 @@
 """Runs one kernel of the library on a chosen size, for profiling and timing.
 
-    python -m lazy_compiler_b200.profile_case OP [--n N] [--rows R --cols C]
+    python profile_case.py OP [--n N] [--rows R --cols C]
            [--m M --n N --k K] [--bh B --seq S] [--warmup W] [--repeat R]
 
 OP is one of add, axpb, relumul, gelu_erf, gelu_tanh, sum, mean, rowsum,
 rmsnorm, softmax, l2norm, gemm_f16, gemm_bf16, gemm_f32, attention_f32, sdpa,
-or mma_probe (``--variant V --groups G``: the tcgen05 issue-pattern probe,
-reported per MMA).  Inputs are seeded
-device tensors; every launch goes through the C ABI.  The mean CUDA-event
-time of the repeated launches is printed (``--repeat`` launches after
-``--warmup``), so the same command line serves an ncu capture (``-k`` the
-kernel, ``-s`` the warm-up launches, ``-c`` one to three launches).
+or general_paths (each golden package's fixed-class plan against the same
+package run as a block program, natively compiled and interpreted; host call
+included).  Inputs are seeded device tensors; every launch goes through the
+C ABI.  The mean CUDA-event time of the repeated launches is printed
+(``--repeat`` launches after ``--warmup``), so the same command line serves
+an ncu capture (``-k`` the kernel, ``-s`` the warm-up launches, ``-c`` one to
+three launches).
 """
 from __future__ import annotations
 
 import argparse
 import ctypes
 import json
+import os
+import sys
+from pathlib import Path
 
-from . import runtime
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from lazy_compiler_b200 import runtime  # noqa: E402
+
+GENERAL_PACKAGES = ["r01_array_sum", "r04_row_sum", "f01_rmsnorm", "f02_row_softmax", "phase9_gelu_attention",
+                    "a02_attention_128", "m02_matmul_rect", "m01_matmul_512"]
+
+
+def general_paths(repeat: int) -> None:
+    """Fixed-class plan vs the block program (native and interpreted) per golden package."""
+    import torch
+
+    from lazy_compiler_b200.blockprog import compile_blockprog
+    from lazy_compiler_b200.compiler import compile_file
+    from lazy_compiler_b200.ir import load_package
+    from lazy_compiler_b200.runner import _torch_dtype, seeded_input
+
+    golden = ROOT / "tests" / "golden" / "packages"
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def time_plan(plan, ptrs, n):
+        for _ in range(3):
+            runtime.launch(plan, ptrs, stream)
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(n):
+            runtime.launch(plan, ptrs, stream)
+        end.record()
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) / n * 1000
+
+    for name in GENERAL_PACKAGES:
+        (ir,) = sorted((golden / name).glob("*.ir.json"))
+        meta = json.loads((golden / name / "meta.json").read_text())
+        bufs = {}
+        for arg in meta["kernels"][0]["args"]:
+            shape = tuple(arg.get("shape") or [1])
+            if arg.get("output"):
+                bufs[arg["name"]] = torch.zeros(shape, device="cuda", dtype=_torch_dtype(arg["dtype"]))
+            else:
+                bufs[arg["name"]] = torch.as_tensor(seeded_input(arg, 0)).to("cuda", _torch_dtype(arg["dtype"]))
+        ptrs = {n: t.data_ptr() for n, t in bufs.items()}
+        fixed = compile_file(ir)
+        pkg = load_package(ir)
+        native = compile_blockprog(pkg, pkg.body[0]).to_json()
+        interpreted = json.loads(json.dumps(native))
+        row = {"package": name, "fixed_op": fixed["op"], "fixed_us": round(time_plan(fixed, ptrs, repeat), 2)}
+        row["block_native_us"] = round(time_plan(native, ptrs, repeat), 2)
+        os.environ["LC_JIT"] = "0"
+        row["block_interpreted_us"] = round(time_plan(interpreted, ptrs, max(3, repeat // 10)), 2)
+        os.environ["LC_JIT"] = "1"
+        print(json.dumps(row), flush=True)
 
 
 def main() -> None:
@@ -31,8 +88,6 @@ def main() -> None:
     ap.add_argument("--k", type=int, default=8192)
     ap.add_argument("--bh", type=int, default=128)
     ap.add_argument("--seq", type=int, default=4096)
-    ap.add_argument("--variant", type=int, default=0)
-    ap.add_argument("--groups", type=int, default=512)
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--repeat", type=int, default=1)
     a = ap.parse_args()
@@ -43,6 +98,9 @@ def main() -> None:
     P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
     s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     op = a.op
+    if op == "general_paths":
+        general_paths(max(a.repeat, 10))
+        return
     if op in ("add", "axpb", "relumul", "gelu_erf", "gelu_tanh", "sum", "mean"):
         n = a.n or (1 << 28 if op not in ("sum", "mean") else 1 << 24)
         x = torch.randn(n, device="cuda", generator=g)
@@ -98,10 +156,6 @@ def main() -> None:
         fn = lambda: runtime.call("lc_attention_f32", 0, 0, P(c), P(q), P(kt), P(v), P(o),  # noqa: E731
                                   bh, sq, sq, d, d, s)
         work, unit = 4 * bh * sq * sq * d, "TFLOP/s"
-    elif op == "mma_probe":
-        fn = lambda: runtime.call("lc_probe_mma", a.variant, a.groups, s)  # noqa: E731
-        sms = torch.cuda.get_device_properties(0).multi_processor_count
-        work, unit = 2 * 128 * 128 * 16 * 8 * a.groups * sms, "TFLOP/s"
     elif op == "sdpa":
         bh, sq, d = a.bh, a.seq, 128
         q = torch.randn(bh, sq, d, device="cuda", generator=g).half()
