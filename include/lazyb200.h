@@ -126,6 +126,39 @@ int lc_mean_f32(const float *x, const float *count, float *out, int64_t n, void 
 int lc_sum_partial_f32(const float *x, int64_t n, double *partial, void *stream);
 int lc_sum_finalize(const double *total, const float *count, float *out, void *stream);
 
+/* Range-sharded sum / mean across the GPUs of one node, one process per GPU,
+ * with the exchange of the shard sums fused into the reduction kernel
+ * (no NCCL call).  No reference counterpart (the reference is single-GPU).
+ *  - lc_peer_mailbox: this device's mailbox (LC_PEER_MAILBOX_BYTES of
+ *    library-owned device memory, created zeroed on first use) and its CUDA
+ *    IPC handle (LC_PEER_HANDLE_BYTES) for the other ranks.
+ *  - lc_peer_open / lc_peer_close: map / unmap a peer's mailbox from its handle
+ *    (peer access over NVLink).
+ *  - lc_sum_peer_f32: reduces x[0..n) (this rank's shard) to an f64 shard sum;
+ *    the kernel's last CTA stores it into every rank's mailbox and waits for
+ *    all `world` shard sums (bounded: 5 s of %globaltimer), adds them in rank
+ *    order and writes out[0] = sum (count == NULL) or sum / count[0], the
+ *    same value on every rank.  `mailboxes` is a host array of `world`
+ *    device pointers (this rank's own mailbox at index `rank`, the mapped
+ *    peers elsewhere).  Each call is one exchange epoch, counted on the
+ *    device (so the call can be captured in a CUDA graph and replayed): all
+ *    ranks must make the same sequence of calls.  A peer that does not
+ *    arrive in time makes out[0] NaN and lc_device_status return
+ *    LC_ERR_TIMEOUT; the ranks then resynchronise with lc_peer_reset.
+ *  - lc_peer_reset: zeroes this device's mailbox (flags and epoch) on the
+ *    stream.  Every rank calls it, between two host barriers, with no
+ *    exchange in flight.
+ *  - Two calls on one rank must not overlap on the GPU (same stream). */
+#define LC_PEER_MAX_RANKS 8
+#define LC_PEER_MAILBOX_BYTES 256
+#define LC_PEER_HANDLE_BYTES 64
+int lc_peer_mailbox(void **mailbox, unsigned char *handle);
+int lc_peer_open(const unsigned char *handle, void **peer_mailbox);
+int lc_peer_close(void *peer_mailbox);
+int lc_peer_reset(void *stream);
+int lc_sum_peer_f32(const float *x, int64_t n, const float *count, float *out,
+                    void *const *mailboxes, int world, int rank, void *stream);
+
 /* lc_sum_f32 without any allocation, for callers that cannot let a library
  * call cudaMalloc: applications whose device memory is owned entirely by
  * their own allocator (a framework's caching pool, or a service that reserves
@@ -211,6 +244,17 @@ int lc_attention_tile_f16q(const void *q, const void *kt, const void *v, void *o
 int lc_gemm(int ab_dtype, int c_dtype, int b_layout, int epilogue, const void *a,
             const void *b, void *c, int64_t m, int64_t n, int64_t k, void *stream);
 
+/* FP32 GEMM, C = epilogue(A @ B + bias), with every output's dot product
+ * accumulated in k order as a Dot2 pair (Ogita, Rump and Oishi 2005,
+ * Algorithm 5.3: TwoProduct by FMA plus TwoSum, ptx_backend.py:571-593) and
+ * read as high + correction while high is finite (:539-552) — the
+ * reference's arithmetic for matmul packages whose meta.json states a
+ * tolerance (:1860-1865).  A [M,K], B [K,N] or [N,K] (b_layout), C [M,N] f32,
+ * bias f32 [N] or NULL.  SIMT; a split contraction adds the compensated
+ * partial sums of its chunks in a fixed order. */
+int lc_gemm_f32_dot2(int b_layout, int epilogue, const float *a, const float *b, const float *bias,
+                     float *c, int64_t m, int64_t n, int64_t k, void *stream);
+
 /* lc_gemm with a bias: C = epilogue(A @ B + bias[col]); bias is f32 [N] (or
  * NULL) and is added, rounded once, before the activation.  Replaces the
  * RegStore epilogue lambdas with a bias load (ptx_tensor.py:431-457) and the
@@ -272,6 +316,14 @@ int lc_gemm_chain(int mma_type, int x_type, int y_type, int z_type, int c_type, 
 int lc_attention_f32(int scale_mode, int epilogue, const void *scale, const void *q,
                      const void *kt, const void *v, void *o, int64_t bh, int64_t s_q,
                      int64_t s_kv, int64_t d, int64_t dv, void *stream);
+
+/* lc_attention_f32 with each score's dot product accumulated as a Dot2 pair
+ * (the compensated dot, ptx_backend.py:571-593), read as high + correction
+ * while high is finite (:539-552): the reference's arithmetic for attention
+ * packages whose meta.json states a tolerance (its policy, :1860-1865). */
+int lc_attention_f32_dot2(int scale_mode, int epilogue, const void *scale, const void *q,
+                          const void *kt, const void *v, void *o, int64_t bh, int64_t s_q,
+                          int64_t s_kv, int64_t d, int64_t dv, void *stream);
 
 /* O = softmax(scale * Q K^T) V per (batch*head); Q,K,V,O f16 [bh, s, d]
  * row-major, softmax statistics in f32, non-causal.  Replaces the

@@ -251,14 +251,12 @@ class BlockCompiler(SerialCompiler):
         self.clear_memo()
         self.uniform_depth += 1
         skip = self.branch("BRZ", p)
-        for inner in s.body:
-            self.statement(inner)
+        self.body(s.body)
         self.clear_memo()
         if s.get("else_body"):
             done = self.branch("BRA")
             self.patch(skip)
-            for inner in s.else_body:
-                self.statement(inner)
+            self.body(s.else_body)
             self.clear_memo()
             self.patch(done)
         else:
@@ -287,6 +285,7 @@ class BlockCompiler(SerialCompiler):
                     if op not in IDENTITY:
                         raise CompileError(f"no identity for accumulator operation {op}")
                     self.put(self.acc_register(inner.name), self.literal(IDENTITY[op], "f32"))
+                    self.clear_low(inner.name)
         if uniform:
             step_v = value(step, 1)
             if step_v < 1:
@@ -310,8 +309,7 @@ class BlockCompiler(SerialCompiler):
         if not uniform:
             self.uniform_depth += 1
         saved = dict(self.env)
-        for inner in s.body:
-            self.statement(inner)
+        self.body(s.body)
         self.env = {**saved, **{n: Val(r, "f32") for n, r in self.accs.items()}}
         if not uniform:
             self.uniform_depth -= 1
@@ -328,6 +326,14 @@ class BlockCompiler(SerialCompiler):
         self.loop_ranges.append((begin, end))
 
     # ------------------------------------------------------------ shuffles and trees
+    def body(self, statements) -> None:
+        """Statements of one body in order, each knowing the statement before it (Dot2 adjacency)."""
+        previous = None
+        for inner in statements:
+            self.previous = previous
+            self.statement(inner)
+            previous = inner
+
     def state_register(self, name: str) -> int:
         """The fixed register of a shuffled or tree state (prepare_state)."""
         if name in self.accs:
@@ -335,6 +341,7 @@ class BlockCompiler(SerialCompiler):
         value = self.lookup(name)
         reg = self.acc_register(name)
         self.put(reg, value)
+        self.clear_low(name)
         return reg
 
     def merge(self, s: Node) -> None:
@@ -343,6 +350,7 @@ class BlockCompiler(SerialCompiler):
             value = self.operation(op, [self.convert(self.lookup(n), "f32") for n in a.args], "f32")
             if a.name in s.state:
                 self.put(self.accs[a.name], value)
+                self.clear_low(a.name)
                 self.env[a.name] = Val(self.accs[a.name], "f32")
             else:
                 self.env[a.name] = self.convert(value, "f32")
@@ -351,8 +359,10 @@ class BlockCompiler(SerialCompiler):
         length = int(s.length)
         if length < 1 or length > 32 or length & (length - 1):
             raise CompileError("shuffle length must be a power of two in 1..32")
-        if self.threads % 32 and length > 1:
-            raise CompileError("shuffles need whole warps")
+        # whole warps, or one partial warp of a power-of-two size the butterfly stays inside
+        partial = self.threads < 32 and not self.threads & (self.threads - 1) and length <= self.threads
+        if self.threads % 32 and length > 1 and not partial:
+            raise CompileError("shuffles need whole warps (or one power-of-two partial warp)")
         self.barrier_allowed("a shuffle")
         for name in s.state:
             self.state_register(name)
@@ -397,6 +407,7 @@ class BlockCompiler(SerialCompiler):
             for buf, a, b in zip(s.bufs, s.state, s.state_b):
                 arr = self.smem[buf][0]
                 self.put(self.accs[a], self.emit("LDS", "f32", slot, aux=arr))
+                self.clear_low(a)
                 self.env[a] = Val(self.accs[a], "f32")
                 self.env[b] = self.emit("LDS", "f32", other, aux=arr)
             self.merge(s)
@@ -409,11 +420,11 @@ class BlockCompiler(SerialCompiler):
         self.env = {**saved, **{n: Val(self.accs[n], "f32") for n in s.state}}
         for buf, name in zip(s.bufs, s.state):
             self.put(self.accs[name], self.emit("LDS", "f32", base, aux=self.smem[buf][0]))
+            self.clear_low(name)
 
     # ------------------------------------------------------------ finishing
     def compile_block(self, body: tuple) -> tuple:
-        for s in body:
-            self.statement(s)
+        self.body(body)
         if not self.writes:
             raise CompileError("block program writes nothing")
         if len({b for b, _ in self.writes}) != 1:

@@ -47,7 +47,7 @@ __device__ __forceinline__ float apply_scale(float dot, float c, float rc, int m
   return __fdiv_rn(dot, c);
 }
 
-template <int DVH, int EPI>
+template <int DVH, int EPI, bool COMP = false>
 __global__ void __launch_bounds__(kThreads) attention_f32_kernel(
     const float *__restrict__ q, const float *__restrict__ kt, const float *__restrict__ v,
     float *__restrict__ o, int s_q, int s_kv, int d, int dv, const float *__restrict__ scale,
@@ -93,19 +93,39 @@ __global__ void __launch_bounds__(kThreads) attention_f32_kernel(
     }
     __syncthreads();
 
-    float s[4][4];
+    float s[4][4], s_low[COMP ? 4 : 1][COMP ? 4 : 1];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
+    if constexpr (COMP) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s_low[i][j] = 0.f;
+    }
     for (int dd = 0; dd < d; ++dd) {
       const float4 a = *reinterpret_cast<const float4 *>(&Qs[dd * QS + ty * 4]);
       const float4 b = *reinterpret_cast<const float4 *>(&Ks[dd * BKV + tx * 4]);
       const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+      if constexpr (COMP) {
+        // the score dot as a Dot2 pair, in the IR's operand order kt * q
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dot2_step(s[i][j], s_low[i][j], bv[j], av[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) s[i][j] = fmaf(av[i], bv[j], s[i][j]);
+      }
+    }
+    if constexpr (COMP) {
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) s[i][j] = fmaf(av[i], bv[j], s[i][j]);
+        for (int j = 0; j < 4; ++j) s[i][j] = dot2_value(s[i][j], s_low[i][j]);
     }
 
 #pragma unroll
@@ -175,7 +195,7 @@ __global__ void __launch_bounds__(kThreads) attention_f32_kernel(
 
 // Any head size: one thread per output element, online softmax over the keys
 // in order, the arithmetic of the tiled kernel.
-template <int EPI>
+template <int EPI, bool COMP = false>
 __global__ void __launch_bounds__(256) attention_f32_direct_kernel(
     const float *__restrict__ q, const float *__restrict__ kt, const float *__restrict__ v,
     float *__restrict__ o, int64_t bh, int s_q, int s_kv, int d, int dv,
@@ -194,8 +214,13 @@ __global__ void __launch_bounds__(256) attention_f32_direct_kernel(
     const float *vb = v + b * s_kv * dv;
     float m = kMaxIdentity, l = 0.f, acc = 0.f;
     for (int key = 0; key < s_kv; ++key) {
-      float dot = 0.f;
-      for (int dd = 0; dd < d; ++dd) dot = fmaf(qr[dd], kb[(int64_t)dd * s_kv + key], dot);
+      float dot = 0.f, dot_low = 0.f;
+      if constexpr (COMP) {
+        for (int dd = 0; dd < d; ++dd) dot2_step(dot, dot_low, kb[(int64_t)dd * s_kv + key], qr[dd]);
+        dot = dot2_value(dot, dot_low);
+      } else {
+        for (int dd = 0; dd < d; ++dd) dot = fmaf(qr[dd], kb[(int64_t)dd * s_kv + key], dot);
+      }
       const float x = apply_scale(dot, c, rc, scale_mode);
       const float m_new = fmaxf(m, x);
       const float alpha = exp_ref(__fsub_rn(m, m_new));
@@ -260,10 +285,10 @@ size_t tiled_smem(int d, int dvh) {
   return (size_t)(d * QS + d * BKV + BKV * 64 * dvh + BKV * BQ) * sizeof(float);
 }
 
-template <int DVH, int EPI>
+template <int DVH, int EPI, bool COMP>
 int launch_tiled(const float *q, const float *kt, const float *v, float *o, int64_t bh, int s_q,
                  int s_kv, int d, int dv, const float *scale, int mode, cudaStream_t s) {
-  auto kernel = attention_f32_kernel<DVH, EPI>;
+  auto kernel = attention_f32_kernel<DVH, EPI, COMP>;
   const size_t smem = tiled_smem(d, DVH);
   if (smem > 48 * 1024) {
     if (int rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -276,17 +301,17 @@ int launch_tiled(const float *q, const float *kt, const float *v, float *o, int6
   return check_launch("lc_attention_f32");
 }
 
-template <int EPI>
+template <int EPI, bool COMP>
 int launch(const float *q, const float *kt, const float *v, float *o, int64_t bh, int s_q,
            int s_kv, int d, int dv, const float *scale, int mode, cudaStream_t s) {
   if (d <= kMaxTiled && dv <= kMaxTiled) {
-    if (dv <= 64) return launch_tiled<1, EPI>(q, kt, v, o, bh, s_q, s_kv, d, dv, scale, mode, s);
-    return launch_tiled<2, EPI>(q, kt, v, o, bh, s_q, s_kv, d, dv, scale, mode, s);
+    if (dv <= 64) return launch_tiled<1, EPI, COMP>(q, kt, v, o, bh, s_q, s_kv, d, dv, scale, mode, s);
+    return launch_tiled<2, EPI, COMP>(q, kt, v, o, bh, s_q, s_kv, d, dv, scale, mode, s);
   }
   const int64_t total = bh * s_q * dv;
   const int64_t blocks = (total + 255) / 256;
   const int64_t cap = 16LL * sm_count();
-  attention_f32_direct_kernel<EPI><<<(int)(blocks < cap ? blocks : cap), 256, 0, s>>>(
+  attention_f32_direct_kernel<EPI, COMP><<<(int)(blocks < cap ? blocks : cap), 256, 0, s>>>(
       q, kt, v, o, bh, s_q, s_kv, d, dv, scale, mode);
   return check_launch("lc_attention_f32 (direct)");
 }
@@ -294,9 +319,10 @@ int launch(const float *q, const float *kt, const float *v, float *o, int64_t bh
 }  // namespace
 }  // namespace lc
 
-extern "C" int lc_attention_f32(int scale_mode, int epilogue, const void *scale, const void *q,
-                                const void *kt, const void *v, void *o, int64_t bh, int64_t s_q,
-                                int64_t s_kv, int64_t d, int64_t dv, void *stream) {
+namespace {
+int attention_f32_entry(bool comp, int scale_mode, int epilogue, const void *scale, const void *q,
+                        const void *kt, const void *v, void *o, int64_t bh, int64_t s_q, int64_t s_kv,
+                        int64_t d, int64_t dv, void *stream) {
   using namespace lc;
   if (scale_mode != LC_SCALE_MUL && scale_mode != LC_SCALE_MUL_RECIP && scale_mode != LC_SCALE_DIV)
     return fail(LC_ERR_INVALID, "lc_attention_f32: unknown scale mode %d", scale_mode);
@@ -316,12 +342,26 @@ extern "C" int lc_attention_f32(int scale_mode, int epilogue, const void *scale,
   auto *of = static_cast<float *>(o);
   auto *sc = static_cast<const float *>(scale);
   cudaStream_t s = as_stream(stream);
-#define LC_ATT(E)                                                                          \
-  if (epilogue == E)                                                                       \
-    return launch<E>(qf, kf, vf, of, bh, (int)s_q, (int)s_kv, (int)d, (int)dv, sc, scale_mode, s);
+#define LC_ATT(E)                                                                                   \
+  if (epilogue == E)                                                                                \
+    return comp ? launch<E, true>(qf, kf, vf, of, bh, (int)s_q, (int)s_kv, (int)d, (int)dv, sc, scale_mode, s) \
+                : launch<E, false>(qf, kf, vf, of, bh, (int)s_q, (int)s_kv, (int)d, (int)dv, sc, scale_mode, s);
   LC_ATT(LC_EPI_NONE) LC_ATT(LC_EPI_GELU_ERF) LC_ATT(LC_EPI_GELU_TANH)
 #undef LC_ATT
   return fail(LC_ERR_INVALID, "lc_attention_f32: bad epilogue");
+}
+}  // namespace
+
+extern "C" int lc_attention_f32(int scale_mode, int epilogue, const void *scale, const void *q,
+                                const void *kt, const void *v, void *o, int64_t bh, int64_t s_q,
+                                int64_t s_kv, int64_t d, int64_t dv, void *stream) {
+  return attention_f32_entry(false, scale_mode, epilogue, scale, q, kt, v, o, bh, s_q, s_kv, d, dv, stream);
+}
+
+extern "C" int lc_attention_f32_dot2(int scale_mode, int epilogue, const void *scale, const void *q,
+                                     const void *kt, const void *v, void *o, int64_t bh, int64_t s_q,
+                                     int64_t s_kv, int64_t d, int64_t dv, void *stream) {
+  return attention_f32_entry(true, scale_mode, epilogue, scale, q, kt, v, o, bh, s_q, s_kv, d, dv, stream);
 }
 
 extern "C" int lc_attention_tile_f16q(const void *q, const void *kt, const void *v, void *o,

@@ -46,6 +46,8 @@ int gemm_tc_launch(bool bf16, bool b_mn, int out, int epi, const void *a, const 
                    const float *bias, void *c, int m, int n, int k, cudaStream_t s, bool pair);
 int gemm_f32(int out, int b_layout, int epi, const void *a, const void *b, const float *bias,
              void *c, int m, int n, int k, cudaStream_t s);
+int gemm_f32_dot2(int b_layout, int epi, const float *a, const float *b, const float *bias, float *c,
+                  int m, int n, int k, cudaStream_t s);
 // lc_gemm_mixed after argument checks (gemm_mixed.cu)
 int gemm_mixed(int mma_type, int a_type, int b_type, int c_type, int b_layout, int epilogue,
                int flags, const void *a, const void *b, const float *bias, void *c, int m, int n,
@@ -101,6 +103,26 @@ struct CompSum {
   }
   __device__ __forceinline__ double value() const { return (double)s + (double)c; }
 };
+
+// One step of the compensated dot product Dot2 (Ogita, Rump and Oishi 2005,
+// "Accurate Sum and Dot Product", Algorithm 5.3): hi + lo += a * b, where the
+// product's rounding residual (by FMA) and the addition's rounding error
+// (TwoSum) accumulate in lo.  Every operation is explicitly rounded, in the
+// order the reference's compensated accumulation uses (ptx_backend.py:571-593).
+__device__ __forceinline__ void dot2_step(float &hi, float &lo, float a, float b) {
+  const float p = __fmul_rn(a, b);
+  const float r = __fmaf_rn(a, b, -p);
+  const float t = __fadd_rn(hi, p);
+  const float d = __fsub_rn(t, hi);
+  const float e = __fadd_rn(__fsub_rn(hi, __fsub_rn(t, d)), __fsub_rn(p, d));
+  lo = __fadd_rn(lo, __fadd_rn(e, r));
+  hi = t;
+}
+// The value of a Dot2 state: the correction counts while hi is finite
+// (ptx_backend.py:539-552).
+__device__ __forceinline__ float dot2_value(float hi, float lo) {
+  return __fadd_rn(hi, fabsf(hi) < INFINITY ? lo : 0.f);
+}
 
 template <class T>
 __device__ __forceinline__ T warp_sum(T v) {

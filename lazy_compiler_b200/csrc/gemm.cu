@@ -715,6 +715,22 @@ extern "C" int lc_gemm(int ab_dtype, int c_dtype, int b_layout, int epilogue, co
   return lc_gemm_ex(ab_dtype, c_dtype, b_layout, epilogue, a, b, nullptr, c, m, n, k, stream);
 }
 
+extern "C" int lc_gemm_f32_dot2(int b_layout, int epilogue, const float *a, const float *b,
+                                const float *bias, float *c, int64_t m, int64_t n, int64_t k,
+                                void *stream) {
+  using namespace lc;
+  if (b_layout != LC_B_KN && b_layout != LC_B_NK)
+    return fail(LC_ERR_INVALID, "lc_gemm_f32_dot2: unknown B layout %d", b_layout);
+  if (epilogue < LC_EPI_NONE || epilogue > LC_EPI_GELU_TANH)
+    return fail(LC_ERR_INVALID, "lc_gemm_f32_dot2: unknown epilogue %d", epilogue);
+  if (m < 0 || n < 0 || k < 0) return fail(LC_ERR_INVALID, "lc_gemm_f32_dot2: negative shape");
+  if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff)
+    return fail(LC_ERR_UNSUPPORTED, "lc_gemm_f32_dot2: dimensions above 2^31-1");
+  if (m == 0 || n == 0) return LC_OK;
+  if (!c || (k > 0 && (!a || !b))) return fail(LC_ERR_INVALID, "lc_gemm_f32_dot2: null buffer");
+  return gemm_f32_dot2(b_layout, epilogue, a, b, bias, c, (int)m, (int)n, (int)k, as_stream(stream));
+}
+
 extern "C" int lc_gemm_path(int ab_dtype, int b_layout, const void *a, const void *b, int64_t m,
                             int64_t n, int64_t k) {
   if (ab_dtype == LC_F32) return lc::gemm_path32(b_layout, a, b, m, n, k);

@@ -9,6 +9,9 @@
 // examples/phase9/generated/phase9_bias_gelu_gemm.
 //
 // Two paths (lc_gemm_path reports which one runs):
+//  * lc_gemm_f32_dot2 (packages that state a tolerance, where the reference
+//    compensates each output's dot product): the SIMT kernel below with every
+//    output a Dot2 pair (dot2_step / dot2_value, common.cuh), 64x64 tiles.
 //  * SIMT (path 0): a persistent FFMA kernel over 128x128 (or, when there are
 //    fewer such tiles than SMs, 64x64) output tiles, 8x8 (4x4) outputs per
 //    thread, k-slices of 8 double-buffered in shared memory.  Small problems and
@@ -103,8 +106,9 @@ __global__ void __launch_bounds__(kThreads) split3_kernel(const float *__restric
 // makes the kernel a guard: it returns unless *flag is non-zero.  With
 // `partial`, blockIdx.y picks the k range [y * k_chunk, (y + 1) * k_chunk) and
 // the raw sums go to partial[y][M][N] (no bias, no activation) for
-// split_k_reduce_kernel.
-template <int TM, int EPI, bool B_NK>
+// split_k_reduce_kernel.  COMP: every output accumulates as a Dot2 pair
+// (dot2_step in k order), read as dot2_value.
+template <int TM, int EPI, bool B_NK, bool COMP = false>
 __global__ void __launch_bounds__(kThreads, 2) gemm_f32_simt_kernel(
     const float *__restrict__ a, const float *__restrict__ b, const float *__restrict__ bias,
     float *__restrict__ c, int m, int n, int k, const int *flag, int k_chunk,
@@ -164,10 +168,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemm_f32_simt_kernel(
     };
 
     float acc[TM][TM];
+    float low[COMP ? TM : 1][COMP ? TM : 1];
 #pragma unroll
     for (int i = 0; i < TM; ++i)
 #pragma unroll
       for (int j = 0; j < TM; ++j) acc[i][j] = 0.f;
+    if constexpr (COMP) {
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TM; ++j) low[i][j] = 0.f;
+    }
 
     load(k_lo);
     store(0);
@@ -186,10 +197,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemm_f32_simt_kernel(
           av[h * 4 + 0] = x.x, av[h * 4 + 1] = x.y, av[h * 4 + 2] = x.z, av[h * 4 + 3] = x.w;
           bv[h * 4 + 0] = y.x, bv[h * 4 + 1] = y.y, bv[h * 4 + 2] = y.z, bv[h * 4 + 3] = y.w;
         }
+        if constexpr (COMP) {
 #pragma unroll
-        for (int i = 0; i < TM; ++i)
+          for (int i = 0; i < TM; ++i)
 #pragma unroll
-          for (int j = 0; j < TM; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+            for (int j = 0; j < TM; ++j) dot2_step(acc[i][j], low[i][j], av[i], bv[j]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < TM; ++i)
+#pragma unroll
+            for (int j = 0; j < TM; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
       }
       if (more) store(buf ^ 1);
       __syncthreads();
@@ -206,7 +224,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemm_f32_simt_kernel(
         float v[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          float x = acc[i][h * 4 + j];
+          float x;
+          if constexpr (COMP) x = dot2_value(acc[i][h * 4 + j], low[i][h * 4 + j]);
+          else x = acc[i][h * 4 + j];
           if (!partial) {
             if (bias && col + j < n) x = __fadd_rn(x, bias[col + j]);
             x = apply_epilogue<EPI>(x);
@@ -244,7 +264,7 @@ __global__ void __launch_bounds__(kThreads) split_k_reduce_kernel(const float *_
   }
 }
 
-template <int TM, int EPI>
+template <int TM, int EPI, bool COMP = false>
 int launch_simt_tm(bool b_nk, const float *a, const float *b, const float *bias, float *c, int m,
                    int n, int k, const int *flag, cudaStream_t s) {
   constexpr int ST = 16 * TM;
@@ -268,9 +288,11 @@ int launch_simt_tm(bool b_nk, const float *a, const float *b, const float *bias,
     float *part = static_cast<float *>(ws);
     dim3 g2((unsigned)grid, (unsigned)splits);
     if (b_nk)
-      gemm_f32_simt_kernel<TM, EPI, true><<<g2, kThreads, 0, s>>>(a, b, bias, c, m, n, k, flag, k_chunk, part);
+      gemm_f32_simt_kernel<TM, EPI, true, COMP><<<g2, kThreads, 0, s>>>(a, b, bias, c, m, n, k, flag, k_chunk,
+                                                                        part);
     else
-      gemm_f32_simt_kernel<TM, EPI, false><<<g2, kThreads, 0, s>>>(a, b, bias, c, m, n, k, flag, k_chunk, part);
+      gemm_f32_simt_kernel<TM, EPI, false, COMP><<<g2, kThreads, 0, s>>>(a, b, bias, c, m, n, k, flag,
+                                                                         k_chunk, part);
     if (int rc = check_launch("lc_gemm (f32 simt, split k)")) return rc;
     const int64_t total = (int64_t)m * n;
     const int64_t blocks = (total + kThreads - 1) / kThreads;
@@ -279,10 +301,21 @@ int launch_simt_tm(bool b_nk, const float *a, const float *b, const float *bias,
     return check_launch("lc_gemm (f32 split-k reduce)");
   }
   if (b_nk)
-    gemm_f32_simt_kernel<TM, EPI, true><<<grid, kThreads, 0, s>>>(a, b, bias, c, m, n, k, flag, 0, nullptr);
+    gemm_f32_simt_kernel<TM, EPI, true, COMP><<<grid, kThreads, 0, s>>>(a, b, bias, c, m, n, k, flag, 0, nullptr);
   else
-    gemm_f32_simt_kernel<TM, EPI, false><<<grid, kThreads, 0, s>>>(a, b, bias, c, m, n, k, flag, 0, nullptr);
+    gemm_f32_simt_kernel<TM, EPI, false, COMP><<<grid, kThreads, 0, s>>>(a, b, bias, c, m, n, k, flag, 0,
+                                                                         nullptr);
   return check_launch("lc_gemm (f32 simt)");
+}
+
+// Dot2-compensated SIMT GEMM (64x64 tiles: two registers per output).
+int launch_simt_dot2(int epi, bool b_nk, const float *a, const float *b, const float *bias, float *c, int m,
+                     int n, int k, cudaStream_t s) {
+#define LC_F32_DOT2(E) \
+  if (epi == E) return launch_simt_tm<4, E, true>(b_nk, a, b, bias, c, m, n, k, nullptr, s);
+  LC_F32_DOT2(LC_EPI_NONE) LC_F32_DOT2(LC_EPI_GELU_ERF) LC_F32_DOT2(LC_EPI_GELU_TANH)
+#undef LC_F32_DOT2
+  return fail(LC_ERR_INVALID, "lc_gemm_f32_dot2: bad epilogue");
 }
 
 int launch_simt(int epi, bool b_nk, const float *a, const float *b, const float *bias, float *c,
@@ -318,6 +351,11 @@ int gemm_path32(int b_layout, const void *a, const void *b, int64_t m, int64_t n
                         aligned(b, 16) && (b_layout == LC_B_NK || n % 8 == 0);
   if (!shape_ok || m * n * k < kSplitMacs) return 0;
   return gemm_path16(b_layout, a, b, m, n, 6 * k);
+}
+
+int gemm_f32_dot2(int b_layout, int epi, const float *a, const float *b, const float *bias, float *c,
+                  int m, int n, int k, cudaStream_t s) {
+  return launch_simt_dot2(epi, b_layout == LC_B_NK, a, b, bias, c, m, n, k, s);
 }
 
 int gemm_f32(int out, int b_layout, int epi, const void *a_, const void *b_, const float *bias,

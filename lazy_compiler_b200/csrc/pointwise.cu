@@ -25,6 +25,13 @@ struct PointwiseArgs {
 };
 
 __device__ __forceinline__ float f(uint32_t w) { return __uint_as_float(w); }
+// Mask of the lanes of the calling thread's warp that exist in its CTA (all 32
+// unless the CTA's thread count leaves this warp partial).
+__device__ __forceinline__ unsigned int warp_lanes() {
+  const unsigned int first = threadIdx.x & ~31u;
+  const unsigned int n = blockDim.x - first;
+  return n >= 32u ? 0xffffffffu : ((1u << n) - 1u);
+}
 __device__ __forceinline__ uint32_t w(float x) { return __float_as_uint(x); }
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -168,10 +175,14 @@ __device__ __forceinline__ void exec_range(const lc_pw_program &g, void *const *
         }
         continue;
       }
-      case LC_PW_SHFL_XOR:
-        __syncwarp();
-        out = __shfl_xor_sync(0xffffffffu, A, aux);
+      case LC_PW_SHFL_XOR: {
+        // the lanes of this warp that exist: a block program's CTA may be one
+        // partial warp (its butterfly is then confined to that power-of-two group)
+        const unsigned int mask = warp_lanes();
+        __syncwarp(mask);
+        out = __shfl_xor_sync(mask, A, aux);
         break;
+      }
       case LC_PW_PACK_F16X2: {
         __half2 h = __floats2half2_rn(f(A), f(B));
         out = *reinterpret_cast<uint32_t *>(&h);
@@ -261,7 +272,7 @@ __device__ __forceinline__ void exec_range(const lc_pw_program &g, void *const *
         continue;
       }
       case LC_PW_BAR: __syncthreads(); continue;
-      case LC_PW_WSYNC: __syncwarp(); continue;
+      case LC_PW_WSYNC: __syncwarp(warp_lanes()); continue;
       case LC_PW_TID: out = threadIdx.x; break;
       case LC_PW_STATE: out = w(states[aux]); break;
       case LC_PW_PARTIAL: out = w(partials[aux]); break;

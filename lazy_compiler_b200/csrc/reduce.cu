@@ -15,6 +15,7 @@
 // writes the fp32 result.  The order of every addition is fixed by the grid,
 // so the result is deterministic; the f64 combine makes it the correctly
 // rounded fp32 value of the exact sum in all but tie cases.
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -58,15 +59,112 @@ __device__ __forceinline__ void accumulate_scalar(CompSum &acc, const float *__r
     acc.add(x[i]);
 }
 
-// mode 0: out = sum; mode 1: out = sum / count[0]; mode 2: partial_out = sum (f64)
+// Peer-memory exchange of the shard sums of one range-sharded reduction (one
+// process per GPU).  Every rank owns one mailbox in its own device memory,
+// with a call counter (the epoch) that only its own kernels touch.  The last
+// CTA of a rank's reduction takes epoch e = counter + 1, stores its f64 shard
+// sum into slot [e & 1][rank] of every rank's mailbox (its own included) over
+// NVLink and raises the flag next to it with a system-scope release; it then
+// waits (bounded) until all flags of that slot in its own mailbox carry e,
+// adds the shard sums in rank order (so every rank computes the same value)
+// and stores e back as the counter.  The epoch lives on the device, so the
+// call can be replayed from a CUDA graph.  Two slots alternate by epoch
+// parity: a rank can only write epoch e+2 into a peer's mailbox after that
+// peer wrote epoch e+1, i.e. after the peer's kernel of epoch e (and its reads
+// of slot e & 1) finished, so no slot is overwritten while it is read.
+struct PeerBox {
+  double partial[2][LC_PEER_MAX_RANKS];
+  unsigned int flag[2][LC_PEER_MAX_RANKS];
+  unsigned int epoch;
+};
+static_assert(sizeof(PeerBox) <= LC_PEER_MAILBOX_BYTES, "mailbox layout exceeds its allocation");
+struct PeerSet {
+  PeerBox *box[LC_PEER_MAX_RANKS];
+  int world, rank;
+  int *err;
+};
+constexpr uint64_t kPeerWaitLimitNs = 5000000000ull;  // ranks may reach the kernel seconds apart
+constexpr int kErrTimeoutPeer = 7;
+
+__device__ __forceinline__ void st_release_sys(unsigned int *p, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int *p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_sys_f64(double *p, double v) {
+  asm volatile("st.relaxed.sys.global.f64 [%0], %1;" ::"l"(p), "d"(v) : "memory");
+}
+__device__ __forceinline__ double ld_relaxed_sys_f64(const double *p) {
+  double v;
+  asm volatile("ld.relaxed.sys.global.f64 %0, [%1];" : "=d"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Run by every thread of the last CTA: exchange `total` with the peers and
+// return the sum over all ranks (NaN if a peer did not arrive in time).
+__device__ double peer_exchange(double total, const PeerSet &peers, double *values, int *failed,
+                                unsigned int *epoch_sh) {
+  PeerBox *mine = peers.box[peers.rank];
+  const int t = threadIdx.x;
+  if (t == 0) {
+    *failed = 0;
+    *epoch_sh = *reinterpret_cast<volatile unsigned int *>(&mine->epoch) + 1u;
+  }
+  __syncthreads();
+  const unsigned int epoch = *epoch_sh;
+  const unsigned int slot = epoch & 1u;
+  if (t < peers.world) {
+    PeerBox *dst = peers.box[t];
+    st_relaxed_sys_f64(&dst->partial[slot][peers.rank], total);
+    st_release_sys(&dst->flag[slot][peers.rank], epoch);  // orders the store above
+  }
+  if (t < peers.world) {
+    const unsigned int *flag = &mine->flag[slot][t];
+    bool ok = ld_acquire_sys(flag) == epoch;
+    if (!ok) {
+      const uint64_t start = globaltimer_ns();
+      for (uint32_t i = 1; !ok; ++i) {
+        ok = ld_acquire_sys(flag) == epoch;
+        if (!ok && (i & 63) == 0 && globaltimer_ns() - start > kPeerWaitLimitNs) break;
+      }
+    }
+    if (ok) {
+      values[t] = ld_relaxed_sys_f64(&mine->partial[slot][t]);
+    } else {
+      values[t] = 0.0;
+      atomicExch(failed, 1);
+      if (peers.err) atomicCAS(peers.err, 0, kErrTimeoutPeer);
+    }
+  }
+  __syncthreads();
+  double sum = 0.0;
+  for (int r = 0; r < peers.world; ++r) sum += values[r];  // rank order on every rank
+  if (t == 0) *reinterpret_cast<volatile unsigned int *>(&mine->epoch) = epoch;
+  return *failed ? __longlong_as_double(0x7ff8000000000000ll) : sum;
+}
+
+// mode 0: out = sum; mode 1: out = sum / count[0]; mode 2: partial_out = sum (f64);
+// mode 3: out = (sum over the ranks of `peers`) [/ count[0] when count != NULL]
 template <bool VEC>
 __global__ void __launch_bounds__(kThreads, kBlocksPerSm) sum_kernel(const float *__restrict__ x, int64_t n,
                                                        double *__restrict__ partials,
                                                        unsigned int *__restrict__ counter,
                                                        int mode, const float *__restrict__ count,
                                                        float *__restrict__ out,
-                                                       double *__restrict__ partial_out) {
+                                                       double *__restrict__ partial_out,
+                                                       const PeerSet peers) {
   __shared__ double scratch[32];
+  __shared__ double values[LC_PEER_MAX_RANKS];
+  __shared__ int failed;
+  __shared__ unsigned int epoch_sh;
   __shared__ bool is_last;
   CompSum acc;
   if (VEC) accumulate(acc, x, n);
@@ -83,11 +181,13 @@ __global__ void __launch_bounds__(kThreads, kBlocksPerSm) sum_kernel(const float
   __threadfence();
   double t = 0.0;
   for (int i = threadIdx.x; i < (int)gridDim.x; i += kThreads) t += __ldcg(partials + i);
-  const double total = block_sum<double>(t, scratch);
+  double total = block_sum<double>(t, scratch);
+  if (mode == 3) total = peer_exchange(total, peers, values, &failed, &epoch_sh);
   if (threadIdx.x == 0) {
     if (mode == 0) out[0] = (float)total;
     else if (mode == 1) out[0] = (float)(total / (double)__ldg(count));
-    else partial_out[0] = total;
+    else if (mode == 2) partial_out[0] = total;
+    else out[0] = count ? (float)(total / (double)__ldg(count)) : (float)total;
     *counter = 0u;  // ready for the next launch on this workspace
   }
 }
@@ -99,9 +199,9 @@ __global__ void finalize_kernel(const double *__restrict__ total, const float *_
 }
 
 int launch_sum(const char *name, const float *x, int64_t n, int mode, const float *count,
-               float *out, double *partial_out, void *stream) {
+               float *out, double *partial_out, void *stream, const PeerSet *peers = nullptr) {
   if (n < 0 || (!x && n > 0)) return fail(LC_ERR_INVALID, "%s: null input or negative length", name);
-  if (mode < 2 && !out) return fail(LC_ERR_INVALID, "%s: null output", name);
+  if ((mode < 2 || mode == 3) && !out) return fail(LC_ERR_INVALID, "%s: null output", name);
   if (mode == 1 && !count) return fail(LC_ERR_INVALID, "%s: null count", name);
   if (mode == 2 && !partial_out) return fail(LC_ERR_INVALID, "%s: null partial", name);
   cudaStream_t s = as_stream(stream);
@@ -114,12 +214,14 @@ int launch_sum(const char *name, const float *x, int64_t n, int mode, const floa
   if (blocks > cap) blocks = cap;
   if (blocks > kMaxPartials) blocks = kMaxPartials;
   if (blocks < 1) blocks = 1;
+  PeerSet none{};
+  const PeerSet &p = peers ? *peers : none;
   if (vec)
     sum_kernel<true><<<(int)blocks, kThreads, 0, s>>>(x, n, ws.partials, ws.counter, mode, count,
-                                                      out, partial_out);
+                                                      out, partial_out, p);
   else
     sum_kernel<false><<<(int)blocks, kThreads, 0, s>>>(x, n, ws.partials, ws.counter, mode, count,
-                                                       out, partial_out);
+                                                       out, partial_out, p);
   return check_launch(name);
 }
 
@@ -198,10 +300,10 @@ extern "C" int lc_sum_f32_noalloc(const float *x, float *out, int64_t n, void *s
     return rc;
   if (vec)
     sum_kernel<true><<<(int)blocks, kThreads, 0, s>>>(x, n, partials, counter, 0, nullptr, out,
-                                                      nullptr);
+                                                      nullptr, PeerSet{});
   else
     sum_kernel<false><<<(int)blocks, kThreads, 0, s>>>(x, n, partials, counter, 0, nullptr, out,
-                                                       nullptr);
+                                                       nullptr, PeerSet{});
   return check_launch("lc_sum_f32_noalloc");
 }
 
@@ -223,4 +325,85 @@ extern "C" int lc_sum_finalize(const double *total, const float *count, float *o
   if (!total || !out) return lc::fail(LC_ERR_INVALID, "lc_sum_finalize: null buffer");
   lc::finalize_kernel<<<1, 1, 0, lc::as_stream(stream)>>>(total, count, out);
   return lc::check_launch("lc_sum_finalize");
+}
+
+// ---------------------------------------------------------------- peer mailboxes
+
+namespace {
+std::mutex g_peer_mutex;
+void *g_peer_mailbox[64] = {nullptr};
+}  // namespace
+
+extern "C" int lc_peer_mailbox(void **mailbox, unsigned char *handle) {
+  using namespace lc;
+  if (!mailbox || !handle) return fail(LC_ERR_INVALID, "lc_peer_mailbox: null argument");
+  int dev = 0;
+  if (int rc = check_cuda(cudaGetDevice(&dev), "lc_peer_mailbox: cudaGetDevice")) return rc;
+  if (dev < 0 || dev >= 64) return fail(LC_ERR_UNSUPPORTED, "lc_peer_mailbox: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_peer_mutex);
+  if (!g_peer_mailbox[dev]) {
+    void *mem = nullptr;
+    if (cudaMalloc(&mem, LC_PEER_MAILBOX_BYTES) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(LC_ERR_NOMEM, "lc_peer_mailbox: cudaMalloc(%d) failed", LC_PEER_MAILBOX_BYTES);
+    }
+    // flags and the epoch counter start at 0; the first call uses epoch 1
+    if (int rc = check_cuda(cudaMemset(mem, 0, LC_PEER_MAILBOX_BYTES), "lc_peer_mailbox: memset")) {
+      cudaFree(mem);
+      return rc;
+    }
+    g_peer_mailbox[dev] = mem;
+  }
+  cudaIpcMemHandle_t h;
+  if (int rc = check_cuda(cudaIpcGetMemHandle(&h, g_peer_mailbox[dev]), "lc_peer_mailbox: cudaIpcGetMemHandle"))
+    return rc;
+  memcpy(handle, &h, LC_PEER_HANDLE_BYTES);
+  *mailbox = g_peer_mailbox[dev];
+  return LC_OK;
+}
+
+extern "C" int lc_peer_open(const unsigned char *handle, void **peer_mailbox) {
+  using namespace lc;
+  if (!handle || !peer_mailbox) return fail(LC_ERR_INVALID, "lc_peer_open: null argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, LC_PEER_HANDLE_BYTES);
+  return check_cuda(cudaIpcOpenMemHandle(peer_mailbox, h, cudaIpcMemLazyEnablePeerAccess),
+                    "lc_peer_open: cudaIpcOpenMemHandle");
+}
+
+extern "C" int lc_peer_close(void *peer_mailbox) {
+  if (!peer_mailbox) return lc::fail(LC_ERR_INVALID, "lc_peer_close: null mailbox");
+  return lc::check_cuda(cudaIpcCloseMemHandle(peer_mailbox), "lc_peer_close: cudaIpcCloseMemHandle");
+}
+
+extern "C" int lc_peer_reset(void *stream) {
+  using namespace lc;
+  int dev = 0;
+  if (int rc = check_cuda(cudaGetDevice(&dev), "lc_peer_reset: cudaGetDevice")) return rc;
+  if (dev < 0 || dev >= 64) return fail(LC_ERR_UNSUPPORTED, "lc_peer_reset: device %d out of range", dev);
+  void *box = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_peer_mutex);
+    box = g_peer_mailbox[dev];
+  }
+  if (!box) return LC_OK;
+  return check_cuda(cudaMemsetAsync(box, 0, LC_PEER_MAILBOX_BYTES, as_stream(stream)), "lc_peer_reset");
+}
+
+extern "C" int lc_sum_peer_f32(const float *x, int64_t n, const float *count, float *out,
+                               void *const *mailboxes, int world, int rank, void *stream) {
+  using namespace lc;
+  if (!mailboxes || world < 1 || world > LC_PEER_MAX_RANKS || rank < 0 || rank >= world)
+    return fail(LC_ERR_INVALID, "lc_sum_peer_f32: bad rank %d of %d (at most %d ranks)", rank, world,
+                LC_PEER_MAX_RANKS);
+  PeerSet peers{};
+  for (int r = 0; r < world; ++r) {
+    if (!mailboxes[r]) return fail(LC_ERR_INVALID, "lc_sum_peer_f32: null mailbox of rank %d", r);
+    if (!aligned(mailboxes[r], 16)) return fail(LC_ERR_ALIGN, "lc_sum_peer_f32: unaligned mailbox");
+    peers.box[r] = static_cast<PeerBox *>(mailboxes[r]);
+  }
+  peers.world = world;
+  peers.rank = rank;
+  if (int rc = device_error_word(&peers.err)) return rc;
+  return launch_sum("lc_sum_peer_f32", x, n, 3, count, out, nullptr, stream, &peers);
 }

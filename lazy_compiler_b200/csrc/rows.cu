@@ -35,10 +35,20 @@ constexpr bool is_dot(int op) { return op >= kRowDot; }
 
 // y * f(x) of the row dot products, rounded once
 template <int OP>
-__device__ __forceinline__ float dot_term(float x, float y) {
-  if constexpr (OP == kRowDotGeluErf) return __fmul_rn(y, gelu_erf(x));
-  else if constexpr (OP == kRowDotGeluTanh) return __fmul_rn(y, gelu_tanh(x));
-  else return __fmul_rn(y, x);
+__device__ __forceinline__ float dot_factor(float x) {
+  if constexpr (OP == kRowDotGeluErf) return gelu_erf(x);
+  else if constexpr (OP == kRowDotGeluTanh) return gelu_tanh(x);
+  else return x;
+}
+// Adds the term y * f(x) to a compensated row sum: the rounded product by
+// TwoSum and its rounding residual (by FMA) into the correction, as the
+// reference's Dot2 accumulation of this product keeps it (ptx_backend.py:571-593).
+template <int OP>
+__device__ __forceinline__ void add_dot_term(CompSum &acc, float x, float y) {
+  const float fx = dot_factor<OP>(x);
+  const float p = __fmul_rn(y, fx);
+  acc.add(p);
+  acc.c = __fadd_rn(acc.c, __fmaf_rn(y, fx, -p));
 }
 
 struct RowArgs {
@@ -95,10 +105,10 @@ __global__ void __launch_bounds__(1024) row_vec_kernel(RowArgs args) {
         const int64_t idx = threadIdx.x + (int64_t)j * T;
         if (idx < c4) {
           const float4 y = ld_stream(yr + idx);
-          acc.add(dot_term<OP>(v[j].x, y.x));
-          acc.add(dot_term<OP>(v[j].y, y.y));
-          acc.add(dot_term<OP>(v[j].z, y.z));
-          acc.add(dot_term<OP>(v[j].w, y.w));
+          add_dot_term<OP>(acc, v[j].x, y.x);
+          add_dot_term<OP>(acc, v[j].y, y.y);
+          add_dot_term<OP>(acc, v[j].z, y.z);
+          add_dot_term<OP>(acc, v[j].w, y.w);
         }
       }
       const double total = block_sum<double>(acc.value(), dscratch);
@@ -176,7 +186,7 @@ __global__ void __launch_bounds__(256) row_scalar_kernel(RowArgs args) {
     } else if constexpr (is_dot(OP)) {
       const float *yr = args.w + row * args.cols;
       CompSum acc;
-      for (int64_t c = threadIdx.x; c < args.cols; c += blockDim.x) acc.add(dot_term<OP>(xr[c], yr[c]));
+      for (int64_t c = threadIdx.x; c < args.cols; c += blockDim.x) add_dot_term<OP>(acc, xr[c], yr[c]);
       const double total = block_sum<double>(acc.value(), dscratch);
       if (threadIdx.x == 0) args.out[row] = (float)total;
     } else if constexpr (OP == kSoftmax) {

@@ -97,7 +97,10 @@ def block_source(prog: dict, layout: dict) -> str:
     consts = [int(c) & 0xFFFFFFFF for c in prog["consts"]]
     smem = layout["smem"]
     lines = [f"extern \"C\" __global__ void __launch_bounds__({threads}) {KERNEL}(const __grid_constant__ JitArgs p) {{",
-             "  extern __shared__ u32 smem[];"]
+             "  extern __shared__ u32 smem[];",
+             "  // lanes of this warp that exist (a CTA may be one partial warp)",
+             "  const u32 lanes = blockDim.x - (threadIdx.x & ~31u) >= 32u ? 0xffffffffu"
+             " : ((1u << (blockDim.x - (threadIdx.x & ~31u))) - 1u);"]
     lines.append("  u32 " + ", ".join(f"r{i} = 0u" for i in range(n_regs)) + ";")
     lines.append("  i64 " + ", ".join(f"x{d} = 0" for d in range(n_axes + len(loops))) + ";")
     lines.append("  for (i64 blk = blockIdx.x; blk < p.blocks; blk += gridDim.x) {")
@@ -167,7 +170,7 @@ def _statements(prog: dict, smem: list, begin: int = 0, end: int | None = None) 
                 body = f"((u32 *)p.buffers[{aux}])[{at}] = {B};"
             stmt = f"if ({cond}) {{ {body} }}"
         elif name == "SHFL_XOR":
-            stmt = f"__syncwarp(); r{dst} = __shfl_xor_sync(0xffffffffu, {A}, {aux});"
+            stmt = f"__syncwarp(lanes); r{dst} = __shfl_xor_sync(lanes, {A}, {aux});"
         elif name == "LDS":
             off, size = smem[aux]
             stmt = f"r{dst} = smem[{off} + clampi((i64)(int){A}, {size}LL)];"
@@ -177,7 +180,7 @@ def _statements(prog: dict, smem: list, begin: int = 0, end: int | None = None) 
         elif name == "BAR":
             stmt = "__syncthreads();"
         elif name == "WSYNC":
-            stmt = "__syncwarp();"
+            stmt = "__syncwarp(lanes);"
         elif name == "BRA":
             stmt = f"goto L{aux};"
         elif name == "BRZ":

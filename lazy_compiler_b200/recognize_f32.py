@@ -39,6 +39,7 @@ from typing import Any
 import numpy as np
 
 from .ir import CompileError, KernelPackage, Node, static_extent
+from .dot2 import compensated_states
 from .post import compile_epilogue
 from .recognize import (_GELU_ERF_ANY, _GELU_ERF_B_ANY, _GELU_TANH_ANY, Plan, _aff, _aff_add, combines_are,
                         fold_combine, online_combine,
@@ -319,10 +320,11 @@ def recognise_attention(pkg: KernelPackage, tile: Node, ev: _Eval) -> Plan:
         merge.update(online_combine(M_, [L_, S_]))
     fixed = _contraction_form(tile, ev, _loop_info(ev, key), s_kv, states, ev.writes, merge)
     check_cover(pkg, _tile_axes(tile), ev.writes, out, fixed)
-    return _plan(pkg, "attention_f32", "lc_attention_f32",
+    comp = bool(compensated_states(pkg.body, pkg))
+    return _plan(pkg, "attention_f32", "lc_attention_f32_dot2" if comp else "lc_attention_f32",
                  {"scale": c, "q": q, "kt": kt, "v": v, "o": out},
                  {"bh": 1, "s_q": s_q, "s_kv": s_kv, "d": d, "dv": dv, "scale_mode": mode,
-                  "epilogue": epi}, {"io": "f32"})
+                  "epilogue": epi, "compensated": comp}, {"io": "f32"})
 
 
 # ----------------------------------------------------------------------------
@@ -359,8 +361,11 @@ def _gemm_plan(pkg: KernelPackage, a: str, b: str, bias: str | None, out: str, l
             raise CompileError("GEMM bias must be a vector over the output columns")
         _f32(pkg, bias)
         bind["bias"] = bias
-    return _plan(pkg, "gemm", "lc_gemm", bind,
-                 {"m": m, "n": n, "k": k, "b_layout": layout, "epilogue": epi}, {"ab": "f32", "c": "f32"})
+    # the reference compensates the dot accumulation when the package states a tolerance
+    comp = bool(compensated_states(pkg.body, pkg))
+    return _plan(pkg, "gemm", "lc_gemm_f32_dot2" if comp else "lc_gemm", bind,
+                 {"m": m, "n": n, "k": k, "b_layout": layout, "epilogue": epi, "compensated": comp},
+                 {"ab": "f32", "c": "f32"})
 
 
 def _split_bias(inner, is_acc_ok, col):

@@ -43,6 +43,11 @@ SIGNATURES = {
     "lc_sum_f32_noalloc": [_P, _P, _I64, _P],
     "lc_sum_partial_f32": [_P, _I64, _P, _P],
     "lc_sum_finalize": [_P, _P, _P, _P],
+    "lc_peer_mailbox": [ctypes.POINTER(_P), ctypes.c_char_p],
+    "lc_peer_open": [ctypes.c_char_p, ctypes.POINTER(_P)],
+    "lc_peer_close": [_P],
+    "lc_peer_reset": [_P],
+    "lc_sum_peer_f32": [_P, _I64, _P, _P, ctypes.POINTER(_P), _INT, _INT, _P],
     "lc_rowsum_f32": [_P, _P, _I64, _I64, _P],
     "lc_rmsnorm_f32": [_P, _P, _P, _P, _P, _I64, _I64, _P],
     "lc_softmax_f32": [_P, _P, _I64, _I64, _P],
@@ -51,6 +56,8 @@ SIGNATURES = {
     "lc_gemm": [_INT, _INT, _INT, _INT, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_ex": [_INT, _INT, _INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "lc_gemm_path": [_INT, _INT, _P, _P, _I64, _I64, _I64],
+    "lc_gemm_f32_dot2": [_INT, _INT, _P, _P, _P, _P, _I64, _I64, _I64, _P],
+    "lc_attention_f32_dot2": [_INT, _INT, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
     "lc_pointwise": [_P, _P, _P],
     "lc_rowprog": [_P, _P, _P, _P],
     "lc_blockprog": [_P, _P, _P, _P],
@@ -273,6 +280,10 @@ def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
     elif op == "rowdot_f32":
         call("lc_rowdot_f32", EPILOGUES[p["activation"]], ptr("x"), ptr("y"), ptr("out"), p["rows"],
              p["cols"], s)
+    elif op == "gemm" and p.get("compensated"):
+        bias = ptr("bias") if "bias" in b else ctypes.c_void_p(0)
+        call("lc_gemm_f32_dot2", B_LAYOUTS[p["b_layout"]], EPILOGUES[p["epilogue"]], ptr("a"), ptr("b"), bias,
+             ptr("c"), p["m"], p["n"], p["k"], s)
     elif op == "gemm":
         d = plan["dtypes"]
         bias = ptr("bias") if "bias" in b else ctypes.c_void_p(0)
@@ -325,7 +336,7 @@ def launch(plan: dict, pointers: dict, stream: int | None = None) -> None:
              DTYPE_CODES[d["z"]], DTYPE_CODES[d["c"]], B_LAYOUTS[p["y_layout"]], B_LAYOUTS[p["z_layout"]],
              ptr("x"), ptr("y"), ptr("z"), ptr("c"), p["m"], p["k"], p["n1"], p["n2"], s)
     elif op == "attention_f32":
-        call("lc_attention_f32", SCALE_MODES[p["scale_mode"]], EPILOGUES[p["epilogue"]],
+        call("lc_attention_f32_dot2" if p.get("compensated") else "lc_attention_f32", SCALE_MODES[p["scale_mode"]], EPILOGUES[p["epilogue"]],
              ptr("scale"), ptr("q"), ptr("kt"), ptr("v"), ptr("o"), p["bh"], p["s_q"], p["s_kv"],
              p["d"], p["dv"], s)
     elif op == "attention_tile_f16q":

@@ -18,7 +18,13 @@ csrc/pointwise.cu:
 * values computed before a loop and read inside it stay live for the whole
   loop (the register allocator extends them across the back edge);
 * every output element must be written exactly once over the tile points
-  and the loop iterations that enclose the write.
+  and the loop iterations that enclose the write;
+* when the package states a tolerance, the dot accumulators the reference
+  compensates (``dot2.compensated_states``) carry a second fixed register
+  with the Dot2 correction: the product statement's update is TwoProduct by
+  FMA plus TwoSum (ptx_backend.py:571-593), every read adds the correction
+  while the high part is finite (:539-552), and every other write clears it
+  (:554-569).
 
 Loops with a per-thread start, a captured end or a non-unit step, and
 conditional statements, are not taken here.
@@ -29,6 +35,7 @@ import math
 
 import numpy as np
 
+from .dot2 import adjacent_dot, compensated_states
 from .ir import CompileError, KernelPackage, Node, static_extent
 from .pointwise import MAX_AXES, MAX_CODE, MAX_CONST, OP, PointwiseCompiler, Program, Val, vm_type
 
@@ -51,6 +58,9 @@ class SerialCompiler(PointwiseCompiler):
         self.n_fixed = 0
         self.store_loops: list = []     # (buffer, form, enclosing loop slots)
         self.active: dict = {}          # loop variable -> its coordinate in the innermost enclosing loop
+        self.compensated = compensated_states(tuple(tile.body), pkg)
+        self.lows: dict = {}            # compensated accumulator -> fixed register of its correction
+        self.previous = None            # the statement before the current one in its body
 
     def affine(self, e) -> dict:
         if isinstance(e, Node) and e.kind == "Var" and e.name in self.active:
@@ -78,6 +88,7 @@ class SerialCompiler(PointwiseCompiler):
         elif k == "Init":
             reg = self.acc_register(s.name)
             self.put(reg, self.literal(float(s.identity), vm_type(s.get("dtype") or "f32")))
+            self.clear_low(s.name)
         elif k == "Write":
             before = len(self.writes)
             super().statement(s)
@@ -99,16 +110,55 @@ class SerialCompiler(PointwiseCompiler):
     def put(self, reg: int, v: Val) -> None:
         self.code.append((OP["MOV"], reg, self.convert(v, "f32").reg, 0, 0, 0, 1, True))
 
+    # ------------------------------------------------------------ compensated (Dot2) states
+    def low_register(self, name: str) -> int:
+        if name not in self.lows:
+            self.lows[name] = -1 - self.n_fixed
+            self.n_fixed += 1
+        return self.lows[name]
+
+    def clear_low(self, name: str) -> None:
+        if name in self.compensated:
+            self.put(self.low_register(name), self.literal(0.0, "f32"))
+
+    def lookup(self, name: str) -> Val:
+        v = super().lookup(name)
+        if name in self.compensated and name in self.accs and v.reg == self.accs[name]:
+            # high + correction while high is finite (a non-finite high stays as it is)
+            low = Val(self.low_register(name), "f32")
+            finite = self.compare("lt", self.emit("FABS", "f32", v), self.literal(float("inf"), "f32"))
+            return self.emit("FADD", "f32", v, self.select(finite, low, self.literal(0.0, "f32"), "f32"))
+        return v
+
+    def compensated_dot(self, s: Node, product: Node) -> None:
+        """Dot2 step: TwoProduct residual by FMA, TwoSum of high and the product, correction sum."""
+        hi = Val(self.acc_register(s.name), "f32")
+        lo = Val(self.low_register(s.name), "f32")
+        p = self.convert(self.lookup(product.name), "f32")
+        a, b = (self.convert(self.lookup(n) if isinstance(n, str) else self.expr(n), "f32") for n in product.args)
+        residual = self.fma(a, b, self.emit("FNEG", "f32", p))
+        total = self.emit("FADD", "f32", hi, p)
+        delta = self.emit("FSUB", "f32", total, hi)
+        error = self.emit("FADD", "f32", self.emit("FSUB", "f32", hi, self.emit("FSUB", "f32", total, delta)),
+                          self.emit("FSUB", "f32", p, delta))
+        self.put(lo.reg, self.emit("FADD", "f32", lo, self.emit("FADD", "f32", error, residual)))
+        self.put(hi.reg, total)
+        self.env[s.name] = hi
+
     def accum(self, s: Node) -> None:
         op = s.op.name if isinstance(s.op, Node) else str(s.op)
-        reg = self.acc_register(s.name)
-        base = self.lookup(s.base) if s.get("base") else Val(reg, "f32")
-        value = self.lookup(s.value) if isinstance(s.value, str) else self.expr(s.value)
         dt = vm_type(s.get("dtype") or "f32")
         if dt != "f32":
             raise CompileError("serial accumulators are f32")
+        if s.name in self.compensated and adjacent_dot(self.previous, s):
+            self.compensated_dot(s, self.previous)
+            return
+        reg = self.acc_register(s.name)
+        base = self.lookup(s.base) if s.get("base") else self.lookup(s.name)
+        value = self.lookup(s.value) if isinstance(s.value, str) else self.expr(s.value)
         new = self.operation(op, [self.convert(base, "f32"), self.convert(value, "f32")], "f32")
         self.put(reg, new)
+        self.clear_low(s.name)
         self.env[s.name] = Val(reg, "f32")
 
     def loop(self, s: Node) -> None:
@@ -138,14 +188,18 @@ class SerialCompiler(PointwiseCompiler):
                     if op not in IDENTITY:
                         raise CompileError(f"no identity for accumulator operation {op}")
                     self.put(self.acc_register(inner.name), self.literal(IDENTITY[op], "f32"))
+                    self.clear_low(inner.name)
         self.__dict__["_memo"] = {}
         count = self.literal(extent, "s32")
         begin = len(self.code)
         self.code.append(None)
         self.loop_stack.append((depth, extent))
         saved = dict(self.env)
+        previous = None
         for inner in s.body:
+            self.previous = previous
             self.statement(inner)
+            previous = inner
         # names bound inside the loop go out of scope; accumulators stay visible
         self.env = {**saved, **{n: Val(r, "f32") for n, r in self.accs.items()}}
         self.loop_stack.pop()
@@ -201,8 +255,11 @@ class SerialCompiler(PointwiseCompiler):
         return out
 
     def compile_serial(self, body: tuple) -> Program:
+        previous = None
         for s in body:
+            self.previous = previous
             self.statement(s)
+            previous = s
         if not self.store_loops:
             raise CompileError("serial program writes nothing")
         out = self.serial_coverage()

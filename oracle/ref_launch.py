@@ -1,4 +1,4 @@
-"""Launches the reference compiler's PTX on the GPU — TEST INFRASTRUCTURE ONLY.
+"""Launches the reference compiler's PTX on the GPU — TEST AND BASELINE INFRASTRUCTURE ONLY.
 
 The PTX in ``oracle/_ref/ptx`` is what the reference's own ``compile_file``
 emitted for each package (``oracle/ref_ptx.py``, hashes checked against the
@@ -7,7 +7,10 @@ reference's records).  This module JIT-loads it with the CUDA driver
 geometry with `.u64` arguments in ``arg_order`` — the reference's launcher
 contract (tools/check_compiler.py:291-422): seeded inputs, outputs prefilled
 with NaN / -1, ``zero_outputs`` zeroed before every launch.  Device memory
-comes from PyTorch; the PTX text is never parsed or modified.
+comes from PyTorch; the PTX text is never parsed or modified.  Used by the
+tests (parity with this backend) and by ``bench.py``'s reference-PTX
+baseline leg (the reference's own kernels timed on the same B200); never by
+the product.
 """
 from __future__ import annotations
 

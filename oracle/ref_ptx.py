@@ -53,6 +53,14 @@ PACKAGES = [
 ]
 
 
+# This repository's own packages of the reference's Dot2 known-answer cases
+# (tests/golden/make_precision.py), compiled by the reference the same way.
+LOCAL_PACKAGES = ["precision_dot_product_and_sum_residual", "precision_dot_seed_false_slabs",
+                  "precision_dot_nested_reset", "precision_dot_shuffle_snapshot",
+                  "precision_dot_half_inputs_float_state", "precision_dot_standalone_initial_update",
+                  "precision_dot_followed_by_explicit_base"]
+
+
 def sha(text: str) -> str:
     return hashlib.sha256(text.encode("ascii")).hexdigest()
 
@@ -80,8 +88,9 @@ def main(reference: Path) -> int:
     (OUT / "ptx").mkdir(parents=True, exist_ok=True)
     manifest = {}
     failures = 0
-    for rel in PACKAGES:
-        folder = reference / rel
+    golden = HERE.parent / "tests" / "golden" / "packages"
+    for rel in PACKAGES + [f"local:{name}" for name in LOCAL_PACKAGES]:
+        folder = golden / rel[6:] if rel.startswith("local:") else reference / rel
         (ir,) = sorted(folder.glob("*.ir.json"))
         name = folder.name
         row = {"source": f"{rel}/{ir.name}"}

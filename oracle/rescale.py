@@ -25,7 +25,8 @@ OUT = HERE / "_ref"
 N28, N24 = 1 << 28, 1 << 24
 ROWS, COLS = 16384, 4096
 
-# name: (source package, {axis name: new extent}, {buffer: new shape}, grid x, {constant: value})
+# name: (source package, {axis name: new extent}, {buffer: new shape}, grid x, {constant: value}
+#        [, {integer literal of the index arithmetic: new value}])
 PLAN = {
     "r02_big_sum": ("problems/r02_big_sum", {"a0": N24}, {"x": [N24]}, 1, {}),
     "r03_mean": ("problems/r03_mean", {"a0": N24}, {"x": [N24]}, 1, {"mean_keepdim_count": float(N24)}),
@@ -37,6 +38,9 @@ PLAN = {
                      N28 // 4 // 256, {}),
     "phase9_gelu_erf_tail": ("examples/phase9/generated/phase9_gelu_erf_tail", {"a0": N28},
                              {"x": [N28], "gelu": [N28]}, N28 // 256, {}),
+    "phase9_gelu_tanh_matrix": ("examples/phase9/generated/phase9_gelu_tanh_matrix", {"a0": N28},
+                                {"x": [N28 // COLS, COLS], "gelu": [N28 // COLS, COLS]}, N28 // 256, {},
+                                {137: COLS}),
     "r04_row_sum": ("problems/r04_row_sum", {"a0": ROWS, "a1": COLS}, {"x": [ROWS, COLS], "sum_1": [ROWS]},
                     ROWS, {}),
     "f01_rmsnorm": ("problems/f01_rmsnorm", {"a0": ROWS, "a1": COLS, "a2": COLS},
@@ -57,14 +61,24 @@ def rescale_body(text: str, axes: dict) -> str:
     return text
 
 
+def rescale_literals(text: str, literals: dict) -> str:
+    for old, new in literals.items():
+        text, count = re.subn(rf"Literal\(value={old}, dtype='int'\)", f"Literal(value={new}, dtype='int')", text)
+        if count == 0:
+            raise ValueError(f"integer literal {old} not found")
+    return text
+
+
 def make(reference: Path, name: str) -> Path:
-    src_rel, axes, shapes, grid_x, constants = PLAN[name]
+    src_rel, axes, shapes, grid_x, constants, *rest = PLAN[name]
+    literals = rest[0] if rest else {}
     src = reference / src_rel
     (ir_path,) = sorted(src.glob("*.ir.json"))
     graph = json.loads(ir_path.read_text())
     for node in graph["nodes"].values():
         if node["op"] == "KernelOp":
-            node["op_fields"]["body"] = [rescale_body(b, axes) for b in node["op_fields"]["body"]]
+            node["op_fields"]["body"] = [rescale_literals(rescale_body(b, axes), literals)
+                                         for b in node["op_fields"]["body"]]
         for out in node.get("outputs", []):
             if out["name"] in shapes:
                 out["shape"] = shapes[out["name"]]

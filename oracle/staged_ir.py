@@ -22,14 +22,19 @@ atomic Writes) and any body built from the same statements:
   seeding loop; integer index division and remainder as on non-negative
   values, TernaryExpr indices per thread.
 
-Scalar rules and accurate float64 transcendentals come from
-oracle/pointwise_ir.py.  It shares only the IR reader with the product.
+When the package states a tolerance, the dot accumulators the reference
+compensates are Dot2 pairs (oracle/dot2_ir.py), read as hi + lo; shuffle and
+tree merges and every other write clear lo.  Scalar rules and accurate
+float64 transcendentals come from oracle/pointwise_ir.py.  It shares only
+the IR reader with the product.
 """
 from __future__ import annotations
 
 import math
 
 import numpy as np
+
+from oracle import dot2_ir
 
 from oracle.pointwise_ir import PointwiseOracle, V, _t, conv
 from oracle.serial_ir import _IDENTITY
@@ -97,8 +102,32 @@ class StagedOracle(PointwiseOracle):
         return np.where(self.mask, flat, 0)
 
     # -------------------------------------------------------- statements
+    # -------------------------------------------------------- compensated (Dot2) states
+    def comp(self) -> set:
+        return self.__dict__.setdefault("_comp", dot2_ir.compensated(self.pkg.body, self.pkg))
+
+    def put(self, name, new, lo=None, masked=True) -> None:
+        """An accumulator's new value where the threads are active; a compensated one
+        keeps (hi, lo) and reads as their value, every other write clearing lo."""
+        new = np.broadcast_to(np.asarray(new, np.float32), (self.n,))
+        lo = np.zeros(self.n, np.float32) if lo is None else np.broadcast_to(lo, (self.n,))
+        old = self.env.get(name)
+        if name in self.comp():
+            pairs = self.__dict__.setdefault("_dot2", {})
+            old_hi, old_lo = pairs.get(name, (np.zeros(self.n, np.float32), np.zeros(self.n, np.float32)))
+            hi = np.where(self.mask, new, old_hi) if masked else np.array(new)
+            lo = np.where(self.mask, lo, old_lo) if masked else np.array(lo)
+            pairs[name] = (hi.astype(np.float32), lo.astype(np.float32))
+            self.env[name] = V(dot2_ir.value(*pairs[name]), "f32")
+        elif masked and old is not None:
+            self.env[name] = V(np.where(self.mask, new, conv(old, "f32").a), "f32")
+        else:
+            self.env[name] = V(np.array(new, np.float32), "f32")
+
     def run_block(self, body) -> None:
+        previous = None
         for s in body:
+            prev, previous = previous, s
             k = s.kind
             if k == "Smem":
                 shape = tuple(int(x) for x in s.extents)
@@ -124,14 +153,18 @@ class StagedOracle(PointwiseOracle):
             elif k in ("Loop", "StridedLoop"):
                 self.loop(s)
             elif k == "Init":
-                self.env[s.name] = V(np.full(self.n, float(s.identity), np.float32), "f32")
+                self.put(s.name, np.full(self.n, float(s.identity), np.float32), masked=False)
+            elif k == "Accum" and s.name in self.__dict__.get("_dot2", {}) and dot2_ir.adjacent(prev, s):
+                hi, lo = self._dot2[s.name]
+                a, b = (conv(self.env[x] if isinstance(x, str) else self.expr(x), "f32").a for x in prev.args)
+                self.put(s.name, *dot2_ir.step(hi, lo, np.broadcast_to(a, (self.n,)), np.broadcast_to(b, (self.n,))))
             elif k == "Accum":
                 opname = s.op.name if hasattr(s.op, "name") else str(s.op)
                 old = self.env[s.name]
                 base = self.env[s.base] if s.get("base") else old
                 value = self.env[s.value] if isinstance(s.value, str) else self.expr(s.value)
                 new = conv(self.op(opname, [conv(base, "f32"), conv(value, "f32")], "f32"), "f32")
-                self.env[s.name] = V(np.where(self.mask, new.a, conv(old, "f32").a), "f32")
+                self.put(s.name, new.a)
             elif k == "Cond":
                 saved = self.mask
                 self.mask = saved & np.broadcast_to(conv(self.expr(s.cond), "pred").a, (self.n,))
@@ -216,10 +249,8 @@ class StagedOracle(PointwiseOracle):
             for inner in s.body:
                 if inner.kind == "Accum":
                     opname = inner.op.name if hasattr(inner.op, "name") else str(inner.op)
-                    old = self.env.get(inner.name)
                     seed = np.full(self.n, _IDENTITY[opname], np.float32)
-                    self.env[inner.name] = V(seed if old is None else np.where(self.mask, seed,
-                                                                               conv(old, "f32").a), "f32")
+                    self.put(inner.name, seed, masked=inner.name in self.env)
         saved = self.mask
         i = 0
         while True:
@@ -237,13 +268,18 @@ class StagedOracle(PointwiseOracle):
     def merge(self, s) -> None:
         for a in s.combine_states:
             opname = a.op.name if hasattr(a.op, "name") else str(a.op)
-            self.env[a.name] = conv(self.op(opname, [conv(self.env[x], "f32") for x in a.args], "f32"), "f32")
+            new = conv(self.op(opname, [conv(self.env[x], "f32") for x in a.args], "f32"), "f32")
+            if a.name in s.state:
+                self.put(a.name, new.a, masked=False)
+            else:
+                self.env[a.name] = new
 
     def shuffle(self, s) -> None:
         """The reference's butterfly: at each level every lane takes the states of
         the lane ``delta`` away and runs the combine statements."""
-        if self.threads % 32 and int(s.length) > 1:
-            raise ValueError("oracle: shuffles need whole warps")
+        partial = self.threads < 32 and not self.threads & (self.threads - 1) and int(s.length) <= self.threads
+        if self.threads % 32 and int(s.length) > 1 and not partial:
+            raise ValueError("oracle: shuffles need whole warps (or one power-of-two partial warp)")
         saved = dict(self.env)
         points = np.arange(self.n)
         delta = int(s.length) // 2
@@ -289,7 +325,7 @@ class StagedOracle(PointwiseOracle):
         self.env = saved
         for buf, name in zip(s.bufs, s.state):
             arr = self.smem[buf]
-            self.env[name] = V(arr[self.block, np.clip(base, 0, arr.shape[1] - 1)], "f32")
+            self.put(name, arr[self.block, np.clip(base, 0, arr.shape[1] - 1)], masked=False)
 
     def result(self) -> dict:
         return {k: v.reshape(tuple(self.pkg.buffers[k].shape) or (1,)) for k, v in self.out.items()}

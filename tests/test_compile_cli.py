@@ -31,15 +31,20 @@ EXPECTED = {
     "phase9_half_gelu_gemm": ("gemm", {"m": 17, "n": 21, "k": 33, "b_layout": "kn", "epilogue": "gelu_tanh"}),
     "generated_tensor": ("gemm", {"m": 11, "n": 19, "k": 7, "b_layout": "kn", "epilogue": "none"}),
     # FP32 contraction classes: staged (cp.async, split-K), serial and block-cooperative schedules
-    "m01_matmul_512": ("gemm", {"m": 512, "n": 512, "k": 512, "b_layout": "kn", "epilogue": "none"}),
-    "m02_matmul_rect": ("gemm", {"m": 128, "n": 64, "k": 256, "b_layout": "kn", "epilogue": "none"}),
-    "phase9_bias_gelu_gemm": ("gemm", {"m": 33, "n": 47, "k": 65, "b_layout": "kn", "epilogue": "gelu_erf"}),
+    # (every one states a tolerance, so the reference compensates its dot products: Dot2)
+    "m01_matmul_512": ("gemm", {"m": 512, "n": 512, "k": 512, "b_layout": "kn", "epilogue": "none",
+                                "compensated": True}),
+    "m02_matmul_rect": ("gemm", {"m": 128, "n": 64, "k": 256, "b_layout": "kn", "epilogue": "none",
+                                 "compensated": True}),
+    "phase9_bias_gelu_gemm": ("gemm", {"m": 33, "n": 47, "k": 65, "b_layout": "kn", "epilogue": "gelu_erf",
+                                       "compensated": True}),
     "a01_attention": ("attention_f32", {"bh": 1, "s_q": 64, "s_kv": 64, "d": 64, "dv": 64,
-                                        "scale_mode": "mul_recip", "epilogue": "none"}),
+                                        "scale_mode": "mul_recip", "epilogue": "none", "compensated": True}),
     "a02_attention_128": ("attention_f32", {"bh": 1, "s_q": 128, "s_kv": 128, "d": 32, "dv": 32,
-                                            "scale_mode": "mul_recip", "epilogue": "none"}),
+                                            "scale_mode": "mul_recip", "epilogue": "none", "compensated": True}),
     "phase9_gelu_attention": ("attention_f32", {"bh": 1, "s_q": 11, "s_kv": 37, "d": 17, "dv": 13,
-                                                "scale_mode": "mul", "epilogue": "gelu_erf"}),
+                                                "scale_mode": "mul", "epilogue": "gelu_erf",
+                                                "compensated": True}),
     "phase9_gelu_row_dot": ("rowdot_f32", {"rows": 19, "cols": 131, "activation": "gelu_erf"}),
     "fragment_attention_tile_f16": ("attention_tile_f16q", {"bh": 1, "s_q": 16, "s_kv": 16, "d": 16,
                                                             "dv": 8}),

@@ -21,7 +21,7 @@ from lazy_compiler_b200.compiler import compile_file
 from lazy_compiler_b200.ir import CompileError
 from lazy_compiler_b200.runner import run_package, seeded_input
 from oracle import expressions as O
-from refptx import RefKernel, manifest
+from oracle.ref_launch import RefKernel, manifest
 
 pytestmark = pytest.mark.gpu
 

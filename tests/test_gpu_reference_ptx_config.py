@@ -16,7 +16,7 @@ import pytest
 
 from lazy_compiler_b200.runner import run_package
 from oracle import expressions as O
-from refptx import REF, RefKernel, manifest_rescaled
+from oracle.ref_launch import REF, RefKernel, manifest_rescaled
 
 pytestmark = pytest.mark.gpu
 
