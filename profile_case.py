@@ -5,9 +5,12 @@
 
 OP is one of add, axpb, relumul, gelu_erf, gelu_tanh, sum, mean, rowsum,
 rmsnorm, softmax, l2norm, gemm_f16, gemm_bf16, gemm_f32, attention_f32, sdpa,
-or general_paths (each golden package's fixed-class plan against the same
+general_paths (each golden package's fixed-class plan against the same
 package run as a block program, natively compiled and interpreted; host call
-included).  Inputs are seeded device tensors; every launch goes through the
+included), or sum_graph (``--repeat`` back-to-back lc_sum_f32 launches on
+``--n`` elements replayed from one CUDA graph over enough rotating copies of
+the input that the others exceed twice the L2, as bench.py times the reduce
+configuration; prints the mean time per launch).  Inputs are seeded device tensors; every launch goes through the
 C ABI.  The mean CUDA-event time of the repeated launches is printed
 (``--repeat`` launches after ``--warmup``), so the same command line serves
 an ncu capture (``-k`` the kernel, ``-s`` the warm-up launches, ``-c`` one to
@@ -29,6 +32,40 @@ from lazy_compiler_b200 import runtime  # noqa: E402
 
 GENERAL_PACKAGES = ["r01_array_sum", "r04_row_sum", "f01_rmsnorm", "f02_row_softmax", "phase9_gelu_attention",
                     "a02_attention_128", "m02_matmul_rect", "m01_matmul_512"]
+
+
+def sum_graph(n: int, repeat: int) -> None:
+    """Per-launch time of lc_sum_f32 on n elements, launched back to back from one CUDA graph."""
+    import torch
+    copies = max(1, -(-2 * 126 * 10 ** 6 // (4 * n)) + 1) if 4 * n < 2 * 126 * 10 ** 6 else 1
+    xs = [torch.rand(n, device="cuda") * 2 - 1 for _ in range(copies)]
+    out = torch.empty(1, device="cuda")
+    stream = torch.cuda.Stream()
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def launch(i):
+        runtime.call("lc_sum_f32", P(xs[i % copies]), P(out), n,
+                     ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            launch(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(repeat):
+            launch(i)
+    times = []
+    for _ in range(5):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            graph.replay()
+            end.record(stream)
+        torch.cuda.synchronize()
+        times.append(start.elapsed_time(end) / repeat)
+    ms = sorted(times)[len(times) // 2]
+    print(json.dumps({"op": "sum_graph", "n": n, "copies": copies, "us_per_launch": round(ms * 1e3, 3),
+                      "GB/s": round(4 * n / (ms / 1e3) / 1e9, 1)}))
 
 
 def general_paths(repeat: int) -> None:
@@ -100,6 +137,10 @@ def main() -> None:
     op = a.op
     if op == "general_paths":
         general_paths(max(a.repeat, 10))
+        return
+    if op == "sum_graph":
+        for n in ([a.n] if a.n else [1024, 1 << 20, 1 << 22, 1 << 23, 1 << 24, 1 << 25, 1 << 26, 1 << 28]):
+            sum_graph(n, max(a.repeat, 20))
         return
     if op in ("add", "axpb", "relumul", "gelu_erf", "gelu_tanh", "sum", "mean"):
         n = a.n or (1 << 28 if op not in ("sum", "mean") else 1 << 24)

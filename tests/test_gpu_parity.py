@@ -86,7 +86,8 @@ def test_golden_package(name, cuda_device):
 @pytest.mark.parametrize("name", PACKAGES)
 @pytest.mark.parametrize("offset", [1, 7])
 def test_package_alternate_seeds_against_oracle(name, offset, cuda_device):
-    """Alternate seeds (the reference harness's seed_offset), checked against the oracle."""
+    """Alternate seeds (the reference harness's seed_offset), checked against the oracle of the plan's
+    class and against the IR oracle chosen from the IR alone (a misclassified package fails the latter)."""
     from lazy_compiler_b200.compiler import compile_file
     from conftest import golden_ir
     meta = golden_meta(name)
@@ -97,6 +98,11 @@ def test_package_alternate_seeds_against_oracle(name, offset, cuda_device):
     out = run_package(golden(name), seed_offset=offset)
     for key, value in ref.items():
         assert_close(out[key], value, meta["rtol"], meta["atol"])
+    # and against what the IR says, with an oracle chosen from the IR alone (not from the plan)
+    from ir_oracles import ir_oracle, supported
+    if supported(golden_ir(name)) and name != "m01_matmul_512":
+        for key, value in ir_oracle(golden_ir(name), arrays).items():
+            assert_close(np.asarray(out[key]).reshape(value.shape), value, meta["rtol"], meta["atol"])
 
 
 # ---------------------------------------------------------------- pointwise edge cases

@@ -18,8 +18,8 @@ import pytest
 
 import pw_vm
 from conftest import golden
+from ir_oracles import ir_oracle
 from lazy_compiler_b200.compiler import compile_file
-from lazy_compiler_b200.ir import load_package
 from oracle import expressions as O
 
 BINARY = ["add", "subtract", "multiply", "maximum", "minimum"]
@@ -78,21 +78,6 @@ def mutate(text: str, seed: int) -> tuple:
     return text, changes
 
 
-def ir_oracle(ir, arrays):
-    pkg = load_package(ir)
-    tile = pkg.body[0]
-    kinds = {s.kind for s in tile.body}
-    if any(k.startswith(("Fragment", "RegFragment", "RegStore", "MmaSync", "Ldmatrix")) for k in kinds):
-        from oracle import fragment_ir
-        return fragment_ir.evaluate(ir, arrays)
-    if tile.get("block_threads"):
-        from oracle import staged_ir
-        return staged_ir.evaluate(ir, arrays)
-    if kinds & {"Loop", "StridedLoop"}:
-        from oracle import serial_ir
-        return serial_ir.evaluate(ir, arrays)
-    from oracle import pointwise_ir
-    return pointwise_ir.evaluate(ir, arrays)
 
 
 def run_plan_cpu(plan, arrays, ir):
