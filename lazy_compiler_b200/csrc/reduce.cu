@@ -108,27 +108,23 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// Run by every thread of the last CTA: exchange `total` with the peers and
+// Run by the first warp of the last CTA: exchange `total` with the peers and
 // return the sum over all ranks (NaN if a peer did not arrive in time).
-__device__ double peer_exchange(double total, const PeerSet &peers, double *values, int *failed,
-                                unsigned int *epoch_sh) {
+__device__ double peer_exchange(double total, const PeerSet &peers) {
   PeerBox *mine = peers.box[peers.rank];
   const int t = threadIdx.x;
-  if (t == 0) {
-    *failed = 0;
-    *epoch_sh = *reinterpret_cast<volatile unsigned int *>(&mine->epoch) + 1u;
-  }
-  __syncthreads();
-  const unsigned int epoch = *epoch_sh;
+  unsigned int epoch = 0;
+  if (t == 0) epoch = *reinterpret_cast<volatile unsigned int *>(&mine->epoch) + 1u;
+  epoch = __shfl_sync(0xffffffffu, epoch, 0);
   const unsigned int slot = epoch & 1u;
+  double value = 0.0;
+  bool ok = true;
   if (t < peers.world) {
     PeerBox *dst = peers.box[t];
     st_relaxed_sys_f64(&dst->partial[slot][peers.rank], total);
     st_release_sys(&dst->flag[slot][peers.rank], epoch);  // orders the store above
-  }
-  if (t < peers.world) {
     const unsigned int *flag = &mine->flag[slot][t];
-    bool ok = ld_acquire_sys(flag) == epoch;
+    ok = ld_acquire_sys(flag) == epoch;
     if (!ok) {
       const uint64_t start = globaltimer_ns();
       for (uint32_t i = 1; !ok; ++i) {
@@ -136,19 +132,14 @@ __device__ double peer_exchange(double total, const PeerSet &peers, double *valu
         if (!ok && (i & 63) == 0 && globaltimer_ns() - start > kPeerWaitLimitNs) break;
       }
     }
-    if (ok) {
-      values[t] = ld_relaxed_sys_f64(&mine->partial[slot][t]);
-    } else {
-      values[t] = 0.0;
-      atomicExch(failed, 1);
-      if (peers.err) atomicCAS(peers.err, 0, kErrTimeoutPeer);
-    }
+    if (ok) value = ld_relaxed_sys_f64(&mine->partial[slot][t]);
+    else if (peers.err) atomicCAS(peers.err, 0, kErrTimeoutPeer);
   }
-  __syncthreads();
+  const bool failed = __any_sync(0xffffffffu, !ok);
   double sum = 0.0;
-  for (int r = 0; r < peers.world; ++r) sum += values[r];  // rank order on every rank
+  for (int r = 0; r < peers.world; ++r) sum += __shfl_sync(0xffffffffu, value, r);  // rank order
   if (t == 0) *reinterpret_cast<volatile unsigned int *>(&mine->epoch) = epoch;
-  return *failed ? __longlong_as_double(0x7ff8000000000000ll) : sum;
+  return failed ? __longlong_as_double(0x7ff8000000000000ll) : sum;
 }
 
 // mode 0: out = sum; mode 1: out = sum / count[0]; mode 2: partial_out = sum (f64);
@@ -162,9 +153,6 @@ __global__ void __launch_bounds__(kThreads, kBlocksPerSm) sum_kernel(const float
                                                        double *__restrict__ partial_out,
                                                        const PeerSet peers) {
   __shared__ double scratch[32];
-  __shared__ double values[LC_PEER_MAX_RANKS];
-  __shared__ int failed;
-  __shared__ unsigned int epoch_sh;
   __shared__ bool is_last;
   CompSum acc;
   if (VEC) accumulate(acc, x, n);
@@ -172,17 +160,19 @@ __global__ void __launch_bounds__(kThreads, kBlocksPerSm) sum_kernel(const float
   const double block_total = block_sum<double>(acc.value(), scratch);
   if (threadIdx.x == 0) {
     partials[blockIdx.x] = block_total;
-    __threadfence();
-    const unsigned int ticket = atomicAdd(counter, 1u);
+    // the ticket releases this CTA's partial and, for the last CTA, acquires all of them
+    unsigned int ticket;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(ticket) : "l"(counter) : "memory");
     is_last = (ticket == gridDim.x - 1);
   }
   __syncthreads();
-  if (!is_last) return;
-  __threadfence();
+  if (!is_last || threadIdx.x >= 32) return;
+  // the last CTA's first warp adds the partials in a fixed order (lane-strided, then
+  // the butterfly), so the result does not depend on which CTA finished last
   double t = 0.0;
-  for (int i = threadIdx.x; i < (int)gridDim.x; i += kThreads) t += __ldcg(partials + i);
-  double total = block_sum<double>(t, scratch);
-  if (mode == 3) total = peer_exchange(total, peers, values, &failed, &epoch_sh);
+  for (int i = threadIdx.x; i < (int)gridDim.x; i += 32) t += __ldcg(partials + i);
+  double total = warp_sum(t);
+  if (mode == 3) total = peer_exchange(total, peers);
   if (threadIdx.x == 0) {
     if (mode == 0) out[0] = (float)total;
     else if (mode == 1) out[0] = (float)(total / (double)__ldg(count));
