@@ -636,6 +636,12 @@ REF_PTX = {
     "reduce": [("sum", "r02_big_sum", 4 << 24), ("mean", "r03_mean", 4 << 24)],
     "rows": [("rmsnorm", "f01_rmsnorm", 8 * ROWS * COLS + 4 * COLS), ("softmax", "f02_row_softmax", 8 * ROWS * COLS),
              ("l2norm", "f03_l2norm", 8 * ROWS * COLS), ("rowsum", "r04_row_sum", 4 * ROWS * COLS + 4 * ROWS)],
+    # the reference's mma.sync GEMM (tanh-GELU epilogue, f16 out) rescaled to 8192^3; ours is timed
+    # on the same buffers through the plan of the same rescaled package (same epilogue and output)
+    "gemm_f16": [("gemm_f16 (tanh-GELU, f16 out)", "phase9_half_gelu_gemm", 2 * 8192 ** 3)],
+    # the reference's scalar attention (a02 schedule, f16 loads, D = 128, 4096 keys) on a slice of
+    # 512 query rows of one head; its rate stands for the whole configuration (linear in rows, heads)
+    "sdpa": [("sdpa_f16", "a02_attention_f16_slice", 4 * 512 * 4096 * 128)],
 }
 
 
@@ -678,6 +684,7 @@ def ref_ptx_baseline(config, ours_ms):
             _, buffers = kernel.run(inputs, keep=True)
             ptrs = {n: t.data_ptr() for n, t in buffers.items()}
             stream = torch.cuda.current_stream().cuda_stream
+            tensor = config in GEMM_SHAPES or config == "sdpa"
             # warm the GPU (clocks ramp down while idle): launch for at least 0.3 s first
             t0 = time.perf_counter()
             while time.perf_counter() - t0 < 0.3:
@@ -692,7 +699,28 @@ def ref_ptx_baseline(config, ours_ms):
                 torch.cuda.synchronize()
                 times.append(start.elapsed_time(end))
             ms = statistics.median(times)
-            ops[op] = {"package": f"{name} (rescaled)", "ms": round(ms, 4), "GB/s": round(nbytes / ms / 1e6, 1),
+            if config == "sdpa":
+                # ours: the configuration's own kernel, compared per flop
+                bh, sq, d = SDPA_SHAPE
+                ours_ms = {op: ours_ms[op] * nbytes / (4 * bh * sq * sq * d)} if op in ours_ms else {}
+            elif tensor:
+                # ours on the same buffers: the plan this backend makes of the same rescaled package
+                from lazy_compiler_b200.compiler import compile_file
+                from lazy_compiler_b200.runtime import launch
+                from oracle.ref_launch import REF
+                (ir,) = sorted((REF.parent.parent / rows[name]["package"]).glob("*.ir.json"))
+                plan = compile_file(ir)
+                for _ in range(3):
+                    launch(plan, ptrs, stream)
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record()
+                for _ in range(REF_PTX_REPEATS):
+                    launch(plan, ptrs, stream)
+                end.record()
+                torch.cuda.synchronize()
+                ours_ms = {op: start.elapsed_time(end) / REF_PTX_REPEATS}
+            rate = {"TFLOP/s": round(nbytes / ms / 1e9, 1)} if tensor else {"GB/s": round(nbytes / ms / 1e6, 1)}
+            ops[op] = {"package": f"{name} (rescaled)", "ms": round(ms, 4), **rate,
                        "ours_ms": round(ours_ms.get(op, float("nan")), 4),
                        "speedup": round(ms / ours_ms[op], 2) if op in ours_ms else None,
                        "grid": kernel.kernel_meta["grid"], "block": kernel.kernel_meta["block"]}
@@ -700,9 +728,13 @@ def ref_ptx_baseline(config, ours_ms):
             total_ms += ms
             del buffers, inputs
         torch.cuda.empty_cache()
+        tensor = config in GEMM_SHAPES or config == "sdpa"
+        note = ("; sdpa: a slice of 512 query rows of one head, its rate extrapolated to the whole "
+                "configuration, ours_ms scaled to the slice's flops" if config == "sdpa" else "")
         return {"kind": "the reference compiler's own PTX (public IR packages rescaled to the configuration "
-                        "size, its meta.json geometry) on this B200",
-                "value": round(total_bytes / total_ms / 1e6, 1), "unit": "GB/s", "ops": ops}
+                        "size, its meta.json geometry) on this B200" + note,
+                "value": round(total_bytes / total_ms / (1e9 if tensor else 1e6), 1),
+                "unit": "TFLOP/s" if tensor else "GB/s", "ops": ops}
     except Exception as exc:  # the leg is a baseline: report, never fail the bench
         return {"unavailable": f"{type(exc).__name__}: {exc}"}
 
