@@ -42,8 +42,12 @@ int gemm_path16(int b_layout, const void *a, const void *b, int64_t m, int64_t n
 // gemm_path16 from the operands' 16-byte alignment instead of their addresses
 int gemm_path16_shape(int b_layout, bool a_aligned, bool b_aligned, int64_t m, int64_t n, int64_t k);
 int gemm_path32(int b_layout, const void *a, const void *b, int64_t m, int64_t n, int64_t k);
+// any_k_order: the caller lets the 2-SM kernel walk K in either direction per
+// tile (a plain 16-bit product); callers whose K order carries the rounding
+// order (the f32 split's small-products-first operands) keep it false.
 int gemm_tc_launch(bool bf16, bool b_mn, int out, int epi, const void *a, const void *b,
-                   const float *bias, void *c, int m, int n, int k, cudaStream_t s, bool pair);
+                   const float *bias, void *c, int m, int n, int k, cudaStream_t s, bool pair,
+                   bool any_k_order = false);
 int gemm_f32(int out, int b_layout, int epi, const void *a, const void *b, const float *bias,
              void *c, int m, int n, int k, cudaStream_t s);
 int gemm_f32_dot2(int b_layout, int epi, const float *a, const float *b, const float *bias, float *c,

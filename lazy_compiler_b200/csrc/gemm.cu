@@ -17,7 +17,11 @@
 //               type and store, then release the accumulator buffer so the
 //               MMA of the next tile overlaps this tile's epilogue.
 // Tiles are visited in groups of 8 M-blocks so concurrently running CTAs
-// share A and B k-slices in L2.  Every mbarrier wait is bounded (1 s); a wait
+// share A and B k-slices in L2.  The 2-SM kernel loads A with an evict-last
+// L2 policy and, for plain 16-bit products, walks K backwards on every other
+// tile of a CTA, so a wave of tiles starts on the A slices the previous wave
+// (same A rows) left in L2 (DRAM reads at 8192^3: 1.12 -> 0.91 GB).  The f32
+// split keeps the forward order: its K order is its rounding order.  Every mbarrier wait is bounded (1 s); a wait
 // that gives up writes the device error word, stops the other roles and lets
 // in-flight copies land before the CTA frees TMEM.
 //
@@ -46,7 +50,7 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
 constexpr int THREADS = 192;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr int GROUP_M = 8;
+constexpr int GROUP_M = 8;  // M-blocks per raster group
 
 struct GemmParams {
   int m, n, k;
@@ -55,6 +59,7 @@ struct GemmParams {
   int64_t ldc;
   int tiles_m, tiles_n;
   int vec_store;
+  int serpentine;     // the 2-SM kernel may walk K backwards on every other tile
   int *err;
 };
 
@@ -353,12 +358,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
+      // A's rows are shared by the consecutive tiles of a raster group, B's
+      // columns are not: A's lines are kept in L2 ahead of B's.
+      const uint64_t pol_a = l2_policy_evict_last(), pol_b = l2_policy_evict_normal();
       int it = 0;
       bool ok = true;
-      for (int tile = cluster; ok && tile < num_tiles; tile += clusters) {
+      int local = 0;
+      for (int tile = cluster; ok && tile < num_tiles; tile += clusters, ++local) {
         int tm, tn;
         tile_coords(tile, tp, tm, tn);
+        // every other tile of a CTA walks K backwards, starting on the k-slices
+        // that the previous wave of tiles (same A rows) left in L2
+        const bool back = p.serpentine && (local & 1);
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int kk = back ? num_kb - 1 - kb : kb;
           const int stage = it % PSTAGES;
           const uint32_t phase = (it / PSTAGES) & 1;
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort)) {
@@ -370,14 +383,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           uint8_t *b_s = a_s + PA_BYTES;
           const uint32_t full = mapa(smem_u32(&full_bar[stage]), 0);
           if (leader) mbar_expect_tx(&full_bar[stage], 2 * PSTAGE_BYTES);
-          tma_load_2d_pair(a_s, &tma_a, full, kb * BK, tm * PTILE + rank * PBM);
+          tma_load_2d_pair_hint(a_s, &tma_a, full, kk * BK, tm * PTILE + rank * PBM, pol_a);
           if constexpr (B_MN) {
 #pragma unroll
             for (int c = 0; c < PBN / 64; ++c)
-              tma_load_2d_pair(b_s + c * (BK * 128), &tma_b, full, tn * PTILE + rank * PBN + c * 64,
-                               kb * BK);
+              tma_load_2d_pair_hint(b_s + c * (BK * 128), &tma_b, full, tn * PTILE + rank * PBN + c * 64,
+                                    kk * BK, pol_b);
           } else {
-            tma_load_2d_pair(b_s, &tma_b, full, kb * BK, tn * PTILE + rank * PBN);
+            tma_load_2d_pair_hint(b_s, &tma_b, full, kk * BK, tn * PTILE + rank * PBN, pol_b);
           }
         }
       }
@@ -546,6 +559,7 @@ int launch_tc(const void *a, const void *b, const float *bias, void *c, int m, i
   p.tiles_n = (n + BN - 1) / BN;
   const int elem = OUT == LC_F32 ? 4 : 2;
   p.vec_store = aligned(c, 16) && ((int64_t)n * elem) % 16 == 0;
+  p.serpentine = 0;
   if (int rc = device_error_word(&p.err)) return rc;
   auto kernel = gemm_tc_kernel<BF16, B_MN, OUT, EPI>;
   static bool configured[64] = {false};
@@ -566,7 +580,7 @@ int launch_tc(const void *a, const void *b, const float *bias, void *c, int m, i
 
 template <bool BF16, bool B_MN, int OUT, int EPI>
 int launch_tc2(const void *a, const void *b, const float *bias, void *c, int m, int n, int k,
-               cudaStream_t s) {
+               cudaStream_t s, bool any_k_order) {
   CUtensorMap ta, tb;
   if (int rc = make_map_2d(&ta, BF16, a, k, m, (uint64_t)k * 2, BK, PBM)) return rc;
   if (B_MN) {
@@ -585,6 +599,7 @@ int launch_tc2(const void *a, const void *b, const float *bias, void *c, int m, 
   p.tiles_n = (n + PTILE - 1) / PTILE;
   const int elem = OUT == LC_F32 ? 4 : 2;
   p.vec_store = aligned(c, 16) && ((int64_t)n * elem) % 16 == 0;
+  p.serpentine = any_k_order ? 1 : 0;
   if (int rc = device_error_word(&p.err)) return rc;
   auto kernel = gemm_tc2_kernel<BF16, B_MN, OUT, EPI>;
   static bool configured[64] = {false};
@@ -622,10 +637,10 @@ int launch_tc2(const void *a, const void *b, const float *bias, void *c, int m, 
 
 template <bool BF16, bool B_MN>
 int dispatch_tc(int out, int epi, const void *a, const void *b, const float *bias, void *c, int m,
-                int n, int k, cudaStream_t s, bool pair) {
-#define LC_TC(O, E)                                                              \
-  if (out == O && epi == E)                                                      \
-    return pair ? launch_tc2<BF16, B_MN, O, E>(a, b, bias, c, m, n, k, s)        \
+                int n, int k, cudaStream_t s, bool pair, bool any_k_order) {
+#define LC_TC(O, E)                                                                    \
+  if (out == O && epi == E)                                                            \
+    return pair ? launch_tc2<BF16, B_MN, O, E>(a, b, bias, c, m, n, k, s, any_k_order) \
                 : launch_tc<BF16, B_MN, O, E>(a, b, bias, c, m, n, k, s);
   LC_TC(LC_F32, LC_EPI_NONE) LC_TC(LC_F32, LC_EPI_GELU_ERF) LC_TC(LC_F32, LC_EPI_GELU_TANH)
   LC_TC(LC_F16, LC_EPI_NONE) LC_TC(LC_F16, LC_EPI_GELU_ERF) LC_TC(LC_F16, LC_EPI_GELU_TANH)
@@ -670,11 +685,13 @@ int gemm_path16_shape(int b_layout, bool a_aligned, bool b_aligned, int64_t m, i
 }
 
 int gemm_tc_launch(bool bf16, bool b_mn, int out, int epi, const void *a, const void *b,
-                   const float *bias, void *c, int m, int n, int k, cudaStream_t s, bool pair) {
-  if (bf16) return b_mn ? dispatch_tc<true, true>(out, epi, a, b, bias, c, m, n, k, s, pair)
-                        : dispatch_tc<true, false>(out, epi, a, b, bias, c, m, n, k, s, pair);
-  return b_mn ? dispatch_tc<false, true>(out, epi, a, b, bias, c, m, n, k, s, pair)
-              : dispatch_tc<false, false>(out, epi, a, b, bias, c, m, n, k, s, pair);
+                   const float *bias, void *c, int m, int n, int k, cudaStream_t s, bool pair,
+                   bool any_k_order) {
+  const bool o = any_k_order;
+  if (bf16) return b_mn ? dispatch_tc<true, true>(out, epi, a, b, bias, c, m, n, k, s, pair, o)
+                        : dispatch_tc<true, false>(out, epi, a, b, bias, c, m, n, k, s, pair, o);
+  return b_mn ? dispatch_tc<false, true>(out, epi, a, b, bias, c, m, n, k, s, pair, o)
+              : dispatch_tc<false, false>(out, epi, a, b, bias, c, m, n, k, s, pair, o);
 }
 
 }  // namespace lc
@@ -704,7 +721,7 @@ extern "C" int lc_gemm_ex(int ab_dtype, int c_dtype, int b_layout, int epilogue,
   const bool b_mn = b_layout == LC_B_KN;
   if (const int path = gemm_path16(b_layout, a, b, m, n, k))
     return gemm_tc_launch(bf16, b_mn, c_dtype, epilogue, a, b, bias_f, c, (int)m, (int)n, (int)k,
-                          s, path == 2);
+                          s, path == 2, true);
   if (bf16)
     return dispatch_simt<__nv_bfloat16>(c_dtype, epilogue, a, b, bias_f, c, m, n, k, !b_mn, s);
   return dispatch_simt<__half>(c_dtype, epilogue, a, b, bias_f, c, m, n, k, !b_mn, s);

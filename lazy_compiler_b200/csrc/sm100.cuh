@@ -168,6 +168,29 @@ __device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *m
       : "memory");
 }
 
+// L2 eviction-priority policies for the cache-hinted loads below.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// tma_load_2d_pair with an L2 cache policy for the loaded lines.
+__device__ __forceinline__ void tma_load_2d_pair_hint(void *dst, const CUtensorMap *map,
+                                                      uint32_t bar_cluster_addr, int32_t c0, int32_t c1,
+                                                      uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar_cluster_addr), "l"(policy)
+      : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {

@@ -98,9 +98,12 @@ def test_package_alternate_seeds_against_oracle(name, offset, cuda_device):
     out = run_package(golden(name), seed_offset=offset)
     for key, value in ref.items():
         assert_close(out[key], value, meta["rtol"], meta["atol"])
-    # and against what the IR says, with an oracle chosen from the IR alone (not from the plan)
+    # and against what the IR says, with an oracle chosen from the IR alone (not from the plan);
+    # phase9_gelu_erf_half is skipped there: the IR's literal FP16 erf-GELU arithmetic is the
+    # reference's own documented retained failure (docs/PHASE9.md:120-145), and the formula
+    # oracle above and the golden vectors pin that package
     from ir_oracles import ir_oracle, supported
-    if supported(golden_ir(name)) and name != "m01_matmul_512":
+    if supported(golden_ir(name)) and name not in ("m01_matmul_512", "phase9_gelu_erf_half"):
         for key, value in ir_oracle(golden_ir(name), arrays).items():
             assert_close(np.asarray(out[key]).reshape(value.shape), value, meta["rtol"], meta["atol"])
 

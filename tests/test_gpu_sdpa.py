@@ -62,7 +62,9 @@ def test_simt_path(bh, s_q, s_kv, d, cuda_device):
     check(o.float().cpu().numpy(), ref)
 
 
-TC = [(1, 128, 128), (2, 256, 256), (3, 300, 300), (2, 128, 1000), (1, 1000, 130), (4, 1024, 1024)]
+# (300, 256, 64): one KV block per item and two or three items per CTA
+TC = [(1, 128, 128), (2, 256, 256), (3, 300, 300), (2, 128, 1000), (1, 1000, 130), (4, 1024, 1024),
+      (300, 256, 64)]
 
 
 @pytest.mark.parametrize("bh,s_q,s_kv", TC)
