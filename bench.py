@@ -719,9 +719,9 @@ def ref_ptx_baseline(config, ours_ms):
                 end.record()
                 torch.cuda.synchronize()
                 ours_ms = {op: start.elapsed_time(end) / REF_PTX_REPEATS}
-            rate = {"TFLOP/s": round(nbytes / ms / 1e9, 1)} if tensor else {"GB/s": round(nbytes / ms / 1e6, 1)}
-            ops[op] = {"package": f"{name} (rescaled)", "ms": round(ms, 4), **rate,
-                       "ours_ms": round(ours_ms.get(op, float("nan")), 4),
+            rate = {"TFLOP/s": sig(nbytes / ms / 1e9)} if tensor else {"GB/s": sig(nbytes / ms / 1e6)}
+            ops[op] = {"package": f"{name} (rescaled)", "ms": sig(ms), **rate,
+                       "ours_ms": sig(ours_ms.get(op, float("nan"))),
                        "speedup": round(ms / ours_ms[op], 2) if op in ours_ms else None,
                        "grid": kernel.kernel_meta["grid"], "block": kernel.kernel_meta["block"]}
             total_bytes += nbytes
@@ -733,10 +733,15 @@ def ref_ptx_baseline(config, ours_ms):
                 "configuration, ours_ms scaled to the slice's flops" if config == "sdpa" else "")
         return {"kind": "the reference compiler's own PTX (public IR packages rescaled to the configuration "
                         "size, its meta.json geometry) on this B200" + note,
-                "value": round(total_bytes / total_ms / (1e9 if tensor else 1e6), 1),
+                "value": sig(total_bytes / total_ms / (1e9 if tensor else 1e6)),
                 "unit": "TFLOP/s" if tensor else "GB/s", "ops": ops}
     except Exception as exc:  # the leg is a baseline: report, never fail the bench
         return {"unavailable": f"{type(exc).__name__}: {exc}"}
+
+
+def sig(x, digits=4):
+    """x to `digits` significant figures (the baselines span six decades)."""
+    return float(f"{x:.{digits}g}")
 
 
 # ---------------------------------------------------------------- CPU reference / baseline
