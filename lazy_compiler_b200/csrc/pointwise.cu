@@ -10,7 +10,9 @@
 // at the same time, a broadcast from the constant bank.
 #include <cuda.h>
 
+#include <cstring>
 #include <mutex>
+#include <string>
 #include <vector>
 
 #include "common.cuh"
@@ -687,9 +689,13 @@ int prepare_blockprog(const char *name, const lc_pw_program *program, const lc_b
 }
 
 // Modules of natively compiled block programs, loaded once per device and image.
+// A loaded native program: the lookup compares the whole image and kernel
+// name, the hash only narrows the search.
 struct JitModule {
   uint64_t key;
   int device;
+  std::vector<uint8_t> image;
+  std::string kernel;
   CUfunction function;
 };
 std::mutex jit_mutex;
@@ -714,26 +720,35 @@ int jit_function(const void *image, size_t size, const char *kernel, CUfunction 
   if (int rc = check_cuda(cudaGetDevice(&dev), "native program: device")) return rc;
   std::lock_guard<std::mutex> guard(jit_mutex);
   for (const JitModule &m : jit_modules)
-    if (m.key == key && m.device == dev) {
+    if (m.key == key && m.device == dev && m.image.size() == size && m.kernel == kernel &&
+        std::memcmp(m.image.data(), image, size) == 0) {
       *out = m.function;
       return LC_OK;
     }
   using LoadFn = CUresult (*)(CUmodule *, const void *);
   using GetFn = CUresult (*)(CUfunction *, CUmodule, const char *);
   using AttrFn = CUresult (*)(CUfunction, CUfunction_attribute, int);
+  using UnloadFn = CUresult (*)(CUmodule);
   auto load = driver_entry<LoadFn>("cuModuleLoadData");
   auto get = driver_entry<GetFn>("cuModuleGetFunction");
   auto attr = driver_entry<AttrFn>("cuFuncSetAttribute");
-  if (!load || !get || !attr) return fail(LC_ERR_CUDA, "lc_jit_blockprog: driver entry points unavailable");
+  auto unload = driver_entry<UnloadFn>("cuModuleUnload");
+  if (!load || !get || !attr || !unload)
+    return fail(LC_ERR_CUDA, "lc_jit_blockprog: driver entry points unavailable");
   cudaFree(nullptr);  // the primary context is current for this thread
   CUmodule module = nullptr;
   CUfunction function = nullptr;
   if (load(&module, image) != CUDA_SUCCESS) return fail(LC_ERR_CUDA, "lc_jit_blockprog: module load failed");
-  if (get(&function, module, kernel) != CUDA_SUCCESS)
+  if (get(&function, module, kernel) != CUDA_SUCCESS) {
+    unload(module);
     return fail(LC_ERR_CUDA, "native program: kernel %s not in the module", kernel);
-  if (attr(function, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, 200 * 1024) != CUDA_SUCCESS)
+  }
+  if (attr(function, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, 200 * 1024) != CUDA_SUCCESS) {
+    unload(module);
     return fail(LC_ERR_CUDA, "lc_jit_blockprog: shared memory attribute");
-  jit_modules.push_back({key, dev, function});
+  }
+  const uint8_t *bytes = static_cast<const uint8_t *>(image);
+  jit_modules.push_back({key, dev, std::vector<uint8_t>(bytes, bytes + size), std::string(kernel), function});
   *out = function;
   return LC_OK;
 }
