@@ -154,6 +154,8 @@ __global__ void __launch_bounds__(kThreads, kBlocksPerSm) sum_kernel(const float
                                                        const PeerSet peers) {
   __shared__ double scratch[32];
   __shared__ bool is_last;
+  pdl_wait();     // x and the workspace may be the previous kernel's
+  pdl_trigger();  // the next kernel may be scheduled while this one drains
   CompSum acc;
   if (VEC) accumulate(acc, x, n);
   else accumulate_scalar(acc, x, n);
@@ -206,12 +208,11 @@ int launch_sum(const char *name, const float *x, int64_t n, int mode, const floa
   if (blocks < 1) blocks = 1;
   PeerSet none{};
   const PeerSet &p = peers ? *peers : none;
-  if (vec)
-    sum_kernel<true><<<(int)blocks, kThreads, 0, s>>>(x, n, ws.partials, ws.counter, mode, count,
-                                                      out, partial_out, p);
-  else
-    sum_kernel<false><<<(int)blocks, kThreads, 0, s>>>(x, n, ws.partials, ws.counter, mode, count,
-                                                       out, partial_out, p);
+  cudaError_t e = vec ? launch_pdl(sum_kernel<true>, dim3((unsigned)blocks), dim3(kThreads), 0, s, x, n,
+                                    ws.partials, ws.counter, mode, count, out, partial_out, p)
+                      : launch_pdl(sum_kernel<false>, dim3((unsigned)blocks), dim3(kThreads), 0, s, x, n,
+                                    ws.partials, ws.counter, mode, count, out, partial_out, p);
+  if (e != cudaSuccess) return check_cuda(e, name);
   return check_launch(name);
 }
 

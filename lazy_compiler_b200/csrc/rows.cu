@@ -74,6 +74,8 @@ template <int OP, int V>
 __global__ void __launch_bounds__(1024) row_vec_kernel(RowArgs args) {
   __shared__ double dscratch[32];
   __shared__ float fscratch[32];
+  pdl_wait();     // the rows may be the previous kernel's output
+  pdl_trigger();
   const int64_t c4 = args.cols >> 2;
   const int T = blockDim.x;
   for (int64_t row = blockIdx.x; row < args.rows; row += gridDim.x) {
@@ -173,6 +175,8 @@ __global__ void __launch_bounds__(1024) row_vec_kernel(RowArgs args) {
 // Scalar fallback: any width and alignment; passes re-read the row from global.
 template <int OP>
 __global__ void __launch_bounds__(256) row_scalar_kernel(RowArgs args) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ double dscratch[32];
   __shared__ float fscratch[32];
   for (int64_t row = blockIdx.x; row < args.rows; row += gridDim.x) {
@@ -231,7 +235,8 @@ int launch_rows(const char *name, const RowArgs &a, void *stream) {
   const bool vec = (a.cols & 3) == 0 && aligned(a.x, 16) && aligned(a.out, 16) &&
                    ((OP != kRmsNorm && !is_dot(OP)) || aligned(a.w, 16)) && c4 <= 8 * 1024;
   if (!vec) {
-    row_scalar_kernel<OP><<<(int)grid, 256, 0, s>>>(a);
+    if (cudaError_t e = launch_pdl(row_scalar_kernel<OP>, dim3((unsigned)grid), dim3(256), 0, s, a))
+      return check_cuda(e, name);
     return check_launch(name);
   }
   int v = 1;
@@ -239,12 +244,9 @@ int launch_rows(const char *name, const RowArgs &a, void *stream) {
   int threads = (int)((c4 + v - 1) / v);
   threads = (threads + 31) & ~31;
   if (threads > 1024) threads = 1024;
-  switch (v) {
-    case 1: row_vec_kernel<OP, 1><<<(int)grid, threads, 0, s>>>(a); break;
-    case 2: row_vec_kernel<OP, 2><<<(int)grid, threads, 0, s>>>(a); break;
-    case 4: row_vec_kernel<OP, 4><<<(int)grid, threads, 0, s>>>(a); break;
-    default: row_vec_kernel<OP, 8><<<(int)grid, threads, 0, s>>>(a); break;
-  }
+  auto kernel = v == 1 ? row_vec_kernel<OP, 1> : v == 2 ? row_vec_kernel<OP, 2>
+               : v == 4 ? row_vec_kernel<OP, 4> : row_vec_kernel<OP, 8>;
+  if (cudaError_t e = launch_pdl(kernel, dim3((unsigned)grid), dim3(threads), 0, s, a)) return check_cuda(e, name);
   return check_launch(name);
 }
 
