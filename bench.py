@@ -11,7 +11,8 @@ Configurations (BASELINE.json ``configs``):
 * ``reduce``: whole-array sum and mean of 2^24 fp32 U[-1,1].
 * ``rows``: RMSNorm (eps 1e-6, w ~ N(1, 0.1)), softmax, L2 norm and row sums
   of X[16384, 4096] fp32.
-* ``gemm_f16`` (8192^3), ``gemm_bf16`` (M4096 N16384 K2048): f32 out.
+* ``gemm_f16`` (8192^3), ``gemm_f16_gelu`` (the same with the optional fused
+  erf-GELU epilogue), ``gemm_bf16`` (M4096 N16384 K2048): f32 out.
 * ``sdpa``: f16 B8 H16 S4096 D128, non-causal.
 
 Timing: the K timed steps are captured in one CUDA graph and replayed between
@@ -60,9 +61,12 @@ N_ELEMENTWISE = 1 << 28
 N_REDUCE = 1 << 24
 ROWS, COLS = 16384, 4096
 L2_BYTES = 126 * 10 ** 6
-SUITE = ("reduce", "rows", "elementwise", "gemm_f16", "gemm_bf16", "sdpa")
+SUITE = ("reduce", "rows", "elementwise", "gemm_f16", "gemm_f16_gelu", "gemm_bf16", "sdpa")
 SDPA_SHAPE = (8 * 16, 4096, 128)
-GEMM_SHAPES = {"gemm_f16": ("f16", 8192, 8192, 8192), "gemm_bf16": ("bf16", 4096, 16384, 2048)}
+GEMM_SHAPES = {"gemm_f16": ("f16", 8192, 8192, 8192), "gemm_f16_gelu": ("f16", 8192, 8192, 8192),
+               "gemm_bf16": ("bf16", 4096, 16384, 2048)}
+# the configuration's optional fused epilogue, measured as its own suite entry
+GEMM_EPILOGUE = {"gemm_f16_gelu": "gelu_erf"}
 
 
 def parse_args():
@@ -346,9 +350,14 @@ def build(config: str, dist, strong: bool, g):
                   (torch.randn(k, n, device=dev, generator=g) / k ** 0.5).to(dt)) for _ in range(r)]
         c = torch.empty(rows, n, device=dev)
         code = 1 if ab == "f16" else 2
-        ops = [Op(f"gemm_{ab}", 2 * rows * n * k,
-                  lambda s: runtime.call("lc_gemm", code, 0, 0, 0, P(s[0]), P(s[1]), P(c), rows, n, k, S()))]
+        epi = GEMM_EPILOGUE.get(config, "none")
+        epi_code = runtime.EPILOGUES[epi]
+        name = f"gemm_{ab}" + ("" if epi == "none" else f"_{epi}")
+        ops = [Op(name, 2 * rows * n * k,
+                  lambda s: runtime.call("lc_gemm", code, 0, 0, epi_code, P(s[0]), P(s[1]), P(c), rows, n, k,
+                                         S()))]
         cfg = {"workload": f"{ab} GEMM M{m} N{n} K{k}, B row-major [K,N], f32 out, A,B ~ N(0,1/sqrt(K))"
+                           + ("" if epi == "none" else ", fused erf-GELU epilogue")
                            + (", M split in row blocks, B replicated" if strong and world > 1 else ""),
                "m": m, "n": n, "k": k, "m_local": rows}
         return Workload(config, "TFLOP/s", ops, slots, 2 * m * n * k, cfg, (), (slots[0], [c]), ab)
@@ -784,10 +793,18 @@ def cpu_run(config, sample_scale):
         a = (rng.standard_normal((rows, k)) / np.sqrt(k)).astype(np.float32)
         b = (rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32)
         a64, b64 = a.astype(np.float64), b.astype(np.float64)
-        ops = [(2 * rows * n * k, lambda: a64 @ b64)]
+        if GEMM_EPILOGUE.get(config) == "gelu_erf":
+            from scipy.special import erf
+
+            def gemm_gelu():
+                y = a64 @ b64
+                return 0.5 * y * (1.0 + erf(y / np.sqrt(2.0)))
+            ops = [(2 * rows * n * k, gemm_gelu)]
+        else:
+            ops = [(2 * rows * n * k, lambda: a64 @ b64)]
         threads = blas_threads()
         desc = (f"{rows} of {m} rows of the {ab} GEMM (1/{sample_scale} of a step) in float64 "
-                f"numpy/BLAS, {threads} threads")
+                f"numpy/BLAS" + (" with the erf-GELU" if config in GEMM_EPILOGUE else "") + f", {threads} threads")
         return ops, desc, threads, "TFLOP/s", (a64, b64)
     lib = oracle_lib()
     threads = lib.oc_threads()
@@ -916,7 +933,7 @@ def run_reference(args):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(sum(times) * 1e3 / args.steps, 3), "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "data": "synthetic (seeded numpy)",
-        "dtype": {"gemm_f16": "f64 (f16 inputs)", "gemm_bf16": "f64 (bf16 inputs)",
+        "dtype": {"gemm_f16": "f64 (f16 inputs)", "gemm_f16_gelu": "f64 (f16 inputs)", "gemm_bf16": "f64 (bf16 inputs)",
                   "sdpa": "f64 (f16 inputs)"}.get(args.config, "f32"),
         "config": {"workload": args.config, "sample": desc, "same_config": scale == 1},
         "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": threads, "kind": "port",

@@ -125,6 +125,8 @@ def main() -> None:
     ap.add_argument("--k", type=int, default=8192)
     ap.add_argument("--bh", type=int, default=128)
     ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--epi", default="none", choices=["none", "gelu_erf", "gelu_tanh"],
+                    help="fused epilogue of gemm_f16 / gemm_bf16")
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--repeat", type=int, default=1)
     a = ap.parse_args()
@@ -178,7 +180,8 @@ def main() -> None:
         B = (torch.randn(k, n, device="cuda", generator=g) / k ** 0.5).to(dt)
         C = torch.empty(m, n, device="cuda")
         code = 1 if op == "gemm_f16" else 2
-        fn = lambda: runtime.call("lc_gemm", code, 0, 0, 0, P(A), P(B), P(C), m, n, k, s)  # noqa: E731
+        epi = runtime.EPILOGUES[a.epi]
+        fn = lambda: runtime.call("lc_gemm", code, 0, 0, epi, P(A), P(B), P(C), m, n, k, s)  # noqa: E731
         work, unit = 2 * m * n * k, "TFLOP/s"
     elif op == "gemm_f32":
         m, n, k = a.m, a.n or 8192, a.k
