@@ -12,7 +12,9 @@
 //
 // Here one CTA of 256 threads owns 64 query rows of one (batch, head): Q is
 // staged once in shared memory (transposed), then per 64-key block Kt and V
-// are staged, each thread computes a 4 x 4 block of scores with FFMA, the row
+// are staged (cp.async into two buffers: the next block's copies are in
+// flight while this one is computed), each thread computes a 4 x 4 block of
+// scores with FFMA, the row
 // max and sum are combined across the 16 threads sharing a row by shuffles,
 // P goes through shared memory and each thread accumulates a 4 x 4 (head
 // size <= 64) or 4 x 8 (<= 128) block of O in registers.  The score is
@@ -41,6 +43,16 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // exp as the reference lowers it
 __device__ __forceinline__ float exp_ref(float x) { return ex2_approx(__fmul_rn(x, kLog2e)); }
 
+// 4-byte asynchronous copy global -> shared; an invalid element is zero-filled
+// (no bytes are read from `src`, which stays a valid address)
+__device__ __forceinline__ void cp_async4(float *dst, const float *src, bool valid) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d), "l"(src), "r"(valid ? 4 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
 __device__ __forceinline__ float apply_scale(float dot, float c, float rc, int mode) {
   if (mode == LC_SCALE_MUL) return __fmul_rn(dot, c);
   if (mode == LC_SCALE_MUL_RECIP) return __fmul_rn(dot, rc);
@@ -55,9 +67,9 @@ __global__ void __launch_bounds__(kThreads) attention_f32_kernel(
   constexpr int DVW = 64 * DVH;  // value columns staged per key
   extern __shared__ float4 smem4[];
   float *Qs = reinterpret_cast<float *>(smem4);  // [d][QS]   Q transposed
-  float *Ks = Qs + d * QS;                        // [d][BKV]  Kt block
-  float *Vs = Ks + d * BKV;                       // [BKV][DVW]
-  float *Ps = Vs + BKV * DVW;                     // [BKV][BQ]  P transposed
+  float *Kbuf = Qs + d * QS;                      // 2 x [d][BKV]  Kt blocks (double-buffered)
+  float *Vbuf = Kbuf + 2 * d * BKV;               // 2 x [BKV][DVW]
+  float *Ps = Vbuf + 2 * BKV * DVW;               // [BKV][BQ]  P transposed
 
   const int t = threadIdx.x, tx = t & 15, ty = t >> 4;
   const int bh = blockIdx.y;
@@ -82,16 +94,32 @@ __global__ void __launch_bounds__(kThreads) attention_f32_kernel(
     for (int j = 0; j < 4 * DVH; ++j) acc[i][j] = 0.f;
   }
 
-  for (int k0 = 0; k0 < s_kv; k0 += BKV) {
+  // Kt / V of the block starting at key k into buffer b, asynchronously (the
+  // next block's copies overlap this block's arithmetic)
+  auto stage = [&](int k, int b) {
+    float *ks = Kbuf + b * d * BKV;
+    float *vs = Vbuf + b * BKV * DVW;
     for (int idx = t; idx < d * BKV; idx += kThreads) {
       const int dd = idx / BKV, key = idx - dd * BKV;
-      Ks[idx] = k0 + key < s_kv ? kb[(int64_t)dd * s_kv + k0 + key] : 0.f;
+      const bool ok = k + key < s_kv;
+      cp_async4(ks + idx, ok ? kb + (int64_t)dd * s_kv + k + key : kb, ok);
     }
     for (int idx = t; idx < BKV * DVW; idx += kThreads) {
       const int key = idx / DVW, col = idx - key * DVW;
-      Vs[idx] = (k0 + key < s_kv && col < dv) ? vb[(int64_t)(k0 + key) * dv + col] : 0.f;
+      const bool ok = k + key < s_kv && col < dv;
+      cp_async4(vs + idx, ok ? vb + (int64_t)(k + key) * dv + col : vb, ok);
     }
+  };
+  stage(0, 0);
+  cp_async_commit();
+  int buf = 0;
+  for (int k0 = 0; k0 < s_kv; k0 += BKV, buf ^= 1) {
+    if (k0 + BKV < s_kv) stage(k0 + BKV, buf ^ 1);  // that buffer's last readers passed the barrier below
+    cp_async_commit();
+    cp_async_wait_1();  // this block's copies (all groups but the newest) have landed
     __syncthreads();
+    const float *Ks = Kbuf + buf * d * BKV;
+    const float *Vs = Vbuf + buf * BKV * DVW;
 
     float s[4][4], s_low[COMP ? 4 : 1][COMP ? 4 : 1];
 #pragma unroll
@@ -174,7 +202,7 @@ __global__ void __launch_bounds__(kThreads) attention_f32_kernel(
           for (int j = 0; j < 4; ++j) acc[i][h * 4 + j] = fmaf(pv[i], wv[j], acc[i][h * 4 + j]);
       }
     }
-    __syncthreads();  // the next block overwrites Ks, Vs and Ps
+    __syncthreads();  // every thread is done with this block's Kt, V and P before they are reused
   }
 
   float *ob = o + (int64_t)bh * s_q * dv;
@@ -282,7 +310,7 @@ __global__ void __launch_bounds__(32 * kTileWarps) attention_tile_f16q_kernel(
 }
 
 size_t tiled_smem(int d, int dvh) {
-  return (size_t)(d * QS + d * BKV + BKV * 64 * dvh + BKV * BQ) * sizeof(float);
+  return (size_t)(d * QS + 2 * d * BKV + 2 * BKV * 64 * dvh + BKV * BQ) * sizeof(float);
 }
 
 template <int DVH, int EPI, bool COMP>
