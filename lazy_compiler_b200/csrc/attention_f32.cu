@@ -10,14 +10,14 @@
 // (ptx_backend.py:1047-1048) and the coupled (max, sum, acc) accumulators of
 // the IR (running max seeded with -1e30).
 //
-// Here one CTA of 256 threads owns 64 query rows of one (batch, head): Q is
+// Here one CTA of 256 threads owns 128 query rows of one (batch, head): Q is
 // staged once in shared memory (transposed), then per 64-key block Kt and V
 // are staged (cp.async into two buffers: the next block's copies are in
-// flight while this one is computed), each thread computes a 4 x 4 block of
-// scores with FFMA, the row
-// max and sum are combined across the 16 threads sharing a row by shuffles,
-// P goes through shared memory and each thread accumulates a 4 x 4 (head
-// size <= 64) or 4 x 8 (<= 128) block of O in registers.  The score is
+// flight while this one is computed), each thread computes an 8 x 4 block of
+// scores with FFMA (two Q and one Kt 16-byte shared loads per 32 FMAs), the
+// row max and sum are combined across the 16 threads sharing a row by
+// shuffles, P goes through shared memory and each thread accumulates an 8 x 4
+// (head size <= 64) or 8 x 8 (<= 128) block of O in registers.  The score is
 // dot * c, dot * (1/c) or dot / c for the 1-element scale buffer c, matching
 // the three forms the IR can take.  Head sizes above 128 take a direct kernel
 // with one thread per output element.
@@ -27,7 +27,8 @@
 namespace lc {
 namespace {
 
-constexpr int BQ = 64;
+constexpr int RPT = 8;         // query rows per thread (a thread computes RPT x 4 scores)
+constexpr int BQ = 16 * RPT;   // query rows per CTA
 constexpr int BKV = 64;
 constexpr int kThreads = 256;
 constexpr int kMaxTiled = 128;
@@ -85,9 +86,9 @@ __global__ void __launch_bounds__(kThreads) attention_f32_kernel(
     Qs[dd * QS + row] = q0 + row < s_q ? qb[(int64_t)(q0 + row) * d + dd] : 0.f;
   }
 
-  float m[4], l[4], acc[4][4 * DVH];
+  float m[RPT], l[RPT], acc[RPT][4 * DVH];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < RPT; ++i) {
     m[i] = kMaxIdentity;
     l[i] = 0.f;
 #pragma unroll
@@ -121,43 +122,45 @@ __global__ void __launch_bounds__(kThreads) attention_f32_kernel(
     const float *Ks = Kbuf + buf * d * BKV;
     const float *Vs = Vbuf + buf * BKV * DVW;
 
-    float s[4][4], s_low[COMP ? 4 : 1][COMP ? 4 : 1];
+    float s[RPT][4], s_low[COMP ? RPT : 1][COMP ? 4 : 1];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < RPT; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
     if constexpr (COMP) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < RPT; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) s_low[i][j] = 0.f;
     }
     for (int dd = 0; dd < d; ++dd) {
-      const float4 a = *reinterpret_cast<const float4 *>(&Qs[dd * QS + ty * 4]);
+      const float4 a0 = *reinterpret_cast<const float4 *>(&Qs[dd * QS + ty * RPT]);
+      const float4 a1 = *reinterpret_cast<const float4 *>(&Qs[dd * QS + ty * RPT + 4]);
       const float4 b = *reinterpret_cast<const float4 *>(&Ks[dd * BKV + tx * 4]);
-      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+      const float av[RPT] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[4] = {b.x, b.y, b.z, b.w};
       if constexpr (COMP) {
         // the score dot as a Dot2 pair, in the IR's operand order kt * q
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < RPT; ++i)
 #pragma unroll
           for (int j = 0; j < 4; ++j) dot2_step(s[i][j], s_low[i][j], bv[j], av[i]);
       } else {
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < RPT; ++i)
 #pragma unroll
           for (int j = 0; j < 4; ++j) s[i][j] = fmaf(av[i], bv[j], s[i][j]);
       }
     }
     if constexpr (COMP) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < RPT; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) s[i][j] = dot2_value(s[i][j], s_low[i][j]);
     }
 
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < RPT; ++i) {
       float mx = -INFINITY;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -183,21 +186,24 @@ __global__ void __launch_bounds__(kThreads) attention_f32_kernel(
       for (int j = 0; j < 4 * DVH; ++j) acc[i][j] = __fmul_rn(acc[i][j], alpha);
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-      *reinterpret_cast<float4 *>(&Ps[(tx * 4 + j) * BQ + ty * 4]) =
-          make_float4(s[0][j], s[1][j], s[2][j], s[3][j]);
+    for (int j = 0; j < 4; ++j) {
+      float4 *dst = reinterpret_cast<float4 *>(&Ps[(tx * 4 + j) * BQ + ty * RPT]);
+      dst[0] = make_float4(s[0][j], s[1][j], s[2][j], s[3][j]);
+      dst[1] = make_float4(s[4][j], s[5][j], s[6][j], s[7][j]);
+    }
     __syncthreads();
 
     const int keys = s_kv - k0 < BKV ? s_kv - k0 : BKV;
     for (int key = 0; key < keys; ++key) {
-      const float4 pr = *reinterpret_cast<const float4 *>(&Ps[key * BQ + ty * 4]);
-      const float pv[4] = {pr.x, pr.y, pr.z, pr.w};
+      const float4 p0 = *reinterpret_cast<const float4 *>(&Ps[key * BQ + ty * RPT]);
+      const float4 p1 = *reinterpret_cast<const float4 *>(&Ps[key * BQ + ty * RPT + 4]);
+      const float pv[RPT] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
       for (int h = 0; h < DVH; ++h) {
         const float4 w = *reinterpret_cast<const float4 *>(&Vs[key * DVW + h * 64 + tx * 4]);
         const float wv[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < RPT; ++i)
 #pragma unroll
           for (int j = 0; j < 4; ++j) acc[i][h * 4 + j] = fmaf(pv[i], wv[j], acc[i][h * 4 + j]);
       }
@@ -207,8 +213,8 @@ __global__ void __launch_bounds__(kThreads) attention_f32_kernel(
 
   float *ob = o + (int64_t)bh * s_q * dv;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int row = q0 + ty * 4 + i;
+  for (int i = 0; i < RPT; ++i) {
+    const int row = q0 + ty * RPT + i;
     if (row >= s_q) continue;
     const float inv = __frcp_rn(l[i]);
 #pragma unroll
