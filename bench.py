@@ -21,7 +21,8 @@ inter-kernel gaps are the device's, not the host launch path's.  Every
 operation's inputs rotate over enough copies that the set a launch does not
 read is larger than twice the L2 (a launch never finds its inputs in L2).
 Per-operation times for the roofline come from a second graph per operation
-(K launches of that operation alone).
+(K launches of that operation alone, or as many more as make the graph run
+2 ms, so that the replay's start cost is not charged to a 15 µs kernel).
 
 Multi-GPU (one process per GPU, torchrun): strong scaling.  The fixed
 BASELINE configuration is partitioned across the ranks (element ranges for
@@ -61,6 +62,8 @@ N_ELEMENTWISE = 1 << 28
 N_REDUCE = 1 << 24
 ROWS, COLS = 16384, 4096
 L2_BYTES = 126 * 10 ** 6
+# a per-operation timing graph runs at least this long (more launches when K are shorter)
+PER_OP_GRAPH_S = 2e-3
 SUITE = ("reduce", "rows", "elementwise", "gemm_f16", "gemm_f16_gelu", "gemm_bf16", "sdpa")
 SDPA_SHAPE = (8 * 16, 4096, 128)
 GEMM_SHAPES = {"gemm_f16": ("f16", 8192, 8192, 8192), "gemm_f16_gelu": ("f16", 8192, 8192, 8192),
@@ -418,8 +421,23 @@ def graph_time(dist, wl: Workload, steps: int, warmup: int, clocks: bool = False
 
     # one untimed replay of each graph (upload), identical on every rank
     replay(step_graph)
-    for gj in op_graphs:
-        replay(gj)
+    reps = []
+    for j, gj in enumerate(op_graphs):
+        # A replay pays a few microseconds before its first kernel starts; a
+        # per-operation graph shorter than PER_OP_GRAPH_S is re-captured with
+        # more launches (the same rotation of inputs) so that this start cost
+        # does not enter the per-launch duration.  Every rank takes the same count.
+        t = dist.max(replay(gj))
+        r = steps
+        if t < PER_OP_GRAPH_S:
+            r = min(steps * 64, math.ceil(steps * PER_OP_GRAPH_S / max(t, 1e-7)))
+            longer = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(longer, stream=stream):
+                for i in range(r):
+                    wl.launch(i, j)
+            op_graphs[j] = longer
+            replay(longer)
+        reps.append(r)
     dist.barrier()
     clock_summary = None
     if clocks:
@@ -430,9 +448,9 @@ def graph_time(dist, wl: Workload, steps: int, warmup: int, clocks: bool = False
         local = replay(step_graph)
     seconds = dist.max(local)
     per_op = {}
-    for op, gj in zip(wl.ops, op_graphs):
+    for op, gj, r in zip(wl.ops, op_graphs, reps):
         dist.barrier()
-        per_op[op.name] = dist.max(replay(gj)) * 1e3 / steps
+        per_op[op.name] = dist.max(replay(gj)) * 1e3 / r
     dist.barrier()
     del step_graph, op_graphs
     launches = steps * sum(op.kernels for op in wl.ops)

@@ -107,3 +107,50 @@ def test_config_size_against_torch_fp32(cuda_device):
     ref64 = O.sdpa(q[h, rows].double().cpu().numpy(), k[h].double().cpu().numpy(),
                    v[h].double().cpu().numpy(), scale)[0]
     check(o[h, rows].float().cpu().numpy(), ref64)
+
+
+def _controlled_scores(block_scores, s_q=256, bh=2, d=128, seed=11):
+    """Q and K whose scores are known exactly: q = (c_row, 0, ...), k = (score, 0, ...).
+
+    block_scores[b](b, rng) gives the 128 raw scores of KV block b; row r's
+    scores are c_r times those (c_r = 1 for even rows, 0.25 for odd rows, so
+    the rows of one warp need different rescales).
+    """
+    rng = np.random.default_rng(seed)
+    s_kv = 128 * len(block_scores)
+    q = np.zeros((bh, s_q, d), np.float16)
+    q[:, 0::2, 0] = 1.0
+    q[:, 1::2, 0] = 0.25
+    k = np.zeros((bh, s_kv, d), np.float16)
+    for b, f in enumerate(block_scores):
+        k[:, 128 * b:128 * (b + 1), 0] = f(b, rng).astype(np.float16)
+    v = rng.standard_normal((bh, s_kv, d)).astype(np.float16)
+    return q, k, v
+
+
+@pytest.mark.parametrize("case", ["max_grows_every_block", "many_near_max", "one_late_spike", "mixed"])
+def test_tcgen05_running_max_paths(case, cuda_device):
+    """Score patterns that exercise the running-max rescale of the tensor-core path.
+
+    max_grows_every_block: every KV block's max exceeds the running max by more
+    than the rescale threshold (a rescale of O every block); many_near_max:
+    whole blocks of scores a few units above the running max, within the
+    threshold; one_late_spike: benign blocks and then one key far above
+    everything before it; mixed: blocks of each kind in turn.
+    """
+    import torch
+    blocks = {
+        "max_grows_every_block": [lambda b, r: r.uniform(0, 1, 128) + 8 * b] * 8,
+        "many_near_max": [lambda b, r: np.where(np.arange(128) == 5, 10.0, r.uniform(-1, 0, 128))]
+        + [lambda b, r: 14.0 + r.uniform(-0.5, 0, 128)] * 7,
+        "one_late_spike": [lambda b, r: r.uniform(-2, 2, 128)] * 6
+        + [lambda b, r: np.where(np.arange(128) == 77, 40.0, r.uniform(-2, 2, 128))]
+        + [lambda b, r: r.uniform(-2, 2, 128)],
+        "mixed": [lambda b, r: r.uniform(-1, 1, 128) + (6 * b if b % 2 else 0) + (3 if b % 3 == 0 else 0)] * 8,
+    }[case]
+    q, k, v = _controlled_scores(blocks)
+    tq, tk, tv = (torch.from_numpy(a).cuda() for a in (q, k, v))
+    assert runtime.library().lc_sdpa_path(P(tq), P(tk), P(tv), P(tq), q.shape[1], k.shape[1], 128) == 1
+    o = run_sdpa(tq, tk, tv, 1.0)
+    ref = O.sdpa_f16(q.astype(np.float32), k.astype(np.float32), v.astype(np.float32), 1.0)[0]
+    check(o.float().cpu().numpy(), ref)
