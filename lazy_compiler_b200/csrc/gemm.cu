@@ -31,8 +31,6 @@
 // and tiny problems take a SIMT kernel with the same arithmetic contract.
 #include <cudaTypedefs.h>
 
-#include <cstring>
-
 #include "common.cuh"
 #include "epilogue.cuh"
 #include "sm100.cuh"
@@ -62,7 +60,7 @@ struct GemmParams {
   int tiles_m, tiles_n;
   int vec_store;
   int serpentine;     // the 2-SM kernel may walk K backwards on every other tile
-  int tma_store;      // the 2-SM kernel stores f32 C tiles by TMA (tma_c is valid)
+  int c_vec8;        // the 2-SM kernel may store f32 C rows as 32-byte vectors
   int *err;
 };
 
@@ -126,6 +124,13 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int gm, int gn0
         if (gn0 + j < p.n) row[j] = to_out<T>(v[j]);
     }
   }
+}
+
+// One 32-byte store of eight f32 values (the address is 32-byte aligned).
+__device__ __forceinline__ void st_global_v8(float *dst, const float *v) {
+  asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "f"(v[0]), "f"(v[1]),
+               "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+               : "memory");
 }
 
 // The 32 f32 results of one accumulator chunk with bias and activation applied
@@ -320,20 +325,11 @@ constexpr int PB_BYTES = BK * PBN * 2;
 constexpr int PSTAGE_BYTES = PA_BYTES + PB_BYTES;
 constexpr int PSMEM_BYTES = PSTAGES * PSTAGE_BYTES + 1024;
 constexpr int PTILE = 256;
-// f32 C through TMA stores: each epilogue warp stages a 32-row x 32-column
-// chunk (128-byte rows, 128-byte swizzle) in one of two 4 KB buffers, so the
-// SM's load/store unit issues 8 shared-memory stores per chunk instead of 8
-// global stores to 32 rows each, which had slowed the MMA thread's barrier
-// polls and the mainloop (measured: 1281 -> 1621 TFLOP/s for a 2048-deep bf16
-// product with the global stores left out).
-constexpr int PEPI_BUF_BYTES = 32 * 128;
-constexpr int PEPI_BYTES = 4 * 2 * PEPI_BUF_BYTES;
 
 template <bool BF16, bool B_MN, int OUT, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tma_a,
-                    const __grid_constant__ CUtensorMap tma_b,
-                    const __grid_constant__ CUtensorMap tma_c, GemmParams p) {
+                    const __grid_constant__ CUtensorMap tma_b, GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -479,9 +475,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       int tm, tn;
       tile_coords(tile, tp, tm, tn);
       const int gm = tm * PTILE + rank * PBM + row;
-      if (OUT == LC_F32 && p.tma_store) {
-        const int row0 = tm * PTILE + rank * PBM + quarter * 32;  // this warp's 32 rows
-        uint8_t *stage = smem + PSTAGES * PSTAGE_BYTES + (warp - 2) * 2 * PEPI_BUF_BYTES;
+      if (OUT == LC_F32 && p.c_vec8) {
+        // f32 C: each thread writes its row's 32 columns of a chunk as four
+        // 32-byte vectors (full sectors).  The epilogue's stores run while the
+        // next tile's MMAs do, and stores of 16 bytes to 32 rows per warp
+        // instruction (256 partial-sector requests per chunk) had kept the
+        // load/store unit, which also serves the MMA thread's barrier polls,
+        // saturated for most of a 2048-deep tile; these take half the requests.
+        float *crow = static_cast<float *>(p.c) + (int64_t)gm * p.ldc;
 #pragma unroll 1
         for (int c = 0; c < PTILE / 32; ++c) {
           uint32_t r[32];
@@ -493,21 +494,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             if (lane == 0) mbar_arrive_cluster(mapa(smem_u32(&tempty_bar[acc]), 0));
           }
           const int gn0 = tn * PTILE + c * 32;
-          float v[32];
-          chunk_values<EPI>(p, gn0, r, v);
-          uint8_t *buf = stage + (c & 1) * PEPI_BUF_BYTES;
-          // the store that used this buffer two chunks ago has read it
-          if (lane == 0) bulk_wait_group_read<1>();
-          __syncwarp();
+          if (gm < p.m && gn0 + 32 <= p.n) {
+            float v[32];
+            chunk_values<EPI>(p, gn0, r, v);
 #pragma unroll
-          for (int q = 0; q < 8; ++q)  // 16-byte piece q of the row at q ^ (row & 7)
-            *reinterpret_cast<float4 *>(buf + lane * 128 + ((q ^ (lane & 7)) << 4)) =
-                make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0 && row0 < p.m && gn0 < p.n) {  // the box's part beyond m, n is not written
-            tma_store_2d(&tma_c, buf, gn0, row0);
-            bulk_commit_group();
+            for (int q = 0; q < 4; ++q) st_global_v8(crow + gn0 + 8 * q, v + 8 * q);
+          } else {
+            store_chunk<OUT, EPI>(p, gm, gn0, r);
           }
         }
       } else {
@@ -523,7 +516,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         if (lane == 0) mbar_arrive_cluster(mapa(smem_u32(&tempty_bar[acc]), 0));
       }
     }
-    if (lane == 0) bulk_wait_group0();
   }
 
   __syncthreads();
@@ -622,7 +614,7 @@ int launch_tc(const void *a, const void *b, const float *bias, void *c, int m, i
   const int elem = OUT == LC_F32 ? 4 : 2;
   p.vec_store = aligned(c, 16) && ((int64_t)n * elem) % 16 == 0;
   p.serpentine = 0;
-  p.tma_store = 0;
+  p.c_vec8 = 0;
   if (int rc = device_error_word(&p.err)) return rc;
   auto kernel = gemm_tc_kernel<BF16, B_MN, OUT, EPI>;
   static bool configured[64] = {false};
@@ -641,26 +633,10 @@ int launch_tc(const void *a, const void *b, const float *bias, void *c, int m, i
   return check_launch("lc_gemm");
 }
 
-// f32 [outer, inner] row-major, box 32 x 32, 128-byte swizzle (the f32 C tile
-// stores of the 2-SM kernel).
-int make_map_2d_f32(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer) {
-  auto fn = encode_fn();
-  if (!fn) return fail(LC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {inner * 4};
-  cuuint32_t box[2] = {32, 32};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims, strides, box,
-                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(LC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return LC_OK;
-}
-
 template <bool BF16, bool B_MN, int OUT, int EPI>
 int launch_tc2(const void *a, const void *b, const float *bias, void *c, int m, int n, int k,
                cudaStream_t s, bool any_k_order) {
-  CUtensorMap ta, tb, tcmap;
+  CUtensorMap ta, tb;
   if (int rc = make_map_2d(&ta, BF16, a, k, m, (uint64_t)k * 2, BK, PBM)) return rc;
   if (B_MN) {
     if (int rc = make_map_2d(&tb, BF16, b, n, k, (uint64_t)n * 2, 64, BK)) return rc;
@@ -679,12 +655,8 @@ int launch_tc2(const void *a, const void *b, const float *bias, void *c, int m, 
   const int elem = OUT == LC_F32 ? 4 : 2;
   p.vec_store = aligned(c, 16) && ((int64_t)n * elem) % 16 == 0;
   p.serpentine = any_k_order ? 1 : 0;
-  // f32 C by TMA stores when its base and rows are 16-byte aligned
-  p.tma_store = OUT == LC_F32 && aligned(c, 16) && n % 4 == 0;
-  memset(&tcmap, 0, sizeof(tcmap));
-  if (p.tma_store)
-    if (int rc = make_map_2d_f32(&tcmap, c, (uint64_t)n, (uint64_t)m)) return rc;
-  const int smem_bytes = PSMEM_BYTES + (OUT == LC_F32 ? PEPI_BYTES : 0);
+  // f32 C rows as 32-byte vectors when its base and rows are 32-byte aligned
+  p.c_vec8 = OUT == LC_F32 && aligned(c, 32) && n % 8 == 0;
   if (int rc = device_error_word(&p.err)) return rc;
   auto kernel = gemm_tc2_kernel<BF16, B_MN, OUT, EPI>;
   static bool configured[64] = {false};
@@ -692,7 +664,7 @@ int launch_tc2(const void *a, const void *b, const float *bias, void *c, int m, 
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
     if (int rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 smem_bytes),
+                                                 PSMEM_BYTES),
                             "gemm (2-SM) smem attribute"))
       return rc;
     configured[dev] = true;
@@ -705,7 +677,7 @@ int launch_tc2(const void *a, const void *b, const float *bias, void *c, int m, 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(sm_count(), 1, 1);
     cfg.blockDim = dim3(THREADS, 1, 1);
-    cfg.dynamicSmemBytes = smem_bytes;
+    cfg.dynamicSmemBytes = PSMEM_BYTES;
     int clusters = 0;
     if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters < 1) {
       cudaGetLastError();
@@ -716,7 +688,7 @@ int launch_tc2(const void *a, const void *b, const float *bias, void *c, int m, 
   int clusters = (dev >= 0 && dev < 64) ? resident[dev] : sm_count() / 2;
   if (clusters > tiles) clusters = tiles;
   if (clusters < 1) clusters = 1;
-  kernel<<<2 * clusters, THREADS, smem_bytes, s>>>(ta, tb, tcmap, p);
+  kernel<<<2 * clusters, THREADS, PSMEM_BYTES, s>>>(ta, tb, p);
   return check_launch("lc_gemm (2-SM)");
 }
 

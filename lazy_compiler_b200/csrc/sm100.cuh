@@ -1,5 +1,5 @@
 // sm_100a building blocks written as inline PTX: mbarriers with time-bounded
-// waits, TMA tensor loads (no multicast) and stores, tcgen05 TMEM allocation, MMA,
+// waits, TMA tensor loads (no multicast), tcgen05 TMEM allocation, MMA,
 // commit and loads, and the shared-memory / instruction descriptors.
 //
 // Descriptor layouts (PTX ISA, tcgen05 "shared memory descriptor" and
@@ -128,39 +128,6 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
       " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
       : "memory");
-}
-
-// 2-D tiled TMA store of a shared-memory box (c0 innermost) into global
-// memory; elements of the box beyond the tensor's extent are not written.
-// The copy joins the thread's current bulk group (see bulk_commit_group).
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int32_t c0,
-                                             int32_t c1) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(smem_u32(src)), "r"(c0), "r"(c1)
-               : "memory");
-}
-
-__device__ __forceinline__ void bulk_commit_group() {
-  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
-
-// Waits until at most N of the thread's committed bulk stores still have to
-// read their shared-memory sources (the others' buffers may be written again).
-template <int N>
-__device__ __forceinline__ void bulk_wait_group_read() {
-  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-
-// Waits until all of the thread's committed bulk stores have completed.
-__device__ __forceinline__ void bulk_wait_group0() {
-  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-}
-
-// Orders this thread's generic-proxy shared-memory writes before later
-// async-proxy (TMA) reads of them.
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- clusters
