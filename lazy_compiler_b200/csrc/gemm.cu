@@ -60,7 +60,7 @@ struct GemmParams {
   int tiles_m, tiles_n;
   int vec_store;
   int serpentine;     // the 2-SM kernel may walk K backwards on every other tile
-  int c_vec8;        // the 2-SM kernel may store f32 C rows as 32-byte vectors
+  int c_vec8;        // f32 C rows may be stored as 32-byte vectors (32-byte aligned)
   int *err;
 };
 
@@ -80,6 +80,13 @@ __device__ __forceinline__ void raise_error(const GemmParams &p, volatile int *a
   atomicCAS(p.err, 0, code);
 }
 
+// One 32-byte store of eight f32 values (the address is 32-byte aligned).
+__device__ __forceinline__ void st_global_v8(float *dst, const float *v) {
+  asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "f"(v[0]), "f"(v[1]),
+               "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+               : "memory");
+}
+
 template <int OUT, int EPI>
 __device__ __forceinline__ void store_chunk(const GemmParams &p, int gm, int gn0,
                                             const uint32_t (&r)[32]) {
@@ -97,7 +104,10 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int gm, int gn0
   const bool full = p.vec_store && gn0 + 32 <= p.n;
   if constexpr (OUT == LC_F32) {
     float *row = static_cast<float *>(p.c) + (int64_t)gm * p.ldc + gn0;
-    if (full) {
+    if (full && p.c_vec8) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) st_global_v8(row + j, v + j);
+    } else if (full) {
 #pragma unroll
       for (int j = 0; j < 32; j += 4)
         *reinterpret_cast<float4 *>(row + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
@@ -124,13 +134,6 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int gm, int gn0
         if (gn0 + j < p.n) row[j] = to_out<T>(v[j]);
     }
   }
-}
-
-// One 32-byte store of eight f32 values (the address is 32-byte aligned).
-__device__ __forceinline__ void st_global_v8(float *dst, const float *v) {
-  asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "f"(v[0]), "f"(v[1]),
-               "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
-               : "memory");
 }
 
 // The 32 f32 results of one accumulator chunk with bias and activation applied
@@ -614,7 +617,7 @@ int launch_tc(const void *a, const void *b, const float *bias, void *c, int m, i
   const int elem = OUT == LC_F32 ? 4 : 2;
   p.vec_store = aligned(c, 16) && ((int64_t)n * elem) % 16 == 0;
   p.serpentine = 0;
-  p.c_vec8 = 0;
+  p.c_vec8 = OUT == LC_F32 && aligned(c, 32) && n % 8 == 0;
   if (int rc = device_error_word(&p.err)) return rc;
   auto kernel = gemm_tc_kernel<BF16, B_MN, OUT, EPI>;
   static bool configured[64] = {false};
