@@ -54,8 +54,16 @@ struct SdpaParams {
   int q_blocks, items;  // QT-tile query blocks per head; work items = heads x q_blocks
   float scale_log2;
   __half *o;
+  int o_vec8;  // O is 32-byte aligned: rows are written with 32-byte stores
   int *err;
 };
+
+// One 32-byte store of eight 32-bit words (the address is 32-byte aligned).
+__device__ __forceinline__ void st_global_v8_b32(void *dst, const uint32_t *v) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "r"(v[0]), "r"(v[1]),
+               "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -423,24 +431,37 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float inv = 1.0f / l;
       const int q = (qb * QT + t) * BQ + row;
       __half *out = p.o + ((int64_t)bh * p.s_q + q) * HEAD;
+      // Each thread writes its row; 32-byte vector stores (full sectors) where
+      // O is 32-byte aligned keep the load/store unit's request count, which
+      // the other tile's barrier polls share, at half that of 16-byte stores.
 #pragma unroll 1
-      for (int c = 0; c < HEAD / 16; ++c) {
-        uint32_t o[16];
-        tmem_ld16(tmem + lane_base + o_col + c * 16, o);
+      for (int c = 0; c < HEAD / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tmem + lane_base + o_col + c * 32, o);
         tmem_wait_ld();
+        if (c == HEAD / 32 - 1) {
+          // O of this tile may now be overwritten by the next item's first PV
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&o_empty[t]);
+        }
         if (q < p.s_q) {
-          uint4 pack[2];
-          __half *h = reinterpret_cast<__half *>(pack);
+          uint32_t h[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) h[i] = __float2half_rn(__uint_as_float(o[i]) * inv);
-          reinterpret_cast<uint4 *>(out + c * 16)[0] = pack[0];
-          reinterpret_cast<uint4 *>(out + c * 16)[1] = pack[1];
+          for (int i = 0; i < 16; ++i) {
+            __half2 hh = __floats2half2_rn(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+            h[i] = *reinterpret_cast<uint32_t *>(&hh);
+          }
+          if (p.o_vec8) {
+            st_global_v8_b32(out + c * 32, h);
+            st_global_v8_b32(out + c * 32 + 16, h + 8);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              reinterpret_cast<uint4 *>(out + c * 32)[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+          }
         }
       }
-      // O of this tile may now be overwritten by the next item's first PV
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_empty[t]);
     }
   }
 
@@ -573,6 +594,7 @@ extern "C" int lc_sdpa_f16(const void *q, const void *k, const void *v, void *o,
   p.n_kv = (int)((s_kv + BKV - 1) / BKV);
   p.scale_log2 = scale * 1.4426950408889634f;
   p.o = static_cast<__half *>(o);
+  p.o_vec8 = aligned(o, 32) ? 1 : 0;
   if (int rc = device_error_word(&p.err)) return rc;
   static bool configured[64] = {false};
   int dev = 0;
