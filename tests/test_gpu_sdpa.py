@@ -154,3 +154,20 @@ def test_tcgen05_running_max_paths(case, cuda_device):
     o = run_sdpa(tq, tk, tv, 1.0)
     ref = O.sdpa_f16(q.astype(np.float32), k.astype(np.float32), v.astype(np.float32), 1.0)[0]
     check(o.float().cpu().numpy(), ref)
+
+
+def test_tcgen05_output_16_byte_aligned_only(cuda_device):
+    """O at a 16-byte (not 32-byte) offset: the tensor-core path's 16-byte row stores."""
+    import torch
+    bh, s, d = 2, 256, 128
+    q, k, v, tq, tk, tv = inputs(bh, s, s, d, seed=21)
+    buf = torch.full((bh * s * d + 8,), float("nan"), dtype=torch.float16, device="cuda")
+    o = buf[8:].view(bh, s, d)
+    assert o.data_ptr() % 32 == 16
+    assert runtime.library().lc_sdpa_path(P(tq), P(tk), P(tv), P(o), s, s, d) == 1
+    scale = 1 / math.sqrt(d)
+    runtime.call("lc_sdpa_f16", P(tq), P(tk), P(tv), P(o), bh, s, s, d, ctypes.c_float(scale), None)
+    runtime.call("lc_device_status", None)
+    ref = O.sdpa_f16(q.astype(np.float32), k.astype(np.float32), v.astype(np.float32), scale)[0]
+    check(o.float().cpu().numpy(), ref)
+    assert torch.isnan(buf[:8]).all()  # nothing written before O
